@@ -1,0 +1,249 @@
+/*
+ * qne.h - C ABI of the B200 decode engine for Qwen3.5-shaped hybrid decoders.
+ *
+ * The model-level entry points replace the public API of the `qwen-kernels` crate
+ * (`kernels/src/model.rs`, struct `Model`); the operator-level entry points replace the
+ * per-kernel WGSL dispatches of `kernels/src/shaders.rs` that the crate's self-checks
+ * (`kernels/src/lib.rs:513-712`) exercise. Every pointer argument of an operator-level
+ * entry point is DEVICE memory unless the comment says "host"; every model-level entry
+ * point takes HOST buffers.
+ *
+ * Status codes: 0 on success, a negative QNE_E* code on failure; qne_last_error() returns
+ * the message of the last failure on the calling thread. No entry point aborts on bad input.
+ * Handles are not thread-safe: one host thread drives one model (as in the reference, where one
+ * inference worker owns the `Model`).
+ */
+#ifndef QNE_H
+#define QNE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Symbols of the shared library; everything else in it is hidden. */
+#if defined(__GNUC__)
+#define QNE_API __attribute__((visibility("default")))
+#else
+#define QNE_API
+#endif
+
+typedef int32_t qne_status;
+
+#define QNE_OK 0
+#define QNE_EINVAL (-1)     /* bad argument, null handle, size out of range */
+#define QNE_ERANGE_CTX (-2) /* context limit (4096 tokens) reached */
+#define QNE_EFORMAT (-3)    /* index.json / weights.bin rejected by validation */
+#define QNE_ECUDA (-4)      /* a CUDA call failed */
+#define QNE_ETIMEOUT (-5)   /* a device wait ran past its deadline */
+#define QNE_ENOSNAP (-6)    /* restore without a snapshot */
+#define QNE_ENOMEM (-7)     /* device allocation failed */
+
+/* Upper bound of the attention context, kernels/src/shaders.rs:34 (MAX_CONTEXT). */
+#define QNE_MAX_CONTEXT 4096
+/* Tokens per KV-cache page. */
+#define QNE_PAGE_TOKENS 16
+
+/* Weight storage kinds of one matrix. kernels/src/lib.rs:141-155 (QMat) defines QNE_Q4; the
+ * other two are the f16 and group-64 kinds the B200 engine adds. */
+#define QNE_KIND_F16 0   /* f16 [rows][k] row-major */
+#define QNE_KIND_Q4 1    /* MatMulNBits block 32: u32 w[rows*k/8], u32 s[rows*k/64] (f16 pairs), u32 z[rows*k/256] (4-bit zp) */
+#define QNE_KIND_Q4G64 2 /* group 64: u32 w[rows*k/8], f16 s[rows*k/64], f16 z[rows*k/64] */
+
+/* GEMV epilogues, kernels/src/shaders.rs:36-43 (Epilogue). */
+#define QNE_EPI_STORE 0      /* y[r] = W x */
+#define QNE_EPI_ACCUMULATE 1 /* y[r] += W x (residual stream) */
+#define QNE_EPI_SWIGLU 2     /* y[r] = silu(W[r] x) * W[r + rows/2] x */
+
+typedef struct qne_model qne_model;
+typedef struct qne_batch qne_batch;
+
+/* One weight matrix in device memory; s and z are unused (NULL) for QNE_KIND_F16. */
+typedef struct qne_matrix {
+  int32_t kind;
+  int32_t rows; /* physical rows (for SwiGLU: gate rows then up rows) */
+  int32_t k;
+  int32_t pad;
+  const void* w;
+  const void* s;
+  const void* z;
+} qne_matrix;
+
+typedef struct qne_model_info {
+  int32_t layers;
+  int32_t hidden;
+  int32_t intermediate;
+  int32_t vocab;
+  int32_t weight_kind;     /* kind of the layer matrices */
+  int32_t embed_kind;      /* kind of the embedding / LM head */
+  int32_t tied_lm_head;    /* 1 when lm_head shares the embedding's bytes */
+  int32_t device;
+  uint64_t weight_bytes;   /* bytes read by one decode token: every matrix once, LM head once */
+  uint64_t device_bytes;   /* device memory held by the model */
+} qne_model_info;
+
+/* ---------------------------------------------------------------------------------------- */
+/* Library                                                                                   */
+/* ---------------------------------------------------------------------------------------- */
+
+/* Message of the last failed call on this thread ("" if none). */
+QNE_API const char* qne_last_error(void);
+QNE_API const char* qne_version(void);
+/* Number of kernel launches this library issued on the calling process so far. */
+QNE_API uint64_t qne_kernel_launches(void);
+
+/* ---------------------------------------------------------------------------------------- */
+/* Model: kernels/src/model.rs (struct Model)                                               */
+/* ---------------------------------------------------------------------------------------- */
+
+/* Model::load, kernels/src/model.rs:171. Parses and validates index.json (host, n bytes, not
+ * NUL-terminated) against weights (host, weights_len bytes) as Index::validate does
+ * (kernels/src/model.rs:51-86), uploads every tensor once per (offset, bytes) pair, and builds
+ * the per-token launch graph. The caller may free both host buffers after the call. */
+QNE_API qne_status qne_model_load(const char* index_json, size_t index_len, const void* weights,
+                          size_t weights_len, int device, qne_model** out);
+QNE_API void qne_model_free(qne_model* m);
+QNE_API qne_status qne_model_info_get(const qne_model* m, qne_model_info* out);
+/* Runs the model's work on `cuda_stream` (a cudaStream_t of the model's device; NULL = the
+ * model's own stream). */
+QNE_API qne_status qne_model_set_stream(qne_model* m, void* cuda_stream);
+/* Model::adapter, kernels/src/model.rs:167. */
+QNE_API const char* qne_adapter(const qne_model* m);
+/* Model::dispatches_per_token, kernels/src/model.rs:309. */
+QNE_API size_t qne_dispatches_per_token(const qne_model* m);
+/* ModelTiles::validate, kernels/src/model.rs:101-109: accepts the reference's tile-profile
+ * JSON for API compatibility (the CUDA kernels choose their own shapes). */
+QNE_API qne_status qne_validate_tiles(const char* tiles_json, size_t len);
+
+/* Model::reset, kernels/src/model.rs:314: clears recurrent state, conv windows, KV cache. */
+QNE_API qne_status qne_reset(qne_model* m);
+/* Model::prefill, kernels/src/model.rs:324: prompt from position 0, one token per step;
+ * afterwards logits hold the prediction after the last id and the greedy pick is stored. */
+QNE_API qne_status qne_prefill(qne_model* m, const uint32_t* ids, uint32_t n);
+/* Model::prefill_chunk, kernels/src/model.rs:349 (prefill_from / prefill_batched are
+ * prefill_chunk with finish_logits = 1). Fails when start + n >= QNE_MAX_CONTEXT. */
+QNE_API qne_status qne_prefill_chunk(qne_model* m, const uint32_t* ids, uint32_t n, uint32_t start,
+                             int finish_logits);
+/* Model::logits, kernels/src/model.rs:374: copies vocab f32 logits to host `out`. */
+QNE_API qne_status qne_logits(qne_model* m, float* out, size_t out_len);
+/* Model::step, kernels/src/model.rs:380: feeds `token` at `pos`, returns the next-token logits
+ * in host `logits_out` (vocab floats). The stored greedy pick is not updated. */
+QNE_API qne_status qne_step(qne_model* m, uint32_t token, uint32_t pos, float* logits_out,
+                    size_t out_len);
+/* Model::snapshot / restore, kernels/src/model.rs:395-414. */
+QNE_API qne_status qne_snapshot(qne_model* m);
+QNE_API qne_status qne_restore(qne_model* m);
+/* Model::last_token, kernels/src/model.rs:417: greedy pick and next position. */
+QNE_API qne_status qne_last_token(qne_model* m, uint32_t* token, uint32_t* pos);
+/* Model::decode, kernels/src/model.rs:426: greedy decoding, `window` tokens per host sync;
+ * ids_out (host, capacity n) receives the first pick then one id per step (UINT32_MAX inside
+ * windows > 1, as in the reference); stops after a stop id. */
+QNE_API qne_status qne_decode(qne_model* m, uint32_t n, uint32_t window, const uint32_t* stop,
+                      uint32_t nstop, uint32_t* ids_out, uint32_t* n_out);
+/* Enqueues `steps` greedy decode steps on the model's stream and returns without waiting
+ * (device-resident loop; used to time the engine). Fails if the context would overflow. */
+QNE_API qne_status qne_decode_async(qne_model* m, uint32_t steps);
+/* Enqueues one host-token step (Model::step without the readback). */
+QNE_API qne_status qne_step_async(qne_model* m, uint32_t token, uint32_t pos);
+/* Waits for the model's stream, polling with a deadline (QNE_ETIMEOUT after timeout_ms). */
+QNE_API qne_status qne_sync(qne_model* m, uint32_t timeout_ms);
+/* Device descriptor of a loaded matrix: "embed", "lm_head" or "layer<i>.<mixer_in|mixer_out|
+ * gate_up|down>" (the index.json names). */
+QNE_API qne_status qne_model_matrix(const qne_model* m, const char* name, qne_matrix* out);
+/* Device pointer of a loaded f32 vector: "final_norm", "layer<i>.<input_norm|post_norm|
+ * attn_norms|conv_w|gdn_params>". */
+QNE_API qne_status qne_model_tensor(const qne_model* m, const char* name, const void** out);
+/* Device pointer of the f32 logits buffer (vocab floats). */
+QNE_API const float* qne_logits_device(const qne_model* m);
+
+/* ---------------------------------------------------------------------------------------- */
+/* Batched decode: independent sequences sharing one weight copy                            */
+/* ---------------------------------------------------------------------------------------- */
+
+/* Creates `batch` independent sequences, each with its own GDN states and a page table of
+ * QNE_MAX_CONTEXT / QNE_PAGE_TOKENS entries into a shared pool of `pool_pages` pages per
+ * attention layer (pool_pages >= batch * 256). The default page table maps sequence b's
+ * logical page i to physical page b * 256 + i. */
+QNE_API qne_status qne_batch_create(qne_model* m, uint32_t batch, uint32_t pool_pages, qne_batch** out);
+QNE_API void qne_batch_free(qne_batch* b);
+/* Replaces the page tables (host, batch x 256 entries, each < pool_pages). */
+QNE_API qne_status qne_batch_set_page_table(qne_batch* b, const uint32_t* table, size_t n);
+QNE_API qne_status qne_batch_reset(qne_batch* b);
+/* One decode step for every sequence: tokens[i] at pos[i] (host arrays of `batch`).
+ * logits_out (host, batch x vocab) and next_out (host, batch greedy picks) may be NULL. */
+QNE_API qne_status qne_batch_step(qne_batch* b, const uint32_t* tokens, const uint32_t* pos,
+                          float* logits_out, uint32_t* next_out);
+/* Enqueues `steps` greedy steps for all sequences (each feeds back its own pick). */
+QNE_API qne_status qne_batch_decode_async(qne_batch* b, uint32_t steps);
+/* Copies the current (token, pos) pairs to host arrays of `batch`. */
+QNE_API qne_status qne_batch_tokens(qne_batch* b, uint32_t* tokens, uint32_t* pos);
+/* Writes synthetic history into sequence `seq` for positions [0, len): K/V pages filled from
+ * (seed) and GDN states and conv windows from (seed); sets (token, pos) = (token, len). Used by
+ * throughput runs whose prompts would take minutes to prefill. */
+QNE_API qne_status qne_batch_fill_synthetic(qne_batch* b, uint32_t seq, uint32_t len, uint32_t token,
+                                    uint64_t seed);
+QNE_API qne_status qne_batch_sync(qne_batch* b, uint32_t timeout_ms);
+
+/* ---------------------------------------------------------------------------------------- */
+/* Operators (device pointers; `stream` is a cudaStream_t or NULL for the legacy stream)     */
+/* ---------------------------------------------------------------------------------------- */
+
+/* gemv / gemv_f16 / gemv_split_f16 + split_reduce, kernels/src/shaders.rs:48-376:
+ * y (= / += / silu-gated) W x for one f32 vector x[k]. For QNE_EPI_SWIGLU, m->rows is the
+ * physical row count and y has m->rows / 2 entries. */
+QNE_API qne_status qne_gemv(const qne_matrix* m, const float* x, float* y, int epilogue, void* stream);
+/* rmsnorm_width (kernels/src/shaders.rs:380-403) fused in front of the GEMV:
+ * x = h * rsqrt(mean(h^2) + eps) * norm_w. */
+QNE_API qne_status qne_rmsnorm_gemv(const qne_matrix* m, const float* h, const float* norm_w, float eps,
+                            float* y, int epilogue, void* stream);
+/* Batched GEMV/GEMM over `batch` f32 vectors x[batch][k] -> y[batch][out_rows]. Uses the
+ * tensor cores for batch >= 2. `scratch` must hold qne_gemm_scratch_bytes(m, batch) bytes. */
+QNE_API size_t qne_gemm_scratch_bytes(const qne_matrix* m, int batch);
+QNE_API qne_status qne_gemm(const qne_matrix* m, const float* x, int batch, float* y, int epilogue,
+                    void* scratch, size_t scratch_bytes, void* stream);
+/* Dequantized rows [row0, row0 + nrows) of m into out[nrows][k] f32, through the same unpack
+ * code as the GEMV (QMat layout, kernels/src/lib.rs:484-497 dequant_row). */
+QNE_API qne_status qne_dequant_rows(const qne_matrix* m, int row0, int nrows, float* out, void* stream);
+/* embed_width, kernels/src/shaders.rs:409-434: h = deq(E[tok[0]]). */
+QNE_API qne_status qne_embed(const qne_matrix* e, const uint32_t* tok, float* h, void* stream);
+/* argmax_partial + argmax_final, kernels/src/shaders.rs:636-699: tok[0] = index of the
+ * largest logit (lowest index among equal maxima, NaN never wins), tok[1] += 1.
+ * `scratch` must hold qne_argmax_scratch_bytes(n) bytes. */
+QNE_API size_t qne_argmax_scratch_bytes(uint32_t n);
+QNE_API qne_status qne_argmax(const float* logits, uint32_t n, uint32_t* tok, void* scratch,
+                      size_t scratch_bytes, void* stream);
+
+/* gdn, kernels/src/shaders.rs:445-520, for `batch` sequences. proj[batch][8224]; conv ring
+ * conv[batch][4][6144] (slot (count-1)%4 receives this step's input, the three before it are the
+ * window); conv_w[6144*4]; state[batch][16][128][128]; params[160] = dt_bias, A_neg_exp,
+ * norm_w; counter[batch] = tokens processed including this one (read only).
+ * out[batch][2048] receives the gated, normalized output (kernels/src/shaders.rs:512-516). */
+QNE_API qne_status qne_gdn_step(const float* proj, float* conv, const float* conv_w, float* state,
+                        const float* params, const uint32_t* counter, float* out, int batch,
+                        void* stream);
+
+/* attention, kernels/src/shaders.rs:531-633, over a paged f16 KV cache, for `batch`
+ * sequences. proj[batch][5120]; norms[512] = q_norm, k_norm; RoPE angles pos * theta^(-2i/64);
+ * kv: pool of `pool_pages` pages, each [2 (K,V)][2 kv heads][16 tokens][256] f16;
+ * page_table[batch][256] (entries < pool_pages); pos[batch] is the current token's position
+ * (its K/V are written to the cache before use). out[batch][2048].
+ * `scratch` must hold qne_attention_scratch_bytes(batch) bytes, zero-filled before first use. */
+QNE_API size_t qne_attention_scratch_bytes(int batch);
+QNE_API qne_status qne_attention_step(const float* proj, const float* norms, double rope_theta, void* kv,
+                              uint32_t pool_pages, const uint32_t* page_table, const uint32_t* pos,
+                              float* out, int batch, void* scratch, size_t scratch_bytes,
+                              void* stream);
+/* Gathers the K and V rows of positions [0, len) of one sequence through its page table into
+ * contiguous out_k/out_v [2 kv heads][len][256] f16 (bit copy). */
+QNE_API qne_status qne_kv_gather(const void* kv, const uint32_t* page_table, uint32_t len, void* out_k,
+                         void* out_v, void* stream);
+
+/* Streaming-read probe, kernels/src/shaders.rs:703-717: XOR of `bytes` (multiple of 16). */
+QNE_API qne_status qne_bandwidth_probe(const void* data, size_t bytes, uint32_t* sink, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QNE_H */

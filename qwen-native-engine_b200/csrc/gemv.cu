@@ -1,0 +1,569 @@
+// Batch-1 GEMV for the decode step: f16, MatMulNBits block-32 int4 and group-64 int4 weights.
+//
+// Follows gemv / gemv_f16 / gemv_split_f16 (kernels/src/shaders.rs:48-376) in what it computes:
+// y[r] (=, +=, silu-gated) sum_k deq(W[r, k]) x[k], accumulated in f32. The B200 design differs:
+//  * one warp owns NR output rows at a time; every lane streams 16-byte chunks of those rows
+//    with L1-bypassing loads, U chunks per row in flight, and reduces with warp shuffles;
+//  * the CTA stages x in shared memory once, through a fused prologue: plain copy, RMSNorm
+//    (rmsnorm_width, kernels/src/shaders.rs:380-403), the gated per-head RMSNorm that ends the
+//    GDN step (kernels/src/shaders.rs:512-516), or embedding gather + RMSNorm
+//    (embed_width, kernels/src/shaders.rs:409-434);
+//  * the epilogue stores, accumulates into the residual stream, applies SwiGLU, or stores logits
+//    and runs the greedy pick (argmax_partial + argmax_final, kernels/src/shaders.rs:636-699) in
+//    the last CTA to finish;
+//  * launches use programmatic dependent launch: the CTA first asks the TMA unit to prefetch its
+//    weight rows into L2, then waits for the previous kernel, so weight streaming overlaps the
+//    previous kernel's tail and the launch gap.
+#include <math.h>
+
+#include <atomic>
+
+#include "gemv.cuh"
+
+namespace qne {
+
+static std::atomic<uint64_t> g_launches{0};
+uint64_t launches_issued() { return g_launches.load(std::memory_order_relaxed); }
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr uint32_t kPrefetchBytes = 96u << 10;  // per CTA, issued before the dependency wait
+constexpr uint32_t kPrefetchPiece = 8u << 10;
+
+template <int KIND>
+struct Fmt;
+template <>
+struct Fmt<kF16> {
+  static constexpr int CV = 8;  // values per 16-byte chunk
+  static __host__ __device__ size_t row_bytes(int k) { return (size_t)k * 2; }
+};
+template <>
+struct Fmt<kQ4> {
+  static constexpr int CV = 32;
+  static __host__ __device__ size_t row_bytes(int k) { return (size_t)k / 2; }
+};
+template <>
+struct Fmt<kQ4G64> {
+  static constexpr int CV = 32;
+  static __host__ __device__ size_t row_bytes(int k) { return (size_t)k / 2; }
+};
+
+// Dequantized value of element (row, i) - the unpack used by dequant_rows and the embedding.
+__device__ __forceinline__ float deq_elem(const Mat& m, long row, int i) {
+  if (m.kind == kF16) {
+    return h2f(__ldg((const uint16_t*)m.w + row * m.k + i));
+  }
+  const uint32_t word = __ldg((const uint32_t*)m.w + row * (m.k / 8) + i / 8);
+  const float q = nib_f(word, 4 * (i % 8));
+  float scale, zp;
+  if (m.kind == kQ4) {
+    q4_scale_zp((const uint32_t*)m.s, (const uint32_t*)m.z, row, m.k, i / 32, scale, zp);
+  } else {
+    q4g64_scale_zp((const uint16_t*)m.s, (const uint16_t*)m.z, row, m.k, i / 64, scale, zp);
+  }
+  return (q - zp) * scale;
+}
+
+// Issues L2 prefetches of rows [r0, r1) (up to `budget` bytes); called by one warp.
+__device__ __forceinline__ void prefetch_rows(const uint8_t* base, size_t row_bytes, long r0,
+                                              long r1, uint32_t budget, int lane) {
+  if (r1 <= r0) return;
+  size_t bytes = (size_t)(r1 - r0) * row_bytes;
+  if (bytes > budget) bytes = budget;
+  bytes &= ~(size_t)15;
+  const uint8_t* p = base + (size_t)r0 * row_bytes;
+  for (size_t off = (size_t)lane * kPrefetchPiece; off < bytes; off += 32 * kPrefetchPiece) {
+    const size_t n = bytes - off < kPrefetchPiece ? bytes - off : kPrefetchPiece;
+    prefetch_l2(p + off, (uint32_t)n);
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// Prologues: stage the f32 input vector of length k in shared memory.
+// ------------------------------------------------------------------------------------------
+template <int PRO>
+__device__ __forceinline__ void stage_x(const GemvArgs& a, float* xs, float* red) {
+  const int k = a.m.k;
+  const int tid = threadIdx.x;
+  if (PRO == kProCopy) {
+    for (int i = tid * 4; i < k; i += kThreads * 4)
+      *reinterpret_cast<float4*>(xs + i) = *reinterpret_cast<const float4*>(a.x + i);
+  } else if (PRO == kProRmsNorm || PRO == kProEmbedNorm) {
+    float ss = 0.f;
+    if (PRO == kProRmsNorm) {
+      for (int i = tid * 4; i < k; i += kThreads * 4) {
+        const float4 v = *reinterpret_cast<const float4*>(a.x + i);
+        *reinterpret_cast<float4*>(xs + i) = v;
+        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+      }
+    } else {
+      // Embedding row of the token the previous step picked (or the host wrote).
+      uint32_t token = a.ctl->token;
+      if (token >= (uint32_t)a.embed.rows) token = (uint32_t)a.embed.rows - 1;
+      for (int i = tid; i < k; i += kThreads) {
+        const float v = deq_elem(a.embed, token, i);
+        xs[i] = v;
+        ss += v * v;
+      }
+      if (blockIdx.x == 0) {
+        for (int i = tid; i < k; i += kThreads) a.h_out[i] = xs[i];
+        if (tid == 0) a.ctl->count += 1;  // one more token entered the conv windows
+      }
+    }
+    const float tot = block_sum<kThreads>(ss, red);
+    const float inv = rsqrtf(tot / (float)k + a.eps);
+    for (int i = tid; i < k; i += kThreads) xs[i] = xs[i] * inv * a.norm_w[i];
+  } else if (PRO == kProGdnGate) {
+    // k == 2048: 16 heads of 128; warp w normalizes heads 2w and 2w+1.
+    const int warp = tid >> 5, lane = tid & 31;
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int head = warp * 2 + hh;
+      const int base = head * kGdnDim + lane * 4;
+      const float4 v = *reinterpret_cast<const float4*>(a.x + base);
+      const float ss = warp_sum(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w);
+      const float inv = rsqrtf(ss / (float)kGdnDim + a.eps);
+      const float4 zz = *reinterpret_cast<const float4*>(a.zgate + base);
+      const float4 nw = *reinterpret_cast<const float4*>(a.norm_w + lane * 4);
+      xs[base + 0] = v.x * inv * silu(zz.x) * nw.x;
+      xs[base + 1] = v.y * inv * silu(zz.y) * nw.y;
+      xs[base + 2] = v.z * inv * silu(zz.z) * nw.z;
+      xs[base + 3] = v.w * inv * silu(zz.w) * nw.w;
+    }
+  }
+  __syncthreads();
+}
+
+// ------------------------------------------------------------------------------------------
+// Chunk dot products: 16 bytes of one row against the matching slice of x in shared memory.
+// ------------------------------------------------------------------------------------------
+__device__ __forceinline__ float dot_f16(const uint4& w, const float* x) {
+  const float2 a = h2f2(w.x), b = h2f2(w.y), c = h2f2(w.z), d = h2f2(w.w);
+  float p0 = a.x * x[0];
+  float p1 = b.x * x[2];
+  float p2 = c.x * x[4];
+  float p3 = d.x * x[6];
+  p0 = fmaf(a.y, x[1], p0);
+  p1 = fmaf(b.y, x[3], p1);
+  p2 = fmaf(c.y, x[5], p2);
+  p3 = fmaf(d.y, x[7], p3);
+  return (p0 + p1) + (p2 + p3);
+}
+
+// sum_n q_n x_n over the 32 nibbles of a chunk (q exact as floats).
+__device__ __forceinline__ float dot_q4_raw(const uint4& w, const float* x) {
+  const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+  float p[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    float s = nib_f(ws[e], 0) * x[8 * e];
+#pragma unroll
+    for (int n = 1; n < 8; ++n) s = fmaf(nib_f(ws[e], 4 * n), x[8 * e + n], s);
+    p[e] = s;
+  }
+  return (p[0] + p[1]) + (p[2] + p[3]);
+}
+
+template <int KIND, int PRO, int EPI, int NR>
+__global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvArgs a) {
+  extern __shared__ __align__(16) float xs[];
+  __shared__ float red[kWarps];
+  __shared__ float bval[kWarps];
+  __shared__ uint32_t bidx[kWarps];
+  __shared__ uint32_t is_last;
+
+  constexpr int CV = Fmt<KIND>::CV;
+  constexpr int PHYS = (EPI == kSwiGlu) ? 2 * NR : NR;
+  constexpr int U = (KIND == kF16) ? (PHYS == 1 ? 8 : 16 / PHYS) : (PHYS == 1 ? 4 : 8 / PHYS);
+  const int k = a.m.k;
+  const int nch = k / CV;
+  const int out_rows = (EPI == kSwiGlu) ? a.m.rows / 2 : a.m.rows;
+  const long half = (EPI == kSwiGlu) ? a.m.rows / 2 : 0;
+  const size_t rb = Fmt<KIND>::row_bytes(k);
+  const int groups = (out_rows + NR - 1) / NR;
+  const int g0 = (int)((long)blockIdx.x * groups / gridDim.x);
+  const int g1 = (int)((long)(blockIdx.x + 1) * groups / gridDim.x);
+  const uint8_t* W = static_cast<const uint8_t*>(a.m.w);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  pdl_launch();
+  if (warp == 0) {
+    const long r0 = (long)g0 * NR;
+    const long r1 = min((long)g1 * NR, (long)out_rows);
+    const uint32_t budget = (EPI == kSwiGlu) ? kPrefetchBytes / 2 : kPrefetchBytes;
+    prefetch_rows(W, rb, r0, r1, budget, lane);
+    if (EPI == kSwiGlu) prefetch_rows(W, rb, half + r0, half + r1, budget, lane);
+  }
+  pdl_wait();
+  stage_x<PRO>(a, xs, red);
+
+  float best_v = -INFINITY;
+  uint32_t best_i = 0xFFFFFFFFu;
+
+  for (int g = g0 + warp; g < g1; g += kWarps) {
+    long rows[PHYS];
+#pragma unroll
+    for (int i = 0; i < NR; ++i) {
+      const long r = min((long)g * NR + i, (long)out_rows - 1);
+      rows[i] = r;
+      if (EPI == kSwiGlu) rows[NR + i] = half + r;
+    }
+    float acc[PHYS];
+#pragma unroll
+    for (int i = 0; i < PHYS; ++i) acc[i] = 0.f;
+
+    for (int base = 0; base < nch; base += 32 * U) {
+      uint4 wv[PHYS][U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int c = base + u * 32 + lane;
+#pragma unroll
+        for (int i = 0; i < PHYS; ++i)
+          wv[i][u] = (c < nch) ? ld_stream(W + (size_t)rows[i] * rb + (size_t)c * 16)
+                               : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int c = base + u * 32 + lane;
+        if (c < nch) {
+          const float* xc = xs + c * CV;
+          if (KIND == kF16) {
+            float xv[8];
+            *reinterpret_cast<float4*>(xv) = *reinterpret_cast<const float4*>(xc);
+            *reinterpret_cast<float4*>(xv + 4) = *reinterpret_cast<const float4*>(xc + 4);
+#pragma unroll
+            for (int i = 0; i < PHYS; ++i) acc[i] += dot_f16(wv[i][u], xv);
+          } else {
+            float xv[32];
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              *reinterpret_cast<float4*>(xv + 4 * j) = *reinterpret_cast<const float4*>(xc + 4 * j);
+            float xsum = 0.f;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) xsum += xv[j];
+#pragma unroll
+            for (int i = 0; i < PHYS; ++i) {
+              float scale, zp;
+              if (KIND == kQ4)
+                q4_scale_zp((const uint32_t*)a.m.s, (const uint32_t*)a.m.z, rows[i], k, c, scale, zp);
+              else
+                q4g64_scale_zp((const uint16_t*)a.m.s, (const uint16_t*)a.m.z, rows[i], k, c / 2,
+                               scale, zp);
+              const float raw = dot_q4_raw(wv[i][u], xv);
+              acc[i] = fmaf(scale, raw - zp * xsum, acc[i]);
+            }
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < PHYS; ++i) acc[i] = warp_sum(acc[i]);
+
+#pragma unroll
+    for (int i = 0; i < NR; ++i) {
+      const long r = (long)g * NR + i;
+      if (r < out_rows) {
+        if (EPI == kArgmax) {
+          const float v = acc[i];
+          if (v > -INFINITY && (v > best_v || (v == best_v && (uint32_t)r < best_i))) {
+            best_v = v;
+            best_i = (uint32_t)r;
+          }
+        }
+        if (lane == i) {
+          if (EPI == kStore || EPI == kArgmax) a.y[r] = acc[i];
+          else if (EPI == kAccumulate) a.y[r] += acc[i];
+          else if (EPI == kSwiGlu) a.y[r] = silu(acc[i]) * acc[NR + i];
+        }
+      }
+    }
+  }
+
+  if (EPI == kArgmax) {
+    // Per-CTA pick, then the last CTA to finish reduces the per-CTA picks.
+    if (lane == 0) {
+      bval[warp] = best_v;
+      bidx[warp] = best_i;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float v = bval[0];
+      uint32_t ix = bidx[0];
+      for (int w = 1; w < kWarps; ++w) {
+        if (bidx[w] != 0xFFFFFFFFu && (ix == 0xFFFFFFFFu || bval[w] > v || (bval[w] == v && bidx[w] < ix))) {
+          v = bval[w];
+          ix = bidx[w];
+        }
+      }
+      a.part_val[blockIdx.x] = v;
+      a.part_idx[blockIdx.x] = ix;
+      __threadfence();
+      const uint32_t t = atomicAdd(a.ticket, 1u);
+      is_last = (t == gridDim.x - 1) ? 1u : 0u;
+    }
+    __syncthreads();
+    if (is_last && warp == 0) {
+      __threadfence();
+      float v = -INFINITY;
+      uint32_t ix = 0xFFFFFFFFu;
+      for (int b = lane; b < (int)gridDim.x; b += 32) {
+        const float bv = __ldcg(a.part_val + b);
+        const uint32_t bi = __ldcg(a.part_idx + b);
+        if (bi != 0xFFFFFFFFu && (ix == 0xFFFFFFFFu || bv > v || (bv == v && bi < ix))) {
+          v = bv;
+          ix = bi;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+        const uint32_t oi = __shfl_xor_sync(0xffffffffu, ix, o);
+        if (oi != 0xFFFFFFFFu && (ix == 0xFFFFFFFFu || ov > v || (ov == v && oi < ix))) {
+          v = ov;
+          ix = oi;
+        }
+      }
+      if (lane == 0) {
+        if (a.update_token) {
+          a.ctl->token = (ix == 0xFFFFFFFFu) ? 0u : ix;
+          a.ctl->pos += 1;
+        }
+        *a.ticket = 0u;
+      }
+    }
+  }
+}
+
+template <int KIND>
+__global__ void dequant_rows_kernel(const Mat m, int row0, int nrows, float* out) {
+  const long total = (long)nrows * m.k;
+  for (long e = (long)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += (long)gridDim.x * blockDim.x) {
+    const long r = e / m.k;
+    const int i = (int)(e % m.k);
+    out[e] = deq_elem(m, row0 + r, i);
+  }
+}
+
+// Standalone greedy pick over n logits (argmax_partial + argmax_final).
+__global__ void __launch_bounds__(256) argmax_kernel(const float* logits, uint32_t n, SeqCtl* ctl,
+                                                     float* part_val, uint32_t* part_idx,
+                                                     uint32_t* ticket) {
+  __shared__ float bv[8];
+  __shared__ uint32_t bi[8];
+  __shared__ uint32_t is_last;
+  pdl_launch();
+  pdl_wait();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float v = -INFINITY;
+  uint32_t ix = 0xFFFFFFFFu;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const float x = logits[i];
+    if (x > -INFINITY && (ix == 0xFFFFFFFFu || x > v)) {  // indices ascend: ties keep the first
+      v = x;
+      ix = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    const uint32_t oi = __shfl_xor_sync(0xffffffffu, ix, o);
+    if (oi != 0xFFFFFFFFu && (ix == 0xFFFFFFFFu || ov > v || (ov == v && oi < ix))) {
+      v = ov;
+      ix = oi;
+    }
+  }
+  if (lane == 0) {
+    bv[warp] = v;
+    bi[warp] = ix;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    v = -INFINITY;
+    ix = 0xFFFFFFFFu;
+    for (int w = 0; w < 8; ++w)
+      if (bi[w] != 0xFFFFFFFFu && (ix == 0xFFFFFFFFu || bv[w] > v || (bv[w] == v && bi[w] < ix))) {
+        v = bv[w];
+        ix = bi[w];
+      }
+    part_val[blockIdx.x] = v;
+    part_idx[blockIdx.x] = ix;
+    __threadfence();
+    is_last = (atomicAdd(ticket, 1u) == gridDim.x - 1) ? 1u : 0u;
+  }
+  __syncthreads();
+  if (is_last && warp == 0) {
+    __threadfence();
+    v = -INFINITY;
+    ix = 0xFFFFFFFFu;
+    for (int b = lane; b < (int)gridDim.x; b += 32) {
+      const float ov = __ldcg(part_val + b);
+      const uint32_t oi = __ldcg(part_idx + b);
+      if (oi != 0xFFFFFFFFu && (ix == 0xFFFFFFFFu || ov > v || (ov == v && oi < ix))) {
+        v = ov;
+        ix = oi;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+      const uint32_t oi = __shfl_xor_sync(0xffffffffu, ix, o);
+      if (oi != 0xFFFFFFFFu && (ix == 0xFFFFFFFFu || ov > v || (ov == v && oi < ix))) {
+        v = ov;
+        ix = oi;
+      }
+    }
+    if (lane == 0) {
+      ctl->token = (ix == 0xFFFFFFFFu) ? 0u : ix;
+      ctl->pos += 1;
+      *ticket = 0u;
+    }
+  }
+}
+
+template <typename Kernel>
+cudaError_t launch_ex(Kernel kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                      bool pdl, const GemvArgs& a) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  count_launch();
+  return cudaLaunchKernelEx(&cfg, kernel, a);
+}
+
+template <int KIND, int PRO, int EPI, int NR>
+cudaError_t launch_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
+  auto kernel = gemv_kernel<KIND, PRO, EPI, NR>;
+  const size_t smem = (size_t)a.m.k * sizeof(float);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  const int out_rows = (EPI == kSwiGlu) ? a.m.rows / 2 : a.m.rows;
+  const int groups = (out_rows + NR - 1) / NR;
+  int grid = (groups + kWarps - 1) / kWarps;
+  if (grid > kNumSms) grid = kNumSms;
+  if (grid < 1) grid = 1;
+  return launch_ex(kernel, dim3(grid), dim3(kThreads), smem, stream, pdl, a);
+}
+
+template <int KIND, int PRO, int EPI>
+cudaError_t launch_nr(const GemvArgs& a, cudaStream_t stream, bool pdl) {
+  // Few output rows: one row per warp so more SMs take part.
+  const int out_rows = (EPI == kSwiGlu) ? a.m.rows / 2 : a.m.rows;
+  if ((out_rows + 1) / 2 < kNumSms * kWarps) return launch_t<KIND, PRO, EPI, 1>(a, stream, pdl);
+  return launch_t<KIND, PRO, EPI, 2>(a, stream, pdl);
+}
+
+template <int KIND>
+cudaError_t launch_kind(const GemvArgs& a, cudaStream_t stream, bool pdl) {
+#define QNE_COMBO(P, E) \
+  if (a.pro == P && a.epi == E) return launch_nr<KIND, P, E>(a, stream, pdl);
+  QNE_COMBO(kProCopy, kStore)
+  QNE_COMBO(kProCopy, kAccumulate)
+  QNE_COMBO(kProCopy, kSwiGlu)
+  QNE_COMBO(kProRmsNorm, kStore)
+  QNE_COMBO(kProRmsNorm, kAccumulate)
+  QNE_COMBO(kProRmsNorm, kSwiGlu)
+  QNE_COMBO(kProRmsNorm, kArgmax)
+  QNE_COMBO(kProEmbedNorm, kStore)
+  QNE_COMBO(kProGdnGate, kAccumulate)
+#undef QNE_COMBO
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+size_t argmax_scratch_bytes() { return 2 * 4 * 256 + 256; }
+void argmax_scratch_carve(void* scratch, float** part_val, uint32_t** part_idx, uint32_t** ticket) {
+  uint8_t* p = static_cast<uint8_t*>(scratch);
+  *part_val = reinterpret_cast<float*>(p);
+  *part_idx = reinterpret_cast<uint32_t*>(p + 4 * 256);
+  *ticket = reinterpret_cast<uint32_t*>(p + 8 * 256);
+}
+
+const char* check_gemv(const GemvArgs& a) {
+  const Mat& m = a.m;
+  if (!m.w || m.rows <= 0 || m.k <= 0) return "matrix has no data or an empty shape";
+  if (m.kind == kF16) {
+    if (m.k % 256) return "f16 GEMV needs k % 256 == 0";
+  } else if (m.kind == kQ4) {
+    if (m.k % 256) return "block-32 int4 GEMV needs k % 256 == 0";
+    if (!m.s || !m.z) return "int4 matrix without scales or zero points";
+  } else if (m.kind == kQ4G64) {
+    if (m.k % 64) return "group-64 int4 GEMV needs k % 64 == 0";
+    if (!m.s || !m.z) return "int4 matrix without scales or zero points";
+  } else {
+    return "unknown weight kind";
+  }
+  if (m.k > 16384) return "k above 16384";
+  if (a.epi == kSwiGlu && (m.rows % 2)) return "SwiGLU needs an even row count";
+  if (a.pro == kProGdnGate && m.k != kMixerOut) return "the GDN gate prologue needs k == 2048";
+  if (!a.y) return "null output";
+  if ((a.pro == kProCopy || a.pro == kProRmsNorm || a.pro == kProGdnGate) && !a.x) return "null input";
+  if ((a.pro == kProRmsNorm || a.pro == kProEmbedNorm || a.pro == kProGdnGate) && !a.norm_w)
+    return "null norm weight";
+  if (a.pro == kProGdnGate && !a.zgate) return "null gate";
+  if (a.pro == kProEmbedNorm && (!a.embed.w || a.embed.k != m.k || !a.ctl || !a.h_out))
+    return "embedding prologue needs an embedding of width k, control words and h";
+  if (a.epi == kArgmax && (!a.part_val || !a.part_idx || !a.ticket || (a.update_token && !a.ctl)))
+    return "argmax epilogue needs scratch";
+  return nullptr;
+}
+
+cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t stream, bool pdl) {
+  switch (a.m.kind) {
+    case kF16: return launch_kind<kF16>(a, stream, pdl);
+    case kQ4: return launch_kind<kQ4>(a, stream, pdl);
+    case kQ4G64: return launch_kind<kQ4G64>(a, stream, pdl);
+  }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_dequant_rows(const Mat& m, int row0, int nrows, float* out, cudaStream_t stream) {
+  const long total = (long)nrows * m.k;
+  int grid = (int)((total + 255) / 256);
+  if (grid > 4 * kNumSms) grid = 4 * kNumSms;
+  if (grid < 1) grid = 1;
+  count_launch();
+  switch (m.kind) {
+    case kF16: dequant_rows_kernel<kF16><<<grid, 256, 0, stream>>>(m, row0, nrows, out); break;
+    case kQ4: dequant_rows_kernel<kQ4><<<grid, 256, 0, stream>>>(m, row0, nrows, out); break;
+    case kQ4G64: dequant_rows_kernel<kQ4G64><<<grid, 256, 0, stream>>>(m, row0, nrows, out); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_argmax(const float* logits, uint32_t n, SeqCtl* ctl, void* scratch,
+                          cudaStream_t stream, bool pdl) {
+  float* pv;
+  uint32_t *pi, *ticket;
+  argmax_scratch_carve(scratch, &pv, &pi, &ticket);
+  int grid = (int)((n + 1023) / 1024);
+  if (grid > kNumSms) grid = kNumSms;
+  if (grid < 1) grid = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  count_launch();
+  return cudaLaunchKernelEx(&cfg, argmax_kernel, logits, n, ctl, pv, pi, ticket);
+}
+
+}  // namespace qne

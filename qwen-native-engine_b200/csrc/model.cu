@@ -1,0 +1,630 @@
+// Decoder runtime: index.json validation (Index::validate, kernels/src/model.rs:51-86), weight
+// upload with (offset, bytes) de-duplication (kernels/src/model.rs:184-194), device state, the
+// per-token launch graph (kernels/src/model.rs:220-269) captured once as CUDA graphs whose
+// kernels are chained by programmatic dependent launch, and the Model API
+// (kernels/src/model.rs:305-449).
+#include <chrono>
+#include <cstring>
+#include <map>
+#include <thread>
+
+#include "gdn.cuh"
+#include "json.hpp"
+#include "model.hpp"
+
+namespace qne {
+
+void cuda_check(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    throw QneError(e == cudaErrorMemoryAllocation ? kENoMem : kECuda,
+                   std::string(what) + ": " + cudaGetErrorString(e));
+  }
+}
+
+namespace {
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cuda_check(cudaSetDevice(dev), "cudaSetDevice");
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+struct TensorEntry {
+  uint64_t offset = 0, bytes = 0;
+};
+
+int kind_of(const std::string& k) {
+  if (k == "f16") return kF16;
+  if (k == "q4") return kQ4;
+  if (k == "q4g64") return kQ4G64;
+  throw QneError(kEFormat, "unsupported matrix kind: " + k);
+}
+
+double num(const Json& j, const char* key, bool required = true, double dflt = 0) {
+  const Json* v = j.get(key);
+  if (!v) {
+    if (required) throw QneError(kEFormat, std::string("index.json: missing config.") + key);
+    return dflt;
+  }
+  if (!v->is_number()) throw QneError(kEFormat, std::string("index.json: config.") + key + " is not a number");
+  return v->num;
+}
+
+int as_int(double v, const char* what) {
+  if (v != (double)(int64_t)v || v < 0 || v > 1e9)
+    throw QneError(kEFormat, std::string("index.json: ") + what + " is not a valid integer");
+  return (int)v;
+}
+
+}  // namespace
+
+void* Model::alloc(size_t bytes, bool track) {
+  void* p = nullptr;
+  cuda_check(cudaMalloc(&p, bytes < 256 ? 256 : bytes), "cudaMalloc");
+  allocations_.push_back(p);
+  device_bytes += bytes;
+  (void)track;
+  return p;
+}
+
+void Model::free_all() {
+  single_.reset();
+  for (void* p : allocations_) cudaFree(p);
+  allocations_.clear();
+  if (host_ctl_) cudaFreeHost(host_ctl_);
+  host_ctl_ = nullptr;
+  if (own_stream_) cudaStreamDestroy(own_stream_);
+  own_stream_ = nullptr;
+}
+
+Model::~Model() {
+  // Never throws: a model that failed half-way through load() is destroyed here too.
+  int prev = -1;
+  if (cudaGetDevice(&prev) != cudaSuccess) {
+    cudaGetLastError();
+    prev = -1;
+  }
+  if (!allocations_.empty() || own_stream_ || host_ctl_) {
+    if (prev != device) cudaSetDevice(device);
+    free_all();
+    if (prev >= 0 && prev != device) cudaSetDevice(prev);
+  }
+  cudaGetLastError();
+}
+
+Model* Model::load(const char* json, size_t json_len, const void* weights, size_t weights_len,
+                   int device) {
+  if (!json || !weights) throw QneError(kEInval, "null index or weights");
+  if (device < 0) throw QneError(kEInval, "negative device index");
+
+  Json index;
+  try {
+    index = Json::parse(json, json_len);
+  } catch (const JsonError& e) {
+    throw QneError(kEFormat, e.what());
+  }
+  const Json* cj = index.get("config");
+  const Json* mj = index.get("matrices");
+  const Json* tj = index.get("tensors");
+  if (!cj || cj->type != Json::Object || !mj || mj->type != Json::Object || !tj || tj->type != Json::Object)
+    throw QneError(kEFormat, "index.json: needs config, matrices and tensors objects");
+
+  std::unique_ptr<Model> m(new Model());
+  m->device = device;
+  Config& c = m->cfg;
+  c.layers = as_int(num(*cj, "layers"), "config.layers");
+  c.every = as_int(num(*cj, "full_attention_every"), "config.full_attention_every");
+  c.hidden = as_int(num(*cj, "hidden"), "config.hidden");
+  c.inter = as_int(num(*cj, "intermediate", false, 0), "config.intermediate");
+  if (c.inter == 0) c.inter = c.hidden == 1024 ? 3584 : 6144;  // kernels/src/model.rs:47-50
+  c.vocab = as_int(num(*cj, "vocab"), "config.vocab");
+  c.theta = num(*cj, "rope_theta");
+  c.rope_dim = as_int(num(*cj, "rope_dim"), "config.rope_dim");
+  // The kernels need: rotary width 64, hidden and intermediate multiples of 256 (16-byte chunks
+  // per lane of a warp, int4 blocks of 32), fixed head geometry (implied by the matrix shapes).
+  if (c.layers < 1 || c.layers > 256 || c.every < 1 || c.hidden < 256 || c.hidden > 8192 ||
+      c.hidden % 256 || c.inter < 256 || c.inter > 16384 || c.inter % 256 || c.vocab < 1 ||
+      c.rope_dim != 64 || !(c.theta > 0))
+    throw QneError(kEFormat, "unsupported model architecture: these kernels need a Qwen3.5-shaped "
+                             "hybrid decoder (rope_dim 64, hidden and intermediate multiples of 256)");
+
+  std::map<std::string, TensorEntry> tensors;
+  for (const auto& kv : tj->obj) {
+    const Json& t = kv.second;
+    const Json* off = t.get("offset");
+    const Json* by = t.get("bytes");
+    if (!off || !by || !off->is_number() || !by->is_number())
+      throw QneError(kEFormat, "invalid tensor range: " + kv.first);
+    TensorEntry e;
+    if (off->num < 0 || by->num < 0 || off->num != (double)(uint64_t)off->num || by->num != (double)(uint64_t)by->num)
+      throw QneError(kEFormat, "invalid tensor range: " + kv.first);
+    e.offset = (uint64_t)off->num;
+    e.bytes = (uint64_t)by->num;
+    // kernels/src/model.rs:56-60: in range, 4-byte aligned, non-empty, whole words.
+    if (e.offset + e.bytes < e.offset || e.offset + e.bytes > weights_len || e.offset % 4 ||
+        e.bytes == 0 || e.bytes % 4)
+      throw QneError(kEFormat, "invalid tensor range: " + kv.first);
+    tensors[kv.first] = e;
+  }
+  auto tensor = [&](const std::string& name, uint64_t expected) -> const TensorEntry& {
+    auto it = tensors.find(name);
+    if (it == tensors.end() || it->second.bytes != expected)
+      throw QneError(kEFormat, "invalid tensor size: " + name);
+    return it->second;
+  };
+  struct MatSpec {
+    std::string name;
+    int kind, rows, k;
+  };
+  std::vector<MatSpec> specs;
+  auto matrix = [&](const std::string& name, int rows, int k) {
+    const Json* s = mj->get(name);
+    if (!s || !s->get("rows") || !s->get("k") || !s->get("rows")->is_number() || !s->get("k")->is_number() ||
+        s->get("rows")->num != rows || s->get("k")->num != k)
+      throw QneError(kEFormat, "invalid matrix shape: " + name);
+    const Json* kj = s->get("kind");
+    const int kind = kind_of(kj && kj->type == Json::String ? kj->str : std::string("q4"));
+    const uint64_t el = (uint64_t)rows * (uint64_t)k;
+    if (kind == kF16) {
+      tensor(name + ".w", el * 2);
+    } else if (kind == kQ4) {
+      tensor(name + ".w", el / 2);
+      tensor(name + ".s", el / 16);
+      tensor(name + ".z", el / 64);
+    } else {
+      if (k % 64) throw QneError(kEFormat, "invalid matrix shape: " + name);
+      tensor(name + ".w", el / 2);
+      tensor(name + ".s", el / 32);
+      tensor(name + ".z", el / 32);
+    }
+    specs.push_back({name, kind, rows, k});
+  };
+  matrix("embed", c.vocab, c.hidden);
+  matrix("lm_head", c.vocab, c.hidden);
+  tensor("final_norm", (uint64_t)c.hidden * 4);
+  for (int i = 0; i < c.layers; ++i) {
+    const bool attn = (i + 1) % c.every == 0;
+    const std::string p = "layer" + std::to_string(i);
+    tensor(p + ".input_norm", (uint64_t)c.hidden * 4);
+    tensor(p + ".post_norm", (uint64_t)c.hidden * 4);
+    matrix(p + ".mixer_in", attn ? kAttnProj : kGdnProj, c.hidden);
+    matrix(p + ".mixer_out", c.hidden, kMixerOut);
+    matrix(p + ".gate_up", c.inter * 2, c.hidden);
+    matrix(p + ".down", c.hidden, c.inter);
+    if (attn) {
+      tensor(p + ".attn_norms", 2048);
+    } else {
+      tensor(p + ".conv_w", 98304);
+      tensor(p + ".gdn_params", 640);
+    }
+  }
+
+  // Validation is done; from here on the device is needed.
+  int ndev = 0;
+  cuda_check(cudaGetDeviceCount(&ndev), "cudaGetDeviceCount");
+  if (device >= ndev) throw QneError(kEInval, "no CUDA device " + std::to_string(device));
+  DeviceGuard guard(device);
+  cudaDeviceProp prop;
+  cuda_check(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+  if (prop.major < 10)
+    throw QneError(kECuda, std::string("device ") + prop.name + " is not sm_100 (this library is built for sm_100a)");
+  m->adapter = std::string(prop.name) + " (sm_" + std::to_string(prop.major) + std::to_string(prop.minor) +
+               "a, " + std::to_string(prop.multiProcessorCount) + " SMs, CUDA device " +
+               std::to_string(device) + ")";
+
+  // Upload every distinct (offset, bytes) range once into one arena, 256-byte aligned.
+  std::map<std::pair<uint64_t, uint64_t>, uint64_t> placed;
+  uint64_t arena_bytes = 0;
+  for (const auto& kv : tensors) {
+    const auto key = std::make_pair(kv.second.offset, kv.second.bytes);
+    if (placed.count(key)) continue;
+    placed[key] = arena_bytes;
+    arena_bytes += (kv.second.bytes + 255) & ~uint64_t(255);
+  }
+  uint8_t* arena = static_cast<uint8_t*>(m->alloc(arena_bytes));
+  m->arena_ = arena;
+  for (const auto& kv : placed)
+    cuda_check(cudaMemcpy(arena + kv.second, static_cast<const uint8_t*>(weights) + kv.first.first,
+                          kv.first.second, cudaMemcpyHostToDevice),
+               "upload weights");
+  auto dptr = [&](const std::string& name) -> const void* {
+    const TensorEntry& e = tensors.at(name);
+    return arena + placed.at(std::make_pair(e.offset, e.bytes));
+  };
+  auto mat = [&](const MatSpec& s) {
+    Mat r;
+    r.kind = s.kind;
+    r.rows = s.rows;
+    r.k = s.k;
+    r.w = dptr(s.name + ".w");
+    if (s.kind != kF16) {
+      r.s = dptr(s.name + ".s");
+      r.z = dptr(s.name + ".z");
+    }
+    return r;
+  };
+  auto mat_bytes = [](const Mat& x) -> uint64_t {
+    const uint64_t el = (uint64_t)x.rows * x.k;
+    if (x.kind == kF16) return el * 2;
+    if (x.kind == kQ4) return el / 2 + el / 16 + el / 64;
+    return el / 2 + el / 16;
+  };
+  size_t si = 0;
+  m->embed = mat(specs[si++]);
+  m->lm_head = mat(specs[si++]);
+  m->tied = m->embed.w == m->lm_head.w;
+  m->final_norm = static_cast<const float*>(dptr("final_norm"));
+  m->embed_kind = m->embed.kind;
+  m->weight_bytes = mat_bytes(m->lm_head) + (uint64_t)c.hidden * 4;
+  for (int i = 0; i < c.layers; ++i) {
+    LayerWeights L;
+    const std::string p = "layer" + std::to_string(i);
+    L.attention = (i + 1) % c.every == 0;
+    L.in = mat(specs[si++]);
+    L.out = mat(specs[si++]);
+    L.gate_up = mat(specs[si++]);
+    L.down = mat(specs[si++]);
+    L.input_norm = static_cast<const float*>(dptr(p + ".input_norm"));
+    L.post_norm = static_cast<const float*>(dptr(p + ".post_norm"));
+    if (L.attention) L.attn_norms = static_cast<const float*>(dptr(p + ".attn_norms"));
+    else {
+      L.conv_w = static_cast<const float*>(dptr(p + ".conv_w"));
+      L.gdn_params = static_cast<const float*>(dptr(p + ".gdn_params"));
+    }
+    m->weight_bytes += mat_bytes(L.in) + mat_bytes(L.out) + mat_bytes(L.gate_up) + mat_bytes(L.down);
+    m->layers.push_back(L);
+  }
+  m->weight_kind = m->layers[0].in.kind;
+
+  std::vector<float> rope((size_t)2 * kMaxContext * kRopeHalf);
+  rope_table_host(rope.data(), c.theta);
+  m->rope = static_cast<float*>(m->alloc(rope.size() * 4));
+  cuda_check(cudaMemcpy(m->rope, rope.data(), rope.size() * 4, cudaMemcpyHostToDevice), "upload rope");
+
+  cuda_check(cudaStreamCreateWithFlags(&m->own_stream_, cudaStreamNonBlocking), "cudaStreamCreate");
+  cuda_check(cudaMallocHost(&m->host_ctl_, (size_t)kMaxContext * 2 * sizeof(uint32_t) + 64), "cudaMallocHost");
+  m->single_.reset(new Runner(m.get(), 1, kPagesPerSeq));
+  m->single_->capture_graphs();
+  m->single_->reset(m->stream());
+  cuda_check(cudaStreamSynchronize(m->stream()), "load");
+  return m.release();
+}
+
+// ------------------------------------------------------------------------------------------
+// Runner
+// ------------------------------------------------------------------------------------------
+Runner::Runner(Model* model, int batch, uint32_t pool_pages) : m(model) {
+  const Config& c = m->cfg;
+  st.batch = batch;
+  st.pool_pages = pool_pages;
+  auto track = [&](size_t bytes) {
+    void* p = m->alloc(bytes);
+    st.buffers.push_back({p, bytes});
+    return p;
+  };
+  st.conv.assign(c.layers, nullptr);
+  st.rec.assign(c.layers, nullptr);
+  st.kv.assign(c.layers, nullptr);
+  for (int i = 0; i < c.layers; ++i) {
+    if (m->layers[i].attention) {
+      st.kv[i] = static_cast<uint16_t*>(track((size_t)pool_pages * kPageElems * 2));
+    } else {
+      st.conv[i] = static_cast<float*>(track((size_t)batch * kConvSlots * kConvChannels * 4));
+      st.rec[i] = static_cast<float*>(track((size_t)batch * kGdnHeads * kGdnDim * kGdnDim * 4));
+    }
+  }
+  st.ctl = static_cast<SeqCtl*>(track((size_t)batch * sizeof(SeqCtl)));
+  st.page_table = static_cast<uint32_t*>(m->alloc((size_t)batch * kPagesPerSeq * 4));
+  std::vector<uint32_t> pt((size_t)batch * kPagesPerSeq);
+  for (size_t i = 0; i < pt.size(); ++i) pt[i] = (uint32_t)i;
+  cuda_check(cudaMemcpy(st.page_table, pt.data(), pt.size() * 4, cudaMemcpyHostToDevice), "page table");
+
+  h = static_cast<float*>(m->alloc((size_t)batch * c.hidden * 4));
+  proj = static_cast<float*>(m->alloc((size_t)batch * kGdnProj * 4));
+  raw = static_cast<float*>(m->alloc((size_t)batch * kMixerOut * 4));
+  act = static_cast<float*>(m->alloc((size_t)batch * c.inter * 4));
+  logits = static_cast<float*>(m->alloc((size_t)batch * c.vocab * 4));
+  argmax_scratch = m->alloc(argmax_scratch_bytes() * batch);
+  cuda_check(cudaMemset(argmax_scratch, 0, argmax_scratch_bytes() * batch), "memset");
+  attn_scratch = m->alloc(attention_scratch_bytes(batch));
+  cuda_check(cudaMemset(attn_scratch, 0, attention_scratch_bytes(batch)), "memset");
+}
+
+Runner::~Runner() {
+  for (auto& g : graph)
+    if (g) cudaGraphExecDestroy(g);
+}
+
+void Runner::record(Variant v, cudaStream_t s) {
+  const Model& M = *m;
+  size_t n = 0;
+  auto gemv = [&](const GemvArgs& a) {
+    if (const char* why = check_gemv(a)) throw QneError(kEInval, why);
+    cuda_check(launch_gemv(a, s, true), "gemv launch");
+    ++n;
+  };
+  for (int i = 0; i < M.cfg.layers; ++i) {
+    const LayerWeights& L = M.layers[i];
+    GemvArgs in;
+    in.m = L.in;
+    in.epi = kStore;
+    in.y = proj;
+    in.norm_w = L.input_norm;
+    if (i == 0) {
+      in.pro = kProEmbedNorm;
+      in.embed = M.embed;
+      in.ctl = st.ctl;
+      in.h_out = h;
+    } else {
+      in.pro = kProRmsNorm;
+      in.x = h;
+    }
+    gemv(in);
+    GemvArgs out;
+    out.m = L.out;
+    out.epi = kAccumulate;
+    out.y = h;
+    out.x = raw;
+    if (L.attention) {
+      AttnArgs at;
+      at.proj = proj;
+      at.norms = L.attn_norms;
+      at.rope = M.rope;
+      at.kv = st.kv[i];
+      at.page_table = st.page_table;
+      at.pos = &st.ctl->pos;
+      at.pos_stride = 4;
+      at.flags = &st.ctl->flags;
+      at.flags_stride = 4;
+      at.out = raw;
+      at.batch = 1;
+      at.scratch = attn_scratch;
+      cuda_check(launch_attention(at, st.pool_pages, 64, s, true), "attention launch");
+      ++n;
+      out.pro = kProCopy;
+    } else {
+      cuda_check(launch_gdn_step(proj, st.conv[i], L.conv_w, st.rec[i], L.gdn_params, &st.ctl->count, 4,
+                                 raw, 1, s, true),
+                 "gdn launch");
+      ++n;
+      out.pro = kProGdnGate;
+      out.zgate = proj + 6144;
+      out.norm_w = L.gdn_params + 32;
+    }
+    gemv(out);
+    GemvArgs gu;
+    gu.m = L.gate_up;
+    gu.pro = kProRmsNorm;
+    gu.x = h;
+    gu.norm_w = L.post_norm;
+    gu.epi = kSwiGlu;
+    gu.y = act;
+    gemv(gu);
+    GemvArgs dn;
+    dn.m = L.down;
+    dn.pro = kProCopy;
+    dn.x = act;
+    dn.epi = kAccumulate;
+    dn.y = h;
+    gemv(dn);
+  }
+  if (v != kLayers) {
+    GemvArgs hd;
+    hd.m = M.lm_head;
+    hd.pro = kProRmsNorm;
+    hd.x = h;
+    hd.norm_w = M.final_norm;
+    hd.epi = kArgmax;
+    hd.y = logits;
+    argmax_scratch_carve(argmax_scratch, &hd.part_val, &hd.part_idx, &hd.ticket);
+    hd.ctl = st.ctl;
+    hd.update_token = (v == kGreedy) ? 1 : 0;
+    gemv(hd);
+  }
+  if (v == kGreedy) launches_per_token = n;
+}
+
+void Runner::capture_graphs() {
+  cudaStream_t cs;
+  cuda_check(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking), "cudaStreamCreate");
+  for (int v = 0; v < kVariants; ++v) {
+    cuda_check(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal), "begin capture");
+    try {
+      record((Variant)v, cs);
+    } catch (...) {
+      cudaGraph_t g;
+      cudaStreamEndCapture(cs, &g);
+      if (g) cudaGraphDestroy(g);
+      cudaStreamDestroy(cs);
+      throw;
+    }
+    cudaGraph_t g = nullptr;
+    cuda_check(cudaStreamEndCapture(cs, &g), "end capture");
+    cudaError_t e = cudaGraphInstantiate(&graph[v], g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) {
+      cudaStreamDestroy(cs);
+      cuda_check(e, "graph instantiate");
+    }
+  }
+  cudaStreamDestroy(cs);
+}
+
+void Runner::launch(Variant v, cudaStream_t s) {
+  cuda_check(cudaGraphLaunch(graph[v], s), "graph launch");
+  for (size_t i = 0; i < (v == kLayers ? launches_per_token - 1 : launches_per_token); ++i) count_launch();
+}
+
+void Runner::reset(cudaStream_t s) {
+  for (auto& b : st.buffers) cuda_check(cudaMemsetAsync(b.first, 0, b.second, s), "reset");
+}
+
+void Runner::snapshot(cudaStream_t s) {
+  if (saved.empty())
+    for (auto& b : st.buffers) saved.push_back({m->alloc(b.second), b.second});
+  for (size_t i = 0; i < st.buffers.size(); ++i)
+    cuda_check(cudaMemcpyAsync(saved[i].first, st.buffers[i].first, st.buffers[i].second,
+                               cudaMemcpyDeviceToDevice, s),
+               "snapshot");
+  has_snapshot = true;
+}
+
+void Runner::restore(cudaStream_t s) {
+  if (!has_snapshot) throw QneError(kENoSnap, "no snapshot taken");
+  for (size_t i = 0; i < st.buffers.size(); ++i)
+    cuda_check(cudaMemcpyAsync(st.buffers[i].first, saved[i].first, st.buffers[i].second,
+                               cudaMemcpyDeviceToDevice, s),
+               "restore");
+}
+
+// ------------------------------------------------------------------------------------------
+// Model API
+// ------------------------------------------------------------------------------------------
+void Model::set_stream(cudaStream_t s) { ext_stream_ = s; }
+
+size_t Model::dispatches_per_token() const { return single_->launches_per_token; }
+const float* Model::logits_device() const { return single_->logits; }
+
+void Model::reset() {
+  DeviceGuard g(device);
+  single_->reset(stream());
+  host_pos_ = 0;
+}
+
+void Model::prefill_chunk(const uint32_t* ids, uint32_t n, uint32_t start, bool finish) {
+  DeviceGuard g(device);
+  if (!ids && n) throw QneError(kEInval, "null ids");
+  if (n == 0 || (uint64_t)start + n >= (uint64_t)kMaxContext)
+    throw QneError(kERangeCtx, "context limit: " + std::to_string(start) + " + " + std::to_string(n) +
+                                   " tokens does not fit in " + std::to_string(kMaxContext));
+  cuda_check(cudaStreamSynchronize(stream()), "prefill");  // host_ctl_ may still feed a copy
+  for (uint32_t i = 0; i < n; ++i) {
+    host_ctl_[2 * i] = ids[i];
+    host_ctl_[2 * i + 1] = start + i;
+  }
+  for (uint32_t i = 0; i < n; ++i) {
+    cuda_check(cudaMemcpyAsync(single_->st.ctl, host_ctl_ + 2 * i, 8, cudaMemcpyHostToDevice, stream()),
+               "prefill token");
+    single_->launch((i + 1 == n && finish) ? Runner::kGreedy : Runner::kLayers, stream());
+  }
+  host_pos_ = finish ? start + n : start + n - 1;
+  sync(600000);
+}
+
+void Model::logits(float* out, size_t n) {
+  DeviceGuard g(device);
+  if (!out || n < (size_t)cfg.vocab) throw QneError(kEInval, "logits buffer shorter than the vocabulary");
+  cuda_check(cudaMemcpyAsync(out, single_->logits, (size_t)cfg.vocab * 4, cudaMemcpyDeviceToHost, stream()),
+             "logits");
+  sync(600000);
+}
+
+void Model::step_async(uint32_t token, uint32_t pos) {
+  if (pos >= (uint32_t)kMaxContext)
+    throw QneError(kERangeCtx, "context limit of " + std::to_string(kMaxContext) + " tokens reached");
+  cuda_check(cudaStreamSynchronize(stream()), "step");
+  host_ctl_[0] = token;
+  host_ctl_[1] = pos;
+  cuda_check(cudaMemcpyAsync(single_->st.ctl, host_ctl_, 8, cudaMemcpyHostToDevice, stream()), "step token");
+  single_->launch(Runner::kStep, stream());
+  host_pos_ = pos;
+}
+
+void Model::step(uint32_t token, uint32_t pos, float* out, size_t n) {
+  DeviceGuard g(device);
+  if (!out || n < (size_t)cfg.vocab) throw QneError(kEInval, "logits buffer shorter than the vocabulary");
+  step_async(token, pos);
+  cuda_check(cudaMemcpyAsync(out, single_->logits, (size_t)cfg.vocab * 4, cudaMemcpyDeviceToHost, stream()),
+             "step logits");
+  sync(600000);
+}
+
+void Model::snapshot() {
+  DeviceGuard g(device);
+  single_->snapshot(stream());
+  saved_pos_ = host_pos_;
+}
+
+void Model::restore() {
+  DeviceGuard g(device);
+  single_->restore(stream());
+  host_pos_ = saved_pos_;
+}
+
+void Model::last_token(uint32_t* token, uint32_t* pos) {
+  DeviceGuard g(device);
+  cuda_check(cudaStreamSynchronize(stream()), "last_token");
+  cuda_check(cudaMemcpyAsync(host_ctl_ + 2 * kMaxContext, single_->st.ctl, 16, cudaMemcpyDeviceToHost, stream()),
+             "last_token");
+  sync(600000);
+  if (token) *token = host_ctl_[2 * kMaxContext];
+  if (pos) *pos = host_ctl_[2 * kMaxContext + 1];
+  host_pos_ = host_ctl_[2 * kMaxContext + 1];
+}
+
+void Model::decode(uint32_t n, uint32_t window, const uint32_t* stop, uint32_t nstop, uint32_t* ids,
+                   uint32_t* n_out) {
+  DeviceGuard g(device);
+  if (!ids || n == 0) throw QneError(kEInval, "decode needs an output buffer of n >= 1 ids");
+  if (window == 0) throw QneError(kEInval, "window must be >= 1");
+  uint32_t first = 0, next_pos = 0;
+  last_token(&first, &next_pos);
+  uint32_t count = 0;
+  ids[count++] = first;
+  auto stopped = [&](uint32_t t) {
+    for (uint32_t i = 0; i < nstop; ++i)
+      if (stop[i] == t) return true;
+    return false;
+  };
+  while (count < n && !stopped(ids[count - 1])) {
+    const uint32_t steps = std::min(window, n - count);
+    if ((uint64_t)next_pos + steps > (uint64_t)kMaxContext) {
+      if (n_out) *n_out = count;
+      throw QneError(kERangeCtx, "context limit of " + std::to_string(kMaxContext) + " tokens reached after " +
+                                     std::to_string(count) + " generated tokens");
+    }
+    next_pos += steps;
+    for (uint32_t s = 0; s < steps; ++s) single_->launch(Runner::kGreedy, stream());
+    cuda_check(cudaMemcpyAsync(host_ctl_ + 2 * kMaxContext, single_->st.ctl, 16, cudaMemcpyDeviceToHost, stream()),
+               "decode readback");
+    sync(600000);
+    if (steps == 1) ids[count++] = host_ctl_[2 * kMaxContext];
+    else
+      for (uint32_t s = 0; s < steps; ++s) ids[count++] = 0xFFFFFFFFu;
+  }
+  host_pos_ = next_pos;
+  if (n_out) *n_out = count;
+}
+
+void Model::decode_async(uint32_t steps) {
+  DeviceGuard g(device);
+  if ((uint64_t)host_pos_ + steps > (uint64_t)kMaxContext)
+    throw QneError(kERangeCtx, "context limit of " + std::to_string(kMaxContext) + " tokens reached");
+  for (uint32_t s = 0; s < steps; ++s) single_->launch(Runner::kGreedy, stream());
+  host_pos_ += steps;
+}
+
+void Model::sync(uint32_t timeout_ms) {
+  DeviceGuard g(device);
+  const auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(timeout_ms);
+  uint32_t spins = 0;
+  for (;;) {
+    const cudaError_t e = cudaStreamQuery(stream());
+    if (e == cudaSuccess) return;
+    if (e != cudaErrorNotReady) cuda_check(e, "stream");
+    const auto now = std::chrono::steady_clock::now();
+    if (now > deadline) throw QneError(kETimeout, "GPU wait exceeded " + std::to_string(timeout_ms) + " ms");
+    if (++spins < 20000) std::this_thread::yield();
+    else std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+}
+
+}  // namespace qne

@@ -1,0 +1,145 @@
+// The decoder runtime behind the C ABI: weight loading and validation, device state, the
+// per-token launch graph, and the Model API of kernels/src/model.rs.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "gemv.cuh"
+
+namespace qne {
+
+struct QneError : std::runtime_error {
+  int code;
+  QneError(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+// Error codes (mirrors qne.h).
+constexpr int kEInval = -1, kERangeCtx = -2, kEFormat = -3, kECuda = -4, kETimeout = -5,
+              kENoSnap = -6, kENoMem = -7;
+
+void cuda_check(cudaError_t e, const char* what);
+
+struct LayerWeights {
+  bool attention = false;
+  Mat in, out, gate_up, down;
+  const float* input_norm = nullptr;
+  const float* post_norm = nullptr;
+  const float* attn_norms = nullptr;  // attention layers: q_norm[256], k_norm[256]
+  const float* conv_w = nullptr;      // GDN layers: [6144][4]
+  const float* gdn_params = nullptr;  // GDN layers: dt_bias[16], A_neg_exp[16], norm_w[128]
+};
+
+struct Config {
+  int layers = 0, every = 4, hidden = 0, inter = 0, vocab = 0, rope_dim = 64;
+  double theta = 1e7;
+};
+
+// Device state of `batch` sequences: GDN conv rings and recurrent states, KV page pools.
+struct SeqState {
+  int batch = 0;
+  uint32_t pool_pages = 0;
+  std::vector<float*> conv;      // per layer (GDN): [batch][4][6144]
+  std::vector<float*> rec;       // per layer (GDN): [batch][16][128][128]
+  std::vector<uint16_t*> kv;     // per layer (attention): [pool_pages][16384] halves
+  SeqCtl* ctl = nullptr;         // [batch]
+  uint32_t* page_table = nullptr;  // [batch][256]
+  std::vector<std::pair<void*, size_t>> buffers;  // everything cleared by reset
+};
+
+class Model;
+
+// Activations and launch graphs of one sequence set.
+class Runner;
+
+class Model {
+ public:
+  static Model* load(const char* json, size_t json_len, const void* weights, size_t weights_len,
+                     int device);
+  ~Model();
+
+  Config cfg;
+  int device = 0;
+  int weight_kind = kF16, embed_kind = kF16;
+  bool tied = false;
+  uint64_t weight_bytes = 0;  // bytes one decode token reads from the weights
+  uint64_t device_bytes = 0;
+  std::string adapter;
+  std::vector<LayerWeights> layers;
+  Mat embed, lm_head;
+  const float* final_norm = nullptr;
+  float* rope = nullptr;  // [2][4096][32]
+
+  // B = 1 API (kernels/src/model.rs)
+  void reset();
+  void prefill_chunk(const uint32_t* ids, uint32_t n, uint32_t start, bool finish_logits);
+  void logits(float* out, size_t n);
+  void step(uint32_t token, uint32_t pos, float* out, size_t n);
+  void step_async(uint32_t token, uint32_t pos);
+  void snapshot();
+  void restore();
+  void last_token(uint32_t* token, uint32_t* pos);
+  void decode(uint32_t n, uint32_t window, const uint32_t* stop, uint32_t nstop, uint32_t* ids,
+              uint32_t* n_out);
+  void decode_async(uint32_t steps);
+  void sync(uint32_t timeout_ms);
+  void set_stream(cudaStream_t s);
+  size_t dispatches_per_token() const;
+  const float* logits_device() const;
+
+  cudaStream_t stream() const { return ext_stream_ ? ext_stream_ : own_stream_; }
+  void* alloc(size_t bytes, bool track = true);  // device allocation owned by the model
+
+  Runner* single() { return single_.get(); }
+
+ private:
+  Model() = default;
+  void free_all();
+  std::vector<void*> allocations_;
+  void* arena_ = nullptr;
+  cudaStream_t own_stream_ = nullptr;
+  cudaStream_t ext_stream_ = nullptr;
+  std::unique_ptr<Runner> single_;
+  uint32_t* host_ctl_ = nullptr;  // pinned staging: (token, pos) pairs
+  uint32_t host_pos_ = 0;         // host mirror of the next position
+  uint32_t saved_pos_ = 0;
+  friend class Runner;
+};
+
+// One set of sequences with its state, activations and captured graphs.
+class Runner {
+ public:
+  Runner(Model* m, int batch, uint32_t pool_pages);
+  ~Runner();
+  Model* m;
+  SeqState st;
+  // activations
+  float* h = nullptr;
+  float* proj = nullptr;
+  float* raw = nullptr;
+  float* act = nullptr;
+  float* logits = nullptr;
+  void* argmax_scratch = nullptr;
+  void* attn_scratch = nullptr;
+  // snapshot copies (allocated on the first snapshot)
+  std::vector<std::pair<void*, size_t>> saved;
+  bool has_snapshot = false;
+
+  enum Variant { kGreedy = 0, kStep = 1, kLayers = 2, kVariants = 3 };
+  cudaGraphExec_t graph[kVariants] = {nullptr, nullptr, nullptr};
+  size_t launches_per_token = 0;
+
+  void record(Variant v, cudaStream_t s);  // enqueue one token's kernels on s
+  void capture_graphs();
+  void launch(Variant v, cudaStream_t s);
+  void reset(cudaStream_t s);
+  void snapshot(cudaStream_t s);
+  void restore(cudaStream_t s);
+};
+
+}  // namespace qne

@@ -1,0 +1,426 @@
+"""Python mirror of the `qwen-kernels` decoder API over the libqne C ABI (include/qne.h).
+
+`Model` follows `kernels/src/model.rs` (struct Model): load / reset / prefill /
+prefill_batched / prefill_from / prefill_chunk / logits / step / snapshot / restore /
+last_token / decode / dispatches_per_token / profile-free adapter string, with the same
+argument meanings and the same failures (context limit, bad index.json, no snapshot), raised
+as `QneError`. `ModelTiles.validate` mirrors kernels/src/model.rs:101-109.
+
+Operators (`gemv`, `rmsnorm_gemv`, `dequant_rows`, `argmax`, `gdn_step`, `attention_step`,
+`kv_gather`, `embed`) take device tensors (torch is used only for device memory and streams)
+and call the sm_100a kernels directly.
+
+The shared library must exist: importing this module raises if libqne.so is missing, and no
+operation falls back to another implementation.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+import numpy as np
+
+MAX_CONTEXT = 4096
+PAGE_TOKENS = 16
+PAGES_PER_SEQ = MAX_CONTEXT // PAGE_TOKENS
+KIND_F16, KIND_Q4, KIND_Q4G64 = 0, 1, 2
+KINDS = {"f16": KIND_F16, "q4": KIND_Q4, "q4g64": KIND_Q4G64}
+EPI_STORE, EPI_ACCUMULATE, EPI_SWIGLU = 0, 1, 2
+EPILOGUES = {"store": EPI_STORE, "accumulate": EPI_ACCUMULATE, "swiglu": EPI_SWIGLU}
+
+_ERRORS = {-1: "EINVAL", -2: "ERANGE_CTX", -3: "EFORMAT", -4: "ECUDA", -5: "ETIMEOUT",
+           -6: "ENOSNAP", -7: "ENOMEM"}
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libqne.so"
+
+
+class QneError(RuntimeError):
+    """A failed libqne call: `code` is the negative QNE_E* status, `name` its symbol."""
+
+    def __init__(self, code: int, message: str):
+        self.code = code
+        self.name = _ERRORS.get(code, str(code))
+        super().__init__(f"{self.name}: {message}")
+
+
+class _Matrix(C.Structure):
+    _fields_ = [("kind", C.c_int32), ("rows", C.c_int32), ("k", C.c_int32), ("pad", C.c_int32),
+                ("w", C.c_void_p), ("s", C.c_void_p), ("z", C.c_void_p)]
+
+
+class _Info(C.Structure):
+    _fields_ = [("layers", C.c_int32), ("hidden", C.c_int32), ("intermediate", C.c_int32),
+                ("vocab", C.c_int32), ("weight_kind", C.c_int32), ("embed_kind", C.c_int32),
+                ("tied_lm_head", C.c_int32), ("device", C.c_int32), ("weight_bytes", C.c_uint64),
+                ("device_bytes", C.c_uint64)]
+
+
+def _load_lib() -> C.CDLL:
+    if not LIB_PATH.exists():
+        raise ImportError(f"libqne.so is not built ({LIB_PATH}); run __graft_entry__.build()")
+    lib = C.CDLL(str(LIB_PATH))
+    P, U32, I32, SZ = C.c_void_p, C.c_uint32, C.c_int, C.c_size_t
+    U32P = C.POINTER(C.c_uint32)
+    FP = C.POINTER(C.c_float)
+    sigs = {
+        "qne_last_error": (C.c_char_p, []),
+        "qne_version": (C.c_char_p, []),
+        "qne_kernel_launches": (C.c_uint64, []),
+        "qne_model_load": (I32, [C.c_char_p, SZ, P, SZ, I32, C.POINTER(P)]),
+        "qne_model_free": (None, [P]),
+        "qne_model_info_get": (I32, [P, C.POINTER(_Info)]),
+        "qne_model_set_stream": (I32, [P, P]),
+        "qne_adapter": (C.c_char_p, [P]),
+        "qne_dispatches_per_token": (SZ, [P]),
+        "qne_validate_tiles": (I32, [C.c_char_p, SZ]),
+        "qne_reset": (I32, [P]),
+        "qne_prefill": (I32, [P, U32P, U32]),
+        "qne_prefill_chunk": (I32, [P, U32P, U32, U32, I32]),
+        "qne_logits": (I32, [P, FP, SZ]),
+        "qne_step": (I32, [P, U32, U32, FP, SZ]),
+        "qne_snapshot": (I32, [P]),
+        "qne_restore": (I32, [P]),
+        "qne_last_token": (I32, [P, U32P, U32P]),
+        "qne_decode": (I32, [P, U32, U32, U32P, U32, U32P, U32P]),
+        "qne_decode_async": (I32, [P, U32]),
+        "qne_step_async": (I32, [P, U32, U32]),
+        "qne_sync": (I32, [P, U32]),
+        "qne_logits_device": (P, [P]),
+        "qne_model_matrix": (I32, [P, C.c_char_p, C.POINTER(_Matrix)]),
+        "qne_model_tensor": (I32, [P, C.c_char_p, C.POINTER(P)]),
+        "qne_batch_create": (I32, [P, U32, U32, C.POINTER(P)]),
+        "qne_batch_free": (None, [P]),
+        "qne_batch_set_page_table": (I32, [P, U32P, SZ]),
+        "qne_batch_reset": (I32, [P]),
+        "qne_batch_step": (I32, [P, U32P, U32P, FP, U32P]),
+        "qne_batch_decode_async": (I32, [P, U32]),
+        "qne_batch_tokens": (I32, [P, U32P, U32P]),
+        "qne_batch_fill_synthetic": (I32, [P, U32, U32, U32, C.c_uint64]),
+        "qne_batch_sync": (I32, [P, U32]),
+        "qne_gemv": (I32, [C.POINTER(_Matrix), P, P, I32, P]),
+        "qne_rmsnorm_gemv": (I32, [C.POINTER(_Matrix), P, P, C.c_float, P, I32, P]),
+        "qne_gemm_scratch_bytes": (SZ, [C.POINTER(_Matrix), I32]),
+        "qne_gemm": (I32, [C.POINTER(_Matrix), P, I32, P, I32, P, SZ, P]),
+        "qne_dequant_rows": (I32, [C.POINTER(_Matrix), I32, I32, P, P]),
+        "qne_embed": (I32, [C.POINTER(_Matrix), P, P, P]),
+        "qne_argmax_scratch_bytes": (SZ, [U32]),
+        "qne_argmax": (I32, [P, U32, P, P, SZ, P]),
+        "qne_gdn_step": (I32, [P, P, P, P, P, P, P, I32, P]),
+        "qne_attention_scratch_bytes": (SZ, [I32]),
+        "qne_attention_step": (I32, [P, P, C.c_double, P, U32, P, P, P, I32, P, SZ, P]),
+        "qne_kv_gather": (I32, [P, P, U32, P, P, P]),
+        "qne_bandwidth_probe": (I32, [P, SZ, P, P]),
+    }
+    for name, (res, args) in sigs.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+lib = _load_lib()
+
+
+def _check(status: int) -> None:
+    if status != 0:
+        raise QneError(status, lib.qne_last_error().decode(errors="replace"))
+
+
+def kernel_launches() -> int:
+    """Kernels libqne has launched in this process."""
+    return int(lib.qne_kernel_launches())
+
+
+def version() -> str:
+    return lib.qne_version().decode()
+
+
+def _u32_array(values) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(values, dtype=np.uint32))
+
+
+def _u32p(a: np.ndarray):
+    return a.ctypes.data_as(C.POINTER(C.c_uint32))
+
+
+def _fp(a: np.ndarray):
+    return a.ctypes.data_as(C.POINTER(C.c_float))
+
+
+class ModelTiles:
+    """The reference's per-matrix tile profile (kernels/src/model.rs:89-145). The CUDA kernels
+    pick their own shapes; profiles are accepted and validated for API compatibility."""
+
+    @staticmethod
+    def validate(profile_json: str) -> None:
+        b = profile_json.encode()
+        _check(lib.qne_validate_tiles(b, len(b)))
+
+
+class Model:
+    """A loaded decoder on one GPU (kernels/src/model.rs:147-450)."""
+
+    def __init__(self, index_json, weights, device: int = 0):
+        if isinstance(index_json, str):
+            index_json = index_json.encode()
+        w = weights
+        if isinstance(w, (bytes, bytearray)):
+            buf = (C.c_char * len(w)).from_buffer_copy(w) if isinstance(w, bytes) else (C.c_char * len(w)).from_buffer(w)
+            ptr, n = C.addressof(buf), len(w)
+        else:
+            arr = np.ascontiguousarray(w).view(np.uint8).reshape(-1)
+            ptr, n = arr.ctypes.data, arr.nbytes
+        h = C.c_void_p()
+        _check(lib.qne_model_load(index_json, len(index_json), C.c_void_p(ptr), n, device, C.byref(h)))
+        self._h = h
+        info = _Info()
+        _check(lib.qne_model_info_get(self._h, C.byref(info)))
+        self.layers = info.layers
+        self.hidden = info.hidden
+        self.intermediate = info.intermediate
+        self.vocab = info.vocab
+        self.weight_kind = info.weight_kind
+        self.embed_kind = info.embed_kind
+        self.tied_lm_head = bool(info.tied_lm_head)
+        self.device = info.device
+        self.weight_bytes = int(info.weight_bytes)
+        self.device_bytes = int(info.device_bytes)
+        self.adapter = lib.qne_adapter(self._h).decode()
+
+    @classmethod
+    def load(cls, index_json, weights, device: int = 0) -> "Model":
+        return cls(index_json, weights, device)
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib.qne_model_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    # -- kernels/src/model.rs API ------------------------------------------------------------
+    def dispatches_per_token(self) -> int:
+        return int(lib.qne_dispatches_per_token(self._h))
+
+    def reset(self) -> None:
+        _check(lib.qne_reset(self._h))
+
+    def prefill(self, ids) -> None:
+        a = _u32_array(ids)
+        _check(lib.qne_prefill(self._h, _u32p(a), len(a)))
+
+    def prefill_batched(self, ids) -> None:
+        self.prefill_from(ids, 0)
+
+    def prefill_from(self, ids, start: int) -> None:
+        self.prefill_chunk(ids, start, True)
+
+    def prefill_chunk(self, ids, start: int, finish_logits: bool) -> None:
+        a = _u32_array(ids)
+        _check(lib.qne_prefill_chunk(self._h, _u32p(a), len(a), start, 1 if finish_logits else 0))
+
+    def logits(self, out: np.ndarray | None = None) -> np.ndarray:
+        out = np.empty(self.vocab, np.float32) if out is None else out
+        _check(lib.qne_logits(self._h, _fp(out), out.size))
+        return out
+
+    def step(self, token: int, pos: int, out: np.ndarray | None = None) -> np.ndarray:
+        out = np.empty(self.vocab, np.float32) if out is None else out
+        _check(lib.qne_step(self._h, token, pos, _fp(out), out.size))
+        return out
+
+    def snapshot(self) -> None:
+        _check(lib.qne_snapshot(self._h))
+
+    def restore(self) -> None:
+        _check(lib.qne_restore(self._h))
+
+    def last_token(self) -> tuple[int, int]:
+        t, p = C.c_uint32(), C.c_uint32()
+        _check(lib.qne_last_token(self._h, C.byref(t), C.byref(p)))
+        return int(t.value), int(p.value)
+
+    def decode(self, n: int, window: int = 1, stop=()) -> list[int]:
+        s = _u32_array(list(stop) or [0])
+        out = np.zeros(max(n, 1), np.uint32)
+        cnt = C.c_uint32()
+        _check(lib.qne_decode(self._h, n, window, _u32p(s), len(stop), _u32p(out), C.byref(cnt)))
+        return [int(x) for x in out[: cnt.value]]
+
+    # -- engine extensions -------------------------------------------------------------------
+    def decode_async(self, steps: int) -> None:
+        _check(lib.qne_decode_async(self._h, steps))
+
+    def step_async(self, token: int, pos: int) -> None:
+        _check(lib.qne_step_async(self._h, token, pos))
+
+    def sync(self, timeout_ms: int = 600_000) -> None:
+        _check(lib.qne_sync(self._h, timeout_ms))
+
+    def set_stream(self, stream_handle: int | None) -> None:
+        _check(lib.qne_model_set_stream(self._h, C.c_void_p(stream_handle or 0)))
+
+    def matrix(self, name: str) -> _Matrix:
+        """Device descriptor of a loaded matrix (index.json name)."""
+        m = _Matrix()
+        _check(lib.qne_model_matrix(self._h, name.encode(), C.byref(m)))
+        return m
+
+    def tensor_ptr(self, name: str) -> int:
+        p = C.c_void_p()
+        _check(lib.qne_model_tensor(self._h, name.encode(), C.byref(p)))
+        return int(p.value)
+
+    def logits_device_ptr(self) -> int:
+        return int(lib.qne_logits_device(self._h) or 0)
+
+
+class Batch:
+    """Independent sequences decoded together on one model's weights."""
+
+    def __init__(self, model: Model, batch: int, pool_pages: int | None = None):
+        self.model = model
+        self.batch = batch
+        self.pool_pages = pool_pages if pool_pages is not None else batch * PAGES_PER_SEQ
+        h = C.c_void_p()
+        _check(lib.qne_batch_create(model._h, batch, self.pool_pages, C.byref(h)))
+        self._h = h
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib.qne_batch_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_page_table(self, table) -> None:
+        a = _u32_array(table).reshape(-1)
+        _check(lib.qne_batch_set_page_table(self._h, _u32p(a), a.size))
+
+    def reset(self) -> None:
+        _check(lib.qne_batch_reset(self._h))
+
+    def step(self, tokens, pos, want_logits: bool = False):
+        t, p = _u32_array(tokens), _u32_array(pos)
+        nxt = np.zeros(self.batch, np.uint32)
+        lg = np.empty((self.batch, self.model.vocab), np.float32) if want_logits else None
+        _check(lib.qne_batch_step(self._h, _u32p(t), _u32p(p), _fp(lg) if lg is not None else None, _u32p(nxt)))
+        return (nxt, lg) if want_logits else nxt
+
+    def decode_async(self, steps: int) -> None:
+        _check(lib.qne_batch_decode_async(self._h, steps))
+
+    def tokens(self):
+        t = np.zeros(self.batch, np.uint32)
+        p = np.zeros(self.batch, np.uint32)
+        _check(lib.qne_batch_tokens(self._h, _u32p(t), _u32p(p)))
+        return t, p
+
+    def fill_synthetic(self, seq: int, length: int, token: int, seed: int) -> None:
+        _check(lib.qne_batch_fill_synthetic(self._h, seq, length, token, seed))
+
+    def sync(self, timeout_ms: int = 600_000) -> None:
+        _check(lib.qne_batch_sync(self._h, timeout_ms))
+
+
+# ---------------------------------------------------------------------------------------------
+# Operators on device tensors (torch tensors or raw pointers)
+# ---------------------------------------------------------------------------------------------
+def _ptr(t) -> int:
+    if t is None:
+        return 0
+    if isinstance(t, int):
+        return t
+    return int(t.data_ptr())
+
+
+def _stream(stream) -> C.c_void_p:
+    if stream is None:
+        try:
+            import torch
+            return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+        except Exception:
+            return C.c_void_p(0)
+    return C.c_void_p(int(stream))
+
+
+def matrix(kind, rows: int, k: int, w, s=None, z=None) -> _Matrix:
+    kind = KINDS[kind] if isinstance(kind, str) else int(kind)
+    return _Matrix(kind, rows, k, 0, _ptr(w), _ptr(s), _ptr(z))
+
+
+def gemv(m: _Matrix, x, y, epilogue="store", stream=None) -> None:
+    epi = EPILOGUES[epilogue] if isinstance(epilogue, str) else int(epilogue)
+    _check(lib.qne_gemv(C.byref(m), _ptr(x), _ptr(y), epi, _stream(stream)))
+
+
+def rmsnorm_gemv(m: _Matrix, h, norm_w, y, epilogue="store", eps: float = 1e-6, stream=None) -> None:
+    epi = EPILOGUES[epilogue] if isinstance(epilogue, str) else int(epilogue)
+    _check(lib.qne_rmsnorm_gemv(C.byref(m), _ptr(h), _ptr(norm_w), eps, _ptr(y), epi, _stream(stream)))
+
+
+def dequant_rows(m: _Matrix, row0: int, nrows: int, out, stream=None) -> None:
+    _check(lib.qne_dequant_rows(C.byref(m), row0, nrows, _ptr(out), _stream(stream)))
+
+
+def embed(m: _Matrix, tok, h, stream=None) -> None:
+    _check(lib.qne_embed(C.byref(m), _ptr(tok), _ptr(h), _stream(stream)))
+
+
+def argmax_scratch_bytes(n: int) -> int:
+    return int(lib.qne_argmax_scratch_bytes(n))
+
+
+def argmax(logits, n: int, tok, scratch, scratch_bytes: int, stream=None) -> None:
+    _check(lib.qne_argmax(_ptr(logits), n, _ptr(tok), _ptr(scratch), scratch_bytes, _stream(stream)))
+
+
+def gdn_step(proj, conv, conv_w, state, params, counter, out, batch: int = 1, stream=None) -> None:
+    _check(lib.qne_gdn_step(_ptr(proj), _ptr(conv), _ptr(conv_w), _ptr(state), _ptr(params), _ptr(counter),
+                            _ptr(out), batch, _stream(stream)))
+
+
+def attention_scratch_bytes(batch: int) -> int:
+    return int(lib.qne_attention_scratch_bytes(batch))
+
+
+def attention_step(proj, norms, theta: float, kv, pool_pages: int, page_table, pos, out, batch, scratch,
+                   scratch_bytes: int, stream=None) -> None:
+    _check(lib.qne_attention_step(_ptr(proj), _ptr(norms), float(theta), _ptr(kv), pool_pages, _ptr(page_table),
+                                  _ptr(pos), _ptr(out), batch, _ptr(scratch), scratch_bytes, _stream(stream)))
+
+
+def kv_gather(kv, page_table, length: int, out_k, out_v, stream=None) -> None:
+    _check(lib.qne_kv_gather(_ptr(kv), _ptr(page_table), length, _ptr(out_k), _ptr(out_v), _stream(stream)))
+
+
+def bandwidth_probe(data, nbytes: int, sink, stream=None) -> None:
+    _check(lib.qne_bandwidth_probe(_ptr(data), nbytes, _ptr(sink), _stream(stream)))
+
+
+def gemm_scratch_bytes(m: _Matrix, batch: int) -> int:
+    return int(lib.qne_gemm_scratch_bytes(C.byref(m), batch))
+
+
+def gemm(m: _Matrix, x, batch: int, y, epilogue="store", scratch=None, scratch_bytes: int = 0, stream=None) -> None:
+    epi = EPILOGUES[epilogue] if isinstance(epilogue, str) else int(epilogue)
+    _check(lib.qne_gemm(C.byref(m), _ptr(x), batch, _ptr(y), epi, _ptr(scratch), scratch_bytes, _stream(stream)))
+
+
+if os.environ.get("QNE_PRINT_VERSION"):
+    print(version())

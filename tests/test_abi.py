@@ -1,0 +1,107 @@
+"""The C ABI library loads and exports every entry point include/qne.h declares; host-side
+validation paths answer with status codes and messages (no device needed)."""
+import json
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import qne
+from qne import synth
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def declared():
+    text = (ROOT / "include" / "qne.h").read_text()
+    return sorted(set(re.findall(r"QNE_API[^;(]*?\b(qne_\w+)\s*\(", text)))
+
+
+def test_header_declares_entry_points():
+    names = declared()
+    assert len(names) >= 40
+    for must in ("qne_model_load", "qne_step", "qne_decode", "qne_prefill_chunk", "qne_snapshot",
+                 "qne_restore", "qne_gemv", "qne_attention_step", "qne_gdn_step", "qne_argmax"):
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol():
+    import subprocess
+    out = subprocess.run(["nm", "-D", "--defined-only", str(qne.LIB_PATH)], capture_output=True, text=True,
+                         check=True).stdout
+    exported = set(re.findall(r" T (qne_\w+)", out))
+    missing = [n for n in declared() if n not in exported]
+    assert not missing, missing
+    for n in declared():
+        assert hasattr(qne.lib, n)
+
+
+def test_version_and_error_state():
+    assert "sm_100a" in qne.version()
+    assert qne.kernel_launches() >= 0
+
+
+def profile(**over):
+    t = {"f16": True, "tpr": 4, "rpw": 32, "rpt": 4, "splits": 1}
+    p = {k: dict(t) for k in ("gdn_in", "attn_in", "out", "gate_up", "down", "lm_head")}
+    for k, v in over.items():
+        p[k].update(v)
+    return json.dumps(p)
+
+
+def test_tile_profile_validation_mirrors_reference_rules():
+    qne.ModelTiles.validate(profile())
+    qne.ModelTiles.validate(profile(down={"splits": 8, "rpw": 16}))
+    for bad in ({"down": {"splits": 0}}, {"lm_head": {"tpr": 0}}, {"out": {"f16": False, "rpt": 2}},
+                {"gate_up": {"tpr": 64, "rpw": 8}}):
+        with pytest.raises(qne.QneError) as e:
+            qne.ModelTiles.validate(profile(**bad))
+        assert e.value.name == "EFORMAT"
+    with pytest.raises(qne.QneError):
+        qne.ModelTiles.validate("{not json")
+
+
+@pytest.fixture(scope="module")
+def tiny():
+    return synth.build(1024, 3584, layers=4, vocab=512, seed=5)
+
+
+def load_err(index, weights):
+    with pytest.raises(qne.QneError) as e:
+        qne.Model(index, weights)
+    return e.value
+
+
+def test_index_validation_rejects_bad_files_before_touching_a_device(tiny):
+    idx = json.loads(tiny.index_json)
+    w = tiny.weights
+    assert load_err("{", w).name == "EFORMAT"
+    bad = json.loads(tiny.index_json)
+    bad["config"]["rope_dim"] = 32
+    assert "architecture" in str(load_err(json.dumps(bad), w))
+    bad = json.loads(tiny.index_json)
+    bad["tensors"]["layer0.post_norm"]["bytes"] += 4
+    assert "invalid tensor size" in str(load_err(json.dumps(bad), w))
+    bad = json.loads(tiny.index_json)
+    bad["tensors"]["layer1.down.w"]["offset"] = int(w.nbytes)
+    assert "invalid tensor range" in str(load_err(json.dumps(bad), w))
+    bad = json.loads(tiny.index_json)
+    bad["tensors"]["layer1.down.w"]["offset"] += 2
+    assert "invalid tensor range" in str(load_err(json.dumps(bad), w))
+    bad = json.loads(tiny.index_json)
+    bad["matrices"]["layer2.gate_up"]["rows"] = 100
+    assert "invalid matrix shape" in str(load_err(json.dumps(bad), w))
+    bad = json.loads(tiny.index_json)
+    del bad["tensors"]["layer3.attn_norms"]
+    assert "invalid tensor size" in str(load_err(json.dumps(bad), w))
+    bad = json.loads(tiny.index_json)
+    bad["matrices"]["layer0.mixer_in"]["kind"] = "q8"
+    assert "kind" in str(load_err(json.dumps(bad), w))
+    # truncated weights: the last tensor now ends past the buffer
+    assert "invalid tensor range" in str(load_err(tiny.index_json, w[: w.nbytes - 4096]))
+    # a valid file gets past validation and stops at the device (no GPU in this container)
+    try:
+        qne.Model(tiny.index_json, w)
+    except qne.QneError as e:
+        assert e.name in ("ECUDA", "EINVAL")
