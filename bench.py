@@ -76,7 +76,7 @@ class Clocks:
         sm = [float(r[1]) for r in rows if len(r) >= 9]
         mx = [float(r[2]) for r in rows if len(r) >= 9]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows if len(r) >= 9 for i in range(4) if "Active" in r[5 + i]})
+        reasons = sorted({names[i] for r in rows if len(r) >= 9 for i in range(4) if r[5 + i].strip() == "Active"})
         return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
                 "reasons": reasons, "samples": len(sm)}
 
@@ -129,7 +129,10 @@ def reference_arm(args, world, rank):
 
 
 def time_gemv_family(model, torch, reps: int = 3):
-    """Live CUDA-event timing of the SwiGLU gate_up GEMV of every layer (the dominant kernel)."""
+    """Live CUDA-event timing of the SwiGLU gate_up GEMV of every layer (the dominant kernel).
+    The stream is first held by a spin kernel so that all launches and events are queued before
+    the GPU reaches them: the events then bracket device execution, not host launch overhead.
+    Rotating over the 24 layers' matrices (1.2 GB) keeps every launch reading from HBM."""
     import qne
     stream = torch.cuda.current_stream()
     H, I = model.hidden, model.intermediate
@@ -141,6 +144,7 @@ def time_gemv_family(model, torch, reps: int = 3):
         qne.rmsnorm_gemv(m, h, g, act, "swiglu", stream=stream.cuda_stream)
     torch.cuda.synchronize()
     events = [torch.cuda.Event(enable_timing=True) for _ in range(reps * len(mats) + 1)]
+    torch.cuda._sleep(100_000_000)
     events[0].record(stream)
     k = 1
     for _ in range(reps):
@@ -155,6 +159,156 @@ def time_gemv_family(model, torch, reps: int = 3):
     return mean_ms, bytes_per_launch
 
 
+def micro(args):
+    """per-kernel microbench (seed 4). Each kernel is timed over enough distinct
+    copies of its inputs that every launch reads HBM (> 126 MB L2 per rotation); launches are queued
+    behind a spin kernel so CUDA events measure device time. One JSON line per case."""
+    import torch
+    import qne
+    torch.cuda.set_device(0)
+    peak, peak_kind = peaks()
+    rng = np.random.default_rng(4)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    sel = set(args.micro.split(","))
+    out = []
+
+    def timed(launch, copies, reps):
+        for i in range(copies):
+            launch(i)
+        torch.cuda.synchronize()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        torch.cuda._sleep(50_000_000)
+        ev[0].record(stream)
+        for r in range(reps):
+            for i in range(copies):
+                launch(i)
+        ev[1].record(stream)
+        torch.cuda.synchronize()
+        return ev[0].elapsed_time(ev[1]) * 1e3 / (reps * copies)  # us per launch
+
+    keep = []
+    if sel & {"all", "gemv"}:
+        for kind in ("f16", "q4g64"):
+            for (K, N) in ((2048, 6144), (6144, 2048), (2048, 4096), (1024, 248320)):
+                el = N * K
+                nbytes = el * 2 if kind == "f16" else el // 2 + el // 16
+                copies = max(1, min(16, int(2.5e8 // nbytes) + 1))
+                mats = []
+                for c in range(copies):
+                    if kind == "f16":
+                        w = torch.from_numpy(rng.standard_normal(el, dtype=np.float32).astype(np.float16)).cuda()
+                        mats.append(qne.matrix("f16", N, K, w))
+                        keep.append(w)
+                    else:
+                        w = torch.randint(-2**31, 2**31 - 1, (el // 8,), dtype=torch.int32, device="cuda")
+                        sc = (torch.rand(el // 64, device="cuda") * 0.01).half()
+                        zp = torch.full((el // 64,), 8.0, device="cuda").half()
+                        mats.append(qne.matrix("q4g64", N, K, w, sc, zp))
+                        keep.extend([w, sc, zp])
+                x = torch.randn(K, device="cuda")
+                y = torch.empty(N, device="cuda")
+                us = timed(lambda i: qne.gemv(mats[i], x, y, "store", stream=stream.cuda_stream), copies,
+                           max(2, 64 // copies))
+                gbs = nbytes / (us * 1e-6) / 1e9
+                out.append({"micro": "gemv", "kind": kind, "K": K, "N": N, "us": round(us, 2),
+                            "GBs": round(gbs, 1), "frac_of_" + peak_kind: round(gbs / peak, 4), "bytes": nbytes})
+                keep.clear()
+    if sel & {"all", "gdn"}:
+        for B in (1, 32):
+            copies = max(2, int(2.5e8 // (B * 16 * 128 * 128 * 4)) + 1)
+            proj = torch.randn(B, 8224, device="cuda")
+            conv_w = torch.rand(6144 * 4, device="cuda") - 0.5
+            prm = torch.cat([torch.zeros(16), torch.full((16,), -0.5), torch.ones(128)]).cuda()
+            states = [torch.randn(B, 16, 128, 128, device="cuda") * 0.1 for _ in range(copies)]
+            rings = [torch.zeros(B, 4, 6144, device="cuda") for _ in range(copies)]
+            ctr = torch.full((B,), 5, dtype=torch.int32, device="cuda")
+            o = torch.empty(B, 2048, device="cuda")
+            us = timed(lambda i: qne.gdn_step(proj, rings[i], conv_w, states[i], prm, ctr, o, B,
+                                              stream=stream.cuda_stream), copies, 4)
+            nbytes = B * 2 * 16 * 128 * 128 * 4
+            gbs = nbytes / (us * 1e-6) / 1e9
+            out.append({"micro": "gdn", "batch": B, "us": round(us, 2), "GBs": round(gbs, 1),
+                        "frac_of_" + peak_kind: round(gbs / peak, 4), "bytes": nbytes,
+                        "note": "gdn_step + gated norm (2 launches)"})
+    if sel & {"all", "attn"}:
+        for B in (1, 32):
+            for ctx in (512, 2048, 4096):
+                pool_pages = B * 256
+                per = pool_pages * 16384 * 2
+                copies = max(1, min(24, int(3e8 // (B * ctx * 2048)) + 1))
+                pools = [torch.randn(pool_pages * 16384, device="cuda").half() for _ in range(copies)]
+                table = torch.randperm(pool_pages, device="cuda", dtype=torch.int64).to(torch.int32)
+                proj = torch.randn(B, 5120, device="cuda")
+                norms = torch.ones(512, device="cuda")
+                pos = torch.full((B,), ctx - 1, dtype=torch.int32, device="cuda")
+                o = torch.empty(B, 2048, device="cuda")
+                nbytes_s = qne.attention_scratch_bytes(B)
+                scratch = torch.zeros(nbytes_s, dtype=torch.uint8, device="cuda")
+                us = timed(lambda i: qne.attention_step(proj, norms, 1e7, pools[i], pool_pages, table, pos, o, B,
+                                                        scratch, nbytes_s, stream=stream.cuda_stream), copies,
+                           max(2, 32 // copies))
+                nbytes = B * ctx * 2048
+                gbs = nbytes / (us * 1e-6) / 1e9
+                out.append({"micro": "attention", "batch": B, "ctx": ctx, "us": round(us, 2), "GBs": round(gbs, 1),
+                            "frac_of_" + peak_kind: round(gbs / peak, 4), "bytes": nbytes})
+                del pools
+    for line in out:
+        print(json.dumps(line), flush=True)
+
+
+def batched_run(torch, qne, synth, rank: int, world: int, barrier, max_over_ranks, warmup: int,
+                steps: int = 64, batch: int = 32):
+    """Qwen3.5-0.8B-shaped f16 (seed 3), `batch` independent sequences per GPU
+    with context lengths uniform in [256, 4032] (so 64 steps stay within 4096), randomly permuted
+    16-token page tables, synthetic history (KV pages, GDN states) written on the device, then
+    `steps` greedy steps. Returns a dict for the JSON line (rank 0) or None."""
+    s = synth.build_config(4)
+    model = qne.Model(s.index_json, s.weights, device=torch.cuda.current_device())
+    stream = torch.cuda.current_stream()
+    model.set_stream(stream.cuda_stream)
+    rng = np.random.default_rng(3 + 1000 * rank)
+    lens = rng.integers(256, 4096 - steps - warmup, batch, endpoint=True)
+    bt = qne.Batch(model, batch)
+    bt.set_page_table(rng.permutation(batch * 256).astype(np.uint32))
+    for b in range(batch):
+        bt.fill_synthetic(b, int(lens[b]), int(rng.integers(0, synth.VOCAB)), 3 + 1000 * rank + b)
+    bt.sync()
+    if warmup:
+        bt.decode_async(warmup)
+        bt.sync()
+    launches0 = qne.kernel_launches()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda._sleep(20_000_000)
+    e0.record(stream)
+    bt.decode_async(steps)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    launches = qne.kernel_launches() - launches0
+    ctx_mean = float(lens.mean()) + warmup + steps / 2
+    weights = model.weight_bytes
+    per_seq = 18 * (2 * 16 * 128 * 128 * 4 + 4 * 6144 * 4 + 6144 * 4) + 6 * 2048 * ctx_mean + model.vocab * 4
+    step_bytes = weights + batch * per_seq
+    peak, kind = peaks()
+    bt.close()
+    model.close()
+    if rank != 0:
+        return None
+    tps = world * batch * steps / (ms * 1e-3)
+    return {"workload": f"config 4: Qwen3.5-0.8B-shaped f16 (seed 3), {batch} sequences per GPU, contexts "
+                        f"U[256,{4096 - steps - warmup}] (mean {lens.mean():.0f}), permuted 16-token pages, "
+                        f"{steps} greedy steps",
+            "value": round(tps, 1), "unit": "tok/s", "n_gpus": world, "ms_per_step": round(ms / steps, 4),
+            "bytes_per_step": int(step_bytes),
+            "step_roofline": {"achieved_gbs": round(step_bytes / (ms / steps * 1e-3) / 1e9, 1), "peak": peak,
+                              "frac": round(step_bytes / (ms / steps * 1e-3) / 1e9 / peak, 4),
+                              "peak_source": kind},
+            "gpu_launches": int(launches)}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -163,8 +317,13 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--prompt", type=int, default=PROMPT)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--micro", default="", help="config-5 microbench: all | gemv,gdn,attn")
+    ap.add_argument("--no-batched", action="store_true", help="skip the config-4 batched decode run")
     args = ap.parse_args()
     world, rank, local = dist_setup()
+    if args.micro:
+        micro(args)
+        return
     if args.impl == "reference":
         reference_arm(args, world, rank)
         return
@@ -191,13 +350,15 @@ def main():
         return float(t.item())
 
     steps = args.steps
-    prompt_len = min(args.prompt, 4096 - steps - 1)
+    prompt_len = min(args.prompt, 4096 - steps)
     if prompt_len < 1 or steps < 1 or args.warmup < 0:
-        raise SystemExit("need --steps >= 1 with prompt + steps <= 4095")
+        raise SystemExit("need 1 <= --steps <= 4095")
 
     s = synth.build_config(2)
     model = qne.Model(s.index_json, s.weights, device=local)
-    stream = torch.cuda.current_stream()
+    # one dedicated stream for the engine and the CUDA events that time it
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
     model.set_stream(stream.cuda_stream)
     prompt = synth.prompt_ids(prompt_len, 1 + 1000 * rank)
     model.reset()
@@ -219,6 +380,7 @@ def main():
     barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda._sleep(20_000_000)  # hold the stream while the host queues the steps
     e0.record(stream)
     model.decode_async(steps)
     e1.record(stream)
@@ -250,6 +412,12 @@ def main():
     peak, peak_kind = peaks()
     achieved = gemv_bytes / (gemv_ms * 1e-3) / 1e9
 
+    dispatches = model.dispatches_per_token()
+    model.close()
+    batched = None
+    if not args.no_batched:
+        batched = batched_run(torch, qne, synth, rank, world, barrier, max_over_ranks, args.warmup)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, cores = cpu_oracle_rate(s, 16, 4, 1)
@@ -280,12 +448,12 @@ def main():
             "step_roofline": {"bytes_per_token": int(tok_bytes), "achieved_gbs": round(tok_bytes * value / world / 1e9, 1),
                               "frac": round(tok_bytes * value / world / 1e9 / peak, 4)},
             "gpu_launches": int(launches),
-            "dispatches_per_token": model.dispatches_per_token(),
+            "dispatches_per_token": dispatches,
             "clocks": clk,
             "cpu_baseline": cpu,
+            "batched": batched,
         }
         print(json.dumps(line), flush=True)
-    model.close()
     if world > 1:
         dist.destroy_process_group()
 

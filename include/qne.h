@@ -172,7 +172,9 @@ QNE_API void qne_batch_free(qne_batch* b);
 QNE_API qne_status qne_batch_set_page_table(qne_batch* b, const uint32_t* table, size_t n);
 QNE_API qne_status qne_batch_reset(qne_batch* b);
 /* One decode step for every sequence: tokens[i] at pos[i] (host arrays of `batch`).
- * logits_out (host, batch x vocab) and next_out (host, batch greedy picks) may be NULL. */
+ * logits_out (host, batch x vocab) and next_out (host, batch greedy picks) may be NULL.
+ * Afterwards sequence i stands at (its greedy pick, pos[i] + 1), so qne_batch_decode_async
+ * continues from there. */
 QNE_API qne_status qne_batch_step(qne_batch* b, const uint32_t* tokens, const uint32_t* pos,
                           float* logits_out, uint32_t* next_out);
 /* Enqueues `steps` greedy steps for all sequences (each feeds back its own pick). */

@@ -1,0 +1,59 @@
+// Kernels and launchers of the batched (independent sequences) decode path.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+#include "gemv.cuh"
+
+namespace qne {
+
+// Y[b][row] for b < batch: W [rows][k] f16 times the activation planes xh/xl [>= 8*ceil(batch/8)][ldx].
+struct GemmArgs {
+  const void* w = nullptr;
+  int rows = 0;  // physical rows (SwiGLU: gate rows then up rows)
+  int k = 0;
+  int batch = 1;
+  int epi = kStore;  // kStore, kAccumulate (f32 y), kSwiGlu (hi/lo planes yh/yl)
+  int row_groups = 1;  // warps of a CTA along rows (1, 2, 4, 8); the rest split k
+  const uint16_t* xh = nullptr;
+  const uint16_t* xl = nullptr;
+  int ldx = 0;
+  float* y = nullptr;
+  uint16_t* yh = nullptr;
+  uint16_t* yl = nullptr;
+  int ldy = 0;
+};
+int gemm_row_groups(int out_rows);
+const char* check_gemm(const GemmArgs& a);
+cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream, bool pdl);
+
+enum PrepMode : int { kPrepCopy = 0, kPrepNorm = 1, kPrepEmbedNorm = 2, kPrepGdnGate = 3 };
+struct PrepArgs {
+  int mode = kPrepCopy;
+  int k = 0;
+  const float* src = nullptr;  // [batch][lds] (copy / norm / gdn gate raw output)
+  int lds = 0;
+  const float* norm_w = nullptr;
+  float eps = 1e-6f;
+  const float* zgate = nullptr;  // gdn gate: proj [batch][8224], z at column 6144
+  Mat embed;                     // embed: matrix, ctl (token, count), h out [batch][ldh]
+  SeqCtl* ctl = nullptr;
+  float* h = nullptr;
+  int ldh = 0;
+  uint16_t* xh = nullptr;
+  uint16_t* xl = nullptr;
+  int ldx = 0;
+};
+cudaError_t launch_prep(const PrepArgs& a, int batch, cudaStream_t stream, bool pdl);
+
+size_t argmax_batched_scratch_bytes(int batch);
+cudaError_t launch_argmax_batched(const float* logits, uint32_t n, size_t ld, int batch, SeqCtl* ctl,
+                                  uint32_t* picks, void* scratch, int update, cudaStream_t stream, bool pdl);
+cudaError_t launch_fill_kv(uint16_t* kv, const uint32_t* table, uint32_t len, uint64_t seed, uint32_t pool_pages,
+                           cudaStream_t stream);
+cudaError_t launch_fill_f32(float* p, size_t n, uint64_t seed, float scale, cudaStream_t stream);
+cudaError_t launch_hilo_to_f32(const uint16_t* hi, const uint16_t* lo, float* out, size_t n, cudaStream_t stream);
+
+}  // namespace qne

@@ -53,6 +53,12 @@ void check_launch(cudaError_t e, const char* what) { cuda_check(e, what); }
 
 extern "C" {
 
+// Error slot shared with the batch entry points (not exported).
+qne_status qne_internal_fail(int code, const char* msg) {
+  g_error = msg ? msg : "";
+  return code;
+}
+
 const char* qne_last_error(void) { return g_error.c_str(); }
 const char* qne_version(void) { return "qne-b200 0.1 (sm_100a)"; }
 uint64_t qne_kernel_launches(void) { return launches_issued(); }

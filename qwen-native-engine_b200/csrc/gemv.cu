@@ -19,6 +19,7 @@
 #include <atomic>
 
 #include "gemv.cuh"
+#include "tma.cuh"
 
 namespace qne {
 
@@ -81,11 +82,33 @@ __device__ __forceinline__ void prefetch_rows(const uint8_t* base, size_t row_by
   }
 }
 
+// Barrier over the 256 threads that stage x: the whole CTA (register kernel) or the consumer
+// warps only (bulk-copy kernel, whose producer warp never joins).
+struct CtaSync {
+  __device__ __forceinline__ void operator()() const { __syncthreads(); }
+};
+struct ConsumerSync {
+  __device__ __forceinline__ void operator()() const { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+};
+
+template <typename Sync>
+__device__ __forceinline__ float sum256(float v, float* red, Sync sync) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  sync();
+  if (l == 0) red[w] = v;
+  sync();
+  float t = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) t += red[i];
+  return t;
+}
+
 // ------------------------------------------------------------------------------------------
 // Prologues: stage the f32 input vector of length k in shared memory.
 // ------------------------------------------------------------------------------------------
-template <int PRO>
-__device__ __forceinline__ void stage_x(const GemvArgs& a, float* xs, float* red) {
+template <int PRO, typename Sync = CtaSync>
+__device__ __forceinline__ void stage_x(const GemvArgs& a, float* xs, float* red, Sync sync = Sync()) {
   const int k = a.m.k;
   const int tid = threadIdx.x;
   if (PRO == kProCopy) {
@@ -113,7 +136,7 @@ __device__ __forceinline__ void stage_x(const GemvArgs& a, float* xs, float* red
         if (tid == 0) a.ctl->count += 1;  // one more token entered the conv windows
       }
     }
-    const float tot = block_sum<kThreads>(ss, red);
+    const float tot = sum256(ss, red, sync);
     const float inv = rsqrtf(tot / (float)k + a.eps);
     for (int i = tid; i < k; i += kThreads) xs[i] = xs[i] * inv * a.norm_w[i];
   } else if (PRO == kProGdnGate) {
@@ -134,7 +157,7 @@ __device__ __forceinline__ void stage_x(const GemvArgs& a, float* xs, float* red
       xs[base + 3] = v.w * inv * silu(zz.w) * nw.w;
     }
   }
-  __syncthreads();
+  sync();
 }
 
 // ------------------------------------------------------------------------------------------
@@ -165,6 +188,208 @@ __device__ __forceinline__ float dot_q4_raw(const uint4& w, const float* x) {
     p[e] = s;
   }
   return (p[0] + p[1]) + (p[2] + p[3]);
+}
+
+// ------------------------------------------------------------------------------------------
+// f16 GEMV streamed by the bulk-copy (TMA) unit.
+//
+// A CTA owns a contiguous range of output rows. Its rows are cut into groups (16 physical rows:
+// 16 plain rows, or 8 gate + 8 up rows for SwiGLU) and each group into 512-element segments;
+// one stage = one group x one segment = 16 KB in shared memory, and a ring of kStagesT stages
+// is kept in flight by one producer thread issuing 1 KB bulk copies (one per row) that complete
+// on the stage's mbarrier. The producer starts before the programmatic-launch wait: weights do
+// not depend on the previous kernel, so up to 80 KB per CTA is already arriving while the
+// previous kernel finishes. Eight consumer warps stage x, then each takes two row slots of every
+// stage (x is read once from shared memory for both), accumulates in f32 across the segments of
+// its rows, and releases the stage.
+// ------------------------------------------------------------------------------------------
+constexpr int kSegE = 512;                 // elements per row segment
+constexpr int kSegB = kSegE * 2;           // bytes per row segment
+constexpr int kSlots = 16;                 // physical rows per stage
+constexpr int kStageB = kSlots * kSegB;    // 16 KB
+constexpr int kStagesT = 5;                // 80 KB ring
+constexpr int kConsumers = 8;
+constexpr int kThreadsT = (kConsumers + 1) * 32;
+
+__host__ __device__ inline size_t tma_smem_bytes(int k) {
+  return 128 + (size_t)kStagesT * kStageB + (size_t)k * 4;
+}
+
+template <int PRO, int EPI>
+__global__ void __launch_bounds__(kThreadsT, 2) gemv_tma_kernel(const GemvArgs a) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw);
+  uint64_t* empty = full + kStagesT;
+  uint8_t* ring = smem_raw + 128;
+  float* xs = reinterpret_cast<float*>(ring + (size_t)kStagesT * kStageB);
+  __shared__ float red[8];
+  __shared__ float bval[8];
+  __shared__ uint32_t bidx[8];
+  __shared__ uint32_t is_last;
+
+  constexpr bool SW = (EPI == kSwiGlu);
+  constexpr int GROUP_OUT = SW ? kSlots / 2 : kSlots;  // output rows per group
+  const int k = a.m.k;
+  const int nseg = k / kSegE;
+  const int out_rows = SW ? a.m.rows / 2 : a.m.rows;
+  const long half = SW ? a.m.rows / 2 : 0;
+  const size_t rb = (size_t)k * 2;
+  const long r0 = (long)blockIdx.x * out_rows / gridDim.x;
+  const long r1 = (long)(blockIdx.x + 1) * out_rows / gridDim.x;
+  const int ngroups = (int)((r1 - r0 + GROUP_OUT - 1) / GROUP_OUT);
+  const int nstages = ngroups * nseg;
+  const uint8_t* W = static_cast<const uint8_t*>(a.m.w);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStagesT; ++i) {
+      mbar_init(smem_u32(full + i), 1);
+      mbar_init(smem_u32(empty + i), kConsumers);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  pdl_launch();
+
+  if (warp == kConsumers) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      for (int q = 0; q < nstages; ++q) {
+        const int slot = q % kStagesT;
+        if (q >= kStagesT && !mbar_wait(smem_u32(empty + slot), ((q / kStagesT) - 1) & 1, a.err)) break;
+        const int grp = q / nseg, sg = q % nseg;
+        const long gr0 = r0 + (long)grp * GROUP_OUT;
+        const int valid = (int)min((long)GROUP_OUT, r1 - gr0);
+        const uint32_t bytes = (uint32_t)(valid * (SW ? 2 : 1)) * kSegB;
+        const uint32_t fb = smem_u32(full + slot);
+        mbar_arrive_expect_tx(fb, bytes);
+        const uint32_t dst = smem_u32(ring + (size_t)slot * kStageB);
+        for (int j = 0; j < valid; ++j) {
+          if (SW) {
+            bulk_g2s(dst + (2 * j) * kSegB, W + (size_t)(gr0 + j) * rb + (size_t)sg * kSegB, kSegB, fb);
+            bulk_g2s(dst + (2 * j + 1) * kSegB, W + (size_t)(half + gr0 + j) * rb + (size_t)sg * kSegB, kSegB, fb);
+          } else {
+            bulk_g2s(dst + j * kSegB, W + (size_t)(gr0 + j) * rb + (size_t)sg * kSegB, kSegB, fb);
+          }
+        }
+      }
+    }
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  pdl_wait();
+  stage_x<PRO>(a, xs, red, ConsumerSync());
+
+  float best_v = -INFINITY;
+  uint32_t best_i = 0xFFFFFFFFu;
+  float acc0 = 0.f, acc1 = 0.f;
+  bool ok = true;
+  for (int q = 0; q < nstages && ok; ++q) {
+    const int slot = q % kStagesT;
+    ok = mbar_wait(smem_u32(full + slot), (q / kStagesT) & 1, a.err);
+    if (!ok) break;
+    const int grp = q / nseg, sg = q % nseg;
+    const long gr0 = r0 + (long)grp * GROUP_OUT;
+    const uint8_t* st = ring + (size_t)slot * kStageB;
+    // row slots 2w and 2w+1 of this stage
+    const int s0 = 2 * warp, s1 = 2 * warp + 1;
+    const long o0 = SW ? gr0 + warp : gr0 + s0;  // output row of slot s0
+    const long o1 = SW ? o0 : gr0 + s1;
+    const bool v0 = o0 < r1, v1 = o1 < r1;
+    const float* xseg = xs + sg * kSegE;
+#pragma unroll
+    for (int m = 0; m < kSegE / 256; ++m) {
+      const int c = lane + 32 * m;
+      float xv[8];
+      *reinterpret_cast<float4*>(xv) = *reinterpret_cast<const float4*>(xseg + c * 8);
+      *reinterpret_cast<float4*>(xv + 4) = *reinterpret_cast<const float4*>(xseg + c * 8 + 4);
+      if (v0) acc0 += dot_f16(*reinterpret_cast<const uint4*>(st + s0 * kSegB + c * 16), xv);
+      if (v1) acc1 += dot_f16(*reinterpret_cast<const uint4*>(st + s1 * kSegB + c * 16), xv);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(empty + slot));
+    if (sg == nseg - 1) {
+      const float t0 = warp_sum(acc0), t1 = warp_sum(acc1);
+      acc0 = acc1 = 0.f;
+      if (SW) {
+        if (v0 && lane == 0) a.y[o0] = silu(t0) * t1;
+      } else {
+        if (EPI == kArgmax) {
+          if (v0 && t0 > -INFINITY && (t0 > best_v || (t0 == best_v && (uint32_t)o0 < best_i))) {
+            best_v = t0;
+            best_i = (uint32_t)o0;
+          }
+          if (v1 && t1 > -INFINITY && (t1 > best_v || (t1 == best_v && (uint32_t)o1 < best_i))) {
+            best_v = t1;
+            best_i = (uint32_t)o1;
+          }
+        }
+        if (lane == 0) {
+          if (EPI == kAccumulate) {
+            if (v0) a.y[o0] += t0;
+            if (v1) a.y[o1] += t1;
+          } else {
+            if (v0) a.y[o0] = t0;
+            if (v1) a.y[o1] = t1;
+          }
+        }
+      }
+    }
+  }
+
+  if (EPI == kArgmax) {
+    if (lane == 0) {
+      bval[warp] = best_v;
+      bidx[warp] = best_i;
+    }
+    ConsumerSync()();
+    if (threadIdx.x == 0) {
+      float v = -INFINITY;
+      uint32_t ix = 0xFFFFFFFFu;
+      for (int w = 0; w < kConsumers; ++w) {
+        if (bidx[w] != 0xFFFFFFFFu && (ix == 0xFFFFFFFFu || bval[w] > v || (bval[w] == v && bidx[w] < ix))) {
+          v = bval[w];
+          ix = bidx[w];
+        }
+      }
+      a.part_val[blockIdx.x] = v;
+      a.part_idx[blockIdx.x] = ix;
+      __threadfence();
+      const uint32_t t = atomicAdd(a.ticket, 1u);
+      is_last = (t == gridDim.x - 1) ? 1u : 0u;
+    }
+    ConsumerSync()();
+    if (is_last && warp == 0) {
+      __threadfence();
+      float v = -INFINITY;
+      uint32_t ix = 0xFFFFFFFFu;
+      for (int b = lane; b < (int)gridDim.x; b += 32) {
+        const float bv = __ldcg(a.part_val + b);
+        const uint32_t bi = __ldcg(a.part_idx + b);
+        if (bi != 0xFFFFFFFFu && (ix == 0xFFFFFFFFu || bv > v || (bv == v && bi < ix))) {
+          v = bv;
+          ix = bi;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+        const uint32_t oi = __shfl_xor_sync(0xffffffffu, ix, o);
+        if (oi != 0xFFFFFFFFu && (ix == 0xFFFFFFFFu || ov > v || (ov == v && oi < ix))) {
+          v = ov;
+          ix = oi;
+        }
+      }
+      if (lane == 0) {
+        if (a.update_token) {
+          a.ctl->token = (ix == 0xFFFFFFFFu) ? 0u : ix;
+          a.ctl->pos += 1;
+        }
+        *a.ticket = 0u;
+      }
+    }
+  }
 }
 
 template <int KIND, int PRO, int EPI, int NR>
@@ -465,8 +690,36 @@ cudaError_t launch_nr(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   return launch_t<KIND, PRO, EPI, 2>(a, stream, pdl);
 }
 
+template <int PRO, int EPI>
+cudaError_t launch_tma(const GemvArgs& a, cudaStream_t stream, bool pdl) {
+  auto kernel = gemv_tma_kernel<PRO, EPI>;
+  const size_t smem = tma_smem_bytes(a.m.k);
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  const int out_rows = (EPI == kSwiGlu) ? a.m.rows / 2 : a.m.rows;
+  const int per_group = (EPI == kSwiGlu) ? kSlots / 2 : kSlots;
+  int grid = (out_rows + per_group - 1) / per_group;
+  if (grid > kNumSms) grid = kNumSms;
+  if (grid < 1) grid = 1;
+  return launch_ex(kernel, dim3(grid), dim3(kThreadsT), smem, stream, pdl, a);
+}
+
 template <int KIND>
 cudaError_t launch_kind(const GemvArgs& a, cudaStream_t stream, bool pdl) {
+  if (KIND == kF16 && a.m.k % kSegE == 0) {
+#define QNE_TCOMBO(P, E) \
+    if (a.pro == P && a.epi == E) return launch_tma<P, E>(a, stream, pdl);
+    QNE_TCOMBO(kProCopy, kStore)
+    QNE_TCOMBO(kProCopy, kAccumulate)
+    QNE_TCOMBO(kProCopy, kSwiGlu)
+    QNE_TCOMBO(kProRmsNorm, kStore)
+    QNE_TCOMBO(kProRmsNorm, kAccumulate)
+    QNE_TCOMBO(kProRmsNorm, kSwiGlu)
+    QNE_TCOMBO(kProRmsNorm, kArgmax)
+    QNE_TCOMBO(kProEmbedNorm, kStore)
+    QNE_TCOMBO(kProGdnGate, kAccumulate)
+#undef QNE_TCOMBO
+  }
 #define QNE_COMBO(P, E) \
   if (a.pro == P && a.epi == E) return launch_nr<KIND, P, E>(a, stream, pdl);
   QNE_COMBO(kProCopy, kStore)

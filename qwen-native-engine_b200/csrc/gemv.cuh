@@ -34,6 +34,7 @@ struct GemvArgs {
   uint32_t* part_idx = nullptr;  // kArgmax scratch: per-CTA best index
   uint32_t* ticket = nullptr;    // kArgmax scratch: CTA completion counter (starts at 0)
   int update_token = 0;          // kArgmax: write the pick to ctl->token and advance ctl->pos
+  uint32_t* err = nullptr;       // optional: receives kFlagTimeout if a bounded wait gives up
 };
 
 // Bytes of scratch the kArgmax epilogue needs.

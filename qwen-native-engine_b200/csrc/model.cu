@@ -346,7 +346,8 @@ Runner::~Runner() {
 void Runner::record(Variant v, cudaStream_t s) {
   const Model& M = *m;
   size_t n = 0;
-  auto gemv = [&](const GemvArgs& a) {
+  auto gemv = [&](GemvArgs a) {
+    a.err = &st.ctl->flags;
     if (const char* why = check_gemv(a)) throw QneError(kEInval, why);
     cuda_check(launch_gemv(a, s, true), "gemv launch");
     ++n;

@@ -1,0 +1,139 @@
+"""Batched decode (independent sequences) on the B200: the tensor-core GEMM
+against the oracle GEMV per sequence, the whole batched step against one oracle model per
+sequence, and page-table permutations that must not change a single bit."""
+import numpy as np
+import pytest
+import torch
+
+import qne
+import refchecks as rc
+from oracle import oracle
+from qne import synth
+
+pytestmark = pytest.mark.gpu
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+@pytest.mark.parametrize("batch", [1, 3, 8, 13, 32])
+@pytest.mark.parametrize("epilogue,rows,k", [("store", 1024, 1024), ("accumulate", 1024, 3584), ("swiglu", 2 * 3584, 1024),
+                                             ("store", 8224, 2048), ("store", 4099, 1024)])
+def test_gemm_matches_gemv_per_sequence(cuda, batch, epilogue, rows, k):
+    rng = np.random.default_rng(batch * 7 + rows)
+    w = (rng.standard_normal(rows * k) * 0.05).astype(np.float16)
+    x = rng.standard_normal((batch, k)).astype(np.float32)
+    out_rows = rows // 2 if epilogue == "swiglu" else rows
+    y0 = rng.standard_normal((batch, out_rows)).astype(np.float32)
+    wd = dev(w)
+    m = qne.matrix("f16", rows, k, wd)
+    xd = dev(x)
+    yd = dev(y0 if epilogue == "accumulate" else np.zeros((batch, out_rows), np.float32))
+    qne.gemm(m, xd, batch, yd, epilogue)
+    torch.cuda.synchronize()
+    got = yd.cpu().numpy()
+    for b in range(batch):
+        want = y0[b].copy() if epilogue == "accumulate" else np.zeros(out_rows, np.float32)
+        oracle.gemv("f16", w, None, None, rows, k, x[b], want, rc.EPI[epilogue])
+        assert rc.rel_err(got[b], want) < 1e-4, b
+
+
+@pytest.fixture(scope="module")
+def tiny(cuda):
+    s = synth.build(1024, 3584, layers=4, vocab=8192, kind="f16", seed=21)
+    m = qne.Model(s.index_json, s.weights)
+    yield s, m
+    m.close()
+
+
+def test_batched_decode_matches_oracle_per_sequence(tiny):
+    s, m = tiny
+    B, L, steps = 5, 12, 16
+    prompts = np.stack([synth.prompt_ids(L, 100 + b, 8192) for b in range(B)])
+    bt = qne.Batch(m, B)
+    for t in range(L):
+        nxt, lg = bt.step(prompts[:, t], np.full(B, t), want_logits=True)
+    ids = [nxt.copy()]
+    cur = nxt.copy()
+    step_logits = []
+    for i in range(steps):
+        cur, lg2 = bt.step(cur, np.full(B, L + i), want_logits=True)
+        ids.append(cur.copy())
+        step_logits.append(lg2.copy())
+    ids = np.stack(ids, 1)
+    om = oracle.OracleModel(s.index_json, s.weights, kv_f16=True)
+    for b in range(B):
+        om.reset()
+        want = om.prefill(prompts[b])
+        err = np.abs(lg[b].astype(np.float64) - want).max()
+        assert err <= 2e-2 and rc.rel_err(lg[b], want) <= 1e-3, (b, err)
+        want_ids, margins = om.greedy(want, L, steps + 1)
+        for i, (a, w_) in enumerate(zip(ids[b], want_ids)):
+            if a != w_:
+                assert margins[i] < 4e-2, (b, i, a, w_, margins[i])
+                break
+    om.close()
+    bt.close()
+
+
+def test_page_table_permutation_is_bit_exact(tiny):
+    s, m = tiny
+    B, L = 3, 40
+    prompts = np.stack([synth.prompt_ids(L, 200 + b, 8192) for b in range(B)])
+    outs = []
+    for perm in (False, True):
+        bt = qne.Batch(m, B)
+        if perm:
+            table = np.random.default_rng(1).permutation(B * 256).astype(np.uint32)
+            bt.set_page_table(table)
+        for t in range(L):
+            nxt, lg = bt.step(prompts[:, t], np.full(B, t), want_logits=True)
+        outs.append((nxt.copy(), lg.copy()))
+        bt.close()
+    assert np.array_equal(outs[0][0], outs[1][0])
+    assert np.array_equal(outs[0][1].view(np.uint32), outs[1][1].view(np.uint32))
+
+
+def test_greedy_decode_async_matches_host_steps(tiny):
+    """batch_step leaves each sequence at (greedy pick, pos + 1), so the device-resident greedy
+    loop continues exactly where a host-driven loop would."""
+    s, m = tiny
+    B, L, steps = 4, 9, 10
+    prompts = np.stack([synth.prompt_ids(L, 300 + b, 8192) for b in range(B)])
+    a = qne.Batch(m, B)
+    h = qne.Batch(m, B)
+    for t in range(L):
+        nxt_a = a.step(prompts[:, t], np.full(B, t))
+        nxt_h = h.step(prompts[:, t], np.full(B, t))
+    assert np.array_equal(nxt_a, nxt_h)
+    tok, pos = a.tokens()
+    assert np.array_equal(tok, nxt_a) and np.all(pos == L)
+    dev_ids, host_ids = [], []
+    cur = nxt_h.copy()
+    for i in range(steps):
+        a.decode_async(1)
+        dev_ids.append(a.tokens()[0].copy())
+        cur = h.step(cur, np.full(B, L + i))
+        host_ids.append(cur.copy())
+    assert np.array_equal(np.stack(dev_ids), np.stack(host_ids))
+    a.close()
+    h.close()
+
+
+def test_context_limit_and_bad_tables(tiny):
+    s, m = tiny
+    bt = qne.Batch(m, 2)
+    with pytest.raises(qne.QneError) as e:
+        bt.step([1, 2], [0, 4096])
+    assert e.value.name == "ERANGE_CTX"
+    with pytest.raises(qne.QneError) as e:
+        bt.set_page_table(np.full(2 * 256, 2 * 256, np.uint32))
+    assert e.value.name == "EINVAL"
+    bt.fill_synthetic(0, 4000, 5, 1)
+    with pytest.raises(qne.QneError) as e:
+        bt.decode_async(200)
+    assert e.value.name == "ERANGE_CTX"
+    bt.close()
+    with pytest.raises(qne.QneError):
+        qne.Batch(m, 33)

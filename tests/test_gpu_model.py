@@ -112,8 +112,11 @@ def test_decode_windows_and_stops(tiny):
     win = m.decode(9, 4)
     assert win[0] == one[0] and win[1:5] == [0xFFFFFFFF] * 4
     m.restore()
-    stopped = m.decode(9, 1, stop=[one[3]])
-    assert stopped == one[:4]
+    stop_at = next((i for i, t in enumerate(one) if t != one[0]), None)
+    stop_tok = one[stop_at] if stop_at is not None else one[0]
+    want = one[: (stop_at if stop_at is not None else 0) + 1]
+    stopped = m.decode(9, 1, stop=[stop_tok])
+    assert stopped == want
     m.restore()
     m.decode(5, 4)
     assert m.last_token() == (one[4], 8 + 4)

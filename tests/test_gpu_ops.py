@@ -29,6 +29,22 @@ def host(t):
     return t.cpu().numpy()
 
 
+_KEEP = []
+
+
+def devmat(kind, rows, k, w, s=None, z=None):
+    """Matrix descriptor over device copies that stay alive until the module ends (the descriptor
+    holds raw pointers; a freed block would be handed to the next allocation)."""
+    tw = dev(w)
+    ts = None if s is None else dev(s)
+    tz = None if z is None else dev(z)
+    _KEEP.append((tw, ts, tz))
+    if len(_KEEP) > 64:
+        torch.cuda.synchronize()
+        del _KEEP[:32]
+    return qne.matrix(kind, rows, k, tw, ts, tz)
+
+
 @pytest.fixture(scope="module")
 def cases():
     return rc.replay()
@@ -41,9 +57,10 @@ def cases():
 def test_gemv_reference_checks(cuda, cases, i):
     c = cases["gemv"][i]
     out_rows = c.rows // 2 if c.epilogue == "swiglu" else c.rows
-    m = qne.matrix("q4", c.rows, c.k, dev(c.w), dev(c.s), dev(c.z))
+    m = devmat("q4", c.rows, c.k, c.w, c.s, c.z)
     y = dev(c.y0 if c.epilogue == "accumulate" else np.zeros(out_rows, np.float32))
-    qne.gemv(m, dev(c.x), y, c.epilogue)
+    x = dev(c.x)
+    qne.gemv(m, x, y, c.epilogue)
     assert rc.rel_err(host(y), GOLDEN[c.name]) < rc.TOL_GEMV
 
 
@@ -63,14 +80,15 @@ def make_matrix(kind, rows, k, rng, zp_random=False):
 
 
 def run_gemv(kind, mat, rows, k, x, epilogue, y0=None, norm=None):
-    m = qne.matrix(kind, rows, k, dev(mat["w"]), None if mat["s"] is None else dev(mat["s"]),
-                   None if mat["z"] is None else dev(mat["z"]))
+    m = devmat(kind, rows, k, mat["w"], mat["s"], mat["z"])
     out_rows = rows // 2 if epilogue == "swiglu" else rows
     y = dev(y0 if y0 is not None else np.zeros(out_rows, np.float32))
+    xd = dev(x)
     if norm is None:
-        qne.gemv(m, dev(x), y, epilogue)
+        qne.gemv(m, xd, y, epilogue)
     else:
-        qne.rmsnorm_gemv(m, dev(x), dev(norm), y, epilogue)
+        nd = dev(norm)
+        qne.rmsnorm_gemv(m, xd, nd, y, epilogue)
     return host(y)
 
 
@@ -122,9 +140,9 @@ def test_rmsnorm_prologue(cuda, kind):
 
 
 def test_gemv_rejects_bad_shapes(cuda):
-    w = dev(np.zeros(100 * 100, np.float16))
     with pytest.raises(qne.QneError) as e:
-        qne.gemv(qne.matrix("f16", 100, 100, w), dev(np.zeros(100, np.float32)), dev(np.zeros(100, np.float32)))
+        m = devmat("f16", 100, 100, np.zeros(100 * 100, np.float16))
+        qne.gemv(m, dev(np.zeros(100, np.float32)), dev(np.zeros(100, np.float32)))
     assert e.value.name == "EINVAL"
 
 
@@ -136,8 +154,7 @@ def test_dequant_bit_exact(cuda, kind):
     rng = np.random.default_rng(21)
     rows, k = 300, 1024
     mat = make_matrix(kind, rows, k, rng, zp_random=True)
-    m = qne.matrix(kind, rows, k, dev(mat["w"]), None if mat["s"] is None else dev(mat["s"]),
-                   None if mat["z"] is None else dev(mat["z"]))
+    m = devmat(kind, rows, k, mat["w"], mat["s"], mat["z"])
     out = torch.empty((rows - 5, k), dtype=torch.float32, device="cuda")
     qne.dequant_rows(m, 5, rows - 5, out)
     want = oracle.dequant_rows(kind, mat["w"], mat["s"], mat["z"], rows, k, 5, rows - 5)
@@ -147,7 +164,7 @@ def test_dequant_bit_exact(cuda, kind):
 
 def test_embed_reference_check(cuda, cases):
     e = cases["embed"]
-    m = qne.matrix("q4", 300, 1024, dev(e["w"]), dev(e["s"]), dev(e["z"]))
+    m = devmat("q4", 300, 1024, e["w"], e["s"], e["z"])
     tok = dev(np.array([7, 41, 0, 0], np.uint32))
     h = torch.empty(1024, dtype=torch.float32, device="cuda")
     qne.embed(m, tok, h)
@@ -367,4 +384,4 @@ def test_bandwidth_probe_xor(cuda):
     sink = dev(np.zeros(1, np.uint32))
     qne.bandwidth_probe(dev(data), data.nbytes, sink)
     want = np.bitwise_xor.reduce(data)
-    assert int(host(sink)[0]) == int(want)
+    assert int(host(sink).view(np.uint32)[0]) == int(want)
