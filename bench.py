@@ -208,11 +208,14 @@ def micro(args):
                         keep.extend([w, sc, zp])
                 x = torch.randn(K, device="cuda")
                 y = torch.empty(N, device="cuda")
-                us = timed(lambda i: qne.gemv(mats[i], x, y, "store", stream=stream.cuda_stream), copies,
-                           max(2, 64 // copies))
-                gbs = nbytes / (us * 1e-6) / 1e9
-                out.append({"micro": "gemv", "kind": kind, "K": K, "N": N, "us": round(us, 2),
-                            "GBs": round(gbs, 1), "frac_of_" + peak_kind: round(gbs / peak, 4), "bytes": nbytes})
+                variants = [(0, 2), (1, 1), (2, 2)] if kind == "f16" else [(0, 2), (1, 1)]
+                for var, cps in variants:
+                    us = timed(lambda i: qne.gemv_ex(mats[i], x, y, "store", var, cps, stream=stream.cuda_stream),
+                               copies, max(2, 64 // copies))
+                    gbs = nbytes / (us * 1e-6) / 1e9
+                    out.append({"micro": "gemv", "kind": kind, "K": K, "N": N, "variant": var, "ctas_per_sm": cps,
+                                "us": round(us, 2), "GBs": round(gbs, 1), "frac_of_" + peak_kind: round(gbs / peak, 4),
+                                "bytes": nbytes})
                 keep.clear()
     if sel & {"all", "gdn"}:
         for B in (1, 32):

@@ -196,6 +196,12 @@ QNE_API qne_status qne_batch_sync(qne_batch* b, uint32_t timeout_ms);
  * y (= / += / silu-gated) W x for one f32 vector x[k]. For QNE_EPI_SWIGLU, m->rows is the
  * physical row count and y has m->rows / 2 entries. */
 QNE_API qne_status qne_gemv(const qne_matrix* m, const float* x, float* y, int epilogue, void* stream);
+/* qne_gemv with an explicit kernel variant (the counterpart of the reference's per-matrix Tile
+ * choice, kernels/src/lib.rs:39-64): 0 = automatic, 1 = register-streamed 16-byte loads,
+ * 2 = bulk-copy (TMA) shared-memory ring (f16, k % 512 == 0). ctas_per_sm (1 or 2) sizes the
+ * grid of variant 1. */
+QNE_API qne_status qne_gemv_ex(const qne_matrix* m, const float* x, float* y, int epilogue, int variant,
+                               int ctas_per_sm, void* stream);
 /* rmsnorm_width (kernels/src/shaders.rs:380-403) fused in front of the GEMV:
  * x = h * rsqrt(mean(h^2) + eps) * norm_w. */
 QNE_API qne_status qne_rmsnorm_gemv(const qne_matrix* m, const float* h, const float* norm_w, float eps,

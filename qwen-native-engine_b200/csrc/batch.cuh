@@ -37,7 +37,7 @@ struct PrepArgs {
   int lds = 0;
   const float* norm_w = nullptr;
   float eps = 1e-6f;
-  const float* zgate = nullptr;  // gdn gate: proj [batch][8224], z at column 6144
+  const float* zgate = nullptr;  // gdn gate: proj [batch][8224] (z read from column 6144)
   Mat embed;                     // embed: matrix, ctl (token, count), h out [batch][ldh]
   SeqCtl* ctl = nullptr;
   float* h = nullptr;

@@ -287,6 +287,24 @@ qne_status qne_gemv(const qne_matrix* m, const float* x, float* y, int epilogue,
   });
 }
 
+qne_status qne_gemv_ex(const qne_matrix* m, const float* x, float* y, int epilogue, int variant, int ctas_per_sm,
+                       void* stream) {
+  return guarded([&] {
+    GemvArgs a;
+    a.m = to_mat(m);
+    a.pro = kProCopy;
+    a.x = x;
+    a.y = y;
+    if (epilogue < 0 || epilogue > 2) throw QneError(kEInval, "unknown epilogue");
+    if (ctas_per_sm != 1 && ctas_per_sm != 2) throw QneError(kEInval, "ctas_per_sm must be 1 or 2");
+    a.epi = epilogue;
+    a.variant = variant;
+    a.ctas_per_sm = ctas_per_sm;
+    if (const char* why = check_gemv(a)) throw QneError(kEInval, why);
+    check_launch(launch_gemv(a, as_stream(stream), false), "gemv");
+  });
+}
+
 qne_status qne_rmsnorm_gemv(const qne_matrix* m, const float* h, const float* norm_w, float eps,
                             float* y, int epilogue, void* stream) {
   return guarded([&] {

@@ -25,6 +25,7 @@ constexpr int kMixerOut = 2048;
 // One KV page: [K, V][kv head][token][dim] f16.
 constexpr int kPageElems = 2 * kKvHeads * kPageTokens * kHeadDim;  // 16384 halves = 32 KB
 constexpr int kNumSms = 148;
+constexpr int kMaxGrid = 512;  // largest 1-D grid of the B=1 kernels (per-CTA reduction slots)
 
 enum WeightKind : int { kF16 = 0, kQ4 = 1, kQ4G64 = 2 };
 enum Epi : int { kStore = 0, kAccumulate = 1, kSwiGlu = 2, kArgmax = 3 };

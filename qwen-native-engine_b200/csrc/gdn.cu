@@ -25,6 +25,10 @@ namespace qne {
 namespace {
 
 constexpr int kSlice = 16;            // value columns per CTA
+
+__device__ __forceinline__ float sel4(const float* r, int i) {
+  return i == 0 ? r[0] : i == 1 ? r[1] : i == 2 ? r[2] : r[3];
+}
 constexpr int kSlices = kGdnDim / kSlice;  // 8
 
 __global__ void __launch_bounds__(256) gdn_step_kernel(const float* __restrict__ proj, float* conv,
@@ -44,37 +48,54 @@ __global__ void __launch_bounds__(256) gdn_step_kernel(const float* __restrict__
   const int s = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int t0 = s * kSlice;
+  const int jg = tid >> 4, tl = tid & 15;  // state slice: column t0 + tl, rows jg*8 .. jg*8+7
+  float* S = state + ((size_t)b * kGdnHeads + h) * kGdnDim * kGdnDim + t0 + tl;
   pdl_launch();
+  // The state slice is not produced by the previous kernel: warm L2 with it while waiting
+  // (a prefetch only moves lines closer; correctness never depends on it).
+  if (tid < kGdnDim) asm volatile("prefetch.global.L2 [%0];" ::"l"(S - tl + (size_t)tid * kGdnDim));
   pdl_wait();
 
+  // Issue every independent load at once: state slice, counter, proj, all four ring slots (the
+  // slot this step overwrites is read too and discarded, which saves waiting for the counter).
+  float sv[8];
+#pragma unroll
+  for (int jj = 0; jj < 8; ++jj) sv[jj] = S[(size_t)(jg * 8 + jj) * kGdnDim];
   const uint32_t cnt = counter[(size_t)b * counter_stride];
+  const float* pr = proj + (size_t)b * kGdnProj;
+  float* ring = conv + (size_t)b * kConvSlots * kConvChannels;
+  const int i = tid & (kGdnDim - 1);
+  const int ch = (tid < kGdnDim ? 0 : 2048) + h * kGdnDim + i;
+  const float x = pr[ch];
+  const float4 w = *reinterpret_cast<const float4*>(conv_w + (size_t)ch * 4);
+  float rv[4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) rv[r] = ring[r * kConvChannels + ch];
+  float vx = 0.f, vrv[4] = {0.f, 0.f, 0.f, 0.f};
+  float4 vw = make_float4(0.f, 0.f, 0.f, 0.f);
+  const int cv = 4096 + h * kGdnDim + t0 + (tid & (kSlice - 1));
+  if (tid < kSlice) {
+    vx = pr[cv];
+    vw = *reinterpret_cast<const float4*>(conv_w + (size_t)cv * 4);
+#pragma unroll
+    for (int r = 0; r < 4; ++r) vrv[r] = ring[r * kConvChannels + cv];
+  }
   const int slot_new = (int)((cnt - 1u) & 3u);
   const int s2 = (int)((cnt - 2u) & 3u);  // previous input
   const int s1 = (int)((cnt - 3u) & 3u);
   const int s0 = (int)((cnt - 4u) & 3u);  // oldest input of the window
-  const float* pr = proj + (size_t)b * kGdnProj;
-  float* ring = conv + (size_t)b * kConvSlots * kConvChannels;
 
   // q (threads 0..127) and k (threads 128..255) channels of head h.
-  const int i = tid & (kGdnDim - 1);
-  const int ch = (tid < kGdnDim ? 0 : 2048) + h * kGdnDim + i;
   float val;
   {
-    const float x = pr[ch];
-    const float4 w = *reinterpret_cast<const float4*>(conv_w + (size_t)ch * 4);
-    const float y = ring[s0 * kConvChannels + ch] * w.x + ring[s1 * kConvChannels + ch] * w.y +
-                    ring[s2 * kConvChannels + ch] * w.z + x * w.w;
+    const float y = sel4(rv, s0) * w.x + sel4(rv, s1) * w.y + sel4(rv, s2) * w.z + x * w.w;
     val = silu(y);
     if (i >= t0 && i < t0 + kSlice) ring[slot_new * kConvChannels + ch] = x;
   }
   if (tid < kSlice) {
-    const int cv = 4096 + h * kGdnDim + t0 + tid;
-    const float x = pr[cv];
-    const float4 w = *reinterpret_cast<const float4*>(conv_w + (size_t)cv * 4);
-    const float y = ring[s0 * kConvChannels + cv] * w.x + ring[s1 * kConvChannels + cv] * w.y +
-                    ring[s2 * kConvChannels + cv] * w.z + x * w.w;
+    const float y = sel4(vrv, s0) * vw.x + sel4(vrv, s1) * vw.y + sel4(vrv, s2) * vw.z + vx * vw.w;
     vs[tid] = silu(y);
-    ring[slot_new * kConvChannels + cv] = x;
+    ring[slot_new * kConvChannels + cv] = vx;
   }
   // L2 norms: warps 0-3 hold q, warps 4-7 hold k.
   const float ss = warp_sum(val * val);
@@ -93,12 +114,6 @@ __global__ void __launch_bounds__(256) gdn_step_kernel(const float* __restrict__
   const float g = expf(params[16 + h] * logf(1.0f + expf(pr[8192 + h] + params[h])));
   const float beta = 1.0f / (1.0f + expf(-pr[8208 + h]));
 
-  // State slice: thread (jg, tl) owns column t0 + tl, rows jg*8 .. jg*8+7.
-  const int jg = tid >> 4, tl = tid & 15;
-  float* S = state + ((size_t)b * kGdnHeads + h) * kGdnDim * kGdnDim + t0 + tl;
-  float sv[8];
-#pragma unroll
-  for (int jj = 0; jj < 8; ++jj) sv[jj] = S[(size_t)(jg * 8 + jj) * kGdnDim];
   float sk = 0.f, sq = 0.f;
 #pragma unroll
   for (int jj = 0; jj < 8; ++jj) {

@@ -262,7 +262,7 @@ __global__ void __launch_bounds__(256) prep_kernel(const PrepArgs a) {
       const float inv = rsqrtf(ss / 128.0f + a.eps);
       for (int j = 0; j < 4; ++j) {
         const int c = head * 128 + lane * 4 + j;
-        const float z = a.zgate[(size_t)b * kGdnProj + c];
+        const float z = a.zgate[(size_t)b * kGdnProj + 6144 + c];  // z block of proj
         __half hi, lo;
         split_hilo(v[j] * inv * silu(z) * a.norm_w[lane * 4 + j], hi, lo);
         xh[c] = __half_as_ushort(hi);

@@ -211,17 +211,21 @@ constexpr int kStagesT = 5;                // 80 KB ring
 constexpr int kConsumers = 8;
 constexpr int kThreadsT = (kConsumers + 1) * 32;
 
+// Ring depth for a given k: 5 stages, 4 when x (and its planes) would keep two CTAs per SM
+// (the running kernel and the next one's early-streaming CTA) from fitting.
+__host__ __device__ inline int tma_stages(int k) { return k <= 4096 ? kStagesT : kStagesT - 1; }
 __host__ __device__ inline size_t tma_smem_bytes(int k) {
-  return 128 + (size_t)kStagesT * kStageB + (size_t)k * 4;
+  return 128 + (size_t)tma_stages(k) * kStageB + (size_t)k * 8;  // barriers, ring, x, x planes
 }
 
 template <int PRO, int EPI>
 __global__ void __launch_bounds__(kThreadsT, 2) gemv_tma_kernel(const GemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw);
-  uint64_t* empty = full + kStagesT;
+  uint64_t* empty = full + kStagesT;  // barrier slots for the deepest ring
   uint8_t* ring = smem_raw + 128;
-  float* xs = reinterpret_cast<float*>(ring + (size_t)kStagesT * kStageB);
+  const int NS = tma_stages(a.m.k);
+  float* xs = reinterpret_cast<float*>(ring + (size_t)NS * kStageB);
   __shared__ float red[8];
   __shared__ float bval[8];
   __shared__ uint32_t bidx[8];
@@ -242,7 +246,7 @@ __global__ void __launch_bounds__(kThreadsT, 2) gemv_tma_kernel(const GemvArgs a
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kStagesT; ++i) {
+    for (int i = 0; i < NS; ++i) {
       mbar_init(smem_u32(full + i), 1);
       mbar_init(smem_u32(empty + i), kConsumers);
     }
@@ -253,24 +257,29 @@ __global__ void __launch_bounds__(kThreadsT, 2) gemv_tma_kernel(const GemvArgs a
 
   if (warp == kConsumers) {
     // ---------------- producer ----------------
-    if (lane == 0) {
-      for (int q = 0; q < nstages; ++q) {
-        const int slot = q % kStagesT;
-        if (q >= kStagesT && !mbar_wait(smem_u32(empty + slot), ((q / kStagesT) - 1) & 1, a.err)) break;
-        const int grp = q / nseg, sg = q % nseg;
-        const long gr0 = r0 + (long)grp * GROUP_OUT;
-        const int valid = (int)min((long)GROUP_OUT, r1 - gr0);
-        const uint32_t bytes = (uint32_t)(valid * (SW ? 2 : 1)) * kSegB;
-        const uint32_t fb = smem_u32(full + slot);
-        mbar_arrive_expect_tx(fb, bytes);
-        const uint32_t dst = smem_u32(ring + (size_t)slot * kStageB);
-        for (int j = 0; j < valid; ++j) {
-          if (SW) {
-            bulk_g2s(dst + (2 * j) * kSegB, W + (size_t)(gr0 + j) * rb + (size_t)sg * kSegB, kSegB, fb);
-            bulk_g2s(dst + (2 * j + 1) * kSegB, W + (size_t)(half + gr0 + j) * rb + (size_t)sg * kSegB, kSegB, fb);
-          } else {
-            bulk_g2s(dst + j * kSegB, W + (size_t)(gr0 + j) * rb + (size_t)sg * kSegB, kSegB, fb);
-          }
+    // lane 0 arms the stage's barrier with the byte count, then lanes 0..15 issue one row
+    // segment each (gate and up segments for SwiGLU), so a stage costs one issue round.
+    for (int q = 0; q < nstages; ++q) {
+      const int slot = q % NS;
+      bool ok = true;
+      if (q >= NS) {
+        if (lane == 0) ok = mbar_wait(smem_u32(empty + slot), ((q / NS) - 1) & 1, a.err);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+      }
+      if (!ok) break;
+      const int grp = q / nseg, sg = q % nseg;
+      const long gr0 = r0 + (long)grp * GROUP_OUT;
+      const int valid = (int)min((long)GROUP_OUT, r1 - gr0);
+      const uint32_t fb = smem_u32(full + slot);
+      if (lane == 0) mbar_arrive_expect_tx(fb, (uint32_t)(valid * (SW ? 2 : 1)) * kSegB);
+      __syncwarp();
+      const uint32_t dst = smem_u32(ring + (size_t)slot * kStageB);
+      if (lane < valid) {
+        if (SW) {
+          bulk_g2s(dst + (2 * lane) * kSegB, W + (size_t)(gr0 + lane) * rb + (size_t)sg * kSegB, kSegB, fb);
+          bulk_g2s(dst + (2 * lane + 1) * kSegB, W + (size_t)(half + gr0 + lane) * rb + (size_t)sg * kSegB, kSegB, fb);
+        } else {
+          bulk_g2s(dst + lane * kSegB, W + (size_t)(gr0 + lane) * rb + (size_t)sg * kSegB, kSegB, fb);
         }
       }
     }
@@ -280,14 +289,24 @@ __global__ void __launch_bounds__(kThreadsT, 2) gemv_tma_kernel(const GemvArgs a
   // ---------------- consumers ----------------
   pdl_wait();
   stage_x<PRO>(a, xs, red, ConsumerSync());
+  // Repack x as two planes (elements 0-3 and 4-7 of every 8-element chunk) so that a warp's
+  // 16-byte loads of consecutive chunks hit consecutive addresses (no bank conflicts).
+  float* xp = xs + k;  // [2][k/2]
+  for (int c = threadIdx.x; c < k / 8; c += 256) {
+    const float4 lo4 = *reinterpret_cast<const float4*>(xs + c * 8);
+    const float4 hi4 = *reinterpret_cast<const float4*>(xs + c * 8 + 4);
+    *reinterpret_cast<float4*>(xp + c * 4) = lo4;
+    *reinterpret_cast<float4*>(xp + k / 2 + c * 4) = hi4;
+  }
+  ConsumerSync()();
 
   float best_v = -INFINITY;
   uint32_t best_i = 0xFFFFFFFFu;
   float acc0 = 0.f, acc1 = 0.f;
   bool ok = true;
   for (int q = 0; q < nstages && ok; ++q) {
-    const int slot = q % kStagesT;
-    ok = mbar_wait(smem_u32(full + slot), (q / kStagesT) & 1, a.err);
+    const int slot = q % NS;
+    ok = mbar_wait(smem_u32(full + slot), (q / NS) & 1, a.err);
     if (!ok) break;
     const int grp = q / nseg, sg = q % nseg;
     const long gr0 = r0 + (long)grp * GROUP_OUT;
@@ -297,13 +316,14 @@ __global__ void __launch_bounds__(kThreadsT, 2) gemv_tma_kernel(const GemvArgs a
     const long o0 = SW ? gr0 + warp : gr0 + s0;  // output row of slot s0
     const long o1 = SW ? o0 : gr0 + s1;
     const bool v0 = o0 < r1, v1 = o1 < r1;
-    const float* xseg = xs + sg * kSegE;
+    const float* xlo = xp + sg * (kSegE / 2);
+    const float* xhi = xp + k / 2 + sg * (kSegE / 2);
 #pragma unroll
     for (int m = 0; m < kSegE / 256; ++m) {
       const int c = lane + 32 * m;
       float xv[8];
-      *reinterpret_cast<float4*>(xv) = *reinterpret_cast<const float4*>(xseg + c * 8);
-      *reinterpret_cast<float4*>(xv + 4) = *reinterpret_cast<const float4*>(xseg + c * 8 + 4);
+      *reinterpret_cast<float4*>(xv) = *reinterpret_cast<const float4*>(xlo + c * 4);
+      *reinterpret_cast<float4*>(xv + 4) = *reinterpret_cast<const float4*>(xhi + c * 4);
       if (v0) acc0 += dot_f16(*reinterpret_cast<const uint4*>(st + s0 * kSegB + c * 16), xv);
       if (v1) acc1 += dot_f16(*reinterpret_cast<const uint4*>(st + s1 * kSegB + c * 16), xv);
     }
@@ -360,6 +380,275 @@ __global__ void __launch_bounds__(kThreadsT, 2) gemv_tma_kernel(const GemvArgs a
       is_last = (t == gridDim.x - 1) ? 1u : 0u;
     }
     ConsumerSync()();
+    if (is_last && warp == 0) {
+      __threadfence();
+      float v = -INFINITY;
+      uint32_t ix = 0xFFFFFFFFu;
+      for (int b = lane; b < (int)gridDim.x; b += 32) {
+        const float bv = __ldcg(a.part_val + b);
+        const uint32_t bi = __ldcg(a.part_idx + b);
+        if (bi != 0xFFFFFFFFu && (ix == 0xFFFFFFFFu || bv > v || (bv == v && bi < ix))) {
+          v = bv;
+          ix = bi;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+        const uint32_t oi = __shfl_xor_sync(0xffffffffu, ix, o);
+        if (oi != 0xFFFFFFFFu && (ix == 0xFFFFFFFFu || ov > v || (ov == v && oi < ix))) {
+          v = ov;
+          ix = oi;
+        }
+      }
+      if (lane == 0) {
+        if (a.update_token) {
+          a.ctl->token = (ix == 0xFFFFFFFFu) ? 0u : ix;
+          a.ctl->pos += 1;
+        }
+        *a.ticket = 0u;
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// int4 GEMV on the tensor cores (B = 1).
+//
+// A warp owns 16 weight rows (plus the 16 matching up rows for SwiGLU) and a slice of k. In
+// every 32-wide k step lane (g, t) loads one 32-bit word (8 nibbles, k = 32s + 8t .. +7) of rows
+// g and g + 8; (w >> 4i) & 0x000F000F | 0x64006400 turns nibbles i and i + 4 into the f16 pair
+// (1024 + n_i, 1024 + n_{i+4}), and subtracting 1024 leaves the exact integers. Two
+// mma.m16n8k16 per step multiply them with x, fed as column 0 = f16(x) and column 1 =
+// f16(x - f16(x)) (columns 2-7 zero); the k order inside a step is permuted identically for
+// weights and x. One step never crosses a quantization block, so after each block lane t = 0
+// (which holds columns 0 and 1) applies scale * (sum_k n_k x_k - zp * sum_k x_k) in f32.
+// Warps of a CTA split k when the matrix has few rows; partial sums meet in shared memory.
+// ------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t nib_pair_f16(uint32_t w, int i) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, 0x000F000F, 0x64006400, 0xEA;" : "=r"(r) : "r"(w >> (4 * i)));  // (a & b) | c
+  uint32_t out;
+  asm("sub.f16x2 %0, %1, %2;" : "=r"(out) : "r"(r), "r"(0x64006400u));
+  return out;
+}
+
+__device__ __forceinline__ void mma_f16(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                        uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+template <int KIND, int PRO, int EPI>
+__global__ void __launch_bounds__(kThreads, 2) gemv_q4_mma_kernel(const GemvArgs a) {
+  extern __shared__ __align__(16) float xs[];  // [k] x, then [2][k/8] uint4 pair planes, then [k/32] block sums
+  __shared__ float red[kWarps];
+  __shared__ float bval[kWarps];
+  __shared__ uint32_t bidx[kWarps];
+  __shared__ uint32_t is_last;
+  __shared__ float part[kWarps][2][16];
+
+  constexpr bool SW = (EPI == kSwiGlu);
+  const int k = a.m.k;
+  const int out_rows = SW ? a.m.rows / 2 : a.m.rows;
+  const long half = SW ? a.m.rows / 2 : 0;
+  const int tiles = (out_rows + 15) / 16;
+  const int RG = a.row_groups, KG = kWarps / RG;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int rg = warp % RG, kg = warp / RG;
+  const int steps = k / 32;
+  const int s0 = kg * steps / KG, s1 = (kg + 1) * steps / KG;
+  const int blk_steps = (KIND == kQ4) ? 1 : 2;  // k32 steps per quantization block
+  const uint32_t* W = static_cast<const uint32_t*>(a.m.w);
+  const size_t wpr = (size_t)k / 8;  // words per row
+
+  pdl_launch();
+  if (warp == 0) {
+    // warm L2 with the first rows of this CTA while the previous kernel finishes
+    const long r0 = (long)blockIdx.x * RG * 16;
+    const long r1 = min(r0 + (long)RG * 16, (long)out_rows);
+    prefetch_rows(reinterpret_cast<const uint8_t*>(W), wpr * 4, r0, r1, kPrefetchBytes, lane);
+    if (SW) prefetch_rows(reinterpret_cast<const uint8_t*>(W), wpr * 4, half + r0, half + r1, kPrefetchBytes, lane);
+  }
+  pdl_wait();
+  stage_x<PRO>(a, xs, red);
+  // pair planes: for every 8-element group G, (x0,x4),(x1,x5),(x2,x6),(x3,x7) as f16x2, hi and lo
+  uint4* xq = reinterpret_cast<uint4*>(xs + k);
+  float* xsum = xs + k + k;  // after 2 * (k/8) uint4 = k floats
+  for (int G = threadIdx.x; G < k / 8; G += kThreads) {
+    const float* x8 = xs + G * 8;
+    uint32_t hw[4], lw[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __half h0 = __float2half_rn(x8[i]), h1 = __float2half_rn(x8[i + 4]);
+      const __half l0 = __float2half_rn(x8[i] - __half2float(h0)), l1 = __float2half_rn(x8[i + 4] - __half2float(h1));
+      hw[i] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+      lw[i] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+    }
+    xq[G] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    xq[k / 8 + G] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+  }
+  for (int b = threadIdx.x; b < k / 32; b += kThreads) {
+    float sum = 0.f;
+    for (int i = 0; i < 32; ++i) sum += xs[b * 32 + i];
+    xsum[b] = sum;
+  }
+  __syncthreads();
+
+  float best_v = -INFINITY;
+  uint32_t best_i = 0xFFFFFFFFu;
+  constexpr int U = SW ? 4 : 8;  // k32 steps loaded ahead
+  // CTA-uniform loop (every warp runs the same iterations: the k-group reduction synchronizes)
+  for (int base = blockIdx.x * RG; base < tiles; base += gridDim.x * RG) {
+    const int tile = base + rg;
+    const bool tile_ok = tile < tiles;
+    const long rA = min((long)tile * 16 + g, (long)out_rows - 1);
+    const long rB = min((long)tile * 16 + g + 8, (long)out_rows - 1);
+    const uint32_t* wA = W + rA * wpr;
+    const uint32_t* wB = W + rB * wpr;
+    const uint32_t* uA = W + (half + rA) * wpr;
+    const uint32_t* uB = W + (half + rB) * wpr;
+    float totA = 0.f, totB = 0.f, utA = 0.f, utB = 0.f;
+    float c[4] = {0.f, 0.f, 0.f, 0.f}, cu[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int sb = s0; sb < s1; sb += U) {
+      uint32_t wa[U], wb[U], ua[U], ub[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int s = sb + u;
+        const bool ok = s < s1;
+        wa[u] = ok ? __ldg(wA + s * 4 + t) : 0u;
+        wb[u] = ok ? __ldg(wB + s * 4 + t) : 0u;
+        if (SW) {
+          ua[u] = ok ? __ldg(uA + s * 4 + t) : 0u;
+          ub[u] = ok ? __ldg(uB + s * 4 + t) : 0u;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int s = sb + u;
+        if (s >= s1) break;
+        uint4 xb = make_uint4(0u, 0u, 0u, 0u);
+        if (g < 2) xb = xq[(size_t)g * (k / 8) + s * 4 + t];
+        mma_f16(c, nib_pair_f16(wa[u], 0), nib_pair_f16(wb[u], 0), nib_pair_f16(wa[u], 1), nib_pair_f16(wb[u], 1),
+                xb.x, xb.y);
+        mma_f16(c, nib_pair_f16(wa[u], 2), nib_pair_f16(wb[u], 2), nib_pair_f16(wa[u], 3), nib_pair_f16(wb[u], 3),
+                xb.z, xb.w);
+        if (SW) {
+          mma_f16(cu, nib_pair_f16(ua[u], 0), nib_pair_f16(ub[u], 0), nib_pair_f16(ua[u], 1), nib_pair_f16(ub[u], 1),
+                  xb.x, xb.y);
+          mma_f16(cu, nib_pair_f16(ua[u], 2), nib_pair_f16(ub[u], 2), nib_pair_f16(ua[u], 3), nib_pair_f16(ub[u], 3),
+                  xb.z, xb.w);
+        }
+        if ((s + 1) % blk_steps == 0) {
+          if (t == 0) {
+            const int blk = s / blk_steps;  // quantization block (q4: 32 values, q4g64: 64 values)
+            const float xsb = (KIND == kQ4) ? xsum[s] : xsum[s - 1] + xsum[s];
+            float sa, za, sb2, zb;
+            if (KIND == kQ4) {
+              q4_scale_zp((const uint32_t*)a.m.s, (const uint32_t*)a.m.z, rA, k, blk, sa, za);
+              q4_scale_zp((const uint32_t*)a.m.s, (const uint32_t*)a.m.z, rB, k, blk, sb2, zb);
+            } else {
+              q4g64_scale_zp((const uint16_t*)a.m.s, (const uint16_t*)a.m.z, rA, k, blk, sa, za);
+              q4g64_scale_zp((const uint16_t*)a.m.s, (const uint16_t*)a.m.z, rB, k, blk, sb2, zb);
+            }
+            totA = fmaf(sa, (c[0] + c[1]) - za * xsb, totA);
+            totB = fmaf(sb2, (c[2] + c[3]) - zb * xsb, totB);
+            if (SW) {
+              float su, zu, sv, zv;
+              if (KIND == kQ4) {
+                q4_scale_zp((const uint32_t*)a.m.s, (const uint32_t*)a.m.z, half + rA, k, blk, su, zu);
+                q4_scale_zp((const uint32_t*)a.m.s, (const uint32_t*)a.m.z, half + rB, k, blk, sv, zv);
+              } else {
+                q4g64_scale_zp((const uint16_t*)a.m.s, (const uint16_t*)a.m.z, half + rA, k, blk, su, zu);
+                q4g64_scale_zp((const uint16_t*)a.m.s, (const uint16_t*)a.m.z, half + rB, k, blk, sv, zv);
+              }
+              utA = fmaf(su, (cu[0] + cu[1]) - zu * xsb, utA);
+              utB = fmaf(sv, (cu[2] + cu[3]) - zv * xsb, utB);
+            }
+          }
+          c[0] = c[1] = c[2] = c[3] = 0.f;
+          if (SW) cu[0] = cu[1] = cu[2] = cu[3] = 0.f;
+        }
+      }
+    }
+    // k-groups meet in shared memory; lane (g, 0) of the row group holds rows g and g + 8
+    if (KG > 1) {
+      __syncthreads();
+      if (t == 0) {
+        part[warp][0][g] = totA;
+        part[warp][0][g + 8] = totB;
+        part[warp][1][g] = utA;
+        part[warp][1][g + 8] = utB;
+      }
+      __syncthreads();
+      if (kg == 0 && t == 0) {
+        for (int q = 1; q < KG; ++q) {
+          totA += part[rg + q * RG][0][g];
+          totB += part[rg + q * RG][0][g + 8];
+          utA += part[rg + q * RG][1][g];
+          utB += part[rg + q * RG][1][g + 8];
+        }
+      }
+    }
+    if (tile_ok && kg == 0 && t == 0) {
+      const long oa = (long)tile * 16 + g, ob = oa + 8;
+      float va = totA, vb = totB;
+      if (SW) {
+        va = silu(totA) * utA;
+        vb = silu(totB) * utB;
+      }
+      if (oa < out_rows) {
+        if (EPI == kAccumulate) a.y[oa] += va;
+        else a.y[oa] = va;
+        if (EPI == kArgmax && va > -INFINITY && (va > best_v || (va == best_v && (uint32_t)oa < best_i))) {
+          best_v = va;
+          best_i = (uint32_t)oa;
+        }
+      }
+      if (ob < out_rows) {
+        if (EPI == kAccumulate) a.y[ob] += vb;
+        else a.y[ob] = vb;
+        if (EPI == kArgmax && vb > -INFINITY && (vb > best_v || (vb == best_v && (uint32_t)ob < best_i))) {
+          best_v = vb;
+          best_i = (uint32_t)ob;
+        }
+      }
+    }
+  }
+  if (EPI == kArgmax) {
+    // lanes without rows hold no candidate; reduce the warp, then the CTA, then the grid
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best_v, o);
+      const uint32_t oi = __shfl_xor_sync(0xffffffffu, best_i, o);
+      if (oi != 0xFFFFFFFFu && (best_i == 0xFFFFFFFFu || ov > best_v || (ov == best_v && oi < best_i))) {
+        best_v = ov;
+        best_i = oi;
+      }
+    }
+    if (lane == 0) {
+      bval[warp] = best_v;
+      bidx[warp] = best_i;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float v = -INFINITY;
+      uint32_t ix = 0xFFFFFFFFu;
+      for (int w = 0; w < kWarps; ++w)
+        if (bidx[w] != 0xFFFFFFFFu && (ix == 0xFFFFFFFFu || bval[w] > v || (bval[w] == v && bidx[w] < ix))) {
+          v = bval[w];
+          ix = bidx[w];
+        }
+      a.part_val[blockIdx.x] = v;
+      a.part_idx[blockIdx.x] = ix;
+      __threadfence();
+      is_last = (atomicAdd(a.ticket, 1u) == gridDim.x - 1) ? 1u : 0u;
+    }
+    __syncthreads();
     if (is_last && warp == 0) {
       __threadfence();
       float v = -INFINITY;
@@ -652,6 +941,7 @@ __global__ void __launch_bounds__(256) argmax_kernel(const float* logits, uint32
 template <typename Kernel>
 cudaError_t launch_ex(Kernel kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
                       bool pdl, const GemvArgs& a) {
+  if (grid.x > (unsigned)kMaxGrid) return cudaErrorInvalidConfiguration;  // argmax slots
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -677,7 +967,8 @@ cudaError_t launch_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   const int out_rows = (EPI == kSwiGlu) ? a.m.rows / 2 : a.m.rows;
   const int groups = (out_rows + NR - 1) / NR;
   int grid = (groups + kWarps - 1) / kWarps;
-  if (grid > kNumSms) grid = kNumSms;
+  const int max_grid = kNumSms * (a.ctas_per_sm == 1 ? 1 : 2);
+  if (grid > max_grid) grid = max_grid;
   if (grid < 1) grid = 1;
   return launch_ex(kernel, dim3(grid), dim3(kThreads), smem, stream, pdl, a);
 }
@@ -688,6 +979,27 @@ cudaError_t launch_nr(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   const int out_rows = (EPI == kSwiGlu) ? a.m.rows / 2 : a.m.rows;
   if ((out_rows + 1) / 2 < kNumSms * kWarps) return launch_t<KIND, PRO, EPI, 1>(a, stream, pdl);
   return launch_t<KIND, PRO, EPI, 2>(a, stream, pdl);
+}
+
+template <int KIND, int PRO, int EPI>
+cudaError_t launch_q4_mma(GemvArgs a, cudaStream_t stream, bool pdl) {
+  auto kernel = gemv_q4_mma_kernel<KIND, PRO, EPI>;
+  const int k = a.m.k;
+  const size_t smem = ((size_t)2 * k + k / 32) * sizeof(float);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  const int out_rows = (EPI == kSwiGlu) ? a.m.rows / 2 : a.m.rows;
+  const int tiles = (out_rows + 15) / 16;
+  const int max_grid = 2 * kNumSms;
+  int rg = 8;
+  while (rg > 1 && (tiles + rg - 1) / rg < max_grid) rg /= 2;
+  a.row_groups = rg;
+  int grid = (tiles + rg - 1) / rg;
+  if (grid > max_grid) grid = max_grid;
+  if (grid < 1) grid = 1;
+  return launch_ex(kernel, dim3(grid), dim3(kThreads), smem, stream, pdl, a);
 }
 
 template <int PRO, int EPI>
@@ -706,7 +1018,9 @@ cudaError_t launch_tma(const GemvArgs& a, cudaStream_t stream, bool pdl) {
 
 template <int KIND>
 cudaError_t launch_kind(const GemvArgs& a, cudaStream_t stream, bool pdl) {
-  if (KIND == kF16 && a.m.k % kSegE == 0) {
+  // Variant 2 (bulk-copy ring) on request; auto picks the register-streamed kernel, which
+  // measures faster on B200 for every decode shape.
+  if (KIND == kF16 && a.variant == 2 && a.m.k % kSegE == 0) {
 #define QNE_TCOMBO(P, E) \
     if (a.pro == P && a.epi == E) return launch_tma<P, E>(a, stream, pdl);
     QNE_TCOMBO(kProCopy, kStore)
@@ -719,6 +1033,20 @@ cudaError_t launch_kind(const GemvArgs& a, cudaStream_t stream, bool pdl) {
     QNE_TCOMBO(kProEmbedNorm, kStore)
     QNE_TCOMBO(kProGdnGate, kAccumulate)
 #undef QNE_TCOMBO
+  }
+  if (KIND != kF16 && a.variant != 1 && a.m.k % 256 == 0) {
+#define QNE_QCOMBO(P, E) \
+    if (a.pro == P && a.epi == E) return launch_q4_mma<KIND, P, E>(a, stream, pdl);
+    QNE_QCOMBO(kProCopy, kStore)
+    QNE_QCOMBO(kProCopy, kAccumulate)
+    QNE_QCOMBO(kProCopy, kSwiGlu)
+    QNE_QCOMBO(kProRmsNorm, kStore)
+    QNE_QCOMBO(kProRmsNorm, kAccumulate)
+    QNE_QCOMBO(kProRmsNorm, kSwiGlu)
+    QNE_QCOMBO(kProRmsNorm, kArgmax)
+    QNE_QCOMBO(kProEmbedNorm, kStore)
+    QNE_QCOMBO(kProGdnGate, kAccumulate)
+#undef QNE_QCOMBO
   }
 #define QNE_COMBO(P, E) \
   if (a.pro == P && a.epi == E) return launch_nr<KIND, P, E>(a, stream, pdl);
@@ -737,16 +1065,19 @@ cudaError_t launch_kind(const GemvArgs& a, cudaStream_t stream, bool pdl) {
 
 }  // namespace
 
-size_t argmax_scratch_bytes() { return 2 * 4 * 256 + 256; }
+// Per-CTA slots of the greedy-pick reduction: every GEMV / argmax grid is capped at kMaxGrid.
+size_t argmax_scratch_bytes() { return 2 * 4 * kMaxGrid + 256; }
 void argmax_scratch_carve(void* scratch, float** part_val, uint32_t** part_idx, uint32_t** ticket) {
   uint8_t* p = static_cast<uint8_t*>(scratch);
   *part_val = reinterpret_cast<float*>(p);
-  *part_idx = reinterpret_cast<uint32_t*>(p + 4 * 256);
-  *ticket = reinterpret_cast<uint32_t*>(p + 8 * 256);
+  *part_idx = reinterpret_cast<uint32_t*>(p + 4 * kMaxGrid);
+  *ticket = reinterpret_cast<uint32_t*>(p + 8 * kMaxGrid);
 }
 
 const char* check_gemv(const GemvArgs& a) {
   const Mat& m = a.m;
+  if (a.variant < 0 || a.variant > 2) return "unknown GEMV variant";
+  if (a.variant == 2 && (m.kind != kF16 || m.k % 512)) return "the bulk-copy GEMV needs f16 weights and k % 512 == 0";
   if (!m.w || m.rows <= 0 || m.k <= 0) return "matrix has no data or an empty shape";
   if (m.kind == kF16) {
     if (m.k % 256) return "f16 GEMV needs k % 256 == 0";

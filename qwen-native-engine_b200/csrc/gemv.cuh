@@ -35,6 +35,9 @@ struct GemvArgs {
   uint32_t* ticket = nullptr;    // kArgmax scratch: CTA completion counter (starts at 0)
   int update_token = 0;          // kArgmax: write the pick to ctl->token and advance ctl->pos
   uint32_t* err = nullptr;       // optional: receives kFlagTimeout if a bounded wait gives up
+  int variant = 0;               // 0 auto, 1 register-streamed loads, 2 bulk-copy (TMA) ring
+  int ctas_per_sm = 2;           // register-streamed kernel: CTAs per SM in the grid (1 or 2)
+  int row_groups = 1;            // set by the launcher (tensor-core int4 kernel)
 };
 
 // Bytes of scratch the kArgmax epilogue needs.

@@ -100,6 +100,7 @@ def _load_lib() -> C.CDLL:
         "qne_batch_sync": (I32, [P, U32]),
         "qne_gemv": (I32, [C.POINTER(_Matrix), P, P, I32, P]),
         "qne_rmsnorm_gemv": (I32, [C.POINTER(_Matrix), P, P, C.c_float, P, I32, P]),
+        "qne_gemv_ex": (I32, [C.POINTER(_Matrix), P, P, I32, I32, I32, P]),
         "qne_gemm_scratch_bytes": (SZ, [C.POINTER(_Matrix), I32]),
         "qne_gemm": (I32, [C.POINTER(_Matrix), P, I32, P, I32, P, SZ, P]),
         "qne_dequant_rows": (I32, [C.POINTER(_Matrix), I32, I32, P, P]),
@@ -367,6 +368,12 @@ def matrix(kind, rows: int, k: int, w, s=None, z=None) -> _Matrix:
 def gemv(m: _Matrix, x, y, epilogue="store", stream=None) -> None:
     epi = EPILOGUES[epilogue] if isinstance(epilogue, str) else int(epilogue)
     _check(lib.qne_gemv(C.byref(m), _ptr(x), _ptr(y), epi, _stream(stream)))
+
+
+def gemv_ex(m: _Matrix, x, y, epilogue="store", variant: int = 0, ctas_per_sm: int = 2, stream=None) -> None:
+    """gemv with an explicit kernel variant (0 auto, 1 register-streamed, 2 bulk-copy ring)."""
+    epi = EPILOGUES[epilogue] if isinstance(epilogue, str) else int(epilogue)
+    _check(lib.qne_gemv_ex(C.byref(m), _ptr(x), _ptr(y), epi, variant, ctas_per_sm, _stream(stream)))
 
 
 def rmsnorm_gemv(m: _Matrix, h, norm_w, y, epilogue="store", eps: float = 1e-6, stream=None) -> None:
