@@ -322,6 +322,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--micro", default="", help="config-5 microbench: all | gemv,gdn,attn")
     ap.add_argument("--no-batched", action="store_true", help="skip the config-4 batched decode run")
+    ap.add_argument("--batched-only", action="store_true", help="run only the config-4 batched decode (profiling)")
+    ap.add_argument("--batched-steps", type=int, default=64)
+    ap.add_argument("--path", default="auto", choices=["auto", "fused", "split"],
+                    help="B=1 launch path: one kernel per op (the default) or the fused layer kernels")
     args = ap.parse_args()
     world, rank, local = dist_setup()
     if args.micro:
@@ -352,6 +356,14 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    if args.batched_only:
+        res = batched_run(torch, qne, synth, rank, world, barrier, max_over_ranks, args.warmup, args.batched_steps)
+        if rank == 0:
+            print(json.dumps({"batched": res}), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
     steps = args.steps
     prompt_len = min(args.prompt, 4096 - steps)
     if prompt_len < 1 or steps < 1 or args.warmup < 0:
@@ -359,6 +371,9 @@ def main():
 
     s = synth.build_config(2)
     model = qne.Model(s.index_json, s.weights, device=local)
+    if args.path != "auto":
+        model.set_fused(args.path == "fused")
+    fused = model.fused
     # one dedicated stream for the engine and the CUDA events that time it
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
@@ -419,7 +434,7 @@ def main():
     model.close()
     batched = None
     if not args.no_batched:
-        batched = batched_run(torch, qne, synth, rank, world, barrier, max_over_ranks, args.warmup)
+        batched = batched_run(torch, qne, synth, rank, world, barrier, max_over_ranks, args.warmup, args.batched_steps)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -434,6 +449,21 @@ def main():
         kv_bytes = 6 * 2048 * (prompt_len + steps / 2)
         state_bytes = 18 * (2 * 16 * 128 * 128 * 4 + 2 * 4 * 6144 * 4)
         tok_bytes = bytes_per_token + kv_bytes + state_bytes + model.vocab * 4
+        step_gbs = tok_bytes * value / world / 1e9
+        if fused:
+            # The fused layer kernel is the whole step: its algorithmic bytes per launch are the
+            # token's bytes over the launches, its mean launch time the step time over them.
+            roof = {"bound": "hbm", "achieved": round(step_gbs, 1), "peak": peak, "unit": "GB/s",
+                    "frac": round(step_gbs / peak, 4), "traffic": None,
+                    "kernel": f"layer_kernel (fused decoder layer; {dispatches} launches per token, the last "
+                              f"with the LM head)", "peak_source": peak_kind,
+                    "mean_launch_us": round(ms / steps / dispatches * 1e3, 2),
+                    "bytes_per_launch": int(tok_bytes / dispatches)}
+        else:
+            roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                    "frac": round(achieved / peak, 4), "traffic": None,
+                    "kernel": "gemv_pipe_kernel<RMSNorm, SwiGLU> (gate_up, 12288x2048)",
+                    "peak_source": peak_kind, "mean_launch_us": round(gemv_ms * 1e3, 2)}
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": steps,
             "warmup": args.warmup, "ms_per_step": round(ms / steps, 4), "higher_is_better": True,
@@ -444,10 +474,7 @@ def main():
                        "parallelism": f"replicas x{world}", "l2": "inputs larger than L2 (3.76 GB of weights per step)"},
             "e2e": {"value": round(world * steps / e2e_s, 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
                     "d2h_bytes_per_step": model.vocab * 4},
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": None,
-                         "kernel": "gemv_kernel<f16, RMSNorm, SwiGLU> (gate_up, 12288x2048)",
-                         "peak_source": peak_kind, "mean_launch_us": round(gemv_ms * 1e3, 2)},
+            "roofline": roof,
             "step_roofline": {"bytes_per_token": int(tok_bytes), "achieved_gbs": round(tok_bytes * value / world / 1e9, 1),
                               "frac": round(tok_bytes * value / world / 1e9 / peak, 4)},
             "gpu_launches": int(launches),

@@ -109,6 +109,24 @@ QNE_API qne_status qne_model_info_get(const qne_model* m, qne_model_info* out);
 /* Runs the model's work on `cuda_stream` (a cudaStream_t of the model's device; NULL = the
  * model's own stream). */
 QNE_API qne_status qne_model_set_stream(qne_model* m, void* cuda_stream);
+/* Chooses how a token's work is launched: enable = 0 (the default) runs one kernel per operation
+ * as kernels/src/model.rs:220-269 dispatches them, chained by programmatic dependent launch;
+ * enable = 1 runs each decoder layer as one launch of a fused kernel whose phases are separated
+ * by grid barriers. Both compute the same results within the logit tolerance and the same
+ * greedy picks. The fused path needs one sequence, f16 weights with k % 256 == 0 and a grid of
+ * two CTAs per SM; QNE_EINVAL if it is requested and not available. No counterpart in the
+ * reference, whose dispatch granularity is fixed. */
+QNE_API qne_status qne_model_set_fused(qne_model* m, int enable);
+/* 1 if the fused layer kernels are in use. */
+QNE_API int qne_model_fused(const qne_model* m);
+/* Diagnostics of the fused path (no counterpart in the reference): with enable = 1 every fused
+ * launch records, per CTA, %globaltimer stamps at its phase boundaries (slots 0-7), grid-barrier
+ * arrivals (8-15) and releases (16-23) into [layer][cta][32] u64 slots, overwritten each token.
+ * qne_model_phase_trace copies up to `cap` slots of the last token and reports how many were
+ * written and the grid size. QNE_EINVAL if the fused path is not available or the trace is off. */
+QNE_API qne_status qne_model_set_phase_trace(qne_model* m, int enable);
+QNE_API qne_status qne_model_phase_trace(qne_model* m, uint64_t* out, size_t cap, size_t* n_out,
+                                         size_t* ctas);
 /* Model::adapter, kernels/src/model.rs:167. */
 QNE_API const char* qne_adapter(const qne_model* m);
 /* Model::dispatches_per_token, kernels/src/model.rs:309. */
@@ -197,7 +215,8 @@ QNE_API qne_status qne_batch_sync(qne_batch* b, uint32_t timeout_ms);
  * physical row count and y has m->rows / 2 entries. */
 QNE_API qne_status qne_gemv(const qne_matrix* m, const float* x, float* y, int epilogue, void* stream);
 /* qne_gemv with an explicit kernel variant (the counterpart of the reference's per-matrix Tile
- * choice, kernels/src/lib.rs:39-64): 0 = automatic, 1 = register-streamed 16-byte loads,
+ * choice, kernels/src/lib.rs:39-64): 0 = automatic (f16: pipelined register streaming with
+ * rows dealt over all warps; int4: tensor-core kernel), 1 = row-group register streaming,
  * 2 = bulk-copy (TMA) shared-memory ring (f16, k % 512 == 0). ctas_per_sm (1 or 2) sizes the
  * grid of variant 1. */
 QNE_API qne_status qne_gemv_ex(const qne_matrix* m, const float* x, float* y, int epilogue, int variant,

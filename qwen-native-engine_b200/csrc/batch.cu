@@ -443,7 +443,8 @@ qne_status qne_batch_fill_synthetic(qne_batch* b, uint32_t seq, uint32_t len, ui
 }
 
 qne_status qne_batch_sync(qne_batch* b, uint32_t timeout_ms) {
-  BATCH(b);
+  if (!b) return bfail(QNE_EINVAL, "null batch handle");
+  Model* M = reinterpret_cast<BatchHandle*>(b)->model;
   return bguard([&] {
     Guard g(M->device);
     sync_stream(M->stream(), timeout_ms);

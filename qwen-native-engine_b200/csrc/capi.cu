@@ -100,6 +100,32 @@ qne_status qne_model_set_stream(qne_model* m, void* cuda_stream) {
   return QNE_OK;
 }
 
+qne_status qne_model_set_fused(qne_model* m, int enable) {
+  MODEL(m);
+  return guarded([&] {
+    if (!M->set_fused(enable != 0))
+      throw QneError(kEInval, "the fused layer kernels need one sequence, f16 weights with k % 256 == 0 and a "
+                              "device that co-schedules the grid");
+  });
+}
+
+qne_status qne_model_set_phase_trace(qne_model* m, int enable) {
+  MODEL(m);
+  return guarded([&] { M->set_phase_trace(enable != 0); });
+}
+
+qne_status qne_model_phase_trace(qne_model* m, uint64_t* out, size_t cap, size_t* n_out, size_t* ctas) {
+  MODEL(m);
+  return guarded([&] {
+    const size_t n = M->read_phase_trace(out, cap, ctas);
+    if (n_out) *n_out = n;
+  });
+}
+
+int qne_model_fused(const qne_model* m) {
+  return m ? (reinterpret_cast<const Model*>(m)->fused() ? 1 : 0) : 0;
+}
+
 const char* qne_adapter(const qne_model* m) {
   return m ? reinterpret_cast<const Model*>(m)->adapter.c_str() : "";
 }

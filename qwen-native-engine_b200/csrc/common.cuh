@@ -38,7 +38,8 @@ struct SeqCtl {
   uint32_t count;
   uint32_t flags;
 };
-constexpr uint32_t kFlagPosClamped = 1u;
+constexpr uint32_t kFlagPosClamped = 1u;  // a position at or past the context limit was clamped
+constexpr uint32_t kFlagTimeout = 2u;     // a bounded device wait gave up
 
 // ------------------------------------------------------------------------------------------
 // Programmatic dependent launch: every kernel issues launch_dependents early (so the next

@@ -19,176 +19,18 @@
 #include <atomic>
 
 #include "gemv.cuh"
+#include "gemv_dev.cuh"
 #include "tma.cuh"
 
 namespace qne {
+
+using namespace dev;
 
 static std::atomic<uint64_t> g_launches{0};
 uint64_t launches_issued() { return g_launches.load(std::memory_order_relaxed); }
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 namespace {
-
-constexpr int kThreads = 256;
-constexpr int kWarps = kThreads / 32;
-constexpr uint32_t kPrefetchBytes = 96u << 10;  // per CTA, issued before the dependency wait
-constexpr uint32_t kPrefetchPiece = 8u << 10;
-
-template <int KIND>
-struct Fmt;
-template <>
-struct Fmt<kF16> {
-  static constexpr int CV = 8;  // values per 16-byte chunk
-  static __host__ __device__ size_t row_bytes(int k) { return (size_t)k * 2; }
-};
-template <>
-struct Fmt<kQ4> {
-  static constexpr int CV = 32;
-  static __host__ __device__ size_t row_bytes(int k) { return (size_t)k / 2; }
-};
-template <>
-struct Fmt<kQ4G64> {
-  static constexpr int CV = 32;
-  static __host__ __device__ size_t row_bytes(int k) { return (size_t)k / 2; }
-};
-
-// Dequantized value of element (row, i) - the unpack used by dequant_rows and the embedding.
-__device__ __forceinline__ float deq_elem(const Mat& m, long row, int i) {
-  if (m.kind == kF16) {
-    return h2f(__ldg((const uint16_t*)m.w + row * m.k + i));
-  }
-  const uint32_t word = __ldg((const uint32_t*)m.w + row * (m.k / 8) + i / 8);
-  const float q = nib_f(word, 4 * (i % 8));
-  float scale, zp;
-  if (m.kind == kQ4) {
-    q4_scale_zp((const uint32_t*)m.s, (const uint32_t*)m.z, row, m.k, i / 32, scale, zp);
-  } else {
-    q4g64_scale_zp((const uint16_t*)m.s, (const uint16_t*)m.z, row, m.k, i / 64, scale, zp);
-  }
-  return (q - zp) * scale;
-}
-
-// Issues L2 prefetches of rows [r0, r1) (up to `budget` bytes); called by one warp.
-__device__ __forceinline__ void prefetch_rows(const uint8_t* base, size_t row_bytes, long r0,
-                                              long r1, uint32_t budget, int lane) {
-  if (r1 <= r0) return;
-  size_t bytes = (size_t)(r1 - r0) * row_bytes;
-  if (bytes > budget) bytes = budget;
-  bytes &= ~(size_t)15;
-  const uint8_t* p = base + (size_t)r0 * row_bytes;
-  for (size_t off = (size_t)lane * kPrefetchPiece; off < bytes; off += 32 * kPrefetchPiece) {
-    const size_t n = bytes - off < kPrefetchPiece ? bytes - off : kPrefetchPiece;
-    prefetch_l2(p + off, (uint32_t)n);
-  }
-}
-
-// Barrier over the 256 threads that stage x: the whole CTA (register kernel) or the consumer
-// warps only (bulk-copy kernel, whose producer warp never joins).
-struct CtaSync {
-  __device__ __forceinline__ void operator()() const { __syncthreads(); }
-};
-struct ConsumerSync {
-  __device__ __forceinline__ void operator()() const { asm volatile("bar.sync 1, 256;" ::: "memory"); }
-};
-
-template <typename Sync>
-__device__ __forceinline__ float sum256(float v, float* red, Sync sync) {
-  v = warp_sum(v);
-  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-  sync();
-  if (l == 0) red[w] = v;
-  sync();
-  float t = 0.f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) t += red[i];
-  return t;
-}
-
-// ------------------------------------------------------------------------------------------
-// Prologues: stage the f32 input vector of length k in shared memory.
-// ------------------------------------------------------------------------------------------
-template <int PRO, typename Sync = CtaSync>
-__device__ __forceinline__ void stage_x(const GemvArgs& a, float* xs, float* red, Sync sync = Sync()) {
-  const int k = a.m.k;
-  const int tid = threadIdx.x;
-  if (PRO == kProCopy) {
-    for (int i = tid * 4; i < k; i += kThreads * 4)
-      *reinterpret_cast<float4*>(xs + i) = *reinterpret_cast<const float4*>(a.x + i);
-  } else if (PRO == kProRmsNorm || PRO == kProEmbedNorm) {
-    float ss = 0.f;
-    if (PRO == kProRmsNorm) {
-      for (int i = tid * 4; i < k; i += kThreads * 4) {
-        const float4 v = *reinterpret_cast<const float4*>(a.x + i);
-        *reinterpret_cast<float4*>(xs + i) = v;
-        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-      }
-    } else {
-      // Embedding row of the token the previous step picked (or the host wrote).
-      uint32_t token = a.ctl->token;
-      if (token >= (uint32_t)a.embed.rows) token = (uint32_t)a.embed.rows - 1;
-      for (int i = tid; i < k; i += kThreads) {
-        const float v = deq_elem(a.embed, token, i);
-        xs[i] = v;
-        ss += v * v;
-      }
-      if (blockIdx.x == 0) {
-        for (int i = tid; i < k; i += kThreads) a.h_out[i] = xs[i];
-        if (tid == 0) a.ctl->count += 1;  // one more token entered the conv windows
-      }
-    }
-    const float tot = sum256(ss, red, sync);
-    const float inv = rsqrtf(tot / (float)k + a.eps);
-    for (int i = tid; i < k; i += kThreads) xs[i] = xs[i] * inv * a.norm_w[i];
-  } else if (PRO == kProGdnGate) {
-    // k == 2048: 16 heads of 128; warp w normalizes heads 2w and 2w+1.
-    const int warp = tid >> 5, lane = tid & 31;
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      const int head = warp * 2 + hh;
-      const int base = head * kGdnDim + lane * 4;
-      const float4 v = *reinterpret_cast<const float4*>(a.x + base);
-      const float ss = warp_sum(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w);
-      const float inv = rsqrtf(ss / (float)kGdnDim + a.eps);
-      const float4 zz = *reinterpret_cast<const float4*>(a.zgate + base);
-      const float4 nw = *reinterpret_cast<const float4*>(a.norm_w + lane * 4);
-      xs[base + 0] = v.x * inv * silu(zz.x) * nw.x;
-      xs[base + 1] = v.y * inv * silu(zz.y) * nw.y;
-      xs[base + 2] = v.z * inv * silu(zz.z) * nw.z;
-      xs[base + 3] = v.w * inv * silu(zz.w) * nw.w;
-    }
-  }
-  sync();
-}
-
-// ------------------------------------------------------------------------------------------
-// Chunk dot products: 16 bytes of one row against the matching slice of x in shared memory.
-// ------------------------------------------------------------------------------------------
-__device__ __forceinline__ float dot_f16(const uint4& w, const float* x) {
-  const float2 a = h2f2(w.x), b = h2f2(w.y), c = h2f2(w.z), d = h2f2(w.w);
-  float p0 = a.x * x[0];
-  float p1 = b.x * x[2];
-  float p2 = c.x * x[4];
-  float p3 = d.x * x[6];
-  p0 = fmaf(a.y, x[1], p0);
-  p1 = fmaf(b.y, x[3], p1);
-  p2 = fmaf(c.y, x[5], p2);
-  p3 = fmaf(d.y, x[7], p3);
-  return (p0 + p1) + (p2 + p3);
-}
-
-// sum_n q_n x_n over the 32 nibbles of a chunk (q exact as floats).
-__device__ __forceinline__ float dot_q4_raw(const uint4& w, const float* x) {
-  const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-  float p[4];
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    float s = nib_f(ws[e], 0) * x[8 * e];
-#pragma unroll
-    for (int n = 1; n < 8; ++n) s = fmaf(nib_f(ws[e], 4 * n), x[8 * e + n], s);
-    p[e] = s;
-  }
-  return (p[0] + p[1]) + (p[2] + p[3]);
-}
 
 // ------------------------------------------------------------------------------------------
 // f16 GEMV streamed by the bulk-copy (TMA) unit.
@@ -412,6 +254,20 @@ __global__ void __launch_bounds__(kThreadsT, 2) gemv_tma_kernel(const GemvArgs a
   }
 }
 
+// f16 GEMV, pipelined register streaming (the default f16 kernel): see dev::Pipe.
+template <int PRO, int EPI>
+__global__ void __launch_bounds__(kThreads, 2) gemv_pipe_kernel(const GemvArgs a) {
+  extern __shared__ __align__(16) float xs[];
+  __shared__ GemvShared sh;
+  Pipe<PRO, EPI> p;
+  p.init(a, blockIdx.x, gridDim.x);
+  pdl_launch();
+  p.prefetch();
+  pdl_wait();
+  p.run(a, xs, sh);
+  if (EPI == kArgmax) argmax_finish(a, blockIdx.x, gridDim.x, sh);
+}
+
 // ------------------------------------------------------------------------------------------
 // int4 GEMV on the tensor cores (B = 1).
 //
@@ -461,8 +317,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4_mma_kernel(const GemvArgs
   const int g = lane >> 2, t = lane & 3;
   const int rg = warp % RG, kg = warp / RG;
   const int steps = k / 32;
-  const int s0 = kg * steps / KG, s1 = (kg + 1) * steps / KG;
   const int blk_steps = (KIND == kQ4) ? 1 : 2;  // k32 steps per quantization block
+  // k slices of the warps cut at quantization-block boundaries
+  const int nblk = steps / blk_steps;
+  const int s0 = (kg * nblk / KG) * blk_steps, s1 = ((kg + 1) * nblk / KG) * blk_steps;
   const uint32_t* W = static_cast<const uint32_t*>(a.m.w);
   const size_t wpr = (size_t)k / 8;  // words per row
 
@@ -981,6 +839,21 @@ cudaError_t launch_nr(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   return launch_t<KIND, PRO, EPI, 2>(a, stream, pdl);
 }
 
+template <int PRO, int EPI>
+cudaError_t launch_pipe(const GemvArgs& a, cudaStream_t stream, bool pdl) {
+  auto kernel = gemv_pipe_kernel<PRO, EPI>;
+  const size_t smem = (size_t)a.m.k * 2 * sizeof(float);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  const int out_rows = (EPI == kSwiGlu) ? a.m.rows / 2 : a.m.rows;
+  int grid = (out_rows + kWarps - 1) / kWarps;  // at least one row per warp
+  if (grid > 2 * kNumSms) grid = 2 * kNumSms;
+  if (grid < 1) grid = 1;
+  return launch_ex(kernel, dim3(grid), dim3(kThreads), smem, stream, pdl, a);
+}
+
 template <int KIND, int PRO, int EPI>
 cudaError_t launch_q4_mma(GemvArgs a, cudaStream_t stream, bool pdl) {
   auto kernel = gemv_q4_mma_kernel<KIND, PRO, EPI>;
@@ -1033,6 +906,20 @@ cudaError_t launch_kind(const GemvArgs& a, cudaStream_t stream, bool pdl) {
     QNE_TCOMBO(kProEmbedNorm, kStore)
     QNE_TCOMBO(kProGdnGate, kAccumulate)
 #undef QNE_TCOMBO
+  }
+  if (KIND == kF16 && a.variant == 0 && a.m.k % 256 == 0) {
+#define QNE_PCOMBO(P, E) \
+    if (a.pro == P && a.epi == E) return launch_pipe<P, E>(a, stream, pdl);
+    QNE_PCOMBO(kProCopy, kStore)
+    QNE_PCOMBO(kProCopy, kAccumulate)
+    QNE_PCOMBO(kProCopy, kSwiGlu)
+    QNE_PCOMBO(kProRmsNorm, kStore)
+    QNE_PCOMBO(kProRmsNorm, kAccumulate)
+    QNE_PCOMBO(kProRmsNorm, kSwiGlu)
+    QNE_PCOMBO(kProRmsNorm, kArgmax)
+    QNE_PCOMBO(kProEmbedNorm, kStore)
+    QNE_PCOMBO(kProGdnGate, kAccumulate)
+#undef QNE_PCOMBO
   }
   if (KIND != kF16 && a.variant != 1 && a.m.k % 256 == 0) {
 #define QNE_QCOMBO(P, E) \

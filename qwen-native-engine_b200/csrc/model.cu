@@ -4,6 +4,7 @@
 // kernels are chained by programmatic dependent launch, and the Model API
 // (kernels/src/model.rs:305-449).
 #include <chrono>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <thread>
@@ -11,6 +12,7 @@
 #include "gdn.cuh"
 #include "json.hpp"
 #include "model.hpp"
+#include "persist.cuh"
 
 namespace qne {
 
@@ -322,6 +324,7 @@ Runner::Runner(Model* model, int batch, uint32_t pool_pages) : m(model) {
     }
   }
   st.ctl = static_cast<SeqCtl*>(track((size_t)batch * sizeof(SeqCtl)));
+  barrier = static_cast<uint32_t*>(track(64));
   st.page_table = static_cast<uint32_t*>(m->alloc((size_t)batch * kPagesPerSeq * 4));
   std::vector<uint32_t> pt((size_t)batch * kPagesPerSeq);
   for (size_t i = 0; i < pt.size(); ++i) pt[i] = (uint32_t)i;
@@ -341,107 +344,180 @@ Runner::Runner(Model* model, int batch, uint32_t pool_pages) : m(model) {
 Runner::~Runner() {
   for (auto& g : graph)
     if (g) cudaGraphExecDestroy(g);
+  for (auto& g : fgraph)
+    if (g) cudaGraphExecDestroy(g);
+}
+
+Runner::LayerArgs Runner::layer_args(int i) const {
+  const Model& M = *m;
+  const LayerWeights& L = M.layers[i];
+  LayerArgs r;
+  r.attention = L.attention;
+  GemvArgs& in = r.in;
+  in.m = L.in;
+  in.epi = kStore;
+  in.y = proj;
+  in.norm_w = L.input_norm;
+  if (i == 0) {
+    in.pro = kProEmbedNorm;
+    in.embed = M.embed;
+    in.ctl = st.ctl;
+    in.h_out = h;
+  } else {
+    in.pro = kProRmsNorm;
+    in.x = h;
+  }
+  GemvArgs& out = r.out;
+  out.m = L.out;
+  out.epi = kAccumulate;
+  out.y = h;
+  out.x = raw;
+  if (L.attention) {
+    AttnArgs& at = r.at;
+    at.proj = proj;
+    at.norms = L.attn_norms;
+    at.rope = M.rope;
+    at.kv = st.kv[i];
+    at.page_table = st.page_table;
+    at.pos = &st.ctl->pos;
+    at.pos_stride = 4;
+    at.flags = &st.ctl->flags;
+    at.flags_stride = 4;
+    at.out = raw;
+    at.batch = 1;
+    at.scratch = attn_scratch;
+    out.pro = kProCopy;
+  } else {
+    r.gdn = dev::GdnArgs{proj, st.conv[i], L.conv_w, st.rec[i], L.gdn_params, &st.ctl->count, 4, raw};
+    out.pro = kProGdnGate;
+    out.zgate = proj + 6144;
+    out.norm_w = L.gdn_params + 32;
+  }
+  GemvArgs& gu = r.gate_up;
+  gu.m = L.gate_up;
+  gu.pro = kProRmsNorm;
+  gu.x = h;
+  gu.norm_w = L.post_norm;
+  gu.epi = kSwiGlu;
+  gu.y = act;
+  GemvArgs& dn = r.down;
+  dn.m = L.down;
+  dn.pro = kProCopy;
+  dn.x = act;
+  dn.epi = kAccumulate;
+  dn.y = h;
+  for (GemvArgs* g : {&r.in, &r.out, &r.gate_up, &r.down}) g->err = &st.ctl->flags;
+  return r;
+}
+
+GemvArgs Runner::head_args(Variant v) const {
+  const Model& M = *m;
+  GemvArgs hd;
+  hd.m = M.lm_head;
+  hd.pro = kProRmsNorm;
+  hd.x = h;
+  hd.norm_w = M.final_norm;
+  hd.epi = kArgmax;
+  hd.y = logits;
+  argmax_scratch_carve(argmax_scratch, &hd.part_val, &hd.part_idx, &hd.ticket);
+  hd.ctl = st.ctl;
+  hd.update_token = (v == kGreedy) ? 1 : 0;
+  hd.err = &st.ctl->flags;
+  return hd;
 }
 
 void Runner::record(Variant v, cudaStream_t s) {
   const Model& M = *m;
   size_t n = 0;
-  auto gemv = [&](GemvArgs a) {
-    a.err = &st.ctl->flags;
+  auto gemv = [&](const GemvArgs& a) {
     if (const char* why = check_gemv(a)) throw QneError(kEInval, why);
     cuda_check(launch_gemv(a, s, true), "gemv launch");
     ++n;
   };
   for (int i = 0; i < M.cfg.layers; ++i) {
-    const LayerWeights& L = M.layers[i];
-    GemvArgs in;
-    in.m = L.in;
-    in.epi = kStore;
-    in.y = proj;
-    in.norm_w = L.input_norm;
-    if (i == 0) {
-      in.pro = kProEmbedNorm;
-      in.embed = M.embed;
-      in.ctl = st.ctl;
-      in.h_out = h;
+    const LayerArgs r = layer_args(i);
+    gemv(r.in);
+    if (r.attention) {
+      cuda_check(launch_attention(r.at, st.pool_pages, 64, s, true), "attention launch");
     } else {
-      in.pro = kProRmsNorm;
-      in.x = h;
-    }
-    gemv(in);
-    GemvArgs out;
-    out.m = L.out;
-    out.epi = kAccumulate;
-    out.y = h;
-    out.x = raw;
-    if (L.attention) {
-      AttnArgs at;
-      at.proj = proj;
-      at.norms = L.attn_norms;
-      at.rope = M.rope;
-      at.kv = st.kv[i];
-      at.page_table = st.page_table;
-      at.pos = &st.ctl->pos;
-      at.pos_stride = 4;
-      at.flags = &st.ctl->flags;
-      at.flags_stride = 4;
-      at.out = raw;
-      at.batch = 1;
-      at.scratch = attn_scratch;
-      cuda_check(launch_attention(at, st.pool_pages, 64, s, true), "attention launch");
-      ++n;
-      out.pro = kProCopy;
-    } else {
-      cuda_check(launch_gdn_step(proj, st.conv[i], L.conv_w, st.rec[i], L.gdn_params, &st.ctl->count, 4,
-                                 raw, 1, s, true),
+      const dev::GdnArgs& g = r.gdn;
+      cuda_check(launch_gdn_step(g.proj, g.conv, g.conv_w, g.state, g.params, g.counter, g.counter_stride, g.out,
+                                 1, s, true),
                  "gdn launch");
-      ++n;
-      out.pro = kProGdnGate;
-      out.zgate = proj + 6144;
-      out.norm_w = L.gdn_params + 32;
     }
-    gemv(out);
-    GemvArgs gu;
-    gu.m = L.gate_up;
-    gu.pro = kProRmsNorm;
-    gu.x = h;
-    gu.norm_w = L.post_norm;
-    gu.epi = kSwiGlu;
-    gu.y = act;
-    gemv(gu);
-    GemvArgs dn;
-    dn.m = L.down;
-    dn.pro = kProCopy;
-    dn.x = act;
-    dn.epi = kAccumulate;
-    dn.y = h;
-    gemv(dn);
+    ++n;
+    gemv(r.out);
+    gemv(r.gate_up);
+    gemv(r.down);
   }
-  if (v != kLayers) {
-    GemvArgs hd;
-    hd.m = M.lm_head;
-    hd.pro = kProRmsNorm;
-    hd.x = h;
-    hd.norm_w = M.final_norm;
-    hd.epi = kArgmax;
-    hd.y = logits;
-    argmax_scratch_carve(argmax_scratch, &hd.part_val, &hd.part_idx, &hd.ticket);
-    hd.ctl = st.ctl;
-    hd.update_token = (v == kGreedy) ? 1 : 0;
-    gemv(hd);
-  }
+  if (v != kLayers) gemv(head_args(v));
   if (v == kGreedy) launches_per_token = n;
 }
 
-void Runner::capture_graphs() {
+// Whether the fused layer kernels can run this model: one sequence, f16 GEMV weights with
+// k % 256 == 0 (the register-streaming pipeline's segments), and a co-resident grid large
+// enough for one CTA per mixer work item.
+bool Runner::fused_supported() {
+  const Model& M = *m;
+  if (st.batch != 1 || M.cfg.layers < 1) return false;
+  auto ok = [](const Mat& x) { return x.kind == kF16 && x.k % 256 == 0 && x.k <= 16384; };
+  int max_k = M.lm_head.k;
+  if (!ok(M.lm_head) || M.embed.k != M.layers[0].in.k) return false;
+  for (const LayerWeights& L : M.layers) {
+    for (const Mat* x : {&L.in, &L.out, &L.gate_up, &L.down}) {
+      if (!ok(*x)) return false;
+      max_k = std::max(max_k, x->k);
+    }
+  }
+  fused_max_k = max_k;
+  fused_ctas = persist_ctas(max_k);
+  return fused_ctas > 0;
+}
+
+void Runner::record_fused(Variant v, cudaStream_t s) {
+  const Model& M = *m;
+  std::vector<LayerLaunch> launches(M.cfg.layers);
+  for (int i = 0; i < M.cfg.layers; ++i) {
+    const LayerArgs r = layer_args(i);
+    LayerLaunch& la = launches[i];
+    la.g[kPhIn] = r.in;
+    la.g[kPhOut] = r.out;
+    la.g[kPhGateUp] = r.gate_up;
+    la.g[kPhDown] = r.down;
+    const bool head = (i + 1 == M.cfg.layers) && v != kLayers;
+    if (head) la.g[kPhHead] = head_args(v);
+    for (int ph : {(int)kPhIn, (int)kPhOut, (int)kPhGateUp, (int)kPhDown})
+      if (const char* why = check_gemv(la.g[ph])) throw QneError(kEInval, why);
+    if (head)
+      if (const char* why = check_gemv(la.g[kPhHead])) throw QneError(kEInval, why);
+    la.attn.a = r.at;
+    la.attn.split = dev::kSub;
+    la.attn.max_splits = dev::kMaxSplits;
+    la.attn.pool_pages = st.pool_pages;
+    la.gdn = r.gdn;
+    la.barrier = reinterpret_cast<unsigned long long*>(barrier);
+    la.err = &st.ctl->flags;
+    la.trace = trace_on ? trace + (size_t)i * fused_ctas * 32 : nullptr;
+    la.xs_bytes = (uint32_t)persist_xs_bytes(fused_max_k);
+  }
+  for (int i = 0; i < M.cfg.layers; ++i) {
+    const bool head = (i + 1 == M.cfg.layers) && v != kLayers;
+    cuda_check(launch_layer(launches[i], M.layers[i].attention, head, fused_ctas, fused_max_k, s, true),
+               "fused layer launch");
+  }
+  if (v == kGreedy) fused_launches_per_token = (size_t)M.cfg.layers;
+}
+
+void Runner::capture_set(cudaGraphExec_t* out, bool fused) {
   cudaStream_t cs;
   cuda_check(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking), "cudaStreamCreate");
   for (int v = 0; v < kVariants; ++v) {
     cuda_check(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal), "begin capture");
     try {
-      record((Variant)v, cs);
+      if (fused) record_fused((Variant)v, cs);
+      else record((Variant)v, cs);
     } catch (...) {
-      cudaGraph_t g;
+      cudaGraph_t g = nullptr;
       cudaStreamEndCapture(cs, &g);
       if (g) cudaGraphDestroy(g);
       cudaStreamDestroy(cs);
@@ -449,7 +525,7 @@ void Runner::capture_graphs() {
     }
     cudaGraph_t g = nullptr;
     cuda_check(cudaStreamEndCapture(cs, &g), "end capture");
-    cudaError_t e = cudaGraphInstantiate(&graph[v], g, 0);
+    cudaError_t e = cudaGraphInstantiate(&out[v], g, 0);
     cudaGraphDestroy(g);
     if (e != cudaSuccess) {
       cudaStreamDestroy(cs);
@@ -459,9 +535,53 @@ void Runner::capture_graphs() {
   cudaStreamDestroy(cs);
 }
 
+// Both launch paths are captured; the per-operation graphs are the default (on the 2B config
+// they measure faster than the fused layer kernels), the fused ones are chosen with set_fused.
+void Runner::capture_graphs() {
+  capture_set(graph, false);
+  use_fused = false;
+  if (fused_supported()) {
+    try {
+      capture_set(fgraph, true);
+    } catch (const QneError&) {
+      // A device that cannot co-schedule the grid lands here; the per-operation graphs remain.
+      for (auto& g : fgraph)
+        if (g) {
+          cudaGraphExecDestroy(g);
+          g = nullptr;
+        }
+      fused_ctas = 0;
+    }
+  }
+}
+
+bool Runner::set_fused(bool on) {
+  if (on && !fgraph[0]) return false;
+  use_fused = on;
+  return true;
+}
+
+bool Runner::set_trace(bool on) {
+  if (!fgraph[0]) return false;
+  if (on == trace_on) return true;
+  if (on && !trace) trace = static_cast<unsigned long long*>(m->alloc((size_t)m->cfg.layers * fused_ctas * 32 * 8));
+  if (on) cuda_check(cudaMemset(trace, 0, (size_t)m->cfg.layers * fused_ctas * 32 * 8), "trace");
+  trace_on = on;
+  for (auto& g : fgraph)
+    if (g) {
+      cudaGraphExecDestroy(g);
+      g = nullptr;
+    }
+  capture_set(fgraph, true);
+  return true;
+}
+
+size_t Runner::per_token() const { return use_fused ? fused_launches_per_token : launches_per_token; }
+
 void Runner::launch(Variant v, cudaStream_t s) {
-  cuda_check(cudaGraphLaunch(graph[v], s), "graph launch");
-  for (size_t i = 0; i < (v == kLayers ? launches_per_token - 1 : launches_per_token); ++i) count_launch();
+  cuda_check(cudaGraphLaunch(use_fused ? fgraph[v] : graph[v], s), "graph launch");
+  const size_t n = use_fused ? fused_launches_per_token : (v == kLayers ? launches_per_token - 1 : launches_per_token);
+  for (size_t i = 0; i < n; ++i) count_launch();
 }
 
 void Runner::reset(cudaStream_t s) {
@@ -491,7 +611,41 @@ void Runner::restore(cudaStream_t s) {
 // ------------------------------------------------------------------------------------------
 void Model::set_stream(cudaStream_t s) { ext_stream_ = s; }
 
-size_t Model::dispatches_per_token() const { return single_->launches_per_token; }
+bool Model::set_fused(bool on) {
+  DeviceGuard g(device);
+  cuda_check(cudaStreamSynchronize(stream()), "set_fused");
+  return single_->set_fused(on);
+}
+
+bool Model::fused() const { return single_->use_fused; }
+
+void Model::set_phase_trace(bool on) {
+  DeviceGuard g(device);
+  cuda_check(cudaStreamSynchronize(stream()), "set_phase_trace");
+  if (!single_->set_trace(on)) throw QneError(kEInval, "the phase trace needs the fused layer kernels");
+}
+
+size_t Model::read_phase_trace(uint64_t* out, size_t cap, size_t* ctas) {
+  DeviceGuard g(device);
+  if (!single_->trace_on) throw QneError(kEInval, "the phase trace is off");
+  const size_t n = std::min(cap, (size_t)cfg.layers * single_->fused_ctas * 32);
+  if (ctas) *ctas = (size_t)single_->fused_ctas;
+  cuda_check(cudaStreamSynchronize(stream()), "read_phase_trace");
+  if (out && n) cuda_check(cudaMemcpy(out, single_->trace, n * 8, cudaMemcpyDeviceToHost), "read_phase_trace");
+  return n;
+}
+
+// A bounded device wait that gave up leaves kFlagTimeout in the control words; the barrier
+// words may then be out of step, so they are cleared with the flag before the error surfaces.
+void Model::check_flags(uint32_t flags) {
+  if (!(flags & kFlagTimeout)) return;
+  cuda_check(cudaMemsetAsync(single_->barrier, 0, 64, stream()), "clear barrier");
+  cuda_check(cudaMemsetAsync(&single_->st.ctl->flags, 0, 4, stream()), "clear flags");
+  cuda_check(cudaStreamSynchronize(stream()), "clear flags");
+  throw QneError(kETimeout, "a device-side wait timed out; the token's results are invalid");
+}
+
+size_t Model::dispatches_per_token() const { return single_->per_token(); }
 const float* Model::logits_device() const { return single_->logits; }
 
 void Model::reset() {
@@ -566,6 +720,7 @@ void Model::last_token(uint32_t* token, uint32_t* pos) {
   cuda_check(cudaMemcpyAsync(host_ctl_ + 2 * kMaxContext, single_->st.ctl, 16, cudaMemcpyDeviceToHost, stream()),
              "last_token");
   sync(600000);
+  check_flags(host_ctl_[2 * kMaxContext + 3]);
   if (token) *token = host_ctl_[2 * kMaxContext];
   if (pos) *pos = host_ctl_[2 * kMaxContext + 1];
   host_pos_ = host_ctl_[2 * kMaxContext + 1];
@@ -597,6 +752,7 @@ void Model::decode(uint32_t n, uint32_t window, const uint32_t* stop, uint32_t n
     cuda_check(cudaMemcpyAsync(host_ctl_ + 2 * kMaxContext, single_->st.ctl, 16, cudaMemcpyDeviceToHost, stream()),
                "decode readback");
     sync(600000);
+    check_flags(host_ctl_[2 * kMaxContext + 3]);
     if (steps == 1) ids[count++] = host_ctl_[2 * kMaxContext];
     else
       for (uint32_t s = 0; s < steps; ++s) ids[count++] = 0xFFFFFFFFu;

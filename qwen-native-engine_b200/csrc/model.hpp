@@ -10,7 +10,10 @@
 #include <vector>
 
 #include "common.cuh"
+#include "gdn.cuh"
+#include "gdn_dev.cuh"
 #include "gemv.cuh"
+#include "persist.cuh"
 
 namespace qne {
 
@@ -89,6 +92,10 @@ class Model {
   void decode_async(uint32_t steps);
   void sync(uint32_t timeout_ms);
   void set_stream(cudaStream_t s);
+  bool set_fused(bool on);
+  bool fused() const;
+  void set_phase_trace(bool on);
+  size_t read_phase_trace(uint64_t* out, size_t cap, size_t* ctas);
   size_t dispatches_per_token() const;
   const float* logits_device() const;
 
@@ -108,6 +115,7 @@ class Model {
   uint32_t* host_ctl_ = nullptr;  // pinned staging: (token, pos) pairs
   uint32_t host_pos_ = 0;         // host mirror of the next position
   uint32_t saved_pos_ = 0;
+  void check_flags(uint32_t flags);  // throws (and clears the barrier) after a device timeout
   friend class Runner;
 };
 
@@ -130,12 +138,36 @@ class Runner {
   std::vector<std::pair<void*, size_t>> saved;
   bool has_snapshot = false;
 
-  enum Variant { kGreedy = 0, kStep = 1, kLayers = 2, kVariants = 3 };
-  cudaGraphExec_t graph[kVariants] = {nullptr, nullptr, nullptr};
-  size_t launches_per_token = 0;
+  uint32_t* barrier = nullptr;  // grid barrier words of the fused layer kernels
+  bool trace_on = false;
+  unsigned long long* trace = nullptr;  // fused path phase timestamps [layers][ctas][32]
 
-  void record(Variant v, cudaStream_t s);  // enqueue one token's kernels on s
+  // Token graphs: kGreedy = layers + LM head + pick (the pick becomes the next token),
+  // kStep = the same without advancing, kLayers = layers only (prefill).
+  enum Variant { kGreedy = 0, kStep = 1, kLayers = 2, kVariants = 3 };
+  cudaGraphExec_t graph[kVariants] = {nullptr, nullptr, nullptr};   // one kernel per op
+  cudaGraphExec_t fgraph[kVariants] = {nullptr, nullptr, nullptr};  // one fused launch per layer
+  size_t launches_per_token = 0;
+  size_t fused_launches_per_token = 0;
+  bool use_fused = false;
+  int fused_ctas = 0, fused_max_k = 0;
+
+  struct LayerArgs {
+    bool attention = false;
+    GemvArgs in, out, gate_up, down;
+    AttnArgs at;
+    dev::GdnArgs gdn{};
+  };
+  LayerArgs layer_args(int i) const;
+  GemvArgs head_args(Variant v) const;
+  void record(Variant v, cudaStream_t s);        // enqueue one token's kernels on s
+  void record_fused(Variant v, cudaStream_t s);  // the same as one fused launch per layer
+  bool set_trace(bool on);
+  bool fused_supported();
+  void capture_set(cudaGraphExec_t* out, bool fused);
   void capture_graphs();
+  bool set_fused(bool on);  // false if the fused kernels are not available
+  size_t per_token() const;
   void launch(Variant v, cudaStream_t s);
   void reset(cudaStream_t s);
   void snapshot(cudaStream_t s);

@@ -8,7 +8,6 @@
 
 namespace qne {
 
-constexpr uint32_t kFlagTimeout = 2u;
 constexpr uint32_t kWaitLimit = 1u << 24;  // try_wait rounds before a wait gives up
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }

@@ -71,6 +71,10 @@ def _load_lib() -> C.CDLL:
         "qne_model_free": (None, [P]),
         "qne_model_info_get": (I32, [P, C.POINTER(_Info)]),
         "qne_model_set_stream": (I32, [P, P]),
+        "qne_model_set_fused": (I32, [P, I32]),
+        "qne_model_fused": (I32, [P]),
+        "qne_model_set_phase_trace": (I32, [P, I32]),
+        "qne_model_phase_trace": (I32, [P, P, SZ, C.POINTER(SZ), C.POINTER(SZ)]),
         "qne_adapter": (C.c_char_p, [P]),
         "qne_dispatches_per_token": (SZ, [P]),
         "qne_validate_tiles": (I32, [C.c_char_p, SZ]),
@@ -271,6 +275,25 @@ class Model:
 
     def set_stream(self, stream_handle: int | None) -> None:
         _check(lib.qne_model_set_stream(self._h, C.c_void_p(stream_handle or 0)))
+
+    def set_fused(self, enable: bool) -> None:
+        """One fused cooperative launch per layer (True) or one kernel per operation (False)."""
+        _check(lib.qne_model_set_fused(self._h, 1 if enable else 0))
+
+    @property
+    def fused(self) -> bool:
+        return bool(lib.qne_model_fused(self._h))
+
+    def set_phase_trace(self, enable: bool) -> None:
+        _check(lib.qne_model_set_phase_trace(self._h, 1 if enable else 0))
+
+    def phase_trace(self) -> np.ndarray:
+        """Last token's fused-path timestamps, shape [layers, ctas, 32] (ns, %globaltimer)."""
+        n, ctas = C.c_size_t(), C.c_size_t()
+        _check(lib.qne_model_phase_trace(self._h, None, 0, C.byref(n), C.byref(ctas)))
+        out = np.zeros(self.layers * ctas.value * 32, np.uint64)
+        _check(lib.qne_model_phase_trace(self._h, out.ctypes.data, out.size, C.byref(n), C.byref(ctas)))
+        return out.reshape(self.layers, ctas.value, 32)
 
     def matrix(self, name: str) -> _Matrix:
         """Device descriptor of a loaded matrix (index.json name)."""

@@ -1,5 +1,6 @@
 """Model-level parity and API semantics on the B200: the whole decode step (CUDA graph of the
-sm_100a kernels) against the CPU oracle on the same random-init weights and token ids.
+sm_100a kernels, either one kernel per operation or one fused launch per layer)
+against the CPU oracle on the same random-init weights and token ids.
 Logits: max-abs <= 2e-2 and rel_err <= 1e-3; greedy streams identical (steps whose oracle top-2
 margin is below the logit tolerance are reported, not failed)."""
 import numpy as np
@@ -37,12 +38,23 @@ def greedy_compare(model, om, prompt, steps):
     return steps
 
 
-@pytest.fixture(scope="module", params=["f16", "q4g64", "q4"])
+def set_path(m, fused):
+    """fused=True selects the fused layer kernels (f16 weights on a B200; an error if they are not
+    available); False the per-operation kernels (the default)."""
+    m.set_fused(fused)
+    assert m.fused == fused
+    assert m.dispatches_per_token() == (m.layers if fused else 5 * m.layers + 1)
+
+
+@pytest.fixture(scope="module", params=[("f16", True), ("f16", False), ("q4g64", False), ("q4", False)],
+                ids=["f16-fused", "f16-split", "q4g64", "q4"])
 def tiny(request, cuda):
-    s = synth.build(1024, 3584, layers=4, vocab=8192, kind=request.param, seed=11)
+    kind, fused = request.param
+    s = synth.build(1024, 3584, layers=4, vocab=8192, kind=kind, seed=11)
     m = qne.Model(s.index_json, s.weights)
+    set_path(m, fused)
     om = oracle.OracleModel(s.index_json, s.weights, kv_f16=True)
-    yield request.param, s, m, om
+    yield kind, s, m, om
     m.close()
     om.close()
 
@@ -147,16 +159,60 @@ def test_restore_without_snapshot(cuda):
     with pytest.raises(qne.QneError) as e:
         m.restore()
     assert e.value.name == "ENOSNAP"
-    assert m.dispatches_per_token() == 4 * 5 + 1
+    assert not m.fused and m.dispatches_per_token() == 4 * 5 + 1  # per-operation path by default
+    m.set_fused(True)
+    assert m.dispatches_per_token() == 4  # one fused launch per layer
     assert "B200" in m.adapter or "sm_10" in m.adapter
     m.close()
 
 
+def test_fused_and_split_paths_agree(cuda):
+    """The two launch paths on one model: logits within the parity tolerance, identical picks,
+    and switching paths mid-sequence keeps the state (both read and write the same buffers)."""
+    s = synth.build(1024, 3584, layers=8, vocab=8192, seed=13)
+    m = qne.Model(s.index_json, s.weights)
+    prompt = synth.prompt_ids(70, 6, 8192)
+    out = {}
+    for fused in (True, False):
+        m.set_fused(fused)
+        m.reset()
+        m.prefill(prompt)
+        out[fused] = (m.logits().copy(), m.decode(12, 1))
+    logits_close(out[True][0], out[False][0].astype(np.float64))
+    assert out[True][1] == out[False][1]
+    m.set_fused(True)
+    m.reset()
+    m.prefill(prompt[:40])
+    m.set_fused(False)
+    m.prefill_chunk(prompt[40:], 40, True)
+    logits_close(m.logits(), out[False][0].astype(np.float64))
+    m.close()
+
+
+def test_fused_kernels_at_a_long_context(cuda):
+    """Attention splits of the fused kernel past one 64-token block and past 8 groups of splits:
+    prefill 600 tokens, then compare against the per-operation kernels."""
+    s = synth.build(1024, 3584, layers=4, vocab=4096, seed=14)
+    m = qne.Model(s.index_json, s.weights)
+    prompt = synth.prompt_ids(600, 7, 4096)
+    res = []
+    for fused in (True, False):
+        m.set_fused(fused)
+        m.reset()
+        m.prefill(prompt)
+        res.append((m.logits().copy(), m.decode(6, 1)))
+    logits_close(res[0][0], res[1][0].astype(np.float64))
+    assert res[0][1] == res[1][1]
+    m.close()
+
+
 @pytest.mark.slow
-def test_config1_full_08b_parity(cuda):
+@pytest.mark.parametrize("fused", [True, False], ids=["fused", "split"])
+def test_config1_full_08b_parity(cuda, fused):
     """0.8B-shaped f16 model (seed 0), 128 prompt ids (seed 0), greedy steps."""
     s = synth.build_config(1)
     m = qne.Model(s.index_json, s.weights)
+    set_path(m, fused)
     om = oracle.OracleModel(s.index_json, s.weights, kv_f16=True)
     prompt = synth.prompt_ids(128, 0)
     n = greedy_compare(m, om, prompt, 32)
@@ -172,6 +228,8 @@ def test_config_2b_short_context_parity(cuda, cfg):
     the CPU oracle takes too long for a test; attention at 4096 is covered by the operator tests)."""
     s = synth.build_config(cfg)
     m = qne.Model(s.index_json, s.weights)
+    if cfg == 2:
+        m.set_fused(True)  # the 2B f16 config runs through the fused layer kernels here
     om = oracle.OracleModel(s.index_json, s.weights, kv_f16=True)
     prompt = synth.prompt_ids(48, cfg)
     n = greedy_compare(m, om, prompt, 32)
