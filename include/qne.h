@@ -230,6 +230,16 @@ QNE_API qne_status qne_rmsnorm_gemv(const qne_matrix* m, const float* h, const f
 QNE_API size_t qne_gemm_scratch_bytes(const qne_matrix* m, int batch);
 QNE_API qne_status qne_gemm(const qne_matrix* m, const float* x, int batch, float* y, int epilogue,
                     void* scratch, size_t scratch_bytes, void* stream);
+/* qne_gemm without any device allocation (no counterpart in the reference, whose buffers are
+ * all created at model load): the same kernels, with x's hi/lo planes and the SwiGLU
+ * intermediate in one static 2 MiB device array instead of a workspace grown with cudaMalloc.
+ * For callers whose device memory is fully planned or who cannot afford an allocation's
+ * synchronization. Rejects calls needing more than 2 MiB (2*Bp*k*2 bytes, plus 2*Bp*out_rows*2
+ * with SwiGLU; Bp = batch rounded up to 8) with QNE_EINVAL. The first call on a device sets up
+ * the array's address; make it before any stream capture. One array per device: overlapping
+ * calls on one device race; serialize them on one stream. */
+QNE_API qne_status qne_gemm_noalloc(const qne_matrix* m, const float* x, int batch, float* y, int epilogue,
+                                    void* stream);
 /* Dequantized rows [row0, row0 + nrows) of m into out[nrows][k] f32, through the same unpack
  * code as the GEMV (QMat layout, kernels/src/lib.rs:484-497 dequant_row). */
 QNE_API qne_status qne_dequant_rows(const qne_matrix* m, int row0, int nrows, float* out, void* stream);

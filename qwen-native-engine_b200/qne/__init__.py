@@ -107,6 +107,7 @@ def _load_lib() -> C.CDLL:
         "qne_gemv_ex": (I32, [C.POINTER(_Matrix), P, P, I32, I32, I32, P]),
         "qne_gemm_scratch_bytes": (SZ, [C.POINTER(_Matrix), I32]),
         "qne_gemm": (I32, [C.POINTER(_Matrix), P, I32, P, I32, P, SZ, P]),
+        "qne_gemm_noalloc": (I32, [C.POINTER(_Matrix), P, I32, P, I32, P]),
         "qne_dequant_rows": (I32, [C.POINTER(_Matrix), I32, I32, P, P]),
         "qne_embed": (I32, [C.POINTER(_Matrix), P, P, P]),
         "qne_argmax_scratch_bytes": (SZ, [U32]),
