@@ -159,6 +159,24 @@ def time_gemv_family(model, torch, reps: int = 3):
     return mean_ms, bytes_per_launch
 
 
+def profile_step4(args):
+    """Small fixed workload for ncu captures: a 2B-shaped decoder cut to 4 layers (32K vocab,
+    seed 3), a 16-token prompt, then 8 greedy tokens on the device, through the launch path chosen
+    by --path. Launch order: model set-up, 16 prompt tokens, 8 decode tokens."""
+    import qne
+    from qne import synth
+    s = synth.build(2048, 6144, layers=4, vocab=32768, seed=3)
+    m = qne.Model(s.index_json, s.weights)
+    if args.path != "auto":
+        m.set_fused(args.path == "fused")
+    m.prefill(synth.prompt_ids(16, 2, 32768))
+    m.decode_async(8)
+    m.sync()
+    print(json.dumps({"micro": "step4", "fused": m.fused, "dispatches_per_token": m.dispatches_per_token(),
+                      "last_token": list(m.last_token())}), flush=True)
+    m.close()
+
+
 def micro(args):
     """per-kernel microbench (seed 4). Each kernel is timed over enough distinct
     copies of its inputs that every launch reads HBM (> 126 MB L2 per rotation); launches are queued
@@ -320,7 +338,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--prompt", type=int, default=PROMPT)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--micro", default="", help="config-5 microbench: all | gemv,gdn,attn")
+    ap.add_argument("--micro", default="", help="config-5 microbench: all | gemv,gdn,attn; "
+                                                     "step4 = the small decode workload of the ncu captures")
     ap.add_argument("--no-batched", action="store_true", help="skip the config-4 batched decode run")
     ap.add_argument("--batched-only", action="store_true", help="run only the config-4 batched decode (profiling)")
     ap.add_argument("--batched-steps", type=int, default=64)
@@ -328,6 +347,9 @@ def main():
                     help="B=1 launch path: one kernel per op (the default) or the fused layer kernels")
     args = ap.parse_args()
     world, rank, local = dist_setup()
+    if args.micro == "step4":
+        profile_step4(args)
+        return
     if args.micro:
         micro(args)
         return
@@ -460,8 +482,10 @@ def main():
                     "mean_launch_us": round(ms / steps / dispatches * 1e3, 2),
                     "bytes_per_launch": int(tok_bytes / dispatches)}
         else:
+            # traffic: DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one gate_up
+            # launch from a full ncu capture (2B shape, cold L2): 50.38 MB read + 0.024 MB written.
             roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                    "frac": round(achieved / peak, 4), "traffic": None,
+                    "frac": round(achieved / peak, 4), "traffic": 50_405_120,
                     "kernel": "gemv_pipe_kernel<RMSNorm, SwiGLU> (gate_up, 12288x2048)",
                     "peak_source": peak_kind, "mean_launch_us": round(gemv_ms * 1e3, 2)}
         line = {
