@@ -59,7 +59,7 @@ __device__ __forceinline__ void prefetch_rows(const uint8_t* base, size_t row_by
   if (bytes > budget) bytes = budget;
   bytes &= ~(size_t)15;
   const uint8_t* p = base + (size_t)r0 * row_bytes;
-  #pragma unroll 1
+#pragma unroll 1
   for (size_t off = (size_t)lane * kPrefetchPiece; off < bytes; off += 32 * kPrefetchPiece) {
     const size_t n = bytes - off < kPrefetchPiece ? bytes - off : kPrefetchPiece;
     prefetch_l2(p + off, (uint32_t)n);
@@ -96,12 +96,12 @@ __device__ __forceinline__ void stage_x(const GemvArgs& a, float* xs, float* red
   const int k = a.m.k;
   const int tid = threadIdx.x;
   if (PRO == kProCopy) {
-        for (int i = tid * 4; i < k; i += kThreads * 4)
+    for (int i = tid * 4; i < k; i += kThreads * 4)
       *reinterpret_cast<float4*>(xs + i) = *reinterpret_cast<const float4*>(a.x + i);
   } else if (PRO == kProRmsNorm || PRO == kProEmbedNorm) {
     float ss = 0.f;
     if (PRO == kProRmsNorm) {
-            for (int i = tid * 4; i < k; i += kThreads * 4) {
+      for (int i = tid * 4; i < k; i += kThreads * 4) {
         const float4 v = *reinterpret_cast<const float4*>(a.x + i);
         *reinterpret_cast<float4*>(xs + i) = v;
         ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
@@ -110,19 +110,19 @@ __device__ __forceinline__ void stage_x(const GemvArgs& a, float* xs, float* red
       // Embedding row of the token the previous step picked (or the host wrote).
       uint32_t token = a.ctl->token;
       if (token >= (uint32_t)a.embed.rows) token = (uint32_t)a.embed.rows - 1;
-            for (int i = tid; i < k; i += kThreads) {
+      for (int i = tid; i < k; i += kThreads) {
         const float v = deq_elem(a.embed, token, i);
         xs[i] = v;
         ss += v * v;
       }
       if (blockIdx.x == 0) {
-                for (int i = tid; i < k; i += kThreads) a.h_out[i] = xs[i];
+        for (int i = tid; i < k; i += kThreads) a.h_out[i] = xs[i];
         if (tid == 0) a.ctl->count += 1;  // one more token entered the conv windows
       }
     }
     const float tot = sum256(ss, red, sync);
     const float inv = rsqrtf(tot / (float)k + a.eps);
-        for (int i = tid; i < k; i += kThreads) xs[i] = xs[i] * inv * a.norm_w[i];
+    for (int i = tid; i < k; i += kThreads) xs[i] = xs[i] * inv * a.norm_w[i];
   } else if (PRO == kProGdnGate) {
     // k == 2048: 16 heads of 128; warp w normalizes heads 2w and 2w+1.
     const int warp = tid >> 5, lane = tid & 31;
@@ -189,9 +189,8 @@ struct GemvShared {
 // all warps get the same number of rows within one. A row is processed in segments of at most
 // 2048 elements (1024 for SwiGLU, whose unit is a gate row plus its up row); while one segment
 // is multiplied, the next segment's 16-byte loads are already in flight in a second register
-// buffer. prefetch() issues the first segment's loads and asks the TMA unit to bring the warp's
-// next rows into L2: it touches weights only, so callers run it before waiting on the
-// producer of x.
+// buffer. prefetch() issues the first segment's loads: it touches weights only, so callers run
+// it before waiting on the producer of x.
 template <int PRO, int EPI>
 struct Pipe {
   static constexpr bool SW = (EPI == kSwiGlu);
@@ -232,17 +231,10 @@ struct Pipe {
     }
   }
 
+  // First unit into registers. (A bulk L2 prefetch of the warp's next rows here was measured
+  // and makes the decode step slower: it competes with the demand stream instead of filling gaps.)
   __device__ __forceinline__ void prefetch() {
     if (units > 0) load(cur, 0);
-        for (int j = 1; j <= 3 && j < my_rows; ++j) {
-      const long row = gw + (long)j * nw;
-#pragma unroll
-      for (int rr = 0; rr < R; ++rr) {
-        const uint8_t* base = W + (size_t)(rr ? half + row : row) * rb;
-                for (size_t off = (size_t)lane * 512; off < rb; off += 32 * 512)
-          prefetch_l2(base + off, (uint32_t)min((size_t)512, rb - off));
-      }
-    }
   }
 
   // Stages x (prologue), then streams every unit. For kArgmax the lane-0 best candidate of each
@@ -251,7 +243,7 @@ struct Pipe {
     const int warp = threadIdx.x >> 5;
     stage_x<PRO>(a, xs, sh.red);
     float* xp = xs + k;  // planes: elements 0-3 and 4-7 of every 8-element chunk
-        for (int c = threadIdx.x; c < k / 8; c += kThreads) {
+    for (int c = threadIdx.x; c < k / 8; c += kThreads) {
       *reinterpret_cast<float4*>(xp + c * 4) = *reinterpret_cast<const float4*>(xs + c * 8);
       *reinterpret_cast<float4*>(xp + k / 2 + c * 4) = *reinterpret_cast<const float4*>(xs + c * 8 + 4);
     }
@@ -262,7 +254,7 @@ struct Pipe {
 #pragma unroll
     for (int rr = 0; rr < R; ++rr) acc[rr] = 0.f;
     uint4 nxt[R][CPL];
-        for (int u = 0; u < units; ++u) {
+    for (int u = 0; u < units; ++u) {
       if (u + 1 < units) load(nxt, u + 1);
       const int sg = u % nseg;
       const float* xlo = xp + (size_t)sg * (seg / 2);
@@ -538,7 +530,7 @@ __device__ __forceinline__ void argmax_finish(const GemvArgs& a, int cta, int nc
     __threadfence();
     float v = -INFINITY;
     uint32_t ix = 0xFFFFFFFFu;
-    #pragma unroll 1
+#pragma unroll 1
     for (int b = lane; b < ncta; b += 32) {
       const float bv = __ldcg(a.part_val + b);
       const uint32_t bi = __ldcg(a.part_idx + b);
