@@ -88,6 +88,35 @@ def dist_setup():
     return world, rank, local
 
 
+def make_collectives(dist, world: int, device: str):
+    """Barrier and max-over-ranks used around every timed region (one process per GPU; gloo on
+    CPU in the tests). Every rank must call them in the same order."""
+    import torch
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    return barrier, max_over_ranks
+
+
+def rank_seed(base: int, rank: int) -> int:
+    """Seed of rank `rank`'s synthetic inputs: every replica decodes its own sequences."""
+    return base + 1000 * rank
+
+
+def aggregate_rate(world: int, units_per_rank: int, max_ms: float) -> float:
+    """Whole-job throughput: the units all ranks processed over the slowest rank's time."""
+    return world * units_per_rank / (max_ms * 1e-3)
+
+
 def cpu_oracle_rate(s, prompt_len: int, tokens: int, seed: int):
     """Oracle decode rate on the host: `tokens` steps after a short untimed prefill."""
     from oracle import oracle
@@ -286,14 +315,17 @@ def batched_run(torch, qne, synth, rank: int, world: int, barrier, max_over_rank
     `steps` greedy steps. Returns a dict for the JSON line (rank 0) or None."""
     s = synth.build_config(4)
     model = qne.Model(s.index_json, s.weights, device=torch.cuda.current_device())
-    stream = torch.cuda.current_stream()
+    # A dedicated stream for the engine and the events that time it (the default stream's handle
+    # is 0, which the engine reads as "use the model's own stream").
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
     model.set_stream(stream.cuda_stream)
-    rng = np.random.default_rng(3 + 1000 * rank)
+    rng = np.random.default_rng(rank_seed(3, rank))
     lens = rng.integers(256, 4096 - steps - warmup, batch, endpoint=True)
     bt = qne.Batch(model, batch)
     bt.set_page_table(rng.permutation(batch * 256).astype(np.uint32))
     for b in range(batch):
-        bt.fill_synthetic(b, int(lens[b]), int(rng.integers(0, synth.VOCAB)), 3 + 1000 * rank + b)
+        bt.fill_synthetic(b, int(lens[b]), int(rng.integers(0, synth.VOCAB)), rank_seed(3, rank) + b)
     bt.sync()
     if warmup:
         bt.decode_async(warmup)
@@ -318,7 +350,7 @@ def batched_run(torch, qne, synth, rank: int, world: int, barrier, max_over_rank
     model.close()
     if rank != 0:
         return None
-    tps = world * batch * steps / (ms * 1e-3)
+    tps = aggregate_rate(world, batch * steps, ms)
     return {"workload": f"config 4: Qwen3.5-0.8B-shaped f16 (seed 3), {batch} sequences per GPU, contexts "
                         f"U[256,{4096 - steps - warmup}] (mean {lens.mean():.0f}), permuted 16-token pages, "
                         f"{steps} greedy steps",
@@ -367,16 +399,7 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    def max_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+    barrier, max_over_ranks = make_collectives(dist, world, "cuda")
 
     if args.batched_only:
         res = batched_run(torch, qne, synth, rank, world, barrier, max_over_ranks, args.warmup, args.batched_steps)
@@ -400,7 +423,7 @@ def main():
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
     model.set_stream(stream.cuda_stream)
-    prompt = synth.prompt_ids(prompt_len, 1 + 1000 * rank)
+    prompt = synth.prompt_ids(prompt_len, rank_seed(1, rank))
     model.reset()
     model.prefill(prompt)
     model.snapshot()
@@ -466,7 +489,7 @@ def main():
                          "(C++ restatement of the reference decoder, all host threads)"}
 
     if rank == 0:
-        value = world * steps / (ms * 1e-3)
+        value = aggregate_rate(world, steps, ms)
         bytes_per_token = model.weight_bytes + 24 * 0  # weights; state/KV listed below
         kv_bytes = 6 * 2048 * (prompt_len + steps / 2)
         state_bytes = 18 * (2 * 16 * 128 * 128 * 4 + 2 * 4 * 6144 * 4)
@@ -496,7 +519,7 @@ def main():
                                    f"KV prefilled to {prompt_len}, {steps} greedy decode steps",
                        "model": "qwen3.5-2b-shaped", "global_batch": world, "seq_len": 4096,
                        "parallelism": f"replicas x{world}", "l2": "inputs larger than L2 (3.76 GB of weights per step)"},
-            "e2e": {"value": round(world * steps / e2e_s, 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
+            "e2e": {"value": round(aggregate_rate(world, steps, e2e_s * 1e3), 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
                     "d2h_bytes_per_step": model.vocab * 4},
             "roofline": roof,
             "step_roofline": {"bytes_per_token": int(tok_bytes), "achieved_gbs": round(tok_bytes * value / world / 1e9, 1),
