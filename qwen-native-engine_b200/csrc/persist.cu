@@ -16,10 +16,9 @@
 // each other's loop-invariant state live and exceed the 128 registers that two CTAs per SM
 // allow.
 //
-// The barrier is a counter plus a generation word in global memory; waiting CTAs poll with a
-// time limit and, on timeout, set kFlagTimeout in the sequence's control word and carry on, so
-// a fault can never hang the GPU. The launch is cooperative, so all CTAs are co-resident.
-#include <cooperative_groups.h>
+// Grid barriers (GridBarrier below) wait with a time limit and, on timeout, set kFlagTimeout in
+// the sequence's control word and carry on, so a fault can never hang the GPU. The grid is the
+// occupancy bound, so all CTAs are co-resident (see launch_layer_t).
 
 #include "attn_dev.cuh"
 #include "gdn_dev.cuh"

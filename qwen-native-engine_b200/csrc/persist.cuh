@@ -1,4 +1,4 @@
-// Host interface of the fused (one cooperative launch per layer) decode kernels.
+// Host interface of the fused (one launch per decoder layer) decode kernels.
 #pragma once
 
 #include <cuda_runtime.h>
