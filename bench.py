@@ -184,7 +184,10 @@ def time_gemv_family(model, torch, reps: int = 3):
     torch.cuda.synchronize()
     durs = [events[i].elapsed_time(events[i + 1]) for i in range(len(events) - 1)]
     mean_ms = float(np.mean(durs))
-    bytes_per_launch = 2 * I * H * 2 + H * 4 + I * 4
+    # bytes per weight: f16; block-32 int4 (+ u32 scale pair per 64, u32 zero points per 256);
+    # group-64 int4 (+ f16 scale and f16 zero point per 64)
+    bpw = {0: 2.0, 1: 0.5 + 4 / 64 + 4 / 256, 2: 0.5 + 4 / 64}[int(mats[0].kind)]
+    bytes_per_launch = int(2 * I * H * bpw) + H * 4 + I * 4
     return mean_ms, bytes_per_launch
 
 
@@ -368,7 +371,10 @@ def main():
     ap.add_argument("--steps", type=int, default=128)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--prompt", type=int, default=PROMPT)
+    ap.add_argument("--prompt", type=int, default=None, help="context tokens before the timed steps "
+                                                            "(default: the config's)")
+    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3],
+                    help="B=1 workload: BASELINE config 1 (0.8B f16), 2 (2B f16, the headline) or 3 (2B int4 g64)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--micro", default="", help="config-5 microbench: all | gemv,gdn,attn; "
                                                      "step4 = the small decode workload of the ncu captures")
@@ -410,11 +416,14 @@ def main():
         return
 
     steps = args.steps
-    prompt_len = min(args.prompt, 4096 - steps)
+    cfg_n = args.config
+    cfg_info = synth.baseline_config(cfg_n)
+    size_name = {"0.8b": "0.8B", "2b": "2B"}[cfg_info["size"]]
+    prompt_len = min(args.prompt if args.prompt is not None else cfg_info["prompt"], 4096 - steps)
     if prompt_len < 1 or steps < 1 or args.warmup < 0:
         raise SystemExit("need 1 <= --steps <= 4095")
 
-    s = synth.build_config(2)
+    s = synth.build_config(cfg_n)
     model = qne.Model(s.index_json, s.weights, device=local)
     if args.path != "auto":
         model.set_fused(args.path == "fused")
@@ -485,8 +494,8 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, cores = cpu_oracle_rate(s, 16, 4, 1)
         cpu = {"value": round(rate, 4), "unit": "tok/s", "cores": cores, "kind": "port",
-               "sample": "4 decode tokens of the same 2B f16 model after a 16-token prefill, CPU oracle "
-                         "(C++ restatement of the reference decoder, all host threads)"}
+               "sample": f"4 decode tokens of the same {size_name} {cfg_info['kind']} model after a 16-token "
+                         "prefill, CPU oracle (C++ restatement of the reference decoder, all host threads)"}
 
     if rank == 0:
         value = aggregate_rate(world, steps, ms)
@@ -507,18 +516,23 @@ def main():
         else:
             # traffic: DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one gate_up
             # launch from a full ncu capture (2B shape, cold L2): 50.38 MB read + 0.024 MB written.
+            f16 = cfg_info["kind"] == "f16"
+            shape = f"{2 * model.intermediate}x{model.hidden}"
             roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                    "frac": round(achieved / peak, 4), "traffic": 50_405_120,
-                    "kernel": "gemv_pipe_kernel<RMSNorm, SwiGLU> (gate_up, 12288x2048)",
+                    "frac": round(achieved / peak, 4), "traffic": 50_405_120 if cfg_n == 2 else None,
+                    "kernel": (f"gemv_pipe_kernel<RMSNorm, SwiGLU> (gate_up, {shape})" if f16 else
+                               f"int4 GEMV <{cfg_info['kind']}, RMSNorm, SwiGLU> (gate_up, {shape})"),
                     "peak_source": peak_kind, "mean_launch_us": round(gemv_ms * 1e3, 2)}
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": steps,
             "warmup": args.warmup, "ms_per_step": round(ms / steps, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-            "config": {"workload": f"config 2: Qwen3.5-2B-shaped f16 hybrid decoder (synthetic, seed 1), B=1 per GPU, "
-                                   f"KV prefilled to {prompt_len}, {steps} greedy decode steps",
-                       "model": "qwen3.5-2b-shaped", "global_batch": world, "seq_len": 4096,
-                       "parallelism": f"replicas x{world}", "l2": "inputs larger than L2 (3.76 GB of weights per step)"},
+            "config": {"workload": f"config {cfg_n}: Qwen3.5-{size_name}-shaped {cfg_info['kind']} hybrid decoder "
+                                   f"(synthetic, seed {cfg_info['seed']}), B=1 per GPU, KV prefilled to {prompt_len}, "
+                                   f"{steps} greedy decode steps",
+                       "model": f"qwen3.5-{size_name.lower()}-shaped", "global_batch": world, "seq_len": 4096,
+                       "parallelism": f"replicas x{world}",
+                       "l2": f"inputs larger than L2 ({model.weight_bytes / 1e9:.2f} GB of weights per step)"},
             "e2e": {"value": round(aggregate_rate(world, steps, e2e_s * 1e3), 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
                     "d2h_bytes_per_step": model.vocab * 4},
             "roofline": roof,

@@ -298,6 +298,21 @@ __device__ __forceinline__ void mma_f16(float* c, uint32_t a0, uint32_t a1, uint
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// int4 GEMV through registers (Q4Pipe): the warp's share of weights, scales and zero points is
+// loaded before the wait on the previous kernel.
+template <int KIND, int PRO, int EPI>
+__global__ void __launch_bounds__(kThreads, 2) gemv_q4pipe_kernel(const GemvArgs a) {
+  extern __shared__ __align__(16) float xs[];
+  __shared__ GemvShared sh;
+  Q4Pipe<KIND, PRO, EPI> p;
+  p.init(a, blockIdx.x, gridDim.x);
+  pdl_launch();
+  p.prefetch(a);
+  pdl_wait();
+  p.run(a, xs, sh);
+  if (EPI == kArgmax) argmax_finish(a, blockIdx.x, gridDim.x, sh);
+}
+
 template <int KIND, int PRO, int EPI>
 __global__ void __launch_bounds__(kThreads, 2) gemv_q4_mma_kernel(const GemvArgs a) {
   extern __shared__ __align__(16) float xs[];  // [k] x, then [2][k/8] uint4 pair planes, then [k/32] block sums
@@ -854,6 +869,28 @@ cudaError_t launch_pipe(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   return launch_ex(kernel, dim3(grid), dim3(kThreads), smem, stream, pdl, a);
 }
 
+// Q4Pipe holds 8 chunks of 32 values per lane and unit: one output row (its gate and up rows
+// for SwiGLU) must fit, i.e. k <= 8192 (4096 with SwiGLU).
+bool q4pipe_fits(const GemvArgs& a) {
+  const int cpl = (a.m.k / 32 + 31) / 32;
+  return a.m.k % 256 == 0 && cpl * (a.epi == kSwiGlu ? 2 : 1) <= 8;
+}
+
+template <int KIND, int PRO, int EPI>
+cudaError_t launch_q4pipe(const GemvArgs& a, cudaStream_t stream, bool pdl) {
+  auto kernel = gemv_q4pipe_kernel<KIND, PRO, EPI>;
+  const size_t smem = ((size_t)2 * a.m.k + a.m.k / 32) * sizeof(float);  // x, transposed x, chunk sums
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  const int out_rows = (EPI == kSwiGlu) ? a.m.rows / 2 : a.m.rows;
+  int grid = (out_rows + kWarps - 1) / kWarps;  // at least one row per warp
+  if (grid > 2 * kNumSms) grid = 2 * kNumSms;
+  if (grid < 1) grid = 1;
+  return launch_ex(kernel, dim3(grid), dim3(kThreads), smem, stream, pdl, a);
+}
+
 template <int KIND, int PRO, int EPI>
 cudaError_t launch_q4_mma(GemvArgs a, cudaStream_t stream, bool pdl) {
   auto kernel = gemv_q4_mma_kernel<KIND, PRO, EPI>;
@@ -921,7 +958,23 @@ cudaError_t launch_kind(const GemvArgs& a, cudaStream_t stream, bool pdl) {
     QNE_PCOMBO(kProGdnGate, kAccumulate)
 #undef QNE_PCOMBO
   }
-  if (KIND != kF16 && a.variant != 1 && a.m.k % 256 == 0) {
+  if constexpr (KIND != kF16) {
+    if (a.variant == 0 && q4pipe_fits(a)) {
+#define QNE_Q4P(P, E) \
+    if (a.pro == P && a.epi == E) return launch_q4pipe<KIND, P, E>(a, stream, pdl);
+      QNE_Q4P(kProCopy, kStore)
+      QNE_Q4P(kProCopy, kAccumulate)
+      QNE_Q4P(kProCopy, kSwiGlu)
+      QNE_Q4P(kProRmsNorm, kStore)
+      QNE_Q4P(kProRmsNorm, kAccumulate)
+      QNE_Q4P(kProRmsNorm, kSwiGlu)
+      QNE_Q4P(kProRmsNorm, kArgmax)
+      QNE_Q4P(kProEmbedNorm, kStore)
+      QNE_Q4P(kProGdnGate, kAccumulate)
+#undef QNE_Q4P
+    }
+  }
+  if (KIND != kF16 && (a.variant == 0 || a.variant == 3) && a.m.k % 256 == 0) {
 #define QNE_QCOMBO(P, E) \
     if (a.pro == P && a.epi == E) return launch_q4_mma<KIND, P, E>(a, stream, pdl);
     QNE_QCOMBO(kProCopy, kStore)
@@ -963,7 +1016,8 @@ void argmax_scratch_carve(void* scratch, float** part_val, uint32_t** part_idx, 
 
 const char* check_gemv(const GemvArgs& a) {
   const Mat& m = a.m;
-  if (a.variant < 0 || a.variant > 2) return "unknown GEMV variant";
+  if (a.variant < 0 || a.variant > 3) return "unknown GEMV variant";
+  if (a.variant == 3 && (m.kind == kF16 || m.k % 256)) return "the tensor-core GEMV needs int4 weights and k % 256 == 0";
   if (a.variant == 2 && (m.kind != kF16 || m.k % 512)) return "the bulk-copy GEMV needs f16 weights and k % 512 == 0";
   if (!m.w || m.rows <= 0 || m.k <= 0) return "matrix has no data or an empty shape";
   if (m.kind == kF16) {

@@ -502,6 +502,203 @@ struct RingPipe {
   }
 };
 
+// ------------------------------------------------------------------------------------------
+// int4 GEMV (block-32 and group-64 layouts), B = 1.
+//
+// A chunk is 16 bytes of one row: 32 nibbles, the values k = 32c .. 32c + 31. Rows are dealt
+// round-robin to the warps of the grid like the f16 pipeline; a unit is `rpu` output rows (their
+// gate and up rows for SwiGLU) packed into kSlots chunk slots per lane, lane l holding chunks
+// l, l + 32, ... of each row. At the decode shapes one unit is a warp's whole share of a layer
+// matrix (3-6 KB), so prefetch() - issued before the wait on the previous kernel - loads all of
+// it, with the chunks' scales and zero points, in a single DRAM round trip. Longer shares (an
+// int4 LM head) stream unit by unit (one buffer: a second one costs spills at 128 registers).
+// ------------------------------------------------------------------------------------------
+
+// sum_n q_n x_n over the 32 nibbles of chunk c. x is staged transposed in shared memory as
+// xt[q][c] = x[32c + 4q .. 32c + 4q + 3] (float4), so the 32 lanes of a warp, which hold 32
+// consecutive chunks, read 32 consecutive float4 for each q: no bank conflicts.
+__device__ __forceinline__ float dot_q4_chunk(const uint4& w, const float4* xt, int nch, int c) {
+  const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+  float p[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float4 a = xt[(size_t)(2 * e) * nch + c];
+    const float4 b = xt[(size_t)(2 * e + 1) * nch + c];
+    float t = nib_f(ws[e], 0) * a.x;
+    t = fmaf(nib_f(ws[e], 4), a.y, t);
+    t = fmaf(nib_f(ws[e], 8), a.z, t);
+    t = fmaf(nib_f(ws[e], 12), a.w, t);
+    t = fmaf(nib_f(ws[e], 16), b.x, t);
+    t = fmaf(nib_f(ws[e], 20), b.y, t);
+    t = fmaf(nib_f(ws[e], 24), b.z, t);
+    p[e] = fmaf(nib_f(ws[e], 28), b.w, t);
+  }
+  return (p[0] + p[1]) + (p[2] + p[3]);
+}
+
+template <int KIND, int PRO, int EPI>
+struct Q4Pipe {
+  static constexpr bool SW = (EPI == kSwiGlu);
+  static constexpr int PH = SW ? 2 : 1;  // physical rows per output row
+  static constexpr int kSlots = 8;       // 16-byte chunks per lane per unit
+  int k, nch, cpl, rpu, out_rows, gw, nw, my_rows, units, lane;
+  long half;
+  size_t rb;
+  const uint8_t* W;
+  uint32_t meta;  // per slot s, bits 4s..4s+3: output row in the unit (3 bits) | up row (bit 3)
+  uint32_t cj;    // per slot s, bits 4s..4s+3: chunk column j (chunk = 32 j + lane)
+  uint4 cur[kSlots];
+  uint32_t cs[kSlots], cz[kSlots];  // raw scale / zero-point words of each slot's chunk
+
+  __device__ __forceinline__ void init(const GemvArgs& a, int cta, int ncta) {
+    k = a.m.k;
+    nch = k / 32;
+    cpl = (nch + 31) / 32;  // chunks per lane per row (the launcher guarantees cpl * PH <= kSlots)
+    rpu = kSlots / (cpl * PH);
+    out_rows = SW ? a.m.rows / 2 : a.m.rows;
+    half = SW ? a.m.rows / 2 : 0;
+    rb = (size_t)k / 2;
+    W = static_cast<const uint8_t*>(a.m.w);
+    lane = threadIdx.x & 31;
+    gw = cta * kWarps + (threadIdx.x >> 5);
+    nw = ncta * kWarps;
+    my_rows = (out_rows > gw) ? (out_rows - gw + nw - 1) / nw : 0;
+    units = (my_rows + rpu - 1) / rpu;
+    meta = 0u;
+    cj = 0u;
+#pragma unroll 1
+    for (int s = 0; s < kSlots; ++s) {  // the only divisions by the runtime row geometry
+      const int q = s / (cpl * PH), which = (s / cpl) % PH, j = s % cpl;
+      meta |= (uint32_t)((q > 7 ? 7 : q) | (which << 3)) << (4 * s);
+      cj |= (uint32_t)j << (4 * s);
+    }
+  }
+
+  __device__ __forceinline__ int slot_q(int s) const { return (int)((meta >> (4 * s)) & 7u); }
+  __device__ __forceinline__ bool slot_up(int s) const { return (meta >> (4 * s + 3)) & 1u; }
+
+  // Slot s of unit u: output row t (or -1), physical row, chunk index c (or -1 past the row).
+  __device__ __forceinline__ void slot(int u, int s, int& t, long& row, int& c) const {
+    const int q = slot_q(s), which = slot_up(s) ? 1 : 0, j = (int)((cj >> (4 * s)) & 15u);
+    t = u * rpu + q;
+    c = j * 32 + lane;
+    if (q >= rpu || t >= my_rows || c >= nch) {
+      t = -1;
+      c = -1;
+      row = 0;
+      return;
+    }
+    row = (long)gw + (long)t * nw + (which ? half : 0);
+  }
+
+  __device__ __forceinline__ void load(const GemvArgs& a, int u) {
+#pragma unroll
+    for (int s = 0; s < kSlots; ++s) {
+      int t, c;
+      long row;
+      slot(u, s, t, row, c);
+      cur[s] = make_uint4(0u, 0u, 0u, 0u);
+      cs[s] = 0u;
+      cz[s] = 0u;
+      if (t >= 0) {
+        cur[s] = ld_stream(W + (size_t)row * rb + (size_t)c * 16);
+        if (KIND == kQ4) {  // block-32: f16 scale pair per 64 values, zero-point nibbles per 256
+          cs[s] = __ldg(static_cast<const uint32_t*>(a.m.s) + row * (k / 64) + c / 2);
+          cz[s] = __ldg(static_cast<const uint32_t*>(a.m.z) + row * (k / 256) + c / 8);
+        } else {  // group-64: f16 scale and f16 zero point per 64 values
+          cs[s] = __ldg(static_cast<const uint16_t*>(a.m.s) + row * (k / 64) + c / 2);
+          cz[s] = __ldg(static_cast<const uint16_t*>(a.m.z) + row * (k / 64) + c / 2);
+        }
+      }
+    }
+  }
+
+  // The first unit (at decode shapes the warp's whole share) into registers: weights and their
+  // quantization parameters only, so callers issue it before waiting on the producer of x.
+  __device__ __forceinline__ void prefetch(const GemvArgs& a) {
+    if (units > 0) load(a, 0);
+  }
+
+  __device__ __forceinline__ void decode(uint32_t sw, uint32_t zw, int c, float& scale, float& zp) const {
+    if (KIND == kQ4) {
+      scale = h2f((uint16_t)((c & 1) ? (sw >> 16) : (sw & 0xFFFFu)));
+      zp = (float)((zw >> (4 * (c % 8))) & 15u);
+    } else {
+      scale = h2f((uint16_t)sw);
+      zp = h2f((uint16_t)zw);
+    }
+  }
+
+  // Stages x (prologue) transposed plus its per-chunk sums, then every unit: per chunk
+  // scale * (sum q x - zp * sum x), summed per output row and reduced over the warp. For kArgmax
+  // the lane-0 best candidate of each warp lands in sh.bval / sh.bidx.
+  __device__ __forceinline__ void run(const GemvArgs& a, float* xs, GemvShared& sh) {
+    const int warp = threadIdx.x >> 5;
+    stage_x<PRO>(a, xs, sh.red);
+    float4* xt = reinterpret_cast<float4*>(xs + k);  // [8][nch] float4, then [nch] chunk sums
+    float* xsum = xs + 2 * k;
+    for (int c = threadIdx.x; c < nch; c += kThreads) {
+      float t = 0.f;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 v = *reinterpret_cast<const float4*>(xs + c * 32 + 4 * q);
+        xt[(size_t)q * nch + c] = v;
+        t += (v.x + v.y) + (v.z + v.w);
+      }
+      xsum[c] = t;
+    }
+    __syncthreads();
+    float best_v = -INFINITY;
+    uint32_t best_i = 0xFFFFFFFFu;
+    for (int u = 0; u < units; ++u) {
+      if (u > 0) load(a, u);  // unit 0 came from prefetch()
+      float acc[kSlots];
+#pragma unroll
+      for (int s = 0; s < kSlots; ++s) {
+        int t, c;
+        long row;
+        slot(u, s, t, row, c);
+        acc[s] = 0.f;
+        if (t >= 0) {
+          float scale, zp;
+          decode(cs[s], cz[s], c, scale, zp);
+          acc[s] = scale * (dot_q4_chunk(cur[s], xt, nch, c) - zp * xsum[c]);
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < kSlots; ++q) {
+        const int t = u * rpu + q;
+        if (q < rpu && t < my_rows) {  // warp-uniform
+          float g = 0.f, up = 0.f;
+#pragma unroll
+          for (int s = 0; s < kSlots; ++s) {
+            if (slot_q(s) == q && s < rpu * cpl * PH) {
+              if (slot_up(s)) up += acc[s];
+              else g += acc[s];
+            }
+          }
+          const float v = warp_sum(g);
+          const float vu = SW ? warp_sum(up) : 0.f;
+          const long row = (long)gw + (long)t * nw;
+          if (EPI == kArgmax && v > -INFINITY && (v > best_v || (v == best_v && (uint32_t)row < best_i))) {
+            best_v = v;
+            best_i = (uint32_t)row;
+          }
+          if (lane == 0) {
+            if (SW) a.y[row] = silu(v) * vu;
+            else if (EPI == kAccumulate) a.y[row] += v;
+            else a.y[row] = v;
+          }
+        }
+      }
+    }
+    if (EPI == kArgmax && lane == 0) {
+      sh.bval[warp] = best_v;
+      sh.bidx[warp] = best_i;
+    }
+  }
+};
+
 __device__ __forceinline__ bool better(float ov, uint32_t oi, float v, uint32_t ix) {
   return oi != 0xFFFFFFFFu && (ix == 0xFFFFFFFFu || ov > v || (ov == v && oi < ix));
 }
