@@ -209,6 +209,38 @@ def profile_step4(args):
     m.close()
 
 
+def profile_prefill(args):
+    """Fixed workload for the prefill launch list: the bench's config (2B f16 by default), its
+    3968-token prompt through qne_prefill_chunk, the first 3936 tokens untimed, then the last
+    32-token chunk (positions 3936..3967, the longest attention context) plus the LM head inside
+    the NVTX range "last_chunk", timed with CUDA events."""
+    import torch
+    import qne
+    from qne import synth
+    torch.cuda.set_device(0)
+    cfg_info = synth.baseline_config(args.config)
+    s = synth.build_config(args.config)
+    m = qne.Model(s.index_json, s.weights)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    m.set_stream(stream.cuda_stream)
+    n = cfg_info["prompt"]
+    prompt = synth.prompt_ids(n, 1)
+    m.prefill_chunk(prompt[: n - 32], 0, False)
+    m.sync()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("last_chunk")
+    e0.record(stream)
+    m.prefill_chunk(prompt[n - 32:], n - 32, True)
+    e1.record(stream)
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    print(json.dumps({"micro": "prefill", "config": args.config, "batched": m.prefill_batched_supported,
+                      "chunk_positions": [n - 32, n - 1], "chunk_ms": round(e0.elapsed_time(e1), 3),
+                      "last_token": list(m.last_token())}), flush=True)
+    m.close()
+
+
 def micro(args):
     """per-kernel microbench (seed 4). Each kernel is timed over enough distinct
     copies of its inputs that every launch reads HBM (> 126 MB L2 per rotation); launches are queued
@@ -377,7 +409,8 @@ def main():
                     help="B=1 workload: BASELINE config 1 (0.8B f16), 2 (2B f16, the headline) or 3 (2B int4 g64)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--micro", default="", help="config-5 microbench: all | gemv,gdn,attn; "
-                                                     "step4 = the small decode workload of the ncu captures")
+                                                     "step4 = the small decode workload of the ncu captures; "
+                                                     "prefill = the last 32-token chunk of the bench prompt")
     ap.add_argument("--no-batched", action="store_true", help="skip the config-4 batched decode run")
     ap.add_argument("--batched-only", action="store_true", help="run only the config-4 batched decode (profiling)")
     ap.add_argument("--batched-steps", type=int, default=64)
@@ -385,6 +418,9 @@ def main():
                     help="B=1 launch path: one kernel per op (the default) or the fused layer kernels")
     args = ap.parse_args()
     world, rank, local = dist_setup()
+    if args.micro == "prefill":
+        profile_prefill(args)
+        return
     if args.micro == "step4":
         profile_step4(args)
         return
@@ -433,8 +469,22 @@ def main():
     torch.cuda.set_stream(stream)
     model.set_stream(stream.cuda_stream)
     prompt = synth.prompt_ids(prompt_len, rank_seed(1, rank))
+    # Batched prompt processing through the public API (qne_prefill_chunk: 32-token chunks on
+    # f16 weights, one token per step on int4), timed on the device. An untimed call first builds
+    # the chunk runner and the launch graphs of the chunk sizes the prompt uses.
     model.reset()
-    model.prefill(prompt)
+    model.prefill_chunk(prompt[: min(prompt_len, 32 + prompt_len % 32)], 0, True)
+    model.reset()
+    model.sync()
+    torch.cuda.synchronize()
+    barrier()
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record(stream)
+    model.prefill_chunk(prompt, 0, True)
+    p1.record(stream)
+    torch.cuda.synchronize()
+    prefill_ms = max_over_ranks(p0.elapsed_time(p1))
+    prefill_batched = model.prefill_batched_supported
     model.snapshot()
     model.sync()
 
@@ -485,6 +535,7 @@ def main():
     achieved = gemv_bytes / (gemv_ms * 1e-3) / 1e9
 
     dispatches = model.dispatches_per_token()
+    model_weight_bytes = model.weight_bytes
     model.close()
     batched = None
     if not args.no_batched:
@@ -543,6 +594,12 @@ def main():
             "clocks": clk,
             "cpu_baseline": cpu,
             "batched": batched,
+            "prefill": {"tokens": prompt_len, "ms": round(prefill_ms, 3),
+                        "tok_per_s": round(aggregate_rate(world, prompt_len, prefill_ms), 1),
+                        "path": ("batched: 32-token chunks, tensor-core GEMMs, chunked GDN scan" if prefill_batched
+                                 else "one token per step (int4 weights)"),
+                        "weight_gbs": (round(model_weight_bytes * -(-prompt_len // 32) / (prefill_ms * 1e-3) / 1e9, 1)
+                                       if prefill_batched else None)},
         }
         print(json.dumps(line), flush=True)
     if world > 1:

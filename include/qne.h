@@ -141,9 +141,16 @@ QNE_API qne_status qne_reset(qne_model* m);
  * afterwards logits hold the prediction after the last id and the greedy pick is stored. */
 QNE_API qne_status qne_prefill(qne_model* m, const uint32_t* ids, uint32_t n);
 /* Model::prefill_chunk, kernels/src/model.rs:349 (prefill_from / prefill_batched are
- * prefill_chunk with finish_logits = 1). Fails when start + n >= QNE_MAX_CONTEXT. */
+ * prefill_chunk with finish_logits = 1). Fails when start + n >= QNE_MAX_CONTEXT. With f16
+ * decoder matrices the ids run in 32-token chunks (tensor-core GEMMs, chunked GDN scan, causal
+ * attention over the appended keys), like the reference's batched prefill list
+ * (kernels/src/model.rs:222-259); otherwise one token per step, like qne_prefill. Afterwards the
+ * control words hold (ids[n-1], start + n - 1), or with finish_logits the logits after the last
+ * id and (greedy pick, start + n). */
 QNE_API qne_status qne_prefill_chunk(qne_model* m, const uint32_t* ids, uint32_t n, uint32_t start,
                              int finish_logits);
+/* 1 if qne_prefill_chunk runs batched chunks on this model, 0 if one token per step. */
+QNE_API int qne_prefill_chunk_batched(const qne_model* m);
 /* Model::logits, kernels/src/model.rs:374: copies vocab f32 logits to host `out`. */
 QNE_API qne_status qne_logits(qne_model* m, float* out, size_t out_len);
 /* Model::step, kernels/src/model.rs:380: feeds `token` at `pos`, returns the next-token logits

@@ -134,8 +134,9 @@ struct AttnItem {
   const uint32_t* pt;
 
   // Stages K and V of tokens sb + 8w .. sb + 8w + 7 (this warp's share of a sub-block): one
-  // 16-byte cp.async per row and lane; tokens outside [l0, l1), the current token (taken from
-  // kc_s / vc_s instead) and rows of an out-of-range page are zero-filled, then one group commits.
+  // 16-byte cp.async per row and lane; tokens outside [l0, l1), the current token when this item
+  // appends it (taken from kc_s / vc_s instead) and rows of an out-of-range page are zero-filled,
+  // then one group commits.
   __device__ __forceinline__ void stage(const KernelArgs& ka, AttnShared& sh, int sb) const {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll 1
@@ -143,7 +144,7 @@ struct AttnItem {
       const int t = warp * 8 + i, l = sb + t;
       uint4* kd = reinterpret_cast<uint4*>(&sh.kst[t][lane * 8]);
       uint4* vd = reinterpret_cast<uint4*>(&sh.vst[t][lane * 8]);
-      const uint32_t page = (l < l1 && l != (int)pos) ? pt[l / kPageTokens] : 0xFFFFFFFFu;
+      const uint32_t page = (l < l1 && !(owner && l == (int)pos)) ? pt[l / kPageTokens] : 0xFFFFFFFFu;
       if (page < ka.pool_pages) {
         cp_async16_attn(kd, kv_row(ka.a.kv, page, 0, kvh, l % kPageTokens) + lane * 8);
         cp_async16_attn(vd, kv_row(ka.a.kv, page, 1, kvh, l % kPageTokens) + lane * 8);
@@ -174,8 +175,8 @@ struct AttnItem {
     if (!valid) return;
     l0 = split * ka.split;
     l1 = min(l0 + ka.split, len);
-    owner = (int)pos >= l0 && (int)pos < l1;
-    pt = a.page_table + (size_t)b * kPagesPerSeq;
+    owner = !a.kv_appended && (int)pos >= l0 && (int)pos < l1;
+    pt = a.page_table + (size_t)b * a.page_table_stride;
     stage(ka, sh, l0);
   }
 
@@ -279,7 +280,7 @@ struct AttnItem {
       for (int i = 0; i < 8; ++i) {
         const int tk = warp * 8 + i, l = sb + tk;
         float kf[8];
-        if (l == (int)pos) {
+        if (owner && l == (int)pos) {
           *reinterpret_cast<float4*>(kf) = *reinterpret_cast<const float4*>(&sh.kc_s[lane * 8]);
           *reinterpret_cast<float4*>(kf + 4) = *reinterpret_cast<const float4*>(&sh.kc_s[lane * 8 + 4]);
         } else {
@@ -335,7 +336,7 @@ struct AttnItem {
         const int tk = warp * 8 + i, l = sb + tk;
         if (l < l1) {
           float vf[8];
-          if (l == (int)pos) {
+          if (owner && l == (int)pos) {
             *reinterpret_cast<float4*>(vf) = *reinterpret_cast<const float4*>(&sh.vc_s[lane * 8]);
             *reinterpret_cast<float4*>(vf + 4) = *reinterpret_cast<const float4*>(&sh.vc_s[lane * 8 + 4]);
           } else {
@@ -359,7 +360,7 @@ struct AttnItem {
       *reinterpret_cast<float4*>(sh.accw(warp) + hh * kHeadDim + lane * 8 + 4) = *reinterpret_cast<float4*>(&acc[hh][4]);
     }
     __syncthreads();
-    Scratch S = carve(a.scratch, a.batch);
+    Scratch S = carve(a.scratch, a.scratch_rows > 0 ? a.scratch_rows : a.batch);
     const size_t sk = (size_t)b * kKvHeads + kvh;  // (sequence, KV head)
     const int hh = t >> 6, d0 = (t & 63) * 4;       // merge mapping
     const int group = split / kGroup, ngroups = (nsplit + kGroup - 1) / kGroup;

@@ -178,7 +178,7 @@ qne_status qne_prefill(qne_model* m, const uint32_t* ids, uint32_t n) {
     // Model::prefill, kernels/src/model.rs:324-335: prompt length 1..4095 from position 0.
     if (n == 0 || n >= (uint32_t)kMaxContext)
       throw QneError(kERangeCtx, "prompt length must be 1.." + std::to_string(kMaxContext));
-    M->prefill_chunk(ids, n, 0, true);
+    M->prefill_chunk(ids, n, 0, true, false);
   });
 }
 
@@ -186,6 +186,11 @@ qne_status qne_prefill_chunk(qne_model* m, const uint32_t* ids, uint32_t n, uint
                              int finish_logits) {
   MODEL(m);
   return guarded([&] { M->prefill_chunk(ids, n, start, finish_logits != 0); });
+}
+
+int qne_prefill_chunk_batched(const qne_model* m) {
+  if (!m) return 0;
+  return reinterpret_cast<const Model*>(m)->prefill_batched_supported() ? 1 : 0;
 }
 
 qne_status qne_logits(qne_model* m, float* out, size_t out_len) {

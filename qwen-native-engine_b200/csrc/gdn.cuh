@@ -18,6 +18,8 @@ cudaError_t launch_gdn_gate(const float* raw, const float* proj, const float* no
                             int batch, cudaStream_t stream, bool pdl);
 
 // Attention over paged f16 KV. pos[b * pos_stride] is the position of the token being decoded.
+// Rows are independent sequences (batched decode) or, with page_table_stride 0 and kv_appended,
+// consecutive tokens of one sequence whose keys and values were appended beforehand (prefill).
 // rope: [4096][32] cos followed by [4096][32] sin (f32).
 struct AttnArgs {
   const float* proj = nullptr;  // [batch][5120]
@@ -32,6 +34,9 @@ struct AttnArgs {
   float* out = nullptr;         // [batch][2048]
   int batch = 1;
   void* scratch = nullptr;
+  int page_table_stride = kPagesPerSeq;  // 0: every row reads one sequence's page table (prefill)
+  int kv_appended = 0;  // 1: every row's own K/V is already in the cache (prefill); no CTA appends
+  int scratch_rows = 0;  // rows `scratch` is laid out for (0: batch); fixed when batch varies
 };
 size_t attention_scratch_bytes(int batch);
 // split_tokens: context tokens per CTA, a multiple of 64. pool_pages bounds the page ids.

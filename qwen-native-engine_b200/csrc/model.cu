@@ -12,6 +12,7 @@
 #include "gdn.cuh"
 #include "json.hpp"
 #include "model.hpp"
+#include "prefill.hpp"
 #include "persist.cuh"
 
 namespace qne {
@@ -78,6 +79,7 @@ void* Model::alloc(size_t bytes, bool track) {
 }
 
 void Model::free_all() {
+  prefill_.reset();
   single_.reset();
   for (void* p : allocations_) cudaFree(p);
   allocations_.clear();
@@ -654,13 +656,22 @@ void Model::reset() {
   host_pos_ = 0;
 }
 
-void Model::prefill_chunk(const uint32_t* ids, uint32_t n, uint32_t start, bool finish) {
+bool Model::prefill_batched_supported() const { return PrefillRunner::supported(*this); }
+
+void Model::prefill_chunk(const uint32_t* ids, uint32_t n, uint32_t start, bool finish, bool batched) {
   DeviceGuard g(device);
   if (!ids && n) throw QneError(kEInval, "null ids");
   if (n == 0 || (uint64_t)start + n >= (uint64_t)kMaxContext)
     throw QneError(kERangeCtx, "context limit: " + std::to_string(start) + " + " + std::to_string(n) +
                                    " tokens does not fit in " + std::to_string(kMaxContext));
-  cuda_check(cudaStreamSynchronize(stream()), "prefill");  // host_ctl_ may still feed a copy
+  cuda_check(cudaStreamSynchronize(stream()), "prefill");  // host staging may still feed a copy
+  if (batched && prefill_batched_supported()) {
+    if (!prefill_) prefill_.reset(new PrefillRunner(this, single_.get()));
+    prefill_->run(ids, n, start, finish, stream());
+    host_pos_ = finish ? start + n : start + n - 1;
+    sync(600000);
+    return;
+  }
   for (uint32_t i = 0; i < n; ++i) {
     host_ctl_[2 * i] = ids[i];
     host_ctl_[2 * i + 1] = start + i;

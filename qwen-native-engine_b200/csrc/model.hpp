@@ -59,6 +59,8 @@ class Model;
 
 // Activations and launch graphs of one sequence set.
 class Runner;
+// Chunked prompt processing on the B = 1 sequence (prefill.cu).
+class PrefillRunner;
 
 class Model {
  public:
@@ -80,7 +82,10 @@ class Model {
 
   // B = 1 API (kernels/src/model.rs)
   void reset();
-  void prefill_chunk(const uint32_t* ids, uint32_t n, uint32_t start, bool finish_logits);
+  // batched: 32-token chunks through tensor-core GEMMs when the weights allow it (f16
+  // matrices), else one token per step like `prefill` (kernels/src/model.rs:324-335).
+  void prefill_chunk(const uint32_t* ids, uint32_t n, uint32_t start, bool finish_logits, bool batched = true);
+  bool prefill_batched_supported() const;
   void logits(float* out, size_t n);
   void step(uint32_t token, uint32_t pos, float* out, size_t n);
   void step_async(uint32_t token, uint32_t pos);
@@ -112,6 +117,7 @@ class Model {
   cudaStream_t own_stream_ = nullptr;
   cudaStream_t ext_stream_ = nullptr;
   std::unique_ptr<Runner> single_;
+  std::unique_ptr<PrefillRunner> prefill_;  // created by the first batched prefill
   uint32_t* host_ctl_ = nullptr;  // pinned staging: (token, pos) pairs
   uint32_t host_pos_ = 0;         // host mirror of the next position
   uint32_t saved_pos_ = 0;

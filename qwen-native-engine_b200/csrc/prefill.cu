@@ -1,0 +1,431 @@
+// Batched prompt processing: the n <= 32 tokens of a chunk go through every layer together
+// (Model::prefill_chunk, kernels/src/model.rs:349-372; its per-chunk dispatch list is built at
+// kernels/src/model.rs:222-259 from the kernels of kernels/src/batch.rs). Per layer:
+//   prep (embedding + RMSNorm at layer 0, RMSNorm after) | GEMM mixer_in (n rows) |
+//   GDN layers: gdn_scan (the recurrence walked token by token, state in registers) |
+//     prep (gated RMSNorm)
+//   attention layers: kv_append (RMSNorm + RoPE of the n keys; K and V rounded to f16 into the
+//     sequence's pages) | attention (one row per token, causal over the cache) | prep (copy)
+//   | GEMM mixer_out (+= h) | prep (RMSNorm) | GEMM gate_up (SwiGLU) | GEMM down (+= h);
+// then chunk_finish advances the sequence's control words by n and leaves the last row's hidden
+// state where the B = 1 LM head reads it. The weights stream once per chunk instead of once per
+// token, so a chunk costs about what one batched decode step of 32 sequences costs.
+//
+// Numerics follow the per-token kernels: the GDN scan and the key normalization repeat the
+// decode kernels' arithmetic per token; the GEMMs accumulate in f32 from f16 weights and hi/lo
+// f16 activations (the batched decode GEMM).
+#include <string>
+
+#include "../../include/qne.h"
+#include "attn_dev.cuh"
+#include "batch.cuh"
+#include "gdn.cuh"
+#include "model.hpp"
+#include "prefill.hpp"
+
+namespace qne {
+namespace {
+
+using namespace dev;
+
+// ------------------------------------------------------------------------------------------
+// Gated DeltaNet over the chunk (batch::gdn, kernels/src/batch.rs:168-255; per-token math
+// kernels/src/shaders.rs:445-520). One CTA per (16-column slice, head), clustered by head: the
+// CTA keeps its 128 x 16 slice of the state in registers (8 values per thread) for the whole
+// chunk and walks the tokens in order. Per token, threads 0..127 run the causal conv + SiLU of
+// the head's q channels and threads 128..255 of its k channels (windows in registers, seeded from
+// the conv ring); each 16-lane half-warp owns one value column (8 state rows per lane), so the
+// dot products S^T k, S^T q and k . q reduce with shuffles. The conv/SiLU outputs go to a shared
+// buffer indexed by token parity, so one __syncthreads per token suffices.
+//
+// The conv ring holds input j at slot j % 4. All 8 CTAs of a head read the head's q/k ring
+// channels before the chunk; they write the last three inputs back only after a cluster barrier
+// that every CTA of the head passes once its reads are done, so no CTA sees a slot overwritten.
+// ------------------------------------------------------------------------------------------
+struct ScanArgs {
+  const float* proj;    // [n][8224] mixer_in rows of the chunk
+  float* conv;          // [4][6144] conv input ring of the sequence
+  const float* conv_w;  // [6144][4]
+  float* state;         // [16][128][128] recurrent state
+  const float* params;  // dt_bias[16], A[16], norm weight[128]
+  const SeqCtl* ctl;    // ctl->count: tokens processed before the chunk
+  int n;
+  float* out;           // [n][2048] raw output (before the gated RMSNorm)
+};
+
+struct ScanShared {
+  float qk[2][2 * kGdnDim];  // per token parity: q channels 0..127, k channels 128..255
+  float red[2][8];           // per token parity: per-warp sums of squares
+};
+
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+
+__global__ void __cluster_dims__(kSlices, 1, 1) __launch_bounds__(256) gdn_scan_kernel(const __grid_constant__ ScanArgs a) {
+  __shared__ ScanShared sh;
+  const int h = blockIdx.y, t0 = blockIdx.x * kSlice;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int col = warp * 2 + (lane >> 4);  // value column t0 + col
+  const int jg = lane & 15;                // state rows jg * 8 .. jg * 8 + 7
+  const int iq = tid & (kGdnDim - 1);
+  const int chqk = (tid < kGdnDim ? 0 : 2048) + h * kGdnDim + iq;
+  const int chv = 4096 + h * kGdnDim + t0 + col;
+  pdl_launch();
+  pdl_wait();
+  const uint32_t cnt0 = a.ctl->count;
+  const float4 w = *reinterpret_cast<const float4*>(a.conv_w + (size_t)chqk * 4);
+  const float4 wv = *reinterpret_cast<const float4*>(a.conv_w + (size_t)chv * 4);
+  const float* ring = a.conv;
+  const int r0 = (int)((cnt0 - 3u) & 3u), r1 = (int)((cnt0 - 2u) & 3u), r2 = (int)((cnt0 - 1u) & 3u);
+  float x0 = ring[r0 * kConvChannels + chqk], x1 = ring[r1 * kConvChannels + chqk], x2 = ring[r2 * kConvChannels + chqk];
+  float v0 = ring[r0 * kConvChannels + chv], v1 = ring[r1 * kConvChannels + chv], v2 = ring[r2 * kConvChannels + chv];
+  float* S = a.state + (size_t)h * kGdnDim * kGdnDim + (size_t)(jg * 8) * kGdnDim + t0 + col;
+  float sv[8];
+#pragma unroll
+  for (int jj = 0; jj < 8; ++jj) sv[jj] = S[(size_t)jj * kGdnDim];
+  cluster_arrive();  // this CTA is done reading the ring
+  const float A = a.params[16 + h], dt_bias = a.params[h];
+  const float* pr = a.proj;
+  float xn = pr[chqk], xvn = pr[chv], an = pr[8192 + h], bn = pr[8208 + h];
+#pragma unroll 1
+  for (int i = 0; i < a.n; ++i) {
+    const float x = xn, xv = xvn, ar = an, br = bn;
+    if (i + 1 < a.n) {
+      pr += kGdnProj;
+      xn = pr[chqk];
+      xvn = pr[chv];
+      an = pr[8192 + h];
+      bn = pr[8208 + h];
+    }
+    const float y = x0 * w.x + x1 * w.y + x2 * w.z + x * w.w;
+    x0 = x1;
+    x1 = x2;
+    x2 = x;
+    const float val = silu(y);
+    const float ss = warp_sum(val * val);
+    const int buf = i & 1;
+    sh.qk[buf][tid] = val;
+    if (lane == 0) sh.red[buf][warp] = ss;
+    const float yv = v0 * wv.x + v1 * wv.y + v2 * wv.z + xv * wv.w;
+    v0 = v1;
+    v1 = v2;
+    v2 = xv;
+    const float vv = silu(yv);
+    const float g = expf(A * logf(1.0f + expf(ar + dt_bias)));
+    const float beta = 1.0f / (1.0f + expf(-br));
+    __syncthreads();
+    const float nq = rsqrtf(sh.red[buf][0] + sh.red[buf][1] + sh.red[buf][2] + sh.red[buf][3] + 1e-6f);
+    const float nk = rsqrtf(sh.red[buf][4] + sh.red[buf][5] + sh.red[buf][6] + sh.red[buf][7] + 1e-6f);
+    float kk[8], sk = 0.f, sq = 0.f, kq = 0.f;
+#pragma unroll
+    for (int jj = 0; jj < 8; ++jj) {
+      const float qv = sh.qk[buf][jg * 8 + jj] * nq * 0.08838834764f;
+      kk[jj] = sh.qk[buf][kGdnDim + jg * 8 + jj] * nk;
+      sk = fmaf(sv[jj], kk[jj], sk);
+      sq = fmaf(sv[jj], qv, sq);
+      kq = fmaf(kk[jj], qv, kq);
+    }
+#pragma unroll
+    for (int o = 1; o < 16; o <<= 1) {
+      sk += __shfl_xor_sync(0xffffffffu, sk, o);
+      sq += __shfl_xor_sync(0xffffffffu, sq, o);
+      kq += __shfl_xor_sync(0xffffffffu, kq, o);
+    }
+    const float dv = beta * (vv - g * sk);
+#pragma unroll
+    for (int jj = 0; jj < 8; ++jj) sv[jj] = g * sv[jj] + dv * kk[jj];
+    if (jg == 0) a.out[(size_t)i * kMixerOut + h * kGdnDim + t0 + col] = g * sq + dv * kq;
+  }
+#pragma unroll
+  for (int jj = 0; jj < 8; ++jj) S[(size_t)jj * kGdnDim] = sv[jj];
+  cluster_wait();  // every CTA of this head is done reading the ring
+  float* wr = a.conv;
+  const uint32_t e = cnt0 + (uint32_t)a.n;  // tokens processed after the chunk
+  const int w0 = (int)((e - 3u) & 3u), w1 = (int)((e - 2u) & 3u), w2 = (int)((e - 1u) & 3u);
+  if (iq >= t0 && iq < t0 + kSlice) {  // this slice's share of the head's q and k channels
+    wr[w0 * kConvChannels + chqk] = x0;
+    wr[w1 * kConvChannels + chqk] = x1;
+    wr[w2 * kConvChannels + chqk] = x2;
+  }
+  if (jg == 0) {
+    wr[w0 * kConvChannels + chv] = v0;
+    wr[w1 * kConvChannels + chv] = v1;
+    wr[w2 * kConvChannels + chv] = v2;
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// Keys and values of the chunk into the cache (batch::kv_prep, kernels/src/batch.rs:290-314):
+// one CTA per (token, KV head); RMSNorm with k_norm, rotate-half RoPE on dims 0..63 at the
+// token's position, both rounded to f16 into the sequence's page. The arithmetic is the
+// attention decode kernel's append, so a chunk writes the same cache rows as per-token steps.
+// ------------------------------------------------------------------------------------------
+struct AppendArgs {
+  const float* proj;          // [n][5120]
+  const float* norms;         // q_norm[256], k_norm[256]
+  const float* rope;          // [2][4096][32]
+  uint16_t* kv;               // page pool
+  const uint32_t* page_table; // [256] pages of the sequence
+  uint32_t pool_pages;
+  const SeqCtl* rows;         // rows[i].pos: position of chunk token i
+};
+
+__global__ void __launch_bounds__(256) kv_append_kernel(const __grid_constant__ AppendArgs a) {
+  __shared__ float red[8];
+  __shared__ float ks[kHeadDim];
+  const int i = blockIdx.x, kvh = blockIdx.y, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  pdl_launch();
+  pdl_wait();
+  uint32_t pos = a.rows[i].pos;
+  if (pos >= (uint32_t)kMaxContext) pos = kMaxContext - 1;  // the host rejects such chunks
+  const float* pr = a.proj + (size_t)i * kAttnProj;
+  const float xk = pr[4096 + kvh * kHeadDim + t];
+  const float ssk = warp_sum(xk * xk);
+  if (lane == 0) red[warp] = ssk;
+  __syncthreads();
+  float sum = 0.f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) sum += red[w];
+  const float kn = xk * rsqrtf(sum / (float)kHeadDim + 1e-6f) * a.norms[kHeadDim + t];
+  ks[t] = kn;
+  __syncthreads();
+  float kr = kn;
+  if (t < 2 * kRopeHalf) {
+    const int j = t & (kRopeHalf - 1);
+    const float c = a.rope[(size_t)pos * kRopeHalf + j];
+    const float sn = a.rope[(size_t)kMaxContext * kRopeHalf + (size_t)pos * kRopeHalf + j];
+    kr = (t < kRopeHalf) ? ks[t] * c - ks[t + kRopeHalf] * sn : ks[t] * c + ks[t - kRopeHalf] * sn;
+  }
+  const uint32_t page = a.page_table[pos / kPageTokens];
+  if (page < a.pool_pages) {
+    uint16_t* kdst = const_cast<uint16_t*>(kv_row(a.kv, page, 0, kvh, pos % kPageTokens));
+    uint16_t* vdst = const_cast<uint16_t*>(kv_row(a.kv, page, 1, kvh, pos % kPageTokens));
+    kdst[t] = __half_as_ushort(__float2half_rn(kr));
+    vdst[t] = __half_as_ushort(__float2half_rn(pr[4608 + kvh * kHeadDim + t]));
+  }
+}
+
+// Advances the sequence past the chunk and hands the last row's hidden state to the B = 1 LM
+// head: control words (last token, its position, count + n), h_out = h_rows[n - 1].
+__global__ void __launch_bounds__(256) chunk_finish_kernel(SeqCtl* ctl, const SeqCtl* rows, int n,
+                                                           const float* h_rows, int hidden, float* h_out) {
+  pdl_launch();
+  pdl_wait();
+  const float* src = h_rows + (size_t)(n - 1) * hidden;
+  for (int i = threadIdx.x; i < hidden; i += blockDim.x) h_out[i] = src[i];
+  if (threadIdx.x == 0) {
+    ctl->token = rows[n - 1].token;
+    ctl->pos = rows[n - 1].pos;
+    ctl->count += (uint32_t)n;
+  }
+}
+
+cudaLaunchConfig_t make_cfg(dim3 grid, dim3 block, cudaStream_t stream, bool pdl, cudaLaunchAttribute* attr) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.stream = stream;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cfg;
+}
+
+}  // namespace
+
+bool PrefillRunner::supported(const Model& m) {
+  for (const LayerWeights& L : m.layers)
+    for (const Mat* w : {&L.in, &L.out, &L.gate_up, &L.down})
+      if (w->kind != kF16 || w->k % 32) return false;
+  return !m.layers.empty();
+}
+
+PrefillRunner::PrefillRunner(Model* model, Runner* single) : m(model), r(single) {
+  const Config& c = m->cfg;
+  ldx0 = c.hidden > kMixerOut ? c.hidden : kMixerOut;
+  h = static_cast<float*>(m->alloc((size_t)kRows * c.hidden * 4));
+  proj = static_cast<float*>(m->alloc((size_t)kRows * kGdnProj * 4));
+  raw = static_cast<float*>(m->alloc((size_t)kRows * kMixerOut * 4));
+  x0h = static_cast<uint16_t*>(m->alloc((size_t)kRows * ldx0 * 2));
+  x0l = static_cast<uint16_t*>(m->alloc((size_t)kRows * ldx0 * 2));
+  x1h = static_cast<uint16_t*>(m->alloc((size_t)kRows * c.inter * 2));
+  x1l = static_cast<uint16_t*>(m->alloc((size_t)kRows * c.inter * 2));
+  for (auto* p : {x0h, x0l}) cuda_check(cudaMemset(p, 0, (size_t)kRows * ldx0 * 2), "memset");
+  for (auto* p : {x1h, x1l}) cuda_check(cudaMemset(p, 0, (size_t)kRows * c.inter * 2), "memset");
+  rows = static_cast<SeqCtl*>(m->alloc((size_t)kRows * sizeof(SeqCtl)));
+  cuda_check(cudaMemset(rows, 0, (size_t)kRows * sizeof(SeqCtl)), "memset");
+  attn_scratch = m->alloc(attention_scratch_bytes(kRows));
+  cuda_check(cudaMemset(attn_scratch, 0, attention_scratch_bytes(kRows)), "memset");
+  cuda_check(cudaMallocHost(&pinned, (size_t)kMaxContext * sizeof(SeqCtl)), "cudaMallocHost");
+}
+
+PrefillRunner::~PrefillRunner() {
+  for (auto& g : graphs)
+    if (g.second) cudaGraphExecDestroy(g.second);
+  if (pinned) cudaFreeHost(pinned);
+}
+
+void PrefillRunner::record(int n, cudaStream_t s) {
+  const Model& M = *m;
+  const Config& c = M.cfg;
+  size_t cnt = 0;
+  auto prep = [&](PrepArgs p) {
+    p.xh = x0h;
+    p.xl = x0l;
+    p.ldx = ldx0;
+    cuda_check(launch_prep(p, n, s, true), "prefill prep");
+    ++cnt;
+  };
+  auto gemm = [&](const Mat& w, const uint16_t* xh, const uint16_t* xl, int ldx, int epi, float* y, uint16_t* yh,
+                  uint16_t* yl, int ldy) {
+    GemmArgs g;
+    g.w = w.w;
+    g.rows = w.rows;
+    g.k = w.k;
+    g.batch = n;
+    g.epi = epi;
+    g.row_groups = gemm_row_groups(epi == kSwiGlu ? w.rows / 2 : w.rows);
+    g.xh = xh;
+    g.xl = xl;
+    g.ldx = ldx;
+    g.y = y;
+    g.yh = yh;
+    g.yl = yl;
+    g.ldy = ldy;
+    if (const char* why = check_gemm(g)) throw QneError(kEInval, why);
+    cuda_check(launch_gemm(g, s, true), "prefill gemm");
+    ++cnt;
+  };
+  cudaLaunchAttribute attr[1];
+  for (int i = 0; i < c.layers; ++i) {
+    const LayerWeights& L = M.layers[i];
+    PrepArgs p;
+    p.k = c.hidden;
+    p.norm_w = L.input_norm;
+    if (i == 0) {
+      p.mode = kPrepEmbedNorm;  // reads rows[b].token; its count increment stays in `rows`
+      p.embed = M.embed;
+      p.ctl = rows;
+      p.h = h;
+      p.ldh = c.hidden;
+    } else {
+      p.mode = kPrepNorm;
+      p.src = h;
+      p.lds = c.hidden;
+    }
+    prep(p);
+    gemm(L.in, x0h, x0l, ldx0, kStore, proj, nullptr, nullptr, L.in.rows);
+    PrepArgs q;
+    q.k = kMixerOut;
+    q.src = raw;
+    q.lds = kMixerOut;
+    if (L.attention) {
+      const AppendArgs ap{proj, L.attn_norms, M.rope, r->st.kv[i], r->st.page_table, r->st.pool_pages, rows};
+      cudaLaunchConfig_t cfg = make_cfg(dim3(n, kKvHeads), dim3(256), s, true, attr);
+      count_launch();
+      cuda_check(cudaLaunchKernelEx(&cfg, kv_append_kernel, ap), "kv append launch");
+      ++cnt;
+      AttnArgs at;
+      at.proj = proj;
+      at.norms = L.attn_norms;
+      at.rope = M.rope;
+      at.kv = r->st.kv[i];
+      at.page_table = r->st.page_table;
+      at.page_table_stride = 0;
+      at.kv_appended = 1;
+      at.pos = &rows->pos;
+      at.pos_stride = 4;
+      at.flags = &r->st.ctl->flags;
+      at.flags_stride = 0;
+      at.out = raw;
+      at.batch = n;
+      at.scratch = attn_scratch;
+      at.scratch_rows = kRows;  // one layout for every chunk size, so tickets stay where they were reset
+      cuda_check(launch_attention(at, r->st.pool_pages, n >= 8 ? 256 : 64, s, true), "prefill attention launch");
+      ++cnt;
+      q.mode = kPrepCopy;
+    } else {
+      const ScanArgs sa{proj, r->st.conv[i], L.conv_w, r->st.rec[i], L.gdn_params, r->st.ctl, n, raw};
+      cudaLaunchConfig_t cfg = make_cfg(dim3(kSlices, kGdnHeads), dim3(256), s, true, attr);
+      count_launch();
+      cuda_check(cudaLaunchKernelEx(&cfg, gdn_scan_kernel, sa), "gdn scan launch");
+      ++cnt;
+      q.mode = kPrepGdnGate;
+      q.zgate = proj;
+      q.norm_w = L.gdn_params + 32;
+    }
+    prep(q);
+    gemm(L.out, x0h, x0l, ldx0, kAccumulate, h, nullptr, nullptr, c.hidden);
+    PrepArgs pn;
+    pn.mode = kPrepNorm;
+    pn.k = c.hidden;
+    pn.src = h;
+    pn.lds = c.hidden;
+    pn.norm_w = L.post_norm;
+    prep(pn);
+    gemm(L.gate_up, x0h, x0l, ldx0, kSwiGlu, nullptr, x1h, x1l, c.inter);
+    gemm(L.down, x1h, x1l, c.inter, kAccumulate, h, nullptr, nullptr, c.hidden);
+  }
+  cudaLaunchConfig_t cfg = make_cfg(dim3(1), dim3(256), s, true, attr);
+  count_launch();
+  cuda_check(cudaLaunchKernelEx(&cfg, chunk_finish_kernel, r->st.ctl, (const SeqCtl*)rows, n, (const float*)h,
+                                c.hidden, r->h),
+             "chunk finish launch");
+  ++cnt;
+  launches[n] = cnt;
+}
+
+cudaGraphExec_t PrefillRunner::graph_for(int n) {
+  auto it = graphs.find(n);
+  if (it != graphs.end()) return it->second;
+  cudaStream_t cs;
+  cuda_check(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking), "cudaStreamCreate");
+  cuda_check(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal), "begin capture");
+  try {
+    record(n, cs);
+  } catch (...) {
+    cudaGraph_t g = nullptr;
+    cudaStreamEndCapture(cs, &g);
+    if (g) cudaGraphDestroy(g);
+    cudaStreamDestroy(cs);
+    throw;
+  }
+  cudaGraph_t g = nullptr;
+  const cudaError_t ec = cudaStreamEndCapture(cs, &g);
+  cudaStreamDestroy(cs);
+  cuda_check(ec, "end capture");
+  cudaGraphExec_t exec = nullptr;
+  const cudaError_t e = cudaGraphInstantiate(&exec, g, 0);
+  cudaGraphDestroy(g);
+  cuda_check(e, "graph instantiate");
+  graphs[n] = exec;
+  return exec;
+}
+
+size_t PrefillRunner::launches_per_chunk(int n) const {
+  auto it = launches.find(n);
+  return it == launches.end() ? 0 : it->second;
+}
+
+void PrefillRunner::run(const uint32_t* ids, uint32_t n, uint32_t start, bool finish, cudaStream_t s) {
+  for (uint32_t i = 0; i < n; ++i) pinned[i] = SeqCtl{ids[i], start + i, 0u, 0u};
+  for (uint32_t c0 = 0; c0 < n; c0 += kRows) {
+    const int cn = (int)std::min<uint32_t>(kRows, n - c0);
+    cudaGraphExec_t g = graph_for(cn);
+    cuda_check(cudaMemcpyAsync(rows, pinned + c0, (size_t)cn * sizeof(SeqCtl), cudaMemcpyHostToDevice, s),
+               "prefill rows");
+    cuda_check(cudaGraphLaunch(g, s), "prefill graph");
+    for (size_t i = 0; i < launches[cn]; ++i) count_launch();
+  }
+  if (finish) {
+    // The LM head of the B = 1 path on the last row: logits, then (greedy pick, start + n).
+    const GemvArgs hd = r->head_args(Runner::kGreedy);
+    if (const char* why = check_gemv(hd)) throw QneError(kEInval, why);
+    cuda_check(launch_gemv(hd, s, false), "prefill head");
+  }
+}
+
+}  // namespace qne

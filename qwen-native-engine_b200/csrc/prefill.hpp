@@ -1,0 +1,50 @@
+// Batched prompt processing for the B = 1 sequence: chunks of up to 32 consecutive tokens per
+// pass through tensor-core GEMMs (Model::prefill_chunk, kernels/src/model.rs:349-372).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <map>
+
+#include "model.hpp"
+
+namespace qne {
+
+class PrefillRunner {
+ public:
+  static constexpr int kRows = 32;  // tokens per chunk (the batched GEMM's batch limit)
+
+  // Whether `m` can run chunks: the decoder matrices must be f16 (the batched GEMM's operand).
+  static bool supported(const Model& m);
+
+  PrefillRunner(Model* m, Runner* single);
+  ~PrefillRunner();
+
+  // Enqueues ids[0..n) at positions start.. on stream s, `kRows` tokens per chunk, on the state
+  // of `single`. Afterwards the control words hold (ids[n-1], start + n - 1) and the token
+  // counter has advanced by n; with `finish` the LM head then runs on the last token, leaving
+  // its logits and (greedy pick, start + n) as the per-token path does. The caller synchronizes
+  // before reusing `ids`' staging (one pinned row array per runner).
+  void run(const uint32_t* ids, uint32_t n, uint32_t start, bool finish, cudaStream_t s);
+
+  size_t launches_per_chunk(int n) const;
+
+ private:
+  void record(int n, cudaStream_t s);
+  cudaGraphExec_t graph_for(int n);
+
+  Model* m;
+  Runner* r;
+  int ldx0 = 0;
+  float* h = nullptr;     // [kRows][hidden] residual stream of the chunk
+  float* proj = nullptr;  // [kRows][8224] mixer_in output
+  float* raw = nullptr;   // [kRows][2048] mixer output before mixer_out
+  uint16_t *x0h = nullptr, *x0l = nullptr, *x1h = nullptr, *x1l = nullptr;  // GEMM operand planes
+  SeqCtl* rows = nullptr;    // [kRows] device: (token, position) of each chunk row
+  SeqCtl* pinned = nullptr;  // [kMaxContext] host staging of the rows of one call
+  void* attn_scratch = nullptr;
+  std::map<int, cudaGraphExec_t> graphs;
+  std::map<int, size_t> launches;
+};
+
+}  // namespace qne

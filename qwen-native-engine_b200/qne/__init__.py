@@ -77,6 +77,7 @@ def _load_lib() -> C.CDLL:
         "qne_model_phase_trace": (I32, [P, P, SZ, C.POINTER(SZ), C.POINTER(SZ)]),
         "qne_adapter": (C.c_char_p, [P]),
         "qne_dispatches_per_token": (SZ, [P]),
+        "qne_prefill_chunk_batched": (I32, [P]),
         "qne_validate_tiles": (I32, [C.c_char_p, SZ]),
         "qne_reset": (I32, [P]),
         "qne_prefill": (I32, [P, U32P, U32]),
@@ -231,6 +232,11 @@ class Model:
 
     def prefill_from(self, ids, start: int) -> None:
         self.prefill_chunk(ids, start, True)
+
+    @property
+    def prefill_batched_supported(self) -> bool:
+        """Whether prefill_chunk runs 32-token batched chunks (f16 weights) on this model."""
+        return bool(lib.qne_prefill_chunk_batched(self._h))
 
     def prefill_chunk(self, ids, start: int, finish_logits: bool) -> None:
         a = _u32_array(ids)
