@@ -370,9 +370,11 @@ def batched_run(torch, qne, synth, rank: int, world: int, barrier, max_over_rank
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda._sleep(20_000_000)
+    torch.cuda.nvtx.range_push("batched_steps")  # the launch-list captures select this range
     e0.record(stream)
     bt.decode_async(steps)
     e1.record(stream)
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     ms = max_over_ranks(e0.elapsed_time(e1))
     launches = qne.kernel_launches() - launches0

@@ -239,6 +239,14 @@ QNE_API qne_status qne_rmsnorm_gemv(const qne_matrix* m, const float* h, const f
 QNE_API size_t qne_gemm_scratch_bytes(const qne_matrix* m, int batch);
 QNE_API qne_status qne_gemm(const qne_matrix* m, const float* x, int batch, float* y, int epilogue,
                     void* scratch, size_t scratch_bytes, void* stream);
+/* qne_gemm with the kernel chosen explicitly (no counterpart in the reference; for comparisons):
+ * QNE_GEMM_TENSOR_CORE = tcgen05 MMAs with TMA-staged tiles and tensor-memory accumulators (the
+ * default of qne_gemm and of the batched decode and prefill paths), QNE_GEMM_MMA_SYNC = warp-level
+ * mma.sync with cp.async staging. Both compute the same sums; only the f32 summation order differs. */
+#define QNE_GEMM_TENSOR_CORE 0
+#define QNE_GEMM_MMA_SYNC 1
+QNE_API qne_status qne_gemm_ex(const qne_matrix* m, const float* x, int batch, float* y, int epilogue,
+                       int impl, void* stream);
 /* qne_gemm without any device allocation (no counterpart in the reference, whose buffers are
  * all created at model load): the same kernels, with x's hi/lo planes and the SwiGLU
  * intermediate in one static 2 MiB device array instead of a workspace grown with cudaMalloc.

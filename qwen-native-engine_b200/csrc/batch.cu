@@ -461,7 +461,13 @@ qne_status qne_gemm(const qne_matrix* m, const float* x, int batch, float* y, in
                     size_t scratch_bytes, void* stream) {
   (void)scratch;
   (void)scratch_bytes;
+  return qne_gemm_ex(m, x, batch, y, epilogue, QNE_GEMM_TENSOR_CORE, stream);
+}
+
+qne_status qne_gemm_ex(const qne_matrix* m, const float* x, int batch, float* y, int epilogue, int impl,
+                       void* stream) {
   return bguard([&] {
+    if (impl != QNE_GEMM_TENSOR_CORE && impl != QNE_GEMM_MMA_SYNC) throw QneError(kEInval, "unknown GEMM kernel");
     if (!m || !x || !y) throw QneError(kEInval, "null argument");
     if (m->kind != QNE_KIND_F16) throw QneError(kEInval, "batched GEMM supports f16 weights");
     if (epilogue < 0 || epilogue > 2) throw QneError(kEInval, "unknown epilogue");
@@ -509,6 +515,7 @@ qne_status qne_gemm(const qne_matrix* m, const float* x, int batch, float* y, in
     g.xl = xl;
     g.ldx = m->k;
     g.ldy = out_rows;
+    g.impl = impl == QNE_GEMM_MMA_SYNC ? kGemmMmaSync : kGemmTensorCore;
     uint16_t* yh = xl + plane / 2;
     uint16_t* yl = yh + (size_t)Bp * out_rows;
     if (epilogue == QNE_EPI_SWIGLU) {

@@ -9,6 +9,8 @@
 
 namespace qne {
 
+enum GemmImpl : int { kGemmTensorCore = 0, kGemmMmaSync = 1 };
+
 // Y[b][row] for b < batch: W [rows][k] f16 times the activation planes xh/xl [>= 8*ceil(batch/8)][ldx].
 struct GemmArgs {
   const void* w = nullptr;
@@ -24,10 +26,16 @@ struct GemmArgs {
   uint16_t* yh = nullptr;
   uint16_t* yl = nullptr;
   int ldy = 0;
+  int x_rows = 0;           // rows allocated in xh/xl (0: 8 * ceil(batch / 8))
+  int impl = kGemmTensorCore;
+  uint32_t* err = nullptr;  // optional: receives kFlagTimeout if a bounded wait gives up
 };
 int gemm_row_groups(int out_rows);
 const char* check_gemm(const GemmArgs& a);
+// impl kGemmTensorCore: tcgen05 + TMA (gemm_tc.cu); kGemmMmaSync: warp-level mma.sync (gemm.cu).
 cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream, bool pdl);
+bool gemm_tc_available();
+cudaError_t launch_gemm_tc(const GemmArgs& a, cudaStream_t stream, bool pdl);
 
 enum PrepMode : int { kPrepCopy = 0, kPrepNorm = 1, kPrepEmbedNorm = 2, kPrepGdnGate = 3 };
 struct PrepArgs {

@@ -452,6 +452,9 @@ const char* check_gemm(const GemmArgs& a) {
 }
 
 cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream, bool pdl) {
+  if (a.impl == kGemmTensorCore && gemm_tc_available() && reinterpret_cast<uintptr_t>(a.w) % 16 == 0 &&
+      reinterpret_cast<uintptr_t>(a.xh) % 16 == 0 && reinterpret_cast<uintptr_t>(a.xl) % 16 == 0)
+    return launch_gemm_tc(a, stream, pdl);
   return a.epi == kSwiGlu ? launch_sw<true>(a, stream, pdl) : launch_sw<false>(a, stream, pdl);
 }
 

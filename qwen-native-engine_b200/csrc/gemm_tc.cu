@@ -1,0 +1,416 @@
+// Batched linear layers on the 5th-generation tensor cores: Y[b] (=, +=, SwiGLU) W X[b] for up
+// to 32 activation rows (batched decode sequences or the tokens of a prompt chunk).
+//
+// Same arithmetic as gemm.cu (the per-token GEMV of kernels/src/shaders.rs:48-250 applied to B
+// rows; the reference's prompt GEMM is batch::gemm, kernels/src/batch.rs:16-99): f16 weights,
+// activations as two f16 planes hi = f16(x), lo = f16(x - hi), both multiplied into one f32
+// accumulator.
+//
+// B200 design (tcgen05 + TMA + TMEM, one CTA of 4 warps per tile):
+//  * a tile is 128 weight rows (SwiGLU: 64 gate rows and the matching 64 up rows) by the whole
+//    activation batch (N = 16 or 32 columns of the MMA, zero-filled past the batch);
+//  * warp 0 lane 0 streams 64-wide k-blocks of the weight tile and of both activation planes
+//    with TMA (128-byte swizzle, the canonical K-major layout of the MMA operands) into a 4-stage
+//    ring guarded by mbarriers; weight loads of the first stages are issued before waiting on the
+//    previous kernel, whose output the activations are;
+//  * warp 1 lane 0 issues tcgen05.mma (M = 128, K = 16, f32 accumulator in tensor memory), two
+//    per k-step (hi and lo planes), and frees each stage with tcgen05.commit;
+//  * split-K runs across the CTAs of a thread-block cluster: every CTA moves its accumulator
+//    from tensor memory to shared memory, and after a cluster barrier each CTA reduces a slice of
+//    the rows over all ranks' shared memory in rank order (deterministic) and applies the
+//    epilogue (store, accumulate, or SwiGLU written as the next GEMM's hi/lo planes).
+// No load uses cluster multicast: every CTA fetches its own tiles.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <math.h>
+
+#include <mutex>
+
+#include "batch.cuh"
+#include "gemv.cuh"
+#include "tma.cuh"
+
+namespace qne {
+namespace {
+
+constexpr int kTcThreads = 128;
+constexpr int kTcStages = 4;
+constexpr int kBK = 64;                 // k per stage: one 128-byte swizzle span of f16
+constexpr int kTileA = 128 * kBK * 2;   // 16 KB of weights per stage
+constexpr int kMaxCluster = 8;
+constexpr int kCtaSlots = 2 * kNumSms;  // two CTAs per SM fit (about 97 KB of shared memory each)
+
+struct TcArgs {
+  int out_rows;     // output rows (SwiGLU: rows / 2)
+  int batch;
+  int kblocks;      // ceil(k / 64)
+  int kb_per_rank;  // k-blocks per cluster rank
+  int half;         // SwiGLU: first up row
+  int epi;
+  float* y;
+  uint16_t* yh;
+  uint16_t* yl;
+  int ldy;
+  uint32_t* err;
+};
+
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
+  // K-major operand, 128-byte swizzle: rows of 128 bytes, 8-row atoms 1024 bytes apart.
+  return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+template <int N>
+__host__ __device__ constexpr uint32_t instr_desc_f16() {
+  // f32 accumulator, f16 A and B, both K-major, M = 128.
+  return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          dst),
+      "l"(map), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_f16(uint32_t tmem, uint64_t ad, uint64_t bd, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
+      "l"(ad), "l"(bd), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+template <int N>
+__device__ __forceinline__ void tmem_load_row(uint32_t taddr, float* v);
+
+template <>
+__device__ __forceinline__ void tmem_load_row<16>(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <>
+__device__ __forceinline__ void tmem_load_row<32>(uint32_t taddr, float* v) {
+  tmem_load_row<16>(taddr, v);
+  tmem_load_row<16>(taddr + 16, v + 16);
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_addr(uint32_t local_addr, uint32_t rank) {
+  uint32_t remote;
+  asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
+  return remote;
+}
+// Volatile keeps the loads after the cluster barrier; callers issue the loads of all ranks
+// before the sums that consume them, so they are in flight together.
+__device__ __forceinline__ float4 ld_cluster_v4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr));
+  return v;
+}
+
+__device__ __forceinline__ void split_hilo_tc(float x, __half& hi, __half& lo) {
+  hi = __float2half_rn(x);
+  lo = __float2half_rn(x - __half2float(hi));
+}
+
+template <int N, bool SW>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap txh,
+                   const __grid_constant__ CUtensorMap txl, const __grid_constant__ TcArgs a) {
+  extern __shared__ uint8_t dsm_raw[];
+  __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], accb;
+  __shared__ uint32_t tmem_slot;
+  constexpr int kTileB = N * kBK * 2;  // one activation plane per stage
+  constexpr int kStage = kTileA + 2 * kTileB;
+  constexpr int kTmemCols = N < 32 ? 32 : N;
+  constexpr int kPitch = N + 4;  // partial rows in shared memory: 16-byte aligned, conflict-free v4 stores
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(base);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t rank = cluster_rank();
+  const int nrank = (int)(gridDim.x);
+  const int tile = blockIdx.y;
+  const int kb0 = (int)rank * a.kb_per_rank;
+  const int nkb = max(0, min(a.kb_per_rank, a.kblocks - kb0));
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
+                 "n"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (tid == 32) {
+    for (int s = 0; s < kTcStages; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    mbar_init(smem_u32(&accb), 1);
+    fence_barrier_init();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  pdl_launch();
+
+  bool ok = true;
+  if (warp == 0 && lane == 0 && nkb > 0) {
+    // Producer. Weight tiles do not depend on the previous kernel: the first stages' weights go
+    // out before the dependency wait, their activation tiles after it.
+    const int r0 = SW ? tile * 64 : tile * 128;
+    auto load_a = [&](int i) {
+      const uint32_t st = sbase + (uint32_t)((i % kTcStages) * kStage);
+      const uint32_t bar = smem_u32(&full[i % kTcStages]);
+      const int kx = (kb0 + i) * kBK;
+      mbar_arrive_expect_tx(bar, (uint32_t)kStage);
+      if (SW) {
+        tma_load_2d(st, &tw, kx, r0, bar);
+        tma_load_2d(st + kTileA / 2, &tw, kx, a.half + r0, bar);
+      } else {
+        tma_load_2d(st, &tw, kx, r0, bar);
+      }
+    };
+    auto load_b = [&](int i) {
+      const uint32_t st = sbase + (uint32_t)((i % kTcStages) * kStage);
+      const uint32_t bar = smem_u32(&full[i % kTcStages]);
+      const int kx = (kb0 + i) * kBK;
+      tma_load_2d(st + kTileA, &txh, kx, 0, bar);
+      tma_load_2d(st + kTileA + kTileB, &txl, kx, 0, bar);
+    };
+    const int pre = min(kTcStages, nkb);
+    for (int i = 0; i < pre; ++i) load_a(i);
+    pdl_wait();
+    for (int i = 0; i < pre; ++i) load_b(i);
+    for (int i = pre; i < nkb; ++i) {
+      if (!mbar_wait(smem_u32(&empty[i % kTcStages]), (uint32_t)((i / kTcStages) + 1) & 1u, a.err)) {
+        ok = false;
+        break;
+      }
+      load_a(i);
+      load_b(i);
+    }
+  } else if (warp == 1 && lane == 0 && nkb > 0) {
+    // MMA issuer: 4 k-steps of 16 per stage, hi and lo planes into one accumulator.
+    constexpr uint32_t idesc = instr_desc_f16<N>();
+    for (int i = 0; i < nkb; ++i) {
+      const int s = i % kTcStages;
+      if (!mbar_wait(smem_u32(&full[s]), (uint32_t)(i / kTcStages) & 1u, a.err)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t st = sbase + (uint32_t)(s * kStage);
+#pragma unroll
+      for (int kk = 0; kk < kBK / 16; ++kk) {
+        const uint64_t ad = smem_desc_sw128(st + kk * 32);
+        mma_f16(tmem, ad, smem_desc_sw128(st + kTileA + kk * 32), idesc, (i | kk) != 0);
+        mma_f16(tmem, ad, smem_desc_sw128(st + kTileA + kTileB + kk * 32), idesc, 1u);
+      }
+      mma_commit(smem_u32(&empty[s]));
+    }
+    mma_commit(smem_u32(&accb));
+  }
+  __syncwarp();
+
+  // Accumulator -> shared memory (the stage ring is free once accb fired: every MMA completed,
+  // so every TMA load it consumed had landed). Thread t holds row t of the tile.
+  pdl_wait();
+  float* part = reinterpret_cast<float*>(base);
+  {
+    float v[N];
+    if (nkb > 0) {
+      if (!mbar_wait(smem_u32(&accb), 0u, a.err)) ok = false;
+      tc_fence_after();
+      tmem_load_row<N>(tmem + ((uint32_t)(warp * 32) << 16), v);
+    } else {
+#pragma unroll
+      for (int c = 0; c < N; ++c) v[c] = 0.f;
+    }
+#pragma unroll
+    for (int c = 0; c < N; c += 4)
+      *reinterpret_cast<float4*>(part + tid * kPitch + c) =
+          ok ? make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  tc_fence_before();
+  cluster_sync_all();
+
+  // Reduction over the cluster's ranks (rank order) and the epilogue, rows of this rank's slice.
+  // Thread work item: one output row j and 4 consecutive batch columns; consecutive threads take
+  // consecutive rows, so each of the 4 output stores is coalesced.
+  constexpr int kOutTile = SW ? 64 : 128;
+  const int slice = kOutTile / nrank;
+  const int o0 = (int)rank * slice;
+  const int B = a.batch;
+  const int groups = (B + 3) / 4;
+  const uint32_t pbase = smem_u32(part);
+  for (int e = tid; e < slice * groups; e += kTcThreads) {
+    const int b0 = (e / slice) * 4, j = o0 + e % slice;
+    const int orow = tile * kOutTile + j;
+    float4 pv[kMaxCluster], pu[kMaxCluster];
+#pragma unroll
+    for (int q = 0; q < kMaxCluster; ++q) {
+      if (q < nrank) {
+        pv[q] = ld_cluster_v4(cluster_addr(pbase + (uint32_t)((j * kPitch + b0) * 4), (uint32_t)q));
+        if (SW) pu[q] = ld_cluster_v4(cluster_addr(pbase + (uint32_t)(((64 + j) * kPitch + b0) * 4), (uint32_t)q));
+      }
+    }
+    float v[4] = {0.f, 0.f, 0.f, 0.f}, u[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int q = 0; q < kMaxCluster; ++q) {
+      if (q < nrank) {
+        v[0] += pv[q].x;
+        v[1] += pv[q].y;
+        v[2] += pv[q].z;
+        v[3] += pv[q].w;
+        if (SW) {
+          u[0] += pu[q].x;
+          u[1] += pu[q].y;
+          u[2] += pu[q].z;
+          u[3] += pu[q].w;
+        }
+      }
+    }
+    if (orow >= a.out_rows) continue;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int b = b0 + i;
+      if (b >= B) break;
+      if (SW) {
+        __half hi, lo;
+        split_hilo_tc(silu(v[i]) * u[i], hi, lo);
+        a.yh[(size_t)b * a.ldy + orow] = __half_as_ushort(hi);
+        a.yl[(size_t)b * a.ldy + orow] = __half_as_ushort(lo);
+      } else if (a.epi == kAccumulate) {
+        a.y[(size_t)b * a.ldy + orow] += v[i];
+      } else {
+        a.y[(size_t)b * a.ldy + orow] = v[i];
+      }
+    }
+  }
+  cluster_sync_all();  // no CTA leaves while another still reads its shared memory
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(kTmemCols) : "memory");
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// Host side
+// ------------------------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    cudaGetLastError();
+  });
+  return fn;
+}
+
+// 2-D f16 tensor [outer][inner] with rows `row_bytes` apart; box = box_inner x box_outer,
+// 128-byte swizzle (box_inner = 64 f16). Out-of-range elements read as zero.
+bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+              uint32_t box_outer) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {(cuuint32_t)kBK, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int N, bool SW>
+cudaError_t launch_tc_nsw(const GemmArgs& g, cudaStream_t stream, bool pdl) {
+  auto kernel = gemm_tc_kernel<N, SW>;
+  constexpr int kStage = kTileA + 2 * N * kBK * 2;
+  const size_t smem = (size_t)kTcStages * kStage + 1024;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  TcArgs a;
+  a.out_rows = SW ? g.rows / 2 : g.rows;
+  a.batch = g.batch;
+  a.kblocks = (g.k + kBK - 1) / kBK;
+  a.half = SW ? g.rows / 2 : 0;
+  a.epi = g.epi;
+  a.y = g.y;
+  a.yh = g.yh;
+  a.yl = g.yl;
+  a.ldy = g.ldy;
+  a.err = g.err;
+  const int out_tile = SW ? 64 : 128;
+  const int tiles = (a.out_rows + out_tile - 1) / out_tile;
+  // Split k over a cluster: the largest power of two that keeps the grid within the CTA slots
+  // and every rank at two k-blocks or more.
+  int ranks = 1;
+  while (ranks < kMaxCluster && tiles * ranks * 2 <= kCtaSlots && a.kblocks >= ranks * 4) ranks *= 2;
+  a.kb_per_rank = (a.kblocks + ranks - 1) / ranks;
+  const int x_rows = g.x_rows > 0 ? g.x_rows : (g.batch + 7) / 8 * 8;
+  CUtensorMap tw, txh, txl;
+  if (!make_map(&tw, g.w, (uint64_t)g.k, (uint64_t)g.rows, (uint64_t)g.k * 2, SW ? 64 : 128) ||
+      !make_map(&txh, g.xh, (uint64_t)g.k, (uint64_t)x_rows, (uint64_t)g.ldx * 2, N) ||
+      !make_map(&txl, g.xl, (uint64_t)g.k, (uint64_t)x_rows, (uint64_t)g.ldx * 2, N))
+    return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ranks, tiles);
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = ranks;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 2 : 1;
+  count_launch();
+  return cudaLaunchKernelEx(&cfg, kernel, tw, txh, txl, a);
+}
+
+}  // namespace
+
+bool gemm_tc_available() { return encode_fn() != nullptr; }
+
+cudaError_t launch_gemm_tc(const GemmArgs& g, cudaStream_t stream, bool pdl) {
+  const bool sw = g.epi == kSwiGlu;
+  if (g.batch <= 16) return sw ? launch_tc_nsw<16, true>(g, stream, pdl) : launch_tc_nsw<16, false>(g, stream, pdl);
+  return sw ? launch_tc_nsw<32, true>(g, stream, pdl) : launch_tc_nsw<32, false>(g, stream, pdl);
+}
+
+}  // namespace qne

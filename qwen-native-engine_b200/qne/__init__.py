@@ -108,6 +108,7 @@ def _load_lib() -> C.CDLL:
         "qne_gemv_ex": (I32, [C.POINTER(_Matrix), P, P, I32, I32, I32, P]),
         "qne_gemm_scratch_bytes": (SZ, [C.POINTER(_Matrix), I32]),
         "qne_gemm": (I32, [C.POINTER(_Matrix), P, I32, P, I32, P, SZ, P]),
+        "qne_gemm_ex": (I32, [C.POINTER(_Matrix), P, I32, P, I32, I32, P]),
         "qne_gemm_noalloc": (I32, [C.POINTER(_Matrix), P, I32, P, I32, P]),
         "qne_dequant_rows": (I32, [C.POINTER(_Matrix), I32, I32, P, P]),
         "qne_embed": (I32, [C.POINTER(_Matrix), P, P, P]),
@@ -454,9 +455,18 @@ def gemm_scratch_bytes(m: _Matrix, batch: int) -> int:
     return int(lib.qne_gemm_scratch_bytes(C.byref(m), batch))
 
 
-def gemm(m: _Matrix, x, batch: int, y, epilogue="store", scratch=None, scratch_bytes: int = 0, stream=None) -> None:
+GEMM_IMPLS = {"tcgen05": 0, "mma_sync": 1}
+
+
+def gemm(m: _Matrix, x, batch: int, y, epilogue="store", scratch=None, scratch_bytes: int = 0, stream=None,
+         impl: str | None = None) -> None:
+    """y[batch][out_rows] (=, +=, SwiGLU) m . x[batch][k]; impl None = qne_gemm's default kernel,
+    else "tcgen05" or "mma_sync" through qne_gemm_ex."""
     epi = EPILOGUES[epilogue] if isinstance(epilogue, str) else int(epilogue)
-    _check(lib.qne_gemm(C.byref(m), _ptr(x), batch, _ptr(y), epi, _ptr(scratch), scratch_bytes, _stream(stream)))
+    if impl is None:
+        _check(lib.qne_gemm(C.byref(m), _ptr(x), batch, _ptr(y), epi, _ptr(scratch), scratch_bytes, _stream(stream)))
+    else:
+        _check(lib.qne_gemm_ex(C.byref(m), _ptr(x), batch, _ptr(y), epi, GEMM_IMPLS[impl], _stream(stream)))
 
 
 if os.environ.get("QNE_PRINT_VERSION"):

@@ -17,10 +17,12 @@ def dev(a):
     return torch.from_numpy(np.ascontiguousarray(a)).cuda()
 
 
-@pytest.mark.parametrize("batch", [1, 3, 8, 13, 32])
+@pytest.mark.parametrize("impl", ["tcgen05", "mma_sync"])
+@pytest.mark.parametrize("batch", [1, 3, 8, 13, 16, 17, 32])
 @pytest.mark.parametrize("epilogue,rows,k", [("store", 1024, 1024), ("accumulate", 1024, 3584), ("swiglu", 2 * 3584, 1024),
-                                             ("store", 8224, 2048), ("store", 4099, 1024)])
-def test_gemm_matches_gemv_per_sequence(cuda, batch, epilogue, rows, k):
+                                             ("store", 8224, 2048), ("store", 4099, 1024), ("accumulate", 2048, 6144),
+                                             ("swiglu", 2 * 6144, 2048), ("store", 1000, 96), ("swiglu", 2 * 200, 4160)])
+def test_gemm_matches_gemv_per_sequence(cuda, impl, batch, epilogue, rows, k):
     rng = np.random.default_rng(batch * 7 + rows)
     w = (rng.standard_normal(rows * k) * 0.05).astype(np.float16)
     x = rng.standard_normal((batch, k)).astype(np.float32)
@@ -30,7 +32,7 @@ def test_gemm_matches_gemv_per_sequence(cuda, batch, epilogue, rows, k):
     m = qne.matrix("f16", rows, k, wd)
     xd = dev(x)
     yd = dev(y0 if epilogue == "accumulate" else np.zeros((batch, out_rows), np.float32))
-    qne.gemm(m, xd, batch, yd, epilogue)
+    qne.gemm(m, xd, batch, yd, epilogue, impl=impl)
     torch.cuda.synchronize()
     got = yd.cpu().numpy()
     for b in range(batch):
