@@ -299,6 +299,30 @@ def micro(args):
                                 "us": round(us, 2), "GBs": round(gbs, 1), "frac_of_" + peak_kind: round(gbs / peak, 4),
                                 "bytes": nbytes})
                 keep.clear()
+    if sel & {"all", "gemm"}:
+        # the batched GEMM on the decoder's shapes (2B and 0.8B), B = 32 and 8 activation rows
+        for (rows, K, epi) in ((8224, 2048, "store"), (2048, 2048, "accumulate"), (12288, 2048, "swiglu"),
+                               (2048, 6144, "accumulate"), (8224, 1024, "store"), (1024, 2048, "accumulate"),
+                               (7168, 1024, "swiglu"), (1024, 3584, "accumulate"), (248320, 1024, "store")):
+            nbytes = rows * K * 2
+            copies = max(1, min(16, int(2.5e8 // nbytes) + 1))
+            mats = []
+            for c in range(copies):
+                w = torch.from_numpy((rng.standard_normal(rows * K, dtype=np.float32) * 0.05).astype(np.float16)).cuda()
+                mats.append(qne.matrix("f16", rows, K, w))
+                keep.append(w)
+            out_rows = rows // 2 if epi == "swiglu" else rows
+            for B in (32, 8):
+                x = torch.randn(B, K, device="cuda")
+                y = torch.zeros(B, out_rows, device="cuda")
+                for impl in ("tcgen05", "mma_sync"):
+                    us = timed(lambda i: qne.gemm(mats[i], x, B, y, epi, stream=stream.cuda_stream, impl=impl),
+                               copies, max(2, 64 // copies))
+                    gbs = nbytes / (us * 1e-6) / 1e9
+                    out.append({"micro": "gemm", "impl": impl, "rows": rows, "K": K, "epilogue": epi, "batch": B,
+                                "us": round(us, 2), "GBs": round(gbs, 1), "frac_of_" + peak_kind: round(gbs / peak, 4),
+                                "bytes": nbytes, "note": "includes qne_gemm's f32 -> hi/lo staging kernel"})
+            keep.clear()
     if sel & {"all", "gdn"}:
         for B in (1, 32):
             copies = max(2, int(2.5e8 // (B * 16 * 128 * 128 * 4)) + 1)

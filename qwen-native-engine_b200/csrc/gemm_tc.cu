@@ -10,7 +10,7 @@
 //  * a tile is 128 weight rows (SwiGLU: 64 gate rows and the matching 64 up rows) by the whole
 //    activation batch (N = 16 or 32 columns of the MMA, zero-filled past the batch);
 //  * warp 0 lane 0 streams 64-wide k-blocks of the weight tile and of both activation planes
-//    with TMA (128-byte swizzle, the canonical K-major layout of the MMA operands) into a 4-stage
+//    with TMA (128-byte swizzle, the canonical K-major layout of the MMA operands) into a 3-stage
 //    ring guarded by mbarriers; weight loads of the first stages are issued before waiting on the
 //    previous kernel, whose output the activations are;
 //  * warp 1 lane 0 issues tcgen05.mma (M = 128, K = 16, f32 accumulator in tensor memory), two
@@ -24,7 +24,9 @@
 #include <cudaTypedefs.h>
 #include <math.h>
 
+#include <map>
 #include <mutex>
+#include <tuple>
 
 #include "batch.cuh"
 #include "gemv.cuh"
@@ -34,11 +36,11 @@ namespace qne {
 namespace {
 
 constexpr int kTcThreads = 128;
-constexpr int kTcStages = 4;
+constexpr int kTcStages = 3;
 constexpr int kBK = 64;                 // k per stage: one 128-byte swizzle span of f16
 constexpr int kTileA = 128 * kBK * 2;   // 16 KB of weights per stage
 constexpr int kMaxCluster = 8;
-constexpr int kCtaSlots = 2 * kNumSms;  // two CTAs per SM fit (about 97 KB of shared memory each)
+constexpr int kCtaSlots = 3 * kNumSms;  // three CTAs per SM fit (about 73 KB of shared memory each)
 
 struct TcArgs {
   int out_rows;     // output rows (SwiGLU: rows / 2)
@@ -354,6 +356,37 @@ bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, 
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Clusters of `ranks` CTAs that can be resident at once (cached per device, kernel and size).
+template <typename K>
+int max_clusters(K kernel, size_t smem, int ranks) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, const void*, int>, int> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const auto key = std::make_tuple(dev, reinterpret_cast<const void*>(kernel), ranks);
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ranks, 1);
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = ranks;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = kCtaSlots / ranks;  // fall back to the three-CTAs-per-SM estimate
+  }
+  cache[key] = n;
+  return n;
+}
+
 template <int N, bool SW>
 cudaError_t launch_tc_nsw(const GemmArgs& g, cudaStream_t stream, bool pdl) {
   auto kernel = gemm_tc_kernel<N, SW>;
@@ -374,10 +407,10 @@ cudaError_t launch_tc_nsw(const GemmArgs& g, cudaStream_t stream, bool pdl) {
   a.err = g.err;
   const int out_tile = SW ? 64 : 128;
   const int tiles = (a.out_rows + out_tile - 1) / out_tile;
-  // Split k over a cluster: the largest power of two that keeps the grid within the CTA slots
-  // and every rank at two k-blocks or more.
+  // Split k over a cluster: the largest power of two whose clusters (one per tile) all fit on
+  // the device at once, with every rank at two k-blocks or more.
   int ranks = 1;
-  while (ranks < kMaxCluster && tiles * ranks * 2 <= kCtaSlots && a.kblocks >= ranks * 4) ranks *= 2;
+  while (ranks < kMaxCluster && a.kblocks >= ranks * 4 && tiles <= max_clusters(kernel, smem, ranks * 2)) ranks *= 2;
   a.kb_per_rank = (a.kblocks + ranks - 1) / ranks;
   const int x_rows = g.x_rows > 0 ? g.x_rows : (g.batch + 7) / 8 * 8;
   CUtensorMap tw, txh, txl;
