@@ -289,6 +289,16 @@ QNE_API qne_status qne_attention_step(const float* proj, const float* norms, dou
                               uint32_t pool_pages, const uint32_t* page_table, const uint32_t* pos,
                               float* out, int batch, void* scratch, size_t scratch_bytes,
                               void* stream);
+/* qne_attention_step with the kernel chosen explicitly (no counterpart in the reference; for
+ * comparisons): QNE_ATTN_TENSOR_CORE = scores and PV product with mma.sync (the default of
+ * qne_attention_step and of every decode path except the fused layer kernels), QNE_ATTN_CUDA_CORE
+ * = per-token dot products reduced across a warp. */
+#define QNE_ATTN_TENSOR_CORE 0
+#define QNE_ATTN_CUDA_CORE 1
+QNE_API qne_status qne_attention_step_ex(const float* proj, const float* norms, double rope_theta, void* kv,
+                                 uint32_t pool_pages, const uint32_t* page_table, const uint32_t* pos,
+                                 float* out, int batch, void* scratch, size_t scratch_bytes, int impl,
+                                 void* stream);
 /* Gathers the K and V rows of positions [0, len) of one sequence through its page table into
  * contiguous out_k/out_v [2 kv heads][len][256] f16 (bit copy). */
 QNE_API qne_status qne_kv_gather(const void* kv, const uint32_t* page_table, uint32_t len, void* out_k,

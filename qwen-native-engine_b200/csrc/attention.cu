@@ -8,10 +8,13 @@
 //   0..pos, times sigmoid(gate_h).
 //
 // B200 design: the cache is paged (16-token f16 pages, per-sequence page tables); one CTA per
-// (context split, KV head, sequence) serves the 4 query heads of the KV head, streams its
-// split's K and V rows with 16-byte loads (K and V of eight tokens in flight per lane), keeps
-// an online softmax per head, and writes a partial (max, sum, 4 x 256 accumulator). The last
-// CTA of each (sequence, KV head) to finish merges the partials and applies the output gate.
+// (context split, KV head, sequence) serves the 4 query heads of the KV head, stages its
+// split's K and V rows in shared memory with cp.async, keeps an online softmax per head, and
+// writes a partial (max, sum, 4 x 256 accumulator). The last CTA of each (sequence, KV head) to
+// finish merges the partials and applies the output gate. The default work item (attn_tc.cuh)
+// computes the scores and the PV product with mma.sync (q and the probabilities as hi + lo f16
+// halves); the CUDA-core item (attn_dev.cuh, also used by the fused layer kernels) reduces each
+// token's dot products across a warp.
 // The CTA whose split holds `pos` normalizes, rotates and appends the current K/V (rounded to
 // f16) and uses the rounded values for that position; no other CTA reads that slot.
 // RoPE angles come from a host-built table (double precision), identical for every consumer.
@@ -20,6 +23,7 @@
 #include <cmath>
 
 #include "attn_dev.cuh"
+#include "attn_tc.cuh"
 #include "gdn.cuh"
 #include "gemv.cuh"
 
@@ -28,11 +32,12 @@ namespace {
 
 using namespace dev;
 
+template <class Item, class Shared>
 __global__ void __launch_bounds__(256, 2) attention_kernel(const KernelArgs ka) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  AttnShared& sh = *reinterpret_cast<AttnShared*>(smem);
+  extern __shared__ __align__(128) uint8_t smem[];
+  Shared& sh = *reinterpret_cast<Shared*>(smem);
   const int item = (blockIdx.z * kKvHeads + blockIdx.y) * ka.max_splits + blockIdx.x;
-  AttnItem it;
+  Item it;
   pdl_launch();
   pdl_wait();
   it.prefetch(ka, sh, item);
@@ -64,13 +69,15 @@ cudaError_t launch_attention(const AttnArgs& a, uint32_t pool_pages, int split_t
   ka.pool_pages = pool_pages;
   const int max_splits = (kMaxContext + split_tokens - 1) / split_tokens;
   ka.max_splits = max_splits;
-  const cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)sizeof(AttnShared));
+  const bool tc = a.impl == 0;
+  auto kernel = tc ? attention_kernel<AttnTcItem, AttnTcShared> : attention_kernel<AttnItem, AttnShared>;
+  const size_t smem = tc ? sizeof(AttnTcShared) : sizeof(AttnShared);
+  const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(max_splits, kKvHeads, a.batch);
   cfg.blockDim = dim3(256);
-  cfg.dynamicSmemBytes = sizeof(AttnShared);
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -78,7 +85,7 @@ cudaError_t launch_attention(const AttnArgs& a, uint32_t pool_pages, int split_t
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
   count_launch();
-  return cudaLaunchKernelEx(&cfg, attention_kernel, ka);
+  return cudaLaunchKernelEx(&cfg, kernel, ka);
 }
 
 cudaError_t launch_kv_gather(const uint16_t* kv, const uint32_t* page_table, uint32_t len,

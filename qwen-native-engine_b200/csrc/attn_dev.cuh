@@ -121,6 +121,157 @@ __device__ __forceinline__ void merge_parts(const float* acc, const float* ml, i
   }
 }
 
+// Writes a split's partial for (sequence b, KV head kvh) -- thread t holds the unnormalized sums
+// o of head t / 64, dims 4 (t % 64) .. +3, and sh.run_m / run_l hold the running max and sum per
+// head -- then merges partials in two ticketed levels (groups of kGroup splits, then groups); the
+// CTA that completes the last merge applies the output gate and stores. Ends with __syncthreads.
+template <class SH>
+__device__ __forceinline__ void attn_merge_store(const AttnArgs& a, SH& sh, int b, int kvh, int split, int nsplit,
+                                               float4 o) {
+  const int t = threadIdx.x;
+  const int hh = t >> 6, d0 = (t & 63) * 4;
+  const float* pr = a.proj + (size_t)b * kAttnProj;
+  Scratch S = carve(a.scratch, a.scratch_rows > 0 ? a.scratch_rows : a.batch);
+  const size_t sk = (size_t)b * kKvHeads + kvh;  // (sequence, KV head)
+  const int group = split / kGroup, ngroups = (nsplit + kGroup - 1) / kGroup;
+  const int gsize = min(kGroup, nsplit - group * kGroup);
+  float* gacc = S.gacc + (sk * kMaxGroups) * kPart;
+  float* gml = S.gml + (sk * kMaxGroups) * kQPerKv * 2;
+  float L = sh.run_l[hh];
+  bool done = nsplit == 1;  // a single split needs no merge
+  if (!done) {
+    float* pacc = S.acc + (sk * kMaxSplits + split) * kPart;
+    float* pml = S.ml + (sk * kMaxSplits + split) * kQPerKv * 2;
+    *reinterpret_cast<float4*>(pacc + hh * kHeadDim + d0) = o;
+    if (t < kQPerKv) {
+      pml[t * 2 + 0] = sh.run_m[t];
+      pml[t * 2 + 1] = sh.run_l[t];
+    }
+    // Merge level 1: the last split of each group of 8 merges the group; level 2: the last
+    // group to finish merges the groups. Each level is entered by one CTA only.
+#pragma unroll 1
+    for (int level = 0; level < 2 && !done; ++level) {
+      const int n = level == 0 ? gsize : ngroups;
+      uint32_t* ticket = level == 0 ? S.gticket + sk * kMaxGroups + group : S.ticket + sk;
+      __threadfence();
+      __syncthreads();
+      if (t == 0) sh.flag = (atomicAdd(ticket, 1u) == (uint32_t)n - 1) ? 1u : 0u;
+      __syncthreads();
+      if (!sh.flag) {
+        __syncthreads();  // shared memory is reused by the next item
+        return;
+      }
+      __threadfence();
+      float M;
+      merge_parts(level == 0 ? S.acc + (sk * kMaxSplits + group * kGroup) * kPart : gacc,
+                  level == 0 ? S.ml + (sk * kMaxSplits + group * kGroup) * kQPerKv * 2 : gml, n, hh, d0, M, L, o);
+      if (t == 0) *ticket = 0u;
+      if (level == 0 && ngroups > 1) {
+        *reinterpret_cast<float4*>(gacc + (size_t)group * kPart + hh * kHeadDim + d0) = o;
+        if ((t & 63) == 0) {
+          gml[((size_t)group * kQPerKv + hh) * 2 + 0] = M;
+          gml[((size_t)group * kQPerKv + hh) * 2 + 1] = L;
+        }
+      } else {
+        done = true;
+      }
+    }
+  }
+  const int h = kvh * kQPerKv + hh;
+  const float4 gate = *reinterpret_cast<const float4*>(pr + 2048 + h * kHeadDim + d0);
+  float4 r;
+  r.x = o.x / L / (1.0f + expf(-gate.x));
+  r.y = o.y / L / (1.0f + expf(-gate.y));
+  r.z = o.z / L / (1.0f + expf(-gate.z));
+  r.w = o.w / L / (1.0f + expf(-gate.w));
+  *reinterpret_cast<float4*>(a.out + (size_t)b * kMixerOut + h * kHeadDim + d0) = r;
+  __syncthreads();  // shared memory is reused by the next item
+}
+
+// Prologue of a work item: q of the 4 heads of KV head kvh (RMSNorm with q_norm, RoPE at pos,
+// times 1/16) into sh.q_s; for the item that holds pos (owner), the current key (RMSNorm with
+// k_norm, RoPE) and value rounded to f16, appended to the cache page and kept in sh.kc_s /
+// sh.vc_s; running max / sum reset. Ends with __syncthreads.
+template <class SH>
+__device__ __forceinline__ void attn_prologue(const KernelArgs& ka, SH& sh, int b, int kvh, uint32_t pos, bool owner,
+                                              const uint32_t* pt) {
+  const AttnArgs& a = ka.a;
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const float* pr = a.proj + (size_t)b * kAttnProj;
+  // ---- q of the 4 heads (and the current k): RMSNorm, RoPE ----
+  const float* rc = a.rope + (size_t)pos * kRopeHalf;                                  // cos
+  const float* rs = a.rope + (size_t)kMaxContext * kRopeHalf + (size_t)pos * kRopeHalf;  // sin
+  {
+    float xq[kQPerKv];
+#pragma unroll
+    for (int hh = 0; hh < kQPerKv; ++hh) {
+      xq[hh] = pr[(kvh * kQPerKv + hh) * kHeadDim + t];
+      const float ss = warp_sum(xq[hh] * xq[hh]);
+      if (lane == 0) sh.red[warp][hh] = ss;
+    }
+    const float xk = owner ? pr[4096 + kvh * kHeadDim + t] : 0.f;
+    const float ssk = warp_sum(xk * xk);
+    if (lane == 0) sh.redk[warp] = ssk;
+    __syncthreads();
+#pragma unroll
+    for (int hh = 0; hh < kQPerKv; ++hh) {
+      float sum = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) sum += sh.red[w][hh];
+      sh.q_s[hh][t] = xq[hh] * rsqrtf(sum / (float)kHeadDim + 1e-6f) * a.norms[t];
+    }
+    if (owner) {
+      float sum = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) sum += sh.redk[w];
+      sh.kc_s[t] = xk * rsqrtf(sum / (float)kHeadDim + 1e-6f) * a.norms[kHeadDim + t];
+    }
+  }
+  __syncthreads();
+  {
+    float qr[kQPerKv];
+    float kr = 0.f;
+#pragma unroll
+    for (int hh = 0; hh < kQPerKv; ++hh) qr[hh] = sh.q_s[hh][t];
+    if (owner) kr = sh.kc_s[t];
+    if (t < 2 * kRopeHalf) {
+      const int i = t & (kRopeHalf - 1);
+      const float c = rc[i], sn = rs[i];
+#pragma unroll
+      for (int hh = 0; hh < kQPerKv; ++hh)
+        qr[hh] = (t < kRopeHalf) ? sh.q_s[hh][t] * c - sh.q_s[hh][t + kRopeHalf] * sn
+                                 : sh.q_s[hh][t] * c + sh.q_s[hh][t - kRopeHalf] * sn;
+      if (owner)
+        kr = (t < kRopeHalf) ? sh.kc_s[t] * c - sh.kc_s[t + kRopeHalf] * sn : sh.kc_s[t] * c + sh.kc_s[t - kRopeHalf] * sn;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int hh = 0; hh < kQPerKv; ++hh) sh.q_s[hh][t] = qr[hh] * 0.0625f;  // 1/sqrt(256), exact
+    if (owner) {
+      // Append the current key and value, rounded to f16, and use the rounded values below.
+      const uint32_t page = pt[pos / kPageTokens];
+      if (page < ka.pool_pages) {
+        const __half kh = __float2half_rn(kr);
+        const __half vh = __float2half_rn(pr[4608 + kvh * kHeadDim + t]);
+        uint16_t* kdst = const_cast<uint16_t*>(kv_row(a.kv, page, 0, kvh, pos % kPageTokens));
+        uint16_t* vdst = const_cast<uint16_t*>(kv_row(a.kv, page, 1, kvh, pos % kPageTokens));
+        kdst[t] = __half_as_ushort(kh);
+        vdst[t] = __half_as_ushort(vh);
+        sh.kc_s[t] = __half2float(kh);
+        sh.vc_s[t] = __half2float(vh);
+      } else {
+        sh.kc_s[t] = 0.f;
+        sh.vc_s[t] = 0.f;
+      }
+    }
+    if (t < kQPerKv) {
+      sh.run_m[t] = -INFINITY;
+      sh.run_l[t] = 0.f;
+    }
+  }
+  __syncthreads();
+}
+
 __device__ __forceinline__ void cp_async16_attn(void* smem, const void* gmem) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)),
                "l"(gmem)
@@ -133,27 +284,24 @@ struct AttnItem {
   bool valid, owner;
   const uint32_t* pt;
 
-  // Stages K and V of tokens sb + 8w .. sb + 8w + 7 (this warp's share of a sub-block): one
-  // 16-byte cp.async per row and lane; tokens outside [l0, l1), the current token when this item
-  // appends it (taken from kc_s / vc_s instead) and rows of an out-of-range page are zero-filled,
-  // then one group commits.
-  __device__ __forceinline__ void stage(const KernelArgs& ka, AttnShared& sh, int sb) const {
+  // Stages K (kind 0) or V (kind 1) of tokens sb + 8w .. sb + 8w + 7 (this warp's share of a
+  // sub-block) and commits them as one cp.async group: one 16-byte cp.async per row and lane.
+  // Tokens outside [l0, l1), the current token when this item appends it (taken from kc_s / vc_s
+  // instead) and rows of an out-of-range page are zero-filled. A lane later reads only the
+  // chunks it staged itself, so a group needs no barrier beyond the lane's own wait.
+  __device__ __forceinline__ void stage(const KernelArgs& ka, AttnShared& sh, int sb, int kind) const {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (sb < l1) {
 #pragma unroll 1
-    for (int i = 0; i < 8; ++i) {
-      const int t = warp * 8 + i, l = sb + t;
-      uint4* kd = reinterpret_cast<uint4*>(&sh.kst[t][lane * 8]);
-      uint4* vd = reinterpret_cast<uint4*>(&sh.vst[t][lane * 8]);
-      const uint32_t page = (l < l1 && !(owner && l == (int)pos)) ? pt[l / kPageTokens] : 0xFFFFFFFFu;
-      if (page < ka.pool_pages) {
-        cp_async16_attn(kd, kv_row(ka.a.kv, page, 0, kvh, l % kPageTokens) + lane * 8);
-        cp_async16_attn(vd, kv_row(ka.a.kv, page, 1, kvh, l % kPageTokens) + lane * 8);
-      } else {
-        *kd = make_uint4(0u, 0u, 0u, 0u);
-        *vd = make_uint4(0u, 0u, 0u, 0u);
+      for (int i = 0; i < 8; ++i) {
+        const int t = warp * 8 + i, l = sb + t;
+        uint4* d = reinterpret_cast<uint4*>(kind == 0 ? &sh.kst[t][lane * 8] : &sh.vst[t][lane * 8]);
+        const uint32_t page = (l < l1 && !(owner && l == (int)pos)) ? pt[l / kPageTokens] : 0xFFFFFFFFu;
+        if (page < ka.pool_pages) cp_async16_attn(d, kv_row(ka.a.kv, page, kind, kvh, l % kPageTokens) + lane * 8);
+        else *d = make_uint4(0u, 0u, 0u, 0u);
       }
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
+    asm volatile("cp.async.commit_group;" ::: "memory");  // an empty group past the split's end
   }
 
   // Item geometry and the first sub-block's K/V staging. Reads the position, the page table and
@@ -177,86 +325,15 @@ struct AttnItem {
     l1 = min(l0 + ka.split, len);
     owner = !a.kv_appended && (int)pos >= l0 && (int)pos < l1;
     pt = a.page_table + (size_t)b * a.page_table_stride;
-    stage(ka, sh, l0);
+    stage(ka, sh, l0, 0);
+    stage(ka, sh, l0, 1);
   }
 
   __device__ __forceinline__ void run(const KernelArgs& ka, AttnShared& sh) {
     const AttnArgs& a = ka.a;
     if (!valid) return;
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-    const float* pr = a.proj + (size_t)b * kAttnProj;
-    // ---- q of the 4 heads (and the current k): RMSNorm, RoPE ----
-    const float* rc = a.rope + (size_t)pos * kRopeHalf;                                  // cos
-    const float* rs = a.rope + (size_t)kMaxContext * kRopeHalf + (size_t)pos * kRopeHalf;  // sin
-    {
-      float xq[kQPerKv];
-#pragma unroll
-      for (int hh = 0; hh < kQPerKv; ++hh) {
-        xq[hh] = pr[(kvh * kQPerKv + hh) * kHeadDim + t];
-        const float ss = warp_sum(xq[hh] * xq[hh]);
-        if (lane == 0) sh.red[warp][hh] = ss;
-      }
-      const float xk = owner ? pr[4096 + kvh * kHeadDim + t] : 0.f;
-      const float ssk = warp_sum(xk * xk);
-      if (lane == 0) sh.redk[warp] = ssk;
-      __syncthreads();
-#pragma unroll
-      for (int hh = 0; hh < kQPerKv; ++hh) {
-        float sum = 0.f;
-#pragma unroll
-        for (int w = 0; w < 8; ++w) sum += sh.red[w][hh];
-        sh.q_s[hh][t] = xq[hh] * rsqrtf(sum / (float)kHeadDim + 1e-6f) * a.norms[t];
-      }
-      if (owner) {
-        float sum = 0.f;
-#pragma unroll
-        for (int w = 0; w < 8; ++w) sum += sh.redk[w];
-        sh.kc_s[t] = xk * rsqrtf(sum / (float)kHeadDim + 1e-6f) * a.norms[kHeadDim + t];
-      }
-    }
-    __syncthreads();
-    {
-      float qr[kQPerKv];
-      float kr = 0.f;
-#pragma unroll
-      for (int hh = 0; hh < kQPerKv; ++hh) qr[hh] = sh.q_s[hh][t];
-      if (owner) kr = sh.kc_s[t];
-      if (t < 2 * kRopeHalf) {
-        const int i = t & (kRopeHalf - 1);
-        const float c = rc[i], sn = rs[i];
-#pragma unroll
-        for (int hh = 0; hh < kQPerKv; ++hh)
-          qr[hh] = (t < kRopeHalf) ? sh.q_s[hh][t] * c - sh.q_s[hh][t + kRopeHalf] * sn
-                                   : sh.q_s[hh][t] * c + sh.q_s[hh][t - kRopeHalf] * sn;
-        if (owner)
-          kr = (t < kRopeHalf) ? sh.kc_s[t] * c - sh.kc_s[t + kRopeHalf] * sn : sh.kc_s[t] * c + sh.kc_s[t - kRopeHalf] * sn;
-      }
-      __syncthreads();
-#pragma unroll
-      for (int hh = 0; hh < kQPerKv; ++hh) sh.q_s[hh][t] = qr[hh] * 0.0625f;  // 1/sqrt(256), exact
-      if (owner) {
-        // Append the current key and value, rounded to f16, and use the rounded values below.
-        const uint32_t page = pt[pos / kPageTokens];
-        if (page < ka.pool_pages) {
-          const __half kh = __float2half_rn(kr);
-          const __half vh = __float2half_rn(pr[4608 + kvh * kHeadDim + t]);
-          uint16_t* kdst = const_cast<uint16_t*>(kv_row(a.kv, page, 0, kvh, pos % kPageTokens));
-          uint16_t* vdst = const_cast<uint16_t*>(kv_row(a.kv, page, 1, kvh, pos % kPageTokens));
-          kdst[t] = __half_as_ushort(kh);
-          vdst[t] = __half_as_ushort(vh);
-          sh.kc_s[t] = __half2float(kh);
-          sh.vc_s[t] = __half2float(vh);
-        } else {
-          sh.kc_s[t] = 0.f;
-          sh.vc_s[t] = 0.f;
-        }
-      }
-      if (t < kQPerKv) {
-        sh.run_m[t] = -INFINITY;
-        sh.run_l[t] = 0.f;
-      }
-    }
-    __syncthreads();
+    attn_prologue(ka, sh, b, kvh, pos, owner, pt);
 
     // This lane's 8 dims of q for the 4 heads stay in registers for the whole split.
     float q[kQPerKv][8];
@@ -271,10 +348,12 @@ struct AttnItem {
 #pragma unroll
       for (int e = 0; e < 8; ++e) acc[hh][e] = 0.f;
 
+    // K and V of a sub-block are separate cp.async groups, committed in the order K0 V0 K1 V1 ...:
+    // K of the next sub-block streams in during this one's softmax and PV, V of the next during
+    // its scores. At each wait the one newer group may stay in flight.
 #pragma unroll 1
     for (int sb = l0; sb < l1; sb += kSub) {
-      if (sb != l0) stage(ka, sh, sb);
-      asm volatile("cp.async.wait_group 0;" ::: "memory");
+      asm volatile("cp.async.wait_group 1;" ::: "memory");  // K(sb) has landed
       // Scores of this warp's 8 tokens (each lane reads only the chunks it staged).
 #pragma unroll 1
       for (int i = 0; i < 8; ++i) {
@@ -303,6 +382,7 @@ struct AttnItem {
           for (int hh = 0; hh < kQPerKv; ++hh) sh.sc[hh][tk] = (l < l1) ? d[hh] : -INFINITY;
         }
       }
+      stage(ka, sh, sb + kSub, 0);  // this lane's K chunks are read: refill them with the next block
       __syncthreads();
       // Block max per head: thread (hh = t / 64, j = t % 64).
       {
@@ -331,6 +411,7 @@ struct AttnItem {
 #pragma unroll
         for (int e = 0; e < 8; ++e) acc[hh][e] *= f;
       }
+      asm volatile("cp.async.wait_group 1;" ::: "memory");  // V(sb) has landed
 #pragma unroll 1
       for (int i = 0; i < 8; ++i) {
         const int tk = warp * 8 + i, l = sb + tk;
@@ -350,8 +431,11 @@ struct AttnItem {
           }
         }
       }
-      __syncthreads();  // sh.sc is rewritten by the next sub-block; accw reuses the K area
+      stage(ka, sh, sb + kSub, 1);  // and the V chunks
+      __syncthreads();  // sh.sc is rewritten by the next sub-block
     }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");  // (only empty groups remain)
+    __syncthreads();  // accw reuses the K area
 
     // Merge the 8 warps' accumulators and write this split's partial.
 #pragma unroll
@@ -360,13 +444,7 @@ struct AttnItem {
       *reinterpret_cast<float4*>(sh.accw(warp) + hh * kHeadDim + lane * 8 + 4) = *reinterpret_cast<float4*>(&acc[hh][4]);
     }
     __syncthreads();
-    Scratch S = carve(a.scratch, a.scratch_rows > 0 ? a.scratch_rows : a.batch);
-    const size_t sk = (size_t)b * kKvHeads + kvh;  // (sequence, KV head)
-    const int hh = t >> 6, d0 = (t & 63) * 4;       // merge mapping
-    const int group = split / kGroup, ngroups = (nsplit + kGroup - 1) / kGroup;
-    const int gsize = min(kGroup, nsplit - group * kGroup);
-    float* gacc = S.gacc + (sk * kMaxGroups) * kPart;
-    float* gml = S.gml + (sk * kMaxGroups) * kQPerKv * 2;
+    const int hh = t >> 6, d0 = (t & 63) * 4;  // merge mapping
     float4 o;
     o.x = o.y = o.z = o.w = 0.f;
 #pragma unroll
@@ -377,55 +455,7 @@ struct AttnItem {
       o.z += v.z;
       o.w += v.w;
     }
-    float L = sh.run_l[hh];
-    bool done = nsplit == 1;  // a single split needs no merge
-    if (!done) {
-      float* pacc = S.acc + (sk * kMaxSplits + split) * kPart;
-      float* pml = S.ml + (sk * kMaxSplits + split) * kQPerKv * 2;
-      *reinterpret_cast<float4*>(pacc + hh * kHeadDim + d0) = o;
-      if (t < kQPerKv) {
-        pml[t * 2 + 0] = sh.run_m[t];
-        pml[t * 2 + 1] = sh.run_l[t];
-      }
-      // Merge level 1: the last split of each group of 8 merges the group; level 2: the last
-      // group to finish merges the groups. Each level is entered by one CTA only.
-#pragma unroll 1
-      for (int level = 0; level < 2 && !done; ++level) {
-        const int n = level == 0 ? gsize : ngroups;
-        uint32_t* ticket = level == 0 ? S.gticket + sk * kMaxGroups + group : S.ticket + sk;
-        __threadfence();
-        __syncthreads();
-        if (t == 0) sh.flag = (atomicAdd(ticket, 1u) == (uint32_t)n - 1) ? 1u : 0u;
-        __syncthreads();
-        if (!sh.flag) {
-          __syncthreads();  // shared memory is reused by the next item
-          return;
-        }
-        __threadfence();
-        float M;
-        merge_parts(level == 0 ? S.acc + (sk * kMaxSplits + group * kGroup) * kPart : gacc,
-                    level == 0 ? S.ml + (sk * kMaxSplits + group * kGroup) * kQPerKv * 2 : gml, n, hh, d0, M, L, o);
-        if (t == 0) *ticket = 0u;
-        if (level == 0 && ngroups > 1) {
-          *reinterpret_cast<float4*>(gacc + (size_t)group * kPart + hh * kHeadDim + d0) = o;
-          if ((t & 63) == 0) {
-            gml[((size_t)group * kQPerKv + hh) * 2 + 0] = M;
-            gml[((size_t)group * kQPerKv + hh) * 2 + 1] = L;
-          }
-        } else {
-          done = true;
-        }
-      }
-    }
-    const int h = kvh * kQPerKv + hh;
-    const float4 gate = *reinterpret_cast<const float4*>(pr + 2048 + h * kHeadDim + d0);
-    float4 r;
-    r.x = o.x / L / (1.0f + expf(-gate.x));
-    r.y = o.y / L / (1.0f + expf(-gate.y));
-    r.z = o.z / L / (1.0f + expf(-gate.z));
-    r.w = o.w / L / (1.0f + expf(-gate.w));
-    *reinterpret_cast<float4*>(a.out + (size_t)b * kMixerOut + h * kHeadDim + d0) = r;
-    __syncthreads();  // shared memory is reused by the next item
+    attn_merge_store(a, sh, b, kvh, split, nsplit, o);
   }
 };
 

@@ -412,7 +412,15 @@ size_t qne_attention_scratch_bytes(int batch) { return batch > 0 ? attention_scr
 qne_status qne_attention_step(const float* proj, const float* norms, double rope_theta, void* kv,
                               uint32_t pool_pages, const uint32_t* page_table, const uint32_t* pos, float* out,
                               int batch, void* scratch, size_t scratch_bytes, void* stream) {
+  return qne_attention_step_ex(proj, norms, rope_theta, kv, pool_pages, page_table, pos, out, batch, scratch,
+                               scratch_bytes, QNE_ATTN_TENSOR_CORE, stream);
+}
+
+qne_status qne_attention_step_ex(const float* proj, const float* norms, double rope_theta, void* kv,
+                                 uint32_t pool_pages, const uint32_t* page_table, const uint32_t* pos, float* out,
+                                 int batch, void* scratch, size_t scratch_bytes, int impl, void* stream) {
   return guarded([&] {
+    if (impl != QNE_ATTN_TENSOR_CORE && impl != QNE_ATTN_CUDA_CORE) throw QneError(kEInval, "unknown attention kernel");
     if (!proj || !norms || !kv || !page_table || !pos || !out || !scratch || batch < 1 || pool_pages == 0)
       throw QneError(kEInval, "null argument, batch < 1 or empty page pool");
     if (!(rope_theta > 0)) throw QneError(kEInval, "rope_theta must be positive");
@@ -427,6 +435,7 @@ qne_status qne_attention_step(const float* proj, const float* norms, double rope
     a.out = out;
     a.batch = batch;
     a.scratch = scratch;
+    a.impl = impl == QNE_ATTN_CUDA_CORE ? 1 : 0;
     check_launch(launch_attention(a, pool_pages, batch >= 8 ? 256 : 64, as_stream(stream), false), "attention");
   });
 }

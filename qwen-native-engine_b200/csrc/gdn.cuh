@@ -37,6 +37,7 @@ struct AttnArgs {
   int page_table_stride = kPagesPerSeq;  // 0: every row reads one sequence's page table (prefill)
   int kv_appended = 0;  // 1: every row's own K/V is already in the cache (prefill); no CTA appends
   int scratch_rows = 0;  // rows `scratch` is laid out for (0: batch); fixed when batch varies
+  int impl = 0;          // 0: tensor-core kernel (mma.sync QK^T and PV), 1: CUDA-core kernel
 };
 size_t attention_scratch_bytes(int batch);
 // split_tokens: context tokens per CTA, a multiple of 64. pool_pages bounds the page ids.

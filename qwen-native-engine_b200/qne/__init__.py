@@ -117,6 +117,7 @@ def _load_lib() -> C.CDLL:
         "qne_gdn_step": (I32, [P, P, P, P, P, P, P, I32, P]),
         "qne_attention_scratch_bytes": (SZ, [I32]),
         "qne_attention_step": (I32, [P, P, C.c_double, P, U32, P, P, P, I32, P, SZ, P]),
+        "qne_attention_step_ex": (I32, [P, P, C.c_double, P, U32, P, P, P, I32, P, SZ, I32, P]),
         "qne_kv_gather": (I32, [P, P, U32, P, P, P]),
         "qne_bandwidth_probe": (I32, [P, SZ, P, P]),
     }
@@ -437,10 +438,19 @@ def attention_scratch_bytes(batch: int) -> int:
     return int(lib.qne_attention_scratch_bytes(batch))
 
 
+ATTN_IMPLS = {"tensor_core": 0, "cuda_core": 1}
+
+
 def attention_step(proj, norms, theta: float, kv, pool_pages: int, page_table, pos, out, batch, scratch,
-                   scratch_bytes: int, stream=None) -> None:
-    _check(lib.qne_attention_step(_ptr(proj), _ptr(norms), float(theta), _ptr(kv), pool_pages, _ptr(page_table),
-                                  _ptr(pos), _ptr(out), batch, _ptr(scratch), scratch_bytes, _stream(stream)))
+                   scratch_bytes: int, stream=None, impl: str | None = None) -> None:
+    """impl None = qne_attention_step's default kernel, else "tensor_core" or "cuda_core"."""
+    if impl is None:
+        _check(lib.qne_attention_step(_ptr(proj), _ptr(norms), float(theta), _ptr(kv), pool_pages, _ptr(page_table),
+                                      _ptr(pos), _ptr(out), batch, _ptr(scratch), scratch_bytes, _stream(stream)))
+    else:
+        _check(lib.qne_attention_step_ex(_ptr(proj), _ptr(norms), float(theta), _ptr(kv), pool_pages,
+                                         _ptr(page_table), _ptr(pos), _ptr(out), batch, _ptr(scratch), scratch_bytes,
+                                         ATTN_IMPLS[impl], _stream(stream)))
 
 
 def kv_gather(kv, page_table, length: int, out_k, out_v, stream=None) -> None:

@@ -285,8 +285,9 @@ def attention_case(rng, pos, batch_table_seed):
     return proj, kc, vc
 
 
-@pytest.mark.parametrize("pos", [0, 1, 15, 16, 17, 63, 64, 65, 200, 1000, 2047, 4095])
-def test_attention_positions_permuted_pages(cuda, pos):
+@pytest.mark.parametrize("impl", ["tensor_core", "cuda_core"])
+@pytest.mark.parametrize("pos", [0, 1, 15, 16, 17, 63, 64, 65, 127, 128, 200, 1000, 2047, 4095])
+def test_attention_positions_permuted_pages(cuda, pos, impl):
     rng = np.random.default_rng(pos)
     pool_pages = 300
     table = rng.permutation(pool_pages)[:256].astype(np.uint32)
@@ -301,7 +302,7 @@ def test_attention_positions_permuted_pages(cuda, pos):
     nbytes = qne.attention_scratch_bytes(1)
     scratch = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
     qne.attention_step(dev(proj), dev(norms), 1e7, pool, pool_pages, dev(table), dev(np.array([pos], np.uint32)),
-                       out, 1, scratch, nbytes)
+                       out, 1, scratch, nbytes, impl=impl)
     rope = oracle.rope_table(1e7)
     want = oracle.attention_step(proj, kc16, vc16, pos, norms, rope, kv_f16=True)
     assert rc.rel_err(host(out), want) < 1e-4
@@ -329,7 +330,8 @@ def test_attention_reference_check(cuda, cases):
     assert rc.rel_err(host(out), GOLDEN["attention"]) < 2e-3
 
 
-def test_attention_batched_ragged(cuda):
+@pytest.mark.parametrize("impl", ["tensor_core", "cuda_core"])
+def test_attention_batched_ragged(cuda, impl):
     rng = np.random.default_rng(9)
     B, pool_pages = 5, 5 * 256
     pos = np.array([0, 16, 333, 2500, 4095], np.uint32)
@@ -354,7 +356,7 @@ def test_attention_batched_ragged(cuda):
     rope = oracle.rope_table(1e7)
     for rep in range(2):  # the completion counters reset themselves
         qne.attention_step(dev(proj), dev(norms), 1e7, dpool, pool_pages, dev(tables), dev(pos), out, B, scratch,
-                           nbytes)
+                           nbytes, impl=impl)
         got = host(out)
         for b in range(B):
             want = oracle.attention_step(proj[b], kcs[b].copy(), vcs[b].copy(), int(pos[b]), norms, rope, True)
