@@ -53,6 +53,12 @@ struct PrepArgs {
   uint16_t* xh = nullptr;
   uint16_t* xl = nullptr;
   int ldx = 0;
+  // Optional (chunked prefill): after a GDN scan of conv_n tokens, commit its last three conv
+  // inputs conv_tail[3][6144] to the ring conv_ring[4][6144] at slots (count + conv_n - 3 + j) % 4.
+  const float* conv_tail = nullptr;
+  float* conv_ring = nullptr;
+  const SeqCtl* conv_ctl = nullptr;
+  int conv_n = 0;
 };
 cudaError_t launch_prep(const PrepArgs& a, int batch, cudaStream_t stream, bool pdl);
 

@@ -248,6 +248,13 @@ __global__ void __launch_bounds__(256) prep_kernel(const PrepArgs a) {
   pdl_wait();
   uint16_t* xh = a.xh + (size_t)b * a.ldx;
   uint16_t* xl = a.xl + (size_t)b * a.ldx;
+  if (a.conv_tail) {
+    const uint32_t e = a.conv_ctl->count + (uint32_t)a.conv_n;
+    for (int i = b * 256 + tid; i < 3 * kConvChannels; i += gridDim.x * 256) {
+      const int j = i / kConvChannels, c = i % kConvChannels;
+      a.conv_ring[(size_t)((e - 3u + (uint32_t)j) & 3u) * kConvChannels + c] = a.conv_tail[i];
+    }
+  }
   if (a.mode == kPrepGdnGate) {
     // K == 2048: 16 heads of 128 (warp w: heads 2w, 2w + 1)
     const int warp = tid >> 5, lane = tid & 31;

@@ -30,17 +30,19 @@ using namespace dev;
 
 // ------------------------------------------------------------------------------------------
 // Gated DeltaNet over the chunk (batch::gdn, kernels/src/batch.rs:168-255; per-token math
-// kernels/src/shaders.rs:445-520). One CTA per (16-column slice, head), clustered by head: the
-// CTA keeps its 128 x 16 slice of the state in registers (8 values per thread) for the whole
-// chunk and walks the tokens in order. Per token, threads 0..127 run the causal conv + SiLU of
-// the head's q channels and threads 128..255 of its k channels (windows in registers, seeded from
-// the conv ring); each 16-lane half-warp owns one value column (8 state rows per lane), so the
-// dot products S^T k, S^T q and k . q reduce with shuffles. The conv/SiLU outputs go to a shared
-// buffer indexed by token parity, so one __syncthreads per token suffices.
-//
+// kernels/src/shaders.rs:445-520). One CTA of 512 threads per (16-column slice, head). Only
+// the state recurrence is sequential, so the kernel runs in two phases:
+//  1. everything that does not depend on the state, for all n tokens at once (every input of the
+//     chunk is requested up front, so the token loops wait on no memory): causal conv + SiLU of
+//     the head's q channels (threads 0..127), k channels (128..255) and this slice's v channels
+//     (256..271), windows in registers seeded from the conv ring; decay g and write strength
+//     beta (272..303); then the L2 normalization of q (times 1/sqrt(128)) and k, and k . q;
+//  2. warp w owns value column w of the 128 x 16 state slice (4 rows per lane, in registers for
+//     the whole chunk) and walks the tokens with no block barrier: S^T k and S^T q by warp
+//     shuffles, the rank-1 update, the output.
 // The conv ring holds input j at slot j % 4. All 8 CTAs of a head read the head's q/k ring
-// channels before the chunk; they write the last three inputs back only after a cluster barrier
-// that every CTA of the head passes once its reads are done, so no CTA sees a slot overwritten.
+// channels, so none of them may overwrite a slot: each writes its channels' last three inputs to
+// `tail` instead, and the gated-norm prep kernel that follows commits them to the ring.
 // ------------------------------------------------------------------------------------------
 struct ScanArgs {
   const float* proj;    // [n][8224] mixer_in rows of the chunk
@@ -51,108 +53,126 @@ struct ScanArgs {
   const SeqCtl* ctl;    // ctl->count: tokens processed before the chunk
   int n;
   float* out;           // [n][2048] raw output (before the gated RMSNorm)
+  float* tail;          // [3][6144]: the chunk's last three conv inputs, oldest first
 };
+
+constexpr int kScanRows = 32;  // tokens per chunk
+constexpr int kScanThreads = 512;
 
 struct ScanShared {
-  float qk[2][2 * kGdnDim];  // per token parity: q channels 0..127, k channels 128..255
-  float red[2][8];           // per token parity: per-warp sums of squares
+  __align__(16) float qk[kScanRows][2 * kGdnDim];  // per token: q channels 0..127, k channels 128..255
+  float red[kScanRows][8];                          // per token: per-warp sums of squares
+  float vv[kScanRows][kSlice];                      // per token: conv + SiLU of this slice's v channels
+  float g[kScanRows], beta[kScanRows], kq[kScanRows];
 };
+static_assert(kScanRows == PrefillRunner::kRows, "the scan holds one chunk's tokens");
 
-__device__ __forceinline__ void cluster_arrive() {
-  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
-
-__global__ void __cluster_dims__(kSlices, 1, 1) __launch_bounds__(256) gdn_scan_kernel(const __grid_constant__ ScanArgs a) {
+__global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_kernel(const __grid_constant__ ScanArgs a) {
   __shared__ ScanShared sh;
   const int h = blockIdx.y, t0 = blockIdx.x * kSlice;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int col = warp * 2 + (lane >> 4);  // value column t0 + col
-  const int jg = lane & 15;                // state rows jg * 8 .. jg * 8 + 7
+  const int n = a.n;
+  // phase-1 roles: a q/k channel (tid < 256), a v channel (256 .. 271)
   const int iq = tid & (kGdnDim - 1);
-  const int chqk = (tid < kGdnDim ? 0 : 2048) + h * kGdnDim + iq;
-  const int chv = 4096 + h * kGdnDim + t0 + col;
+  const bool is_qk = tid < 2 * kGdnDim, is_v = tid >= 2 * kGdnDim && tid < 2 * kGdnDim + kSlice;
+  const int ch = is_qk ? (tid < kGdnDim ? 0 : 2048) + h * kGdnDim + iq : 4096 + h * kGdnDim + t0 + (tid & 15);
   pdl_launch();
   pdl_wait();
   const uint32_t cnt0 = a.ctl->count;
-  const float4 w = *reinterpret_cast<const float4*>(a.conv_w + (size_t)chqk * 4);
-  const float4 wv = *reinterpret_cast<const float4*>(a.conv_w + (size_t)chv * 4);
-  const float* ring = a.conv;
   const int r0 = (int)((cnt0 - 3u) & 3u), r1 = (int)((cnt0 - 2u) & 3u), r2 = (int)((cnt0 - 1u) & 3u);
-  float x0 = ring[r0 * kConvChannels + chqk], x1 = ring[r1 * kConvChannels + chqk], x2 = ring[r2 * kConvChannels + chqk];
-  float v0 = ring[r0 * kConvChannels + chv], v1 = ring[r1 * kConvChannels + chv], v2 = ring[r2 * kConvChannels + chv];
-  float* S = a.state + (size_t)h * kGdnDim * kGdnDim + (size_t)(jg * 8) * kGdnDim + t0 + col;
-  float sv[8];
+  const bool conv_thread = is_qk || is_v;
+  float4 w = make_float4(0.f, 0.f, 0.f, 0.f);
+  float x0 = 0.f, x1 = 0.f, x2 = 0.f;
+  float xs[kScanRows];
+  if (conv_thread) {
+    w = *reinterpret_cast<const float4*>(a.conv_w + (size_t)ch * 4);
+    x0 = a.conv[r0 * kConvChannels + ch];
+    x1 = a.conv[r1 * kConvChannels + ch];
+    x2 = a.conv[r2 * kConvChannels + ch];
 #pragma unroll
-  for (int jj = 0; jj < 8; ++jj) sv[jj] = S[(size_t)jj * kGdnDim];
-  cluster_arrive();  // this CTA is done reading the ring
-  const float A = a.params[16 + h], dt_bias = a.params[h];
-  const float* pr = a.proj;
-  float xn = pr[chqk], xvn = pr[chv], an = pr[8192 + h], bn = pr[8208 + h];
+    for (int i = 0; i < kScanRows; ++i) xs[i] = i < n ? a.proj[(size_t)i * kGdnProj + ch] : 0.f;
+  }
+  // phase-2 role: value column `warp`, state rows 4 lane .. 4 lane + 3
+  float* S = a.state + (size_t)h * kGdnDim * kGdnDim + (size_t)(lane * 4) * kGdnDim + t0 + warp;
+  float sv[4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) sv[r] = S[(size_t)r * kGdnDim];
+
+  // ---- phase 1 ----
+  const int gt = tid - (2 * kGdnDim + kSlice);
+  if (gt >= 0 && gt < n) {
+    const float* pr = a.proj + (size_t)gt * kGdnProj;
+    sh.g[gt] = expf(a.params[16 + h] * logf(1.0f + expf(pr[8192 + h] + a.params[h])));
+    sh.beta[gt] = 1.0f / (1.0f + expf(-pr[8208 + h]));
+  }
+  if (conv_thread) {
+#pragma unroll
+    for (int i = 0; i < kScanRows; ++i) {
+      if (i < n) {
+        const float y = x0 * w.x + x1 * w.y + x2 * w.z + xs[i] * w.w;
+        x0 = x1;
+        x1 = x2;
+        x2 = xs[i];
+        const float val = silu(y);
+        if (is_qk) {
+          sh.qk[i][tid] = val;
+          const float ss = warp_sum(val * val);
+          if (lane == 0) sh.red[i][warp] = ss;
+        } else {
+          sh.vv[i][tid & 15] = val;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  for (int e = tid; e < n * 2 * kGdnDim; e += kScanThreads) {
+    const int i = e >> 8, c = e & 255;
+    const float* r = sh.red[i];
+    sh.qk[i][c] *= c < kGdnDim ? rsqrtf(r[0] + r[1] + r[2] + r[3] + 1e-6f) * 0.08838834764f
+                               : rsqrtf(r[4] + r[5] + r[6] + r[7] + 1e-6f);
+  }
+  __syncthreads();
+  for (int i = warp; i < n; i += kScanThreads / 32) {
+    float p = 0.f;
+#pragma unroll
+    for (int c = lane; c < kGdnDim; c += 32) p = fmaf(sh.qk[i][kGdnDim + c], sh.qk[i][c], p);
+    p = warp_sum(p);
+    if (lane == 0) sh.kq[i] = p;
+  }
+  __syncthreads();
+
+  // ---- phase 2: the recurrence, one value column per warp, no block barrier ----
 #pragma unroll 1
-  for (int i = 0; i < a.n; ++i) {
-    const float x = xn, xv = xvn, ar = an, br = bn;
-    if (i + 1 < a.n) {
-      pr += kGdnProj;
-      xn = pr[chqk];
-      xvn = pr[chv];
-      an = pr[8192 + h];
-      bn = pr[8208 + h];
-    }
-    const float y = x0 * w.x + x1 * w.y + x2 * w.z + x * w.w;
-    x0 = x1;
-    x1 = x2;
-    x2 = x;
-    const float val = silu(y);
-    const float ss = warp_sum(val * val);
-    const int buf = i & 1;
-    sh.qk[buf][tid] = val;
-    if (lane == 0) sh.red[buf][warp] = ss;
-    const float yv = v0 * wv.x + v1 * wv.y + v2 * wv.z + xv * wv.w;
-    v0 = v1;
-    v1 = v2;
-    v2 = xv;
-    const float vv = silu(yv);
-    const float g = expf(A * logf(1.0f + expf(ar + dt_bias)));
-    const float beta = 1.0f / (1.0f + expf(-br));
-    __syncthreads();
-    const float nq = rsqrtf(sh.red[buf][0] + sh.red[buf][1] + sh.red[buf][2] + sh.red[buf][3] + 1e-6f);
-    const float nk = rsqrtf(sh.red[buf][4] + sh.red[buf][5] + sh.red[buf][6] + sh.red[buf][7] + 1e-6f);
-    float kk[8], sk = 0.f, sq = 0.f, kq = 0.f;
+  for (int i = 0; i < n; ++i) {
+    const float4 q4 = *reinterpret_cast<const float4*>(&sh.qk[i][lane * 4]);
+    const float4 k4 = *reinterpret_cast<const float4*>(&sh.qk[i][kGdnDim + lane * 4]);
+    float sk = sv[0] * k4.x, sq = sv[0] * q4.x;
+    sk = fmaf(sv[1], k4.y, sk);
+    sq = fmaf(sv[1], q4.y, sq);
+    sk = fmaf(sv[2], k4.z, sk);
+    sq = fmaf(sv[2], q4.z, sq);
+    sk = fmaf(sv[3], k4.w, sk);
+    sq = fmaf(sv[3], q4.w, sq);
 #pragma unroll
-    for (int jj = 0; jj < 8; ++jj) {
-      const float qv = sh.qk[buf][jg * 8 + jj] * nq * 0.08838834764f;
-      kk[jj] = sh.qk[buf][kGdnDim + jg * 8 + jj] * nk;
-      sk = fmaf(sv[jj], kk[jj], sk);
-      sq = fmaf(sv[jj], qv, sq);
-      kq = fmaf(kk[jj], qv, kq);
-    }
-#pragma unroll
-    for (int o = 1; o < 16; o <<= 1) {
+    for (int o = 16; o > 0; o >>= 1) {
       sk += __shfl_xor_sync(0xffffffffu, sk, o);
       sq += __shfl_xor_sync(0xffffffffu, sq, o);
-      kq += __shfl_xor_sync(0xffffffffu, kq, o);
     }
-    const float dv = beta * (vv - g * sk);
-#pragma unroll
-    for (int jj = 0; jj < 8; ++jj) sv[jj] = g * sv[jj] + dv * kk[jj];
-    if (jg == 0) a.out[(size_t)i * kMixerOut + h * kGdnDim + t0 + col] = g * sq + dv * kq;
+    const float g = sh.g[i];
+    const float dv = sh.beta[i] * (sh.vv[i][warp] - g * sk);
+    sv[0] = g * sv[0] + dv * k4.x;
+    sv[1] = g * sv[1] + dv * k4.y;
+    sv[2] = g * sv[2] + dv * k4.z;
+    sv[3] = g * sv[3] + dv * k4.w;
+    if (lane == 0) a.out[(size_t)i * kMixerOut + h * kGdnDim + t0 + warp] = g * sq + dv * sh.kq[i];
   }
 #pragma unroll
-  for (int jj = 0; jj < 8; ++jj) S[(size_t)jj * kGdnDim] = sv[jj];
-  cluster_wait();  // every CTA of this head is done reading the ring
-  float* wr = a.conv;
-  const uint32_t e = cnt0 + (uint32_t)a.n;  // tokens processed after the chunk
-  const int w0 = (int)((e - 3u) & 3u), w1 = (int)((e - 2u) & 3u), w2 = (int)((e - 1u) & 3u);
-  if (iq >= t0 && iq < t0 + kSlice) {  // this slice's share of the head's q and k channels
-    wr[w0 * kConvChannels + chqk] = x0;
-    wr[w1 * kConvChannels + chqk] = x1;
-    wr[w2 * kConvChannels + chqk] = x2;
-  }
-  if (jg == 0) {
-    wr[w0 * kConvChannels + chv] = v0;
-    wr[w1 * kConvChannels + chv] = v1;
-    wr[w2 * kConvChannels + chv] = v2;
+  for (int r = 0; r < 4; ++r) S[(size_t)r * kGdnDim] = sv[r];
+  // this slice's share of the head's q and k channels, and its own v channels
+  if ((is_qk && iq >= t0 && iq < t0 + kSlice) || is_v) {
+    a.tail[ch] = x0;
+    a.tail[kConvChannels + ch] = x1;
+    a.tail[2 * kConvChannels + ch] = x2;
   }
 }
 
@@ -257,6 +277,7 @@ PrefillRunner::PrefillRunner(Model* model, Runner* single) : m(model), r(single)
   for (auto* p : {x1h, x1l}) cuda_check(cudaMemset(p, 0, (size_t)kRows * c.inter * 2), "memset");
   rows = static_cast<SeqCtl*>(m->alloc((size_t)kRows * sizeof(SeqCtl)));
   cuda_check(cudaMemset(rows, 0, (size_t)kRows * sizeof(SeqCtl)), "memset");
+  conv_tail = static_cast<float*>(m->alloc((size_t)3 * kConvChannels * 4));
   attn_scratch = m->alloc(attention_scratch_bytes(kRows));
   cuda_check(cudaMemset(attn_scratch, 0, attention_scratch_bytes(kRows)), "memset");
   cuda_check(cudaMallocHost(&pinned, (size_t)kMaxContext * sizeof(SeqCtl)), "cudaMallocHost");
@@ -348,14 +369,18 @@ void PrefillRunner::record(int n, cudaStream_t s) {
       ++cnt;
       q.mode = kPrepCopy;
     } else {
-      const ScanArgs sa{proj, r->st.conv[i], L.conv_w, r->st.rec[i], L.gdn_params, r->st.ctl, n, raw};
-      cudaLaunchConfig_t cfg = make_cfg(dim3(kSlices, kGdnHeads), dim3(256), s, true, attr);
+      const ScanArgs sa{proj, r->st.conv[i], L.conv_w, r->st.rec[i], L.gdn_params, r->st.ctl, n, raw, conv_tail};
+      cudaLaunchConfig_t cfg = make_cfg(dim3(kSlices, kGdnHeads), dim3(kScanThreads), s, true, attr);
       count_launch();
       cuda_check(cudaLaunchKernelEx(&cfg, gdn_scan_kernel, sa), "gdn scan launch");
       ++cnt;
       q.mode = kPrepGdnGate;
       q.zgate = proj;
       q.norm_w = L.gdn_params + 32;
+      q.conv_tail = conv_tail;  // the prep also commits the scan's conv inputs to the ring
+      q.conv_ring = r->st.conv[i];
+      q.conv_ctl = r->st.ctl;
+      q.conv_n = n;
     }
     prep(q);
     gemm(L.out, x0h, x0l, ldx0, kAccumulate, h, nullptr, nullptr, c.hidden);

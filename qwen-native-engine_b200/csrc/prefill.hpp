@@ -43,6 +43,7 @@ class PrefillRunner {
   SeqCtl* rows = nullptr;    // [kRows] device: (token, position) of each chunk row
   SeqCtl* pinned = nullptr;  // [kMaxContext] host staging of the rows of one call
   void* attn_scratch = nullptr;
+  float* conv_tail = nullptr;  // [3][6144] last conv inputs of a chunk, from the GDN scan to the prep
   std::map<int, cudaGraphExec_t> graphs;
   std::map<int, size_t> launches;
 };
