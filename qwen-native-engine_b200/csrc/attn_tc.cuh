@@ -27,8 +27,10 @@ struct AttnTcShared {
   __align__(16) float q_s[kQPerKv][kHeadDim];
   __align__(16) float kc_s[kHeadDim];  // the current token's key and value (f16-rounded)
   __align__(16) float vc_s[kHeadDim];
-  float spart[2][kQPerKv][kSub];  // scores of the two dim halves
-  float sc[kQPerKv][kSub];        // probabilities of the sub-block
+  // Rows padded by 8 floats so the 4 heads' rows start in different banks (the PV fragment loads
+  // read the same token offset of all 4 heads at once).
+  float spart[2][kQPerKv][kSub + 8];  // scores of the two dim halves
+  float sc[kQPerKv][kSub + 8];        // probabilities of the sub-block
   float red[8][kQPerKv];
   float redk[8];
   float blk_scale[kQPerKv];

@@ -10,7 +10,7 @@
 //  * a tile is 128 weight rows (SwiGLU: 64 gate rows and the matching 64 up rows) by the whole
 //    activation batch (N = 16 or 32 columns of the MMA, zero-filled past the batch);
 //  * warp 0 lane 0 streams 64-wide k-blocks of the weight tile and of both activation planes
-//    with TMA (128-byte swizzle, the canonical K-major layout of the MMA operands) into a 3-stage
+//    with TMA (128-byte swizzle, the canonical K-major layout of the MMA operands) into a 6-stage
 //    ring guarded by mbarriers; weight loads of the first stages are issued before waiting on the
 //    previous kernel, whose output the activations are;
 //  * warp 1 lane 0 issues tcgen05.mma (M = 128, K = 16, f32 accumulator in tensor memory), two
@@ -36,11 +36,11 @@ namespace qne {
 namespace {
 
 constexpr int kTcThreads = 128;
-constexpr int kTcStages = 3;
+constexpr int kTcStages = 6;
 constexpr int kBK = 64;                 // k per stage: one 128-byte swizzle span of f16
 constexpr int kTileA = 128 * kBK * 2;   // 16 KB of weights per stage
 constexpr int kMaxCluster = 8;
-constexpr int kCtaSlots = 3 * kNumSms;  // three CTAs per SM fit (about 73 KB of shared memory each)
+constexpr int kCtaSlots = kNumSms;  // one CTA per SM fits (about 145 KB of shared memory)
 
 struct TcArgs {
   int out_rows;     // output rows (SwiGLU: rows / 2)
@@ -381,7 +381,7 @@ int max_clusters(K kernel, size_t smem, int ranks) {
   int n = 0;
   if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess) {
     cudaGetLastError();
-    n = kCtaSlots / ranks;  // fall back to the three-CTAs-per-SM estimate
+    n = kCtaSlots / ranks;  // fall back to the one-CTA-per-SM estimate
   }
   cache[key] = n;
   return n;
