@@ -8,8 +8,11 @@ path; NCCL is used only for the barrier and the max-over-ranks timing).
 
   value   device-resident greedy decode (CUDA-graph replays, GPU argmax feeding the next
           embedding), CUDA events on the engine's stream, max over ranks.
-  e2e     the reference's agent loop through the public API: qne_step(token, pos) per token with
-          the logits (993 KB f32) read back to pinned host memory and the greedy pick on the host.
+  e2e     the agent's per-token loop through the public API with device sampling:
+          qne_step_sample(token, pos) with the reference's default sampling options (temperature
+          0.6, top_k 20, top_p 0.95), 8 bytes (token id) in and 8 bytes (token, status) out per
+          token. `e2e_host_logits` is the reference agent's own loop: qne_step per token with the
+          logits (993 KB f32) read back to pinned host memory and the pick made on the host.
   roofline  the dominant kernel (f16 GEMV, SwiGLU gate_up of all 24 layers) timed live with CUDA
           events: algorithmic bytes per launch / mean launch time vs MEASURED_PEAKS.json.
   cpu_baseline  the CPU oracle (C++ restatement of the reference decoder) on the host cores,
@@ -555,6 +558,23 @@ def main():
         tok = int(np.argmax(logits))
     e2e_s = max_over_ranks(time.perf_counter() - t0)
 
+    # e2e: the same loop with the draw on the device (qne_step_sample, reference sampling defaults)
+    sampler = qne.Sampler(model, temperature=0.6, top_k=20, top_p=0.95, seed=rank_seed(42, rank))
+    model.restore()
+    model.sync()
+    tok, pos = model.last_token()
+    for i in range(min(args.warmup, 2)):
+        model.step_sample(sampler, tok, pos)
+    model.restore()
+    model.sync()
+    tok, pos = model.last_token()
+    barrier()
+    t0 = time.perf_counter()
+    for i in range(steps):
+        tok = model.step_sample(sampler, tok, pos + i)
+    e2e_sampled_s = max_over_ranks(time.perf_counter() - t0)
+    sampler.close()
+
     # the dominant kernel, timed live
     gemv_ms, gemv_bytes = time_gemv_family(model, torch)
     peak, peak_kind = peaks()
@@ -610,8 +630,12 @@ def main():
                        "model": f"qwen3.5-{size_name.lower()}-shaped", "global_batch": world, "seq_len": 4096,
                        "parallelism": f"replicas x{world}",
                        "l2": f"inputs larger than L2 ({model.weight_bytes / 1e9:.2f} GB of weights per step)"},
-            "e2e": {"value": round(aggregate_rate(world, steps, e2e_s * 1e3), 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
-                    "d2h_bytes_per_step": model.vocab * 4},
+            "e2e": {"value": round(aggregate_rate(world, steps, e2e_sampled_s * 1e3), 2), "unit": "tok/s",
+                    "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8,
+                    "loop": "qne_step_sample: decode step + device sampling (T 0.6, top_k 20, top_p 0.95)"},
+            "e2e_host_logits": {"value": round(aggregate_rate(world, steps, e2e_s * 1e3), 2), "unit": "tok/s",
+                                "h2d_bytes_per_step": 8, "d2h_bytes_per_step": model.vocab * 4,
+                                "loop": "qne_step + logits to pinned host memory + host pick (the reference agent's)"},
             "roofline": roof,
             "step_roofline": {"bytes_per_token": int(tok_bytes), "achieved_gbs": round(tok_bytes * value / world / 1e9, 1),
                               "frac": round(tok_bytes * value / world / 1e9 / peak, 4)},

@@ -151,6 +151,40 @@ QNE_API qne_status qne_prefill_chunk(qne_model* m, const uint32_t* ids, uint32_t
                              int finish_logits);
 /* 1 if qne_prefill_chunk runs batched chunks on this model, 0 if one token per step. */
 QNE_API int qne_prefill_chunk_batched(const qne_model* m);
+/* Token sampling on the device (Sampler, src/sampling.rs:30-134, the agent's sampler; the
+ * reference samples on the host after reading the logits back). A sampler draws from the model's
+ * current logits (after qne_step, qne_prefill or qne_prefill_chunk with finish_logits) and
+ * returns only the token: greedy when temperature <= 0, else temperature + top_k (1..256 here;
+ * 0 counts as 1) + top_p over the allowed tokens, drawing from the reference's xorshift64
+ * generator seeded with `seed`. presence_penalty is subtracted from the logit of every token this
+ * sampler already returned, except when a mask is given. Equal logits rank by lower token index.
+ * Free every sampler before its model. */
+typedef struct qne_sampling {
+  float temperature;
+  uint32_t top_k;
+  float top_p;
+  uint64_t seed;
+  float presence_penalty;
+} qne_sampling;
+typedef struct qne_sampler qne_sampler;
+QNE_API qne_status qne_sampler_create(qne_model* m, const qne_sampling* opts, qne_sampler** out);
+QNE_API void qne_sampler_free(qne_sampler* s);
+/* Sampler::try_sample (src/sampling.rs:58-67) with the agent's tool-call bias
+ * (agent/src/session.rs:400-404): `bias` is added to logit `bias_token` first (bias 0: none).
+ * mask (host, optional): bit (i % 32) of word i / 32 allows token i; tokens at or past
+ * mask_tokens are not allowed. Fails with QNE_EINVAL and the reference's messages ("non-finite
+ * model logits", "no finite token is allowed by the sampling mask"); a failed draw leaves the
+ * generator where it was. */
+QNE_API qne_status qne_sampler_sample(qne_sampler* s, const uint32_t* mask, uint32_t mask_tokens, int32_t bias_token,
+                              float bias, uint32_t* token_out);
+/* The same draw from `logits` (DEVICE, vocab floats of the sampler's model) instead of the
+ * model's own logits (operator level: sampling any row, e.g. one sequence of a batch). */
+QNE_API qne_status qne_sampler_sample_device(qne_sampler* s, const float* logits, const uint32_t* mask,
+                                     uint32_t mask_tokens, int32_t bias_token, float bias, uint32_t* token_out);
+/* qne_step (no logits copied to the host) followed by qne_sampler_sample: the agent's per-token
+ * loop (agent/src/session.rs:390-420) with 8 bytes of readback instead of vocab floats. */
+QNE_API qne_status qne_step_sample(qne_model* m, qne_sampler* s, uint32_t token, uint32_t pos, const uint32_t* mask,
+                           uint32_t mask_tokens, int32_t bias_token, float bias, uint32_t* token_out);
 /* Model::logits, kernels/src/model.rs:374: copies vocab f32 logits to host `out`. */
 QNE_API qne_status qne_logits(qne_model* m, float* out, size_t out_len);
 /* Model::step, kernels/src/model.rs:380: feeds `token` at `pos`, returns the next-token logits

@@ -27,18 +27,6 @@ void cuda_check(cudaError_t e, const char* what) {
 
 namespace {
 
-struct DeviceGuard {
-  int prev = -1;
-  explicit DeviceGuard(int dev) {
-    cudaGetDevice(&prev);
-    if (prev != dev) cuda_check(cudaSetDevice(dev), "cudaSetDevice");
-  }
-  ~DeviceGuard() {
-    int cur = -1;
-    cudaGetDevice(&cur);
-    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
-  }
-};
 
 struct TensorEntry {
   uint64_t offset = 0, bytes = 0;

@@ -28,6 +28,20 @@ constexpr int kEInval = -1, kERangeCtx = -2, kEFormat = -3, kECuda = -4, kETimeo
 
 void cuda_check(cudaError_t e, const char* what);
 
+// Makes `dev` current for the guard's lifetime (the previous device is restored).
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cuda_check(cudaSetDevice(dev), "cudaSetDevice");
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
 struct LayerWeights {
   bool attention = false;
   Mat in, out, gate_up, down;

@@ -16,6 +16,7 @@ operation falls back to another implementation.
 from __future__ import annotations
 
 import ctypes as C
+import weakref
 import os
 from pathlib import Path
 
@@ -47,6 +48,11 @@ class QneError(RuntimeError):
 class _Matrix(C.Structure):
     _fields_ = [("kind", C.c_int32), ("rows", C.c_int32), ("k", C.c_int32), ("pad", C.c_int32),
                 ("w", C.c_void_p), ("s", C.c_void_p), ("z", C.c_void_p)]
+
+
+class _Sampling(C.Structure):
+    _fields_ = [("temperature", C.c_float), ("top_k", C.c_uint32), ("top_p", C.c_float), ("seed", C.c_uint64),
+                ("presence_penalty", C.c_float)]
 
 
 class _Info(C.Structure):
@@ -120,6 +126,11 @@ def _load_lib() -> C.CDLL:
         "qne_attention_step_ex": (I32, [P, P, C.c_double, P, U32, P, P, P, I32, P, SZ, I32, P]),
         "qne_kv_gather": (I32, [P, P, U32, P, P, P]),
         "qne_bandwidth_probe": (I32, [P, SZ, P, P]),
+        "qne_sampler_create": (I32, [P, C.POINTER(_Sampling), C.POINTER(P)]),
+        "qne_sampler_free": (None, [P]),
+        "qne_sampler_sample": (I32, [P, U32P, U32, C.c_int32, C.c_float, U32P]),
+        "qne_sampler_sample_device": (I32, [P, P, U32P, U32, C.c_int32, C.c_float, U32P]),
+        "qne_step_sample": (I32, [P, P, U32, U32, U32P, U32, C.c_int32, C.c_float, U32P]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(lib, name)
@@ -202,6 +213,10 @@ class Model:
         return cls(index_json, weights, device)
 
     def close(self) -> None:
+        for ref in getattr(self, "_samplers", []):  # samplers are freed before their model
+            smp = ref()
+            if smp is not None:
+                smp.close()
         if getattr(self, "_h", None):
             lib.qne_model_free(self._h)
             self._h = None
@@ -253,6 +268,15 @@ class Model:
         out = np.empty(self.vocab, np.float32) if out is None else out
         _check(lib.qne_step(self._h, token, pos, _fp(out), out.size))
         return out
+
+    def step_sample(self, sampler: "Sampler", token: int, pos: int, mask=None, bias_token: int = -1,
+                    bias: float = 0.0) -> int:
+        """qne_step_sample: one step, then a draw on the device; returns only the token."""
+        words, n = _mask_words(mask)
+        out = C.c_uint32()
+        _check(lib.qne_step_sample(self._h, sampler._h, token, pos, _u32p(words) if words is not None else None, n,
+                                   bias_token, float(bias), C.byref(out)))
+        return int(out.value)
 
     def snapshot(self) -> None:
         _check(lib.qne_snapshot(self._h))
@@ -477,6 +501,55 @@ def gemm(m: _Matrix, x, batch: int, y, epilogue="store", scratch=None, scratch_b
         _check(lib.qne_gemm(C.byref(m), _ptr(x), batch, _ptr(y), epi, _ptr(scratch), scratch_bytes, _stream(stream)))
     else:
         _check(lib.qne_gemm_ex(C.byref(m), _ptr(x), batch, _ptr(y), epi, GEMM_IMPLS[impl], _stream(stream)))
+
+
+def _mask_words(mask):
+    """Allowed-token mask (bool array, length = mask tokens) -> (uint32 words, mask tokens)."""
+    if mask is None:
+        return None, 0
+    m = np.asarray(mask, dtype=bool)
+    bits = np.zeros((m.size + 31) // 32 * 32, dtype=bool)
+    bits[: m.size] = m
+    words = np.packbits(bits.reshape(-1, 32)[:, ::-1], axis=1).view(">u4").astype(np.uint32).ravel()
+    return np.ascontiguousarray(words), m.size
+
+
+class Sampler:
+    """Device-side token sampler of one generation (qne_sampler_*): the reference's
+    Sampler::try_sample (src/sampling.rs) over the model's current logits or a device row."""
+
+    def __init__(self, model: Model, temperature: float = 0.6, top_k: int = 20, top_p: float = 0.95, seed: int = 42,
+                 presence_penalty: float = 0.0):
+        opts = _Sampling(temperature, top_k, top_p, seed, presence_penalty)
+        h = C.c_void_p()
+        _check(lib.qne_sampler_create(model._h, C.byref(opts), C.byref(h)))
+        self._h = h
+        self.model = model
+        if not hasattr(model, "_samplers"):
+            model._samplers = []
+        model._samplers.append(weakref.ref(self))
+
+    def sample(self, mask=None, bias_token: int = -1, bias: float = 0.0, logits=None) -> int:
+        """Draw from the model's logits, or from `logits` (a device tensor of vocab floats)."""
+        words, n = _mask_words(mask)
+        out = C.c_uint32()
+        mp = _u32p(words) if words is not None else None
+        if logits is None:
+            _check(lib.qne_sampler_sample(self._h, mp, n, bias_token, float(bias), C.byref(out)))
+        else:
+            _check(lib.qne_sampler_sample_device(self._h, _ptr(logits), mp, n, bias_token, float(bias), C.byref(out)))
+        return int(out.value)
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib.qne_sampler_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 if os.environ.get("QNE_PRINT_VERSION"):
