@@ -4,11 +4,12 @@
 // same per-token graph (kernels/src/model.rs:220-269) to `batch` sequences at once, each with its
 // own GDN conv windows and recurrent states, its own position, and its own page table into a
 // shared pool of 16-token f16 KV pages. Per step and layer:
-//   prep (RMSNorm -> hi/lo) | GEMM mixer_in | GDN step + gated norm prep, or paged attention +
-//   copy prep | GEMM mixer_out (+= h) | prep (RMSNorm) | GEMM gate_up (SwiGLU -> hi/lo) |
-//   GEMM down (+= h);  then prep (final norm) | GEMM lm_head | per-sequence greedy pick.
-// All launches of one step are captured once into a CUDA graph (programmatic dependent launch
-// between kernels).
+//   GEMM mixer_in | GDN step + gated norm prep, or paged attention + copy prep | GEMM mixer_out
+//   (+= h) | GEMM gate_up (SwiGLU -> hi/lo) | GEMM down (+= h);  before the first layer the
+//   embedding prep, after the last the GEMM lm_head and the per-sequence greedy pick.
+// The RMSNorms before mixer_in, gate_up and the LM head are folded into the GEMMs on either side
+// (GemmArgs::norm_w_out / sumsq_in), so a step is 6 launches per layer plus 3. All launches of one
+// step are captured once into a CUDA graph (programmatic dependent launch between kernels).
 #include <chrono>
 #include <cstring>
 #include <string>
@@ -32,6 +33,8 @@ class BatchRunner {
   SeqState st;
   float *h = nullptr, *proj = nullptr, *raw = nullptr, *logits = nullptr;
   uint16_t *x0h = nullptr, *x0l = nullptr, *x1h = nullptr, *x1l = nullptr;
+  uint16_t *xnh = nullptr, *xnl = nullptr;  // planes of h * norm weight (RMSNorm folded into the GEMMs)
+  float* sumsq = nullptr;                   // [hidden / 16][32] partial sums of h^2
   int ldx0 = 0;
   uint32_t* picks = nullptr;
   void* argmax_scratch = nullptr;
@@ -99,6 +102,11 @@ BatchRunner::BatchRunner(Model* model, int batch, uint32_t pool) : m(model), B(b
   x1l = static_cast<uint16_t*>(m->alloc((size_t)Bp * c.inter * 2));
   for (auto* p : {x0h, x0l}) cuda_check(cudaMemset(p, 0, (size_t)Bp * ldx0 * 2), "memset");
   for (auto* p : {x1h, x1l}) cuda_check(cudaMemset(p, 0, (size_t)Bp * c.inter * 2), "memset");
+  xnh = static_cast<uint16_t*>(m->alloc((size_t)Bp * c.hidden * 2));
+  xnl = static_cast<uint16_t*>(m->alloc((size_t)Bp * c.hidden * 2));
+  for (auto* p : {xnh, xnl}) cuda_check(cudaMemset(p, 0, (size_t)Bp * c.hidden * 2), "memset");
+  sumsq = static_cast<float*>(m->alloc((size_t)(c.hidden / 16) * 32 * 4));
+  cuda_check(cudaMemset(sumsq, 0, (size_t)(c.hidden / 16) * 32 * 4), "memset");
   picks = static_cast<uint32_t*>(m->alloc((size_t)B * 4));
   argmax_scratch = m->alloc(argmax_batched_scratch_bytes(B));
   cuda_check(cudaMemset(argmax_scratch, 0, argmax_batched_scratch_bytes(B)), "memset");
@@ -125,8 +133,11 @@ void BatchRunner::record(bool greedy, cudaStream_t s) {
     cuda_check(launch_prep(p, B, s, true), "prep launch");
     ++n;
   };
+  // RMSNorm folded into the GEMMs: the GEMM that updates h writes the planes of h * (next norm
+  // weight) and partial sums of h^2; the GEMM that reads those planes applies 1 / rms.
+  const int slots = c.hidden / 16;
   auto gemm = [&](const Mat& w, const uint16_t* xh, const uint16_t* xl, int ldx, int epi, float* y, uint16_t* yh,
-                  uint16_t* yl, int ldy) {
+                  uint16_t* yl, int ldy, const float* norm_out, bool norm_in) {
     if (w.kind != kF16) throw QneError(kEInval, "batched decode supports f16 weights only");
     GemmArgs g;
     g.w = w.w;
@@ -142,28 +153,42 @@ void BatchRunner::record(bool greedy, cudaStream_t s) {
     g.yh = yh;
     g.yl = yl;
     g.ldy = ldy;
+    if (norm_out) {
+      g.norm_w_out = norm_out;
+      g.out_xh = xnh;
+      g.out_xl = xnl;
+      g.out_ldx = c.hidden;
+      g.sumsq_out = sumsq;
+    }
+    if (norm_in) {
+      g.sumsq_in = sumsq;
+      g.sumsq_slots = slots;
+      g.norm_k = c.hidden;
+    }
     if (const char* why = check_gemm(g)) throw QneError(kEInval, why);
     cuda_check(launch_gemm(g, s, true), "gemm launch");
     ++n;
   };
+  {
+    PrepArgs p;  // embedding rows -> h, planes of h * input_norm[0], sums of squares
+    p.mode = kPrepEmbedNorm;
+    p.k = c.hidden;
+    p.norm_w = M.layers[0].input_norm;
+    p.embed = M.embed;
+    p.ctl = st.ctl;
+    p.h = h;
+    p.ldh = c.hidden;
+    p.sumsq_out = sumsq;
+    p.sumsq_slots = slots;
+    p.xh = xnh;
+    p.xl = xnl;
+    p.ldx = c.hidden;
+    cuda_check(launch_prep(p, B, s, true), "prep launch");
+    ++n;
+  }
   for (int i = 0; i < c.layers; ++i) {
     const LayerWeights& L = M.layers[i];
-    PrepArgs p;
-    p.k = c.hidden;
-    p.norm_w = L.input_norm;
-    if (i == 0) {
-      p.mode = kPrepEmbedNorm;
-      p.embed = M.embed;
-      p.ctl = st.ctl;
-      p.h = h;
-      p.ldh = c.hidden;
-    } else {
-      p.mode = kPrepNorm;
-      p.src = h;
-      p.lds = c.hidden;
-    }
-    prep(p);
-    gemm(L.in, x0h, x0l, ldx0, kStore, proj, nullptr, nullptr, L.in.rows);
+    gemm(L.in, xnh, xnl, c.hidden, kStore, proj, nullptr, nullptr, L.in.rows, nullptr, true);
     PrepArgs q;
     q.k = kMixerOut;
     q.src = raw;
@@ -195,25 +220,12 @@ void BatchRunner::record(bool greedy, cudaStream_t s) {
       q.norm_w = L.gdn_params + 32;
     }
     prep(q);
-    gemm(L.out, x0h, x0l, ldx0, kAccumulate, h, nullptr, nullptr, c.hidden);
-    PrepArgs r;
-    r.mode = kPrepNorm;
-    r.k = c.hidden;
-    r.src = h;
-    r.lds = c.hidden;
-    r.norm_w = L.post_norm;
-    prep(r);
-    gemm(L.gate_up, x0h, x0l, ldx0, kSwiGlu, nullptr, x1h, x1l, c.inter);
-    gemm(L.down, x1h, x1l, c.inter, kAccumulate, h, nullptr, nullptr, c.hidden);
+    gemm(L.out, x0h, x0l, ldx0, kAccumulate, h, nullptr, nullptr, c.hidden, L.post_norm, false);
+    gemm(L.gate_up, xnh, xnl, c.hidden, kSwiGlu, nullptr, x1h, x1l, c.inter, nullptr, true);
+    const float* next_norm = i + 1 < c.layers ? M.layers[i + 1].input_norm : M.final_norm;
+    gemm(L.down, x1h, x1l, c.inter, kAccumulate, h, nullptr, nullptr, c.hidden, next_norm, false);
   }
-  PrepArgs f;
-  f.mode = kPrepNorm;
-  f.k = c.hidden;
-  f.src = h;
-  f.lds = c.hidden;
-  f.norm_w = M.final_norm;
-  prep(f);
-  gemm(M.lm_head, x0h, x0l, ldx0, kStore, logits, nullptr, nullptr, c.vocab);
+  gemm(M.lm_head, xnh, xnl, c.hidden, kStore, logits, nullptr, nullptr, c.vocab, nullptr, true);
   cuda_check(launch_argmax_batched(logits, (uint32_t)c.vocab, (size_t)c.vocab, B, st.ctl, picks, argmax_scratch,
                                    greedy ? 1 : 0, s, true),
              "argmax launch");

@@ -29,6 +29,21 @@ struct GemmArgs {
   int x_rows = 0;           // rows allocated in xh/xl (0: 8 * ceil(batch / 8))
   int impl = kGemmTensorCore;
   uint32_t* err = nullptr;  // optional: receives kFlagTimeout if a bounded wait gives up
+  // RMSNorm folded into the GEMMs on either side of it (tensor-core kernel only). Producer (an
+  // accumulating GEMM that updates the residual h): also writes the planes out_xh/out_xl of
+  // h * norm_w_out for the next GEMM and, per 16-row block of h and per column b,
+  // sumsq_out[block * 32 + b] = sum of h^2. Consumer (the next GEMM, which reads those planes):
+  // scales column b of its result by rsqrt(sum_q sumsq_in[q * 32 + b] / norm_k + eps) before
+  // the epilogue (for SwiGLU, both halves).
+  const float* norm_w_out = nullptr;
+  uint16_t* out_xh = nullptr;
+  uint16_t* out_xl = nullptr;
+  int out_ldx = 0;
+  float* sumsq_out = nullptr;
+  const float* sumsq_in = nullptr;
+  int sumsq_slots = 0;
+  int norm_k = 0;
+  float eps = 1e-6f;
 };
 int gemm_row_groups(int out_rows);
 const char* check_gemm(const GemmArgs& a);
@@ -59,6 +74,11 @@ struct PrepArgs {
   float* conv_ring = nullptr;
   const SeqCtl* conv_ctl = nullptr;
   int conv_n = 0;
+  // Optional (norm and embedding modes): RMSNorm folded into the next GEMM (GemmArgs::sumsq_in):
+  // the planes hold x * norm_w, and sumsq_out[q * 32 + b] receives the row's sum of squares for
+  // q = 0 and zero for 0 < q < sumsq_slots.
+  float* sumsq_out = nullptr;
+  int sumsq_slots = 0;
 };
 cudaError_t launch_prep(const PrepArgs& a, int batch, cudaStream_t stream, bool pdl);
 

@@ -302,6 +302,10 @@ __global__ void __launch_bounds__(256) prep_kernel(const PrepArgs a) {
   if (a.mode != kPrepCopy) {
     const float tot = block_sum<256>(ss, red);
     inv = rsqrtf(tot / (float)K + a.eps);
+    if (a.sumsq_out) {  // folded into the next GEMM: it applies 1 / rms
+      inv = 1.f;
+      for (int q = tid; q < a.sumsq_slots; q += 256) a.sumsq_out[q * 32 + b] = q == 0 ? tot : 0.f;
+    }
   }
   for (int i = tid; i < K; i += 256) {
     const float v = a.mode == kPrepCopy ? src[i] : src[i] * inv * a.norm_w[i];
@@ -455,6 +459,11 @@ const char* check_gemm(const GemmArgs& a) {
   if (!a.xh || !a.xl || a.ldx < a.k || a.ldx % 8) return "bad activation planes";
   if (a.epi == kSwiGlu ? (!a.yh || !a.yl) : !a.y) return "null output";
   if (a.row_groups != 1 && a.row_groups != 2 && a.row_groups != 4 && a.row_groups != 8) return "bad row groups";
+  if (a.norm_w_out && (a.epi != kAccumulate || !a.out_xh || !a.out_xl || !a.sumsq_out || a.rows % 16))
+    return "a folded-norm producer accumulates, writes planes and partials, rows % 16 == 0";
+  if (a.sumsq_in && (a.sumsq_slots < 1 || a.norm_k < 1)) return "a folded-norm consumer needs its partials";
+  if ((a.norm_w_out || a.sumsq_in) && (a.impl != kGemmTensorCore || !gemm_tc_available()))
+    return "the folded RMSNorm needs the tensor-core GEMM";
   return nullptr;
 }
 

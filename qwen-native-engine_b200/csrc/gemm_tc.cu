@@ -40,6 +40,7 @@ constexpr int kTcStages = 6;
 constexpr int kBK = 64;                 // k per stage: one 128-byte swizzle span of f16
 constexpr int kTileA = 128 * kBK * 2;   // 16 KB of weights per stage
 constexpr int kMaxCluster = 8;
+constexpr int kSumsqLd = 32;  // folded-norm partials: [16-row block][32 columns]
 constexpr int kCtaSlots = kNumSms;  // one CTA per SM fits (about 145 KB of shared memory)
 
 struct TcArgs {
@@ -54,6 +55,15 @@ struct TcArgs {
   uint16_t* yl;
   int ldy;
   uint32_t* err;
+  // folded RMSNorm (see GemmArgs)
+  const float* norm_w_out;
+  uint16_t* out_xh;
+  uint16_t* out_xl;
+  int out_ldx;
+  float* sumsq_out;
+  const float* sumsq_in;
+  int sumsq_slots, norm_k;
+  float eps;
 };
 
 __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
@@ -150,6 +160,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   extern __shared__ uint8_t dsm_raw[];
   __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], accb;
   __shared__ uint32_t tmem_slot;
+  __shared__ float inv_s[32];
   constexpr int kTileB = N * kBK * 2;  // one activation plane per stage
   constexpr int kStage = kTileA + 2 * kTileB;
   constexpr int kTmemCols = N < 32 ? 32 : N;
@@ -266,54 +277,98 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   // Reduction over the cluster's ranks (rank order) and the epilogue, rows of this rank's slice.
   // Thread work item: one output row j and 4 consecutive batch columns; consecutive threads take
-  // consecutive rows, so each of the 4 output stores is coalesced.
+  // consecutive rows, so each of the 4 output stores is coalesced, and a half-warp covers one
+  // 16-row block of one column group (the unit of the folded-norm partial sums).
   constexpr int kOutTile = SW ? 64 : 128;
   const int slice = kOutTile / nrank;
   const int o0 = (int)rank * slice;
   const int B = a.batch;
   const int groups = (B + 3) / 4;
+  const int total = slice * groups;
   const uint32_t pbase = smem_u32(part);
-  for (int e = tid; e < slice * groups; e += kTcThreads) {
+  if (a.sumsq_in) {
+    // consumer of a folded RMSNorm: 1 / rms of each activation row from the producer's partials
+    if (tid < B) {
+      float ss = 0.f;
+      for (int q = 0; q < a.sumsq_slots; ++q) ss += a.sumsq_in[q * kSumsqLd + tid];
+      inv_s[tid] = rsqrtf(ss / (float)a.norm_k + a.eps);
+    }
+    __syncthreads();
+  }
+#pragma unroll 1
+  for (int base = 0; base < total; base += kTcThreads) {
+    const int e = base + tid;
+    const bool act = e < total;
     const int b0 = (e / slice) * 4, j = o0 + e % slice;
     const int orow = tile * kOutTile + j;
-    float4 pv[kMaxCluster], pu[kMaxCluster];
-#pragma unroll
-    for (int q = 0; q < kMaxCluster; ++q) {
-      if (q < nrank) {
-        pv[q] = ld_cluster_v4(cluster_addr(pbase + (uint32_t)((j * kPitch + b0) * 4), (uint32_t)q));
-        if (SW) pu[q] = ld_cluster_v4(cluster_addr(pbase + (uint32_t)(((64 + j) * kPitch + b0) * 4), (uint32_t)q));
-      }
-    }
     float v[4] = {0.f, 0.f, 0.f, 0.f}, u[4] = {0.f, 0.f, 0.f, 0.f};
+    if (act) {
+      float4 pv[kMaxCluster], pu[kMaxCluster];
 #pragma unroll
-    for (int q = 0; q < kMaxCluster; ++q) {
-      if (q < nrank) {
-        v[0] += pv[q].x;
-        v[1] += pv[q].y;
-        v[2] += pv[q].z;
-        v[3] += pv[q].w;
-        if (SW) {
-          u[0] += pu[q].x;
-          u[1] += pu[q].y;
-          u[2] += pu[q].z;
-          u[3] += pu[q].w;
+      for (int q = 0; q < kMaxCluster; ++q) {
+        if (q < nrank) {
+          pv[q] = ld_cluster_v4(cluster_addr(pbase + (uint32_t)((j * kPitch + b0) * 4), (uint32_t)q));
+          if (SW) pu[q] = ld_cluster_v4(cluster_addr(pbase + (uint32_t)(((64 + j) * kPitch + b0) * 4), (uint32_t)q));
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < kMaxCluster; ++q) {
+        if (q < nrank) {
+          v[0] += pv[q].x;
+          v[1] += pv[q].y;
+          v[2] += pv[q].z;
+          v[3] += pv[q].w;
+          if (SW) {
+            u[0] += pu[q].x;
+            u[1] += pu[q].y;
+            u[2] += pu[q].z;
+            u[3] += pu[q].w;
+          }
         }
       }
     }
-    if (orow >= a.out_rows) continue;
+    float sq[4] = {0.f, 0.f, 0.f, 0.f};
+    if (act && orow < a.out_rows) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int b = b0 + i;
-      if (b >= B) break;
-      if (SW) {
-        __half hi, lo;
-        split_hilo_tc(silu(v[i]) * u[i], hi, lo);
-        a.yh[(size_t)b * a.ldy + orow] = __half_as_ushort(hi);
-        a.yl[(size_t)b * a.ldy + orow] = __half_as_ushort(lo);
-      } else if (a.epi == kAccumulate) {
-        a.y[(size_t)b * a.ldy + orow] += v[i];
-      } else {
-        a.y[(size_t)b * a.ldy + orow] = v[i];
+      for (int i = 0; i < 4; ++i) {
+        const int b = b0 + i;
+        if (b >= B) break;
+        if (a.sumsq_in) {
+          v[i] *= inv_s[b];
+          u[i] *= inv_s[b];
+        }
+        if (SW) {
+          __half hi, lo;
+          split_hilo_tc(silu(v[i]) * u[i], hi, lo);
+          a.yh[(size_t)b * a.ldy + orow] = __half_as_ushort(hi);
+          a.yl[(size_t)b * a.ldy + orow] = __half_as_ushort(lo);
+        } else if (a.epi == kAccumulate) {
+          const float hn = a.y[(size_t)b * a.ldy + orow] + v[i];
+          a.y[(size_t)b * a.ldy + orow] = hn;
+          if (a.norm_w_out) {
+            // producer of a folded RMSNorm: the next GEMM's planes of h * norm_w, and h^2
+            __half hi, lo;
+            split_hilo_tc(hn * a.norm_w_out[orow], hi, lo);
+            a.out_xh[(size_t)b * a.out_ldx + orow] = __half_as_ushort(hi);
+            a.out_xl[(size_t)b * a.out_ldx + orow] = __half_as_ushort(lo);
+            sq[i] = hn * hn;
+          }
+        } else {
+          a.y[(size_t)b * a.ldy + orow] = v[i];
+        }
+      }
+    }
+    if (a.sumsq_out) {
+      // sums over the 16 rows of this half-warp's block, one partial per (block, column)
+#pragma unroll
+      for (int o = 1; o < 16; o <<= 1)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) sq[i] += __shfl_xor_sync(0xffffffffu, sq[i], o);
+      const int blk = (tile * kOutTile + j) / 16;
+      if (act && (j & 15) == 0 && blk * 16 < a.out_rows) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (b0 + i < B) a.sumsq_out[blk * kSumsqLd + b0 + i] = sq[i];
       }
     }
   }
@@ -405,6 +460,15 @@ cudaError_t launch_tc_nsw(const GemmArgs& g, cudaStream_t stream, bool pdl) {
   a.yl = g.yl;
   a.ldy = g.ldy;
   a.err = g.err;
+  a.norm_w_out = g.norm_w_out;
+  a.out_xh = g.out_xh;
+  a.out_xl = g.out_xl;
+  a.out_ldx = g.out_ldx;
+  a.sumsq_out = g.sumsq_out;
+  a.sumsq_in = g.sumsq_in;
+  a.sumsq_slots = g.sumsq_slots;
+  a.norm_k = g.norm_k;
+  a.eps = g.eps;
   const int out_tile = SW ? 64 : 128;
   const int tiles = (a.out_rows + out_tile - 1) / out_tile;
   // Split k over a cluster: the largest power of two whose clusters (one per tile) all fit on

@@ -1,12 +1,13 @@
 // Batched prompt processing: the n <= 32 tokens of a chunk go through every layer together
 // (Model::prefill_chunk, kernels/src/model.rs:349-372; its per-chunk dispatch list is built at
-// kernels/src/model.rs:222-259 from the kernels of kernels/src/batch.rs). Per layer:
-//   prep (embedding + RMSNorm at layer 0, RMSNorm after) | GEMM mixer_in (n rows) |
+// kernels/src/model.rs:222-259 from the kernels of kernels/src/batch.rs). First the embedding
+// prep, then per layer (the RMSNorms are folded into the GEMMs on either side of them):
+//   GEMM mixer_in (n rows) |
 //   GDN layers: gdn_scan (the recurrence walked token by token, state in registers) |
 //     prep (gated RMSNorm)
 //   attention layers: kv_append (RMSNorm + RoPE of the n keys; K and V rounded to f16 into the
 //     sequence's pages) | attention (one row per token, causal over the cache) | prep (copy)
-//   | GEMM mixer_out (+= h) | prep (RMSNorm) | GEMM gate_up (SwiGLU) | GEMM down (+= h);
+//   | GEMM mixer_out (+= h) | GEMM gate_up (SwiGLU) | GEMM down (+= h);
 // then chunk_finish advances the sequence's control words by n and leaves the last row's hidden
 // state where the B = 1 LM head reads it. The weights stream once per chunk instead of once per
 // token, so a chunk costs about what one batched decode step of 32 sequences costs.
@@ -275,6 +276,11 @@ PrefillRunner::PrefillRunner(Model* model, Runner* single) : m(model), r(single)
   x1l = static_cast<uint16_t*>(m->alloc((size_t)kRows * c.inter * 2));
   for (auto* p : {x0h, x0l}) cuda_check(cudaMemset(p, 0, (size_t)kRows * ldx0 * 2), "memset");
   for (auto* p : {x1h, x1l}) cuda_check(cudaMemset(p, 0, (size_t)kRows * c.inter * 2), "memset");
+  xnh = static_cast<uint16_t*>(m->alloc((size_t)kRows * c.hidden * 2));
+  xnl = static_cast<uint16_t*>(m->alloc((size_t)kRows * c.hidden * 2));
+  for (auto* p : {xnh, xnl}) cuda_check(cudaMemset(p, 0, (size_t)kRows * c.hidden * 2), "memset");
+  sumsq = static_cast<float*>(m->alloc((size_t)(c.hidden / 16) * 32 * 4));
+  cuda_check(cudaMemset(sumsq, 0, (size_t)(c.hidden / 16) * 32 * 4), "memset");
   rows = static_cast<SeqCtl*>(m->alloc((size_t)kRows * sizeof(SeqCtl)));
   cuda_check(cudaMemset(rows, 0, (size_t)kRows * sizeof(SeqCtl)), "memset");
   conv_tail = static_cast<float*>(m->alloc((size_t)3 * kConvChannels * 4));
@@ -300,8 +306,11 @@ void PrefillRunner::record(int n, cudaStream_t s) {
     cuda_check(launch_prep(p, n, s, true), "prefill prep");
     ++cnt;
   };
+  // RMSNorm folded into the GEMMs: the GEMM that updates h writes the planes of h * (next norm
+  // weight) and partial sums of h^2; the GEMM that reads those planes applies 1 / rms.
+  const int slots = c.hidden / 16;
   auto gemm = [&](const Mat& w, const uint16_t* xh, const uint16_t* xl, int ldx, int epi, float* y, uint16_t* yh,
-                  uint16_t* yl, int ldy) {
+                  uint16_t* yl, int ldy, const float* norm_out, bool norm_in) {
     GemmArgs g;
     g.w = w.w;
     g.rows = w.rows;
@@ -316,29 +325,43 @@ void PrefillRunner::record(int n, cudaStream_t s) {
     g.yh = yh;
     g.yl = yl;
     g.ldy = ldy;
+    if (norm_out) {
+      g.norm_w_out = norm_out;
+      g.out_xh = xnh;
+      g.out_xl = xnl;
+      g.out_ldx = c.hidden;
+      g.sumsq_out = sumsq;
+    }
+    if (norm_in) {
+      g.sumsq_in = sumsq;
+      g.sumsq_slots = slots;
+      g.norm_k = c.hidden;
+    }
     if (const char* why = check_gemm(g)) throw QneError(kEInval, why);
     cuda_check(launch_gemm(g, s, true), "prefill gemm");
     ++cnt;
   };
   cudaLaunchAttribute attr[1];
+  {
+    PrepArgs p;  // embedding rows (reads rows[b].token) -> h, planes of h * input_norm[0], sums
+    p.mode = kPrepEmbedNorm;
+    p.k = c.hidden;
+    p.norm_w = M.layers[0].input_norm;
+    p.embed = M.embed;
+    p.ctl = rows;
+    p.h = h;
+    p.ldh = c.hidden;
+    p.sumsq_out = sumsq;
+    p.sumsq_slots = slots;
+    p.xh = xnh;
+    p.xl = xnl;
+    p.ldx = c.hidden;
+    cuda_check(launch_prep(p, n, s, true), "prefill prep");
+    ++cnt;
+  }
   for (int i = 0; i < c.layers; ++i) {
     const LayerWeights& L = M.layers[i];
-    PrepArgs p;
-    p.k = c.hidden;
-    p.norm_w = L.input_norm;
-    if (i == 0) {
-      p.mode = kPrepEmbedNorm;  // reads rows[b].token; its count increment stays in `rows`
-      p.embed = M.embed;
-      p.ctl = rows;
-      p.h = h;
-      p.ldh = c.hidden;
-    } else {
-      p.mode = kPrepNorm;
-      p.src = h;
-      p.lds = c.hidden;
-    }
-    prep(p);
-    gemm(L.in, x0h, x0l, ldx0, kStore, proj, nullptr, nullptr, L.in.rows);
+    gemm(L.in, xnh, xnl, c.hidden, kStore, proj, nullptr, nullptr, L.in.rows, nullptr, true);
     PrepArgs q;
     q.k = kMixerOut;
     q.src = raw;
@@ -383,16 +406,11 @@ void PrefillRunner::record(int n, cudaStream_t s) {
       q.conv_n = n;
     }
     prep(q);
-    gemm(L.out, x0h, x0l, ldx0, kAccumulate, h, nullptr, nullptr, c.hidden);
-    PrepArgs pn;
-    pn.mode = kPrepNorm;
-    pn.k = c.hidden;
-    pn.src = h;
-    pn.lds = c.hidden;
-    pn.norm_w = L.post_norm;
-    prep(pn);
-    gemm(L.gate_up, x0h, x0l, ldx0, kSwiGlu, nullptr, x1h, x1l, c.inter);
-    gemm(L.down, x1h, x1l, c.inter, kAccumulate, h, nullptr, nullptr, c.hidden);
+    gemm(L.out, x0h, x0l, ldx0, kAccumulate, h, nullptr, nullptr, c.hidden, L.post_norm, false);
+    gemm(L.gate_up, xnh, xnl, c.hidden, kSwiGlu, nullptr, x1h, x1l, c.inter, nullptr, true);
+    // the next layer's input norm (after the last layer the B = 1 LM head normalizes h itself)
+    const float* next_norm = i + 1 < c.layers ? M.layers[i + 1].input_norm : nullptr;
+    gemm(L.down, x1h, x1l, c.inter, kAccumulate, h, nullptr, nullptr, c.hidden, next_norm, false);
   }
   cudaLaunchConfig_t cfg = make_cfg(dim3(1), dim3(256), s, true, attr);
   count_launch();

@@ -40,6 +40,8 @@ class PrefillRunner {
   float* proj = nullptr;  // [kRows][8224] mixer_in output
   float* raw = nullptr;   // [kRows][2048] mixer output before mixer_out
   uint16_t *x0h = nullptr, *x0l = nullptr, *x1h = nullptr, *x1l = nullptr;  // GEMM operand planes
+  uint16_t *xnh = nullptr, *xnl = nullptr;  // planes of h * norm weight (RMSNorm folded into the GEMMs)
+  float* sumsq = nullptr;                   // [hidden / 16][32] partial sums of h^2
   SeqCtl* rows = nullptr;    // [kRows] device: (token, position) of each chunk row
   SeqCtl* pinned = nullptr;  // [kMaxContext] host staging of the rows of one call
   void* attn_scratch = nullptr;

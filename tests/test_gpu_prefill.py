@@ -60,8 +60,9 @@ def test_batched_prefill_matches_oracle(tiny, n):
     m.prefill_chunk(prompt, 0, True)
     launched = qne.kernel_launches() - launches0
     chunks = -(-n // 32)
-    per_chunk = 8 * m.layers + 1  # prep, GEMM, mixer (2 kernels on attention layers), prep, 3 GEMMs, prep
-    assert launched == chunks * per_chunk + m.layers // 4 * chunks + 1  # + kv_append per attention layer, + LM head
+    # embedding prep + per layer (GEMM, mixer, prep, 3 GEMMs) + chunk finish; kv_append per attention layer
+    per_chunk = 6 * m.layers + 2 + m.layers // 4
+    assert launched == chunks * per_chunk + 1  # + the LM head
     if n > 2:
         assert launched < n * m.dispatches_per_token()  # the weights stream once per chunk
     got = m.logits()
