@@ -129,6 +129,10 @@ __device__ __forceinline__ uint32_t cluster_rank() {
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
   return r;
 }
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
@@ -253,9 +257,49 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
   __syncwarp();
 
+  // Epilogue geometry. Thread work item: one output row j and 4 consecutive batch columns;
+  // consecutive threads take consecutive rows, so each of the 4 output stores is coalesced, and a
+  // half-warp covers one 16-row block of one column group (the unit of the folded-norm partials).
+  constexpr int kOutTile = SW ? 64 : 128;
+  constexpr int kIt = kOutTile * 8 / kTcThreads;  // work items per thread at most (1 rank, 32 columns)
+  const int slice = kOutTile / nrank;
+  const int o0 = (int)rank * slice;
+  const int B = a.batch;
+  const int groups = (B + 3) / 4;
+  const int total = slice * groups;
+  auto item_of = [&](int it, int& b0, int& j) {
+    const int e = it * kTcThreads + tid;
+    b0 = (e / slice) * 4;
+    j = o0 + e % slice;
+    return e < total;
+  };
+
+  // What depends only on the previous kernel is fetched while the MMAs run: the consumer's 1/rms
+  // per activation row (warps 2-3, unrolled loads, fixed summation order) and the residual values
+  // an accumulating epilogue adds to.
+  pdl_wait();
+  if (a.sumsq_in && tid >= 64 && tid < 64 + B) {
+    const int b = tid - 64;
+    float ss = 0.f;
+#pragma unroll 8
+    for (int q = 0; q < a.sumsq_slots; ++q) ss += a.sumsq_in[q * kSumsqLd + b];
+    inv_s[b] = rsqrtf(ss / (float)a.norm_k + a.eps);
+  }
+  float yv[SW ? 1 : kIt][4];
+  if (!SW && a.epi == kAccumulate) {
+#pragma unroll
+    for (int it = 0; it < (SW ? 1 : kIt); ++it) {
+      int b0, j;
+      const bool act = item_of(it, b0, j);
+      const int orow = tile * kOutTile + j;
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        yv[it][i] = (act && orow < a.out_rows && b0 + i < B) ? a.y[(size_t)(b0 + i) * a.ldy + orow] : 0.f;
+    }
+  }
+
   // Accumulator -> shared memory (the stage ring is free once accb fired: every MMA completed,
   // so every TMA load it consumed had landed). Thread t holds row t of the tile.
-  pdl_wait();
   float* part = reinterpret_cast<float*>(base);
   {
     float v[N];
@@ -273,35 +317,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           ok ? make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]) : make_float4(0.f, 0.f, 0.f, 0.f);
   }
   tc_fence_before();
-  cluster_sync_all();
+  cluster_sync_all();  // every rank's partial is in its shared memory (and inv_s is visible)
 
-  // Reduction over the cluster's ranks (rank order) and the epilogue, rows of this rank's slice.
-  // Thread work item: one output row j and 4 consecutive batch columns; consecutive threads take
-  // consecutive rows, so each of the 4 output stores is coalesced, and a half-warp covers one
-  // 16-row block of one column group (the unit of the folded-norm partial sums).
-  constexpr int kOutTile = SW ? 64 : 128;
-  const int slice = kOutTile / nrank;
-  const int o0 = (int)rank * slice;
-  const int B = a.batch;
-  const int groups = (B + 3) / 4;
-  const int total = slice * groups;
+  // Reduction over the cluster's ranks, in rank order: all remote reads first, then this CTA
+  // signals that it is done reading, and the epilogue math and stores overlap the other ranks.
   const uint32_t pbase = smem_u32(part);
-  if (a.sumsq_in) {
-    // consumer of a folded RMSNorm: 1 / rms of each activation row from the producer's partials
-    if (tid < B) {
-      float ss = 0.f;
-      for (int q = 0; q < a.sumsq_slots; ++q) ss += a.sumsq_in[q * kSumsqLd + tid];
-      inv_s[tid] = rsqrtf(ss / (float)a.norm_k + a.eps);
+  float vv[kIt][4], uu[SW ? kIt : 1][4];
+#pragma unroll
+  for (int it = 0; it < kIt; ++it) {
+    int b0, j;
+    const bool act = item_of(it, b0, j);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      vv[it][i] = 0.f;
+      if (SW) uu[SW ? it : 0][i] = 0.f;
     }
-    __syncthreads();
-  }
-#pragma unroll 1
-  for (int base = 0; base < total; base += kTcThreads) {
-    const int e = base + tid;
-    const bool act = e < total;
-    const int b0 = (e / slice) * 4, j = o0 + e % slice;
-    const int orow = tile * kOutTile + j;
-    float v[4] = {0.f, 0.f, 0.f, 0.f}, u[4] = {0.f, 0.f, 0.f, 0.f};
     if (act) {
       float4 pv[kMaxCluster], pu[kMaxCluster];
 #pragma unroll
@@ -314,36 +344,46 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
       for (int q = 0; q < kMaxCluster; ++q) {
         if (q < nrank) {
-          v[0] += pv[q].x;
-          v[1] += pv[q].y;
-          v[2] += pv[q].z;
-          v[3] += pv[q].w;
+          vv[it][0] += pv[q].x;
+          vv[it][1] += pv[q].y;
+          vv[it][2] += pv[q].z;
+          vv[it][3] += pv[q].w;
           if (SW) {
-            u[0] += pu[q].x;
-            u[1] += pu[q].y;
-            u[2] += pu[q].z;
-            u[3] += pu[q].w;
+            uu[SW ? it : 0][0] += pu[q].x;
+            uu[SW ? it : 0][1] += pu[q].y;
+            uu[SW ? it : 0][2] += pu[q].z;
+            uu[SW ? it : 0][3] += pu[q].w;
           }
         }
       }
     }
+  }
+  cluster_arrive();
+
+#pragma unroll
+  for (int it = 0; it < kIt; ++it) {
+    if (it * kTcThreads >= total) break;  // uniform across the CTA
+    int b0, j;
+    const bool act = item_of(it, b0, j);
+    const int orow = tile * kOutTile + j;
     float sq[4] = {0.f, 0.f, 0.f, 0.f};
     if (act && orow < a.out_rows) {
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int b = b0 + i;
         if (b >= B) break;
+        float v = vv[it][i], u = SW ? uu[SW ? it : 0][i] : 0.f;
         if (a.sumsq_in) {
-          v[i] *= inv_s[b];
-          u[i] *= inv_s[b];
+          v *= inv_s[b];
+          u *= inv_s[b];
         }
         if (SW) {
           __half hi, lo;
-          split_hilo_tc(silu(v[i]) * u[i], hi, lo);
+          split_hilo_tc(silu(v) * u, hi, lo);
           a.yh[(size_t)b * a.ldy + orow] = __half_as_ushort(hi);
           a.yl[(size_t)b * a.ldy + orow] = __half_as_ushort(lo);
         } else if (a.epi == kAccumulate) {
-          const float hn = a.y[(size_t)b * a.ldy + orow] + v[i];
+          const float hn = yv[SW ? 0 : it][i] + v;
           a.y[(size_t)b * a.ldy + orow] = hn;
           if (a.norm_w_out) {
             // producer of a folded RMSNorm: the next GEMM's planes of h * norm_w, and h^2
@@ -354,7 +394,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             sq[i] = hn * hn;
           }
         } else {
-          a.y[(size_t)b * a.ldy + orow] = v[i];
+          a.y[(size_t)b * a.ldy + orow] = v;
         }
       }
     }
@@ -372,7 +412,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
     }
   }
-  cluster_sync_all();  // no CTA leaves while another still reads its shared memory
+  cluster_wait();  // no CTA leaves while another still reads its shared memory
   if (warp == 0) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(kTmemCols) : "memory");
