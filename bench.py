@@ -120,6 +120,18 @@ def aggregate_rate(world: int, units_per_rank: int, max_ms: float) -> float:
     return world * units_per_rank / (max_ms * 1e-3)
 
 
+def cpu_model() -> str:
+    """The host CPU's model name (from /proc/cpuinfo), for the CPU-baseline record."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def cpu_oracle_rate(s, prompt_len: int, tokens: int, seed: int):
     """Oracle decode rate on the host: `tokens` steps after a short untimed prefill."""
     from oracle import oracle
@@ -151,7 +163,8 @@ def reference_arm(args, world, rank):
         "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
         "config": {"workload": "config 2: Qwen3.5-2B-shaped f16 (seed 1), B=1 greedy decode", "global_batch": 1,
                    "seq_len": 4096, "parallelism": "cpu"},
-        "cpu_baseline": {"value": round(rate, 4), "unit": "tok/s", "cores": cores, "kind": "port",
+        "cpu_baseline": {"value": round(rate, 4), "unit": "tok/s", "cores": cores, "cpu_model": cpu_model(),
+                         "kind": "port",
                          "sample": f"{steps} decode tokens of the 2B f16 model after a 16-token prefill (the CPU "
                                    f"restatement of the reference WGSL decoder; attention at context 16-32 instead of "
                                    f"3968 changes <2% of the bytes per token)"},
@@ -590,7 +603,7 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, cores = cpu_oracle_rate(s, 16, 4, 1)
-        cpu = {"value": round(rate, 4), "unit": "tok/s", "cores": cores, "kind": "port",
+        cpu = {"value": round(rate, 4), "unit": "tok/s", "cores": cores, "cpu_model": cpu_model(), "kind": "port",
                "sample": f"4 decode tokens of the same {size_name} {cfg_info['kind']} model after a 16-token "
                          "prefill, CPU oracle (C++ restatement of the reference decoder, all host threads)"}
 
