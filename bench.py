@@ -1,6 +1,6 @@
-"""Decode throughput of the B200 engine on BASELINE.json's headline workload, one JSON line.
+"""Decode throughput of the B200 engine on the headline benchmark workload, one JSON line.
 
-Default workload: Qwen3.5-2B-shaped f16 hybrid decoder (synthetic, seed 1),
+Default workload (benchmark config 2): Qwen3.5-2B-shaped f16 hybrid decoder (synthetic, seed 1),
 batch 1 per GPU, KV cache prefilled to 3968 tokens, then greedy decode steps (one step = one
 token of one sequence per GPU) up to the 4096 limit. With N GPUs (torchrun) every rank decodes
 its own independent sequence on its own weight replica (weak scaling, no collective on the data
@@ -258,7 +258,7 @@ def profile_prefill(args):
 
 
 def micro(args):
-    """per-kernel microbench (seed 4). Each kernel is timed over enough distinct
+    """benchmark config 5: per-kernel microbench (seed 4). Each kernel is timed over enough distinct
     copies of its inputs that every launch reads HBM (> 126 MB L2 per rotation); launches are queued
     behind a spin kernel so CUDA events measure device time. One JSON line per case."""
     import torch
@@ -384,7 +384,7 @@ def micro(args):
 
 def batched_run(torch, qne, synth, rank: int, world: int, barrier, max_over_ranks, warmup: int,
                 steps: int = 64, batch: int = 32):
-    """Qwen3.5-0.8B-shaped f16 (seed 3), `batch` independent sequences per GPU
+    """benchmark config 4: Qwen3.5-0.8B-shaped f16 (seed 3), `batch` independent sequences per GPU
     with context lengths uniform in [256, 4032] (so 64 steps stay within 4096), randomly permuted
     16-token page tables, synthetic history (KV pages, GDN states) written on the device, then
     `steps` greedy steps. Returns a dict for the JSON line (rank 0) or None."""
@@ -448,7 +448,7 @@ def main():
     ap.add_argument("--prompt", type=int, default=None, help="context tokens before the timed steps "
                                                             "(default: the config's)")
     ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3],
-                    help="B=1 workload: BASELINE config 1 (0.8B f16), 2 (2B f16, the headline) or 3 (2B int4 g64)")
+                    help="B=1 workload: benchmark config 1 (0.8B f16), 2 (2B f16, the headline) or 3 (2B int4 g64)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--micro", default="", help="config-5 microbench: all | gemv,gdn,attn; "
                                                      "step4 = the small decode workload of the ncu captures; "

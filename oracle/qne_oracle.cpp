@@ -14,7 +14,7 @@
 //                      the host greedy rule of src/sampling.rs:86-94)
 //   per-token graph    kernels/src/model.rs:220-269
 // Deliberate differences, each switchable where the reference behaviour is wanted:
-//   * weights may also be f16 or group-64 int4 with f16 zero points;
+//   * weights may also be f16 or group-64 int4 with f16 zero points (benchmark configs);
 //   * the KV cache may hold f16-rounded keys/values, the current token included (kv_f16 = 1);
 //   * RoPE angles come from a double-precision table (rope_table) instead of f32 pow/sin/cos.
 // All accumulation is f32; transcendental functions are the host libm's. Work is spread over a

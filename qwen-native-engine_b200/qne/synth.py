@@ -7,7 +7,7 @@ matrix entry carries a "kind": "f16", "q4" (the converter's MatMulNBits block-32
 default when absent) or "q4g64" (u4 packed 8 per u32, group 64 along k, f16 scale, f16 zero
 point).
 
-Values: f16 weights N(0, std) rounded to f16; int4 weights uniform nibbles,
+Values (benchmark configs): f16 weights N(0, std) rounded to f16; int4 weights uniform nibbles,
 scales |N(0, scale_std)|, zero point 8; all norm weights 1; conv weights U(-0.5, 0.5);
 GDN params dt_bias 0, A_neg_exp -0.5, norm 1 (the prototype's choices, kernels/src/lib.rs:773,777).
 Every tensor draws from its own generator seeded by (seed, tensor index), so generation can run
@@ -155,7 +155,7 @@ def build(hidden: int, intermediate: int, *, layers: int = 24, every: int = 4, v
 
 
 def baseline_config(n: int) -> dict:
-    """BASELINE.json configs 1-4 as build() keyword arguments plus the workload."""
+    """the benchmark configs 1-4 as build() keyword arguments plus the workload."""
     if n == 1:
         return dict(size="0.8b", kind="f16", seed=0, prompt=128, steps=128, batch=1)
     if n == 2:

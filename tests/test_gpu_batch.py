@@ -1,4 +1,4 @@
-"""Batched decode (independent sequences) on the B200: the tensor-core GEMM
+"""Batched decode (independent sequences, benchmark config 4) on the B200: the tensor-core GEMM
 against the oracle GEMV per sequence, the whole batched step against one oracle model per
 sequence, and page-table permutations that must not change a single bit."""
 import numpy as np

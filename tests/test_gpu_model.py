@@ -212,7 +212,7 @@ def test_fused_kernels_at_a_long_context(cuda):
 @pytest.mark.slow
 @pytest.mark.parametrize("fused", [True, False], ids=["fused", "split"])
 def test_config1_full_08b_parity(cuda, fused):
-    """0.8B-shaped f16 model (seed 0), 128 prompt ids (seed 0), greedy steps."""
+    """benchmark config 1: 0.8B-shaped f16 model (seed 0), 128 prompt ids (seed 0), greedy steps."""
     s = synth.build_config(1)
     m = qne.Model(s.index_json, s.weights)
     set_path(m, fused)
@@ -227,7 +227,7 @@ def test_config1_full_08b_parity(cuda, fused):
 @pytest.mark.slow
 @pytest.mark.parametrize("cfg", [2, 3])
 def test_config_2b_short_context_parity(cuda, cfg):
-    """BASELINE configs 2 (f16) and 3 (int4 g64) at a short context (the full 3968-token prefill on
+    """benchmark configs 2 (f16) and 3 (int4 g64) at a short context (the full 3968-token prefill on
     the CPU oracle takes too long for a test; attention at 4096 is covered by the operator tests)."""
     s = synth.build_config(cfg)
     m = qne.Model(s.index_json, s.weights)

@@ -98,7 +98,7 @@ def oracle_gemv(kind, mat, rows, k, x, epilogue, y0=None):
     return oracle.gemv(kind, mat["w"], mat["s"], mat["z"], rows, k, x, y, rc.EPI[epilogue])
 
 
-# BASELINE config 5 shapes (K x N): 2048x6144, 6144x2048, 2048x4096, 1024x248320.
+# benchmark config 5 shapes (K x N): 2048x6144, 6144x2048, 2048x4096, 1024x248320.
 SHAPES = [(6144, 2048), (2048, 6144), (4096, 2048), (248320, 1024)]
 
 

@@ -168,7 +168,7 @@ def test_int4_weights_fall_back_to_per_token(cuda):
 
 @pytest.mark.slow
 def test_config2_batched_prefill_of_the_bench_prompt(cuda):
-    """BASELINE config 2 (2B f16): the bench's 3968-token prompt through the batched path and
+    """benchmark config 2 (2B f16): the bench's 3968-token prompt through the batched path and
     through the per-token path: logits within the tolerance, 32 identical greedy tokens."""
     s = synth.build_config(2)
     m = qne.Model(s.index_json, s.weights)

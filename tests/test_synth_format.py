@@ -1,6 +1,6 @@
 """The synthetic writer produces the converter's weights.bin / index.json format
 (scripts/convert_weights.py:35-66): 256-byte aligned tensors, tied embedding stored once,
-per-kind tensor sizes, the BASELINE value distributions."""
+per-kind tensor sizes, the benchmark value distributions."""
 import json
 
 import numpy as np
