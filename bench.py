@@ -227,8 +227,8 @@ def profile_step4(args):
 
 def profile_prefill(args):
     """Fixed workload for the prefill launch list: the bench's config (2B f16 by default), its
-    3968-token prompt through qne_prefill_chunk, the first 3936 tokens untimed, then the last
-    32-token chunk (positions 3936..3967, the longest attention context) plus the LM head inside
+    3968-token prompt through qne_prefill_chunk, the first 3904 tokens untimed, then the last
+    64-token chunk (positions 3904..3967, the longest attention context) plus the LM head inside
     the NVTX range "last_chunk", timed with CUDA events."""
     import torch
     import qne
@@ -242,17 +242,18 @@ def profile_prefill(args):
     m.set_stream(stream.cuda_stream)
     n = cfg_info["prompt"]
     prompt = synth.prompt_ids(n, 1)
-    m.prefill_chunk(prompt[: n - 32], 0, False)
+    c = qne.PREFILL_CHUNK_TOKENS
+    m.prefill_chunk(prompt[: n - c], 0, False)
     m.sync()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.nvtx.range_push("last_chunk")
     e0.record(stream)
-    m.prefill_chunk(prompt[n - 32:], n - 32, True)
+    m.prefill_chunk(prompt[n - c:], n - c, True)
     e1.record(stream)
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     print(json.dumps({"micro": "prefill", "config": args.config, "batched": m.prefill_batched_supported,
-                      "chunk_positions": [n - 32, n - 1], "chunk_ms": round(e0.elapsed_time(e1), 3),
+                      "chunk_positions": [n - c, n - 1], "chunk_ms": round(e0.elapsed_time(e1), 3),
                       "last_token": list(m.last_token())}), flush=True)
     m.close()
 
@@ -452,7 +453,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--micro", default="", help="config-5 microbench: all | gemv,gdn,attn; "
                                                      "step4 = the small decode workload of the ncu captures; "
-                                                     "prefill = the last 32-token chunk of the bench prompt")
+                                                     "prefill = the last 64-token chunk of the bench prompt")
     ap.add_argument("--no-batched", action="store_true", help="skip the config-4 batched decode run")
     ap.add_argument("--batched-only", action="store_true", help="run only the config-4 batched decode (profiling)")
     ap.add_argument("--batched-steps", type=int, default=64)
@@ -511,11 +512,12 @@ def main():
     torch.cuda.set_stream(stream)
     model.set_stream(stream.cuda_stream)
     prompt = synth.prompt_ids(prompt_len, rank_seed(1, rank))
-    # Batched prompt processing through the public API (qne_prefill_chunk: 32-token chunks on
+    # Batched prompt processing through the public API (qne_prefill_chunk: 64-token chunks on
     # f16 weights, one token per step on int4), timed on the device. An untimed call first builds
     # the chunk runner and the launch graphs of the chunk sizes the prompt uses.
     model.reset()
-    model.prefill_chunk(prompt[: min(prompt_len, 32 + prompt_len % 32)], 0, True)
+    chunk = qne.PREFILL_CHUNK_TOKENS
+    model.prefill_chunk(prompt[: min(prompt_len, chunk + prompt_len % chunk)], 0, True)
     model.reset()
     model.sync()
     torch.cuda.synchronize()
@@ -545,9 +547,11 @@ def main():
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda._sleep(20_000_000)  # hold the stream while the host queues the steps
+    torch.cuda.nvtx.range_push("decode_steps")  # the launch-list captures select this range
     e0.record(stream)
     model.decode_async(steps)
     e1.record(stream)
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     barrier()
     ms = max_over_ranks(e0.elapsed_time(e1))
@@ -659,9 +663,9 @@ def main():
             "batched": batched,
             "prefill": {"tokens": prompt_len, "ms": round(prefill_ms, 3),
                         "tok_per_s": round(aggregate_rate(world, prompt_len, prefill_ms), 1),
-                        "path": ("batched: 32-token chunks, tensor-core GEMMs, chunked GDN scan" if prefill_batched
+                        "path": (f"batched: {chunk}-token chunks, tensor-core GEMMs, chunked GDN scan" if prefill_batched
                                  else "one token per step (int4 weights)"),
-                        "weight_gbs": (round(model_weight_bytes * -(-prompt_len // 32) / (prefill_ms * 1e-3) / 1e9, 1)
+                        "weight_gbs": (round(model_weight_bytes * -(-prompt_len // chunk) / (prefill_ms * 1e-3) / 1e9, 1)
                                        if prefill_batched else None)},
         }
         print(json.dumps(line), flush=True)

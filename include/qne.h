@@ -142,7 +142,7 @@ QNE_API qne_status qne_reset(qne_model* m);
 QNE_API qne_status qne_prefill(qne_model* m, const uint32_t* ids, uint32_t n);
 /* Model::prefill_chunk, kernels/src/model.rs:349 (prefill_from / prefill_batched are
  * prefill_chunk with finish_logits = 1). Fails when start + n >= QNE_MAX_CONTEXT. With f16
- * decoder matrices the ids run in 32-token chunks (tensor-core GEMMs, chunked GDN scan, causal
+ * decoder matrices the ids run in 64-token chunks (tensor-core GEMMs, chunked GDN scan, causal
  * attention over the appended keys), like the reference's batched prefill list
  * (kernels/src/model.rs:222-259); otherwise one token per step, like qne_prefill. Afterwards the
  * control words hold (ids[n-1], start + n - 1), or with finish_logits the logits after the last
@@ -268,7 +268,7 @@ QNE_API qne_status qne_gemv_ex(const qne_matrix* m, const float* x, float* y, in
  * x = h * rsqrt(mean(h^2) + eps) * norm_w. */
 QNE_API qne_status qne_rmsnorm_gemv(const qne_matrix* m, const float* h, const float* norm_w, float eps,
                             float* y, int epilogue, void* stream);
-/* Batched GEMV/GEMM over `batch` f32 vectors x[batch][k] -> y[batch][out_rows]. Uses the
+/* Batched GEMV/GEMM over `batch` (1..64) f32 vectors x[batch][k] -> y[batch][out_rows]. Uses the
  * tensor cores for batch >= 2. `scratch` must hold qne_gemm_scratch_bytes(m, batch) bytes. */
 QNE_API size_t qne_gemm_scratch_bytes(const qne_matrix* m, int batch);
 QNE_API qne_status qne_gemm(const qne_matrix* m, const float* x, int batch, float* y, int epilogue,
@@ -276,7 +276,8 @@ QNE_API qne_status qne_gemm(const qne_matrix* m, const float* x, int batch, floa
 /* qne_gemm with the kernel chosen explicitly (no counterpart in the reference; for comparisons):
  * QNE_GEMM_TENSOR_CORE = tcgen05 MMAs with TMA-staged tiles and tensor-memory accumulators (the
  * default of qne_gemm and of the batched decode and prefill paths), QNE_GEMM_MMA_SYNC = warp-level
- * mma.sync with cp.async staging. Both compute the same sums; only the f32 summation order differs. */
+ * mma.sync with cp.async staging (batch 1..32). Both compute the same sums; only the f32 summation
+ * order differs. */
 #define QNE_GEMM_TENSOR_CORE 0
 #define QNE_GEMM_MMA_SYNC 1
 QNE_API qne_status qne_gemm_ex(const qne_matrix* m, const float* x, int batch, float* y, int epilogue,

@@ -34,7 +34,7 @@ class BatchRunner {
   float *h = nullptr, *proj = nullptr, *raw = nullptr, *logits = nullptr;
   uint16_t *x0h = nullptr, *x0l = nullptr, *x1h = nullptr, *x1l = nullptr;
   uint16_t *xnh = nullptr, *xnl = nullptr;  // planes of h * norm weight (RMSNorm folded into the GEMMs)
-  float* sumsq = nullptr;                   // [hidden / 16][32] partial sums of h^2
+  float* sumsq = nullptr;                   // [hidden / 16][kGemmMaxRows] partial sums of h^2
   int ldx0 = 0;
   uint32_t* picks = nullptr;
   void* argmax_scratch = nullptr;
@@ -105,8 +105,8 @@ BatchRunner::BatchRunner(Model* model, int batch, uint32_t pool) : m(model), B(b
   xnh = static_cast<uint16_t*>(m->alloc((size_t)Bp * c.hidden * 2));
   xnl = static_cast<uint16_t*>(m->alloc((size_t)Bp * c.hidden * 2));
   for (auto* p : {xnh, xnl}) cuda_check(cudaMemset(p, 0, (size_t)Bp * c.hidden * 2), "memset");
-  sumsq = static_cast<float*>(m->alloc((size_t)(c.hidden / 16) * 32 * 4));
-  cuda_check(cudaMemset(sumsq, 0, (size_t)(c.hidden / 16) * 32 * 4), "memset");
+  sumsq = static_cast<float*>(m->alloc((size_t)(c.hidden / 16) * kGemmMaxRows * 4));
+  cuda_check(cudaMemset(sumsq, 0, (size_t)(c.hidden / 16) * kGemmMaxRows * 4), "memset");
   picks = static_cast<uint32_t*>(m->alloc((size_t)B * 4));
   argmax_scratch = m->alloc(argmax_batched_scratch_bytes(B));
   cuda_check(cudaMemset(argmax_scratch, 0, argmax_batched_scratch_bytes(B)), "memset");
@@ -483,7 +483,8 @@ qne_status qne_gemm_ex(const qne_matrix* m, const float* x, int batch, float* y,
     if (!m || !x || !y) throw QneError(kEInval, "null argument");
     if (m->kind != QNE_KIND_F16) throw QneError(kEInval, "batched GEMM supports f16 weights");
     if (epilogue < 0 || epilogue > 2) throw QneError(kEInval, "unknown epilogue");
-    if (batch < 1 || batch > 32) throw QneError(kEInval, "batch must be 1..32");
+    if (batch < 1 || batch > (impl == QNE_GEMM_MMA_SYNC ? 32 : kGemmMaxRows))
+      throw QneError(kEInval, impl == QNE_GEMM_MMA_SYNC ? "batch must be 1..32" : "batch must be 1..64");
     if (m->k % 32 || m->k <= 0 || m->rows <= 0) throw QneError(kEInval, "batched GEMM needs k % 32 == 0");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     // Stage x as hi/lo planes (8-row padded) in a per-device workspace that lives until exit.

@@ -10,6 +10,9 @@
 namespace qne {
 
 enum GemmImpl : int { kGemmTensorCore = 0, kGemmMmaSync = 1 };
+// Activation rows one batched GEMM takes: 64 on the tensor-core kernel, 32 on the mma.sync one.
+// Also the column stride of the folded-norm partials (GemmArgs::sumsq_out / sumsq_in).
+constexpr int kGemmMaxRows = 64;
 
 // Y[b][row] for b < batch: W [rows][k] f16 times the activation planes xh/xl [>= 8*ceil(batch/8)][ldx].
 struct GemmArgs {
@@ -32,8 +35,8 @@ struct GemmArgs {
   // RMSNorm folded into the GEMMs on either side of it (tensor-core kernel only). Producer (an
   // accumulating GEMM that updates the residual h): also writes the planes out_xh/out_xl of
   // h * norm_w_out for the next GEMM and, per 16-row block of h and per column b,
-  // sumsq_out[block * 32 + b] = sum of h^2. Consumer (the next GEMM, which reads those planes):
-  // scales column b of its result by rsqrt(sum_q sumsq_in[q * 32 + b] / norm_k + eps) before
+  // sumsq_out[block * kGemmMaxRows + b] = sum of h^2. Consumer (the next GEMM, which reads those
+  // planes): scales column b of its result by rsqrt(sum_q sumsq_in[q * kGemmMaxRows + b] / norm_k + eps) before
   // the epilogue (for SwiGLU, both halves).
   const float* norm_w_out = nullptr;
   uint16_t* out_xh = nullptr;
@@ -75,7 +78,7 @@ struct PrepArgs {
   const SeqCtl* conv_ctl = nullptr;
   int conv_n = 0;
   // Optional (norm and embedding modes): RMSNorm folded into the next GEMM (GemmArgs::sumsq_in):
-  // the planes hold x * norm_w, and sumsq_out[q * 32 + b] receives the row's sum of squares for
+  // the planes hold x * norm_w, and sumsq_out[q * kGemmMaxRows + b] receives the row's sum of squares for
   // q = 0 and zero for 0 < q < sumsq_slots.
   float* sumsq_out = nullptr;
   int sumsq_slots = 0;

@@ -304,7 +304,7 @@ __global__ void __launch_bounds__(256) prep_kernel(const PrepArgs a) {
     inv = rsqrtf(tot / (float)K + a.eps);
     if (a.sumsq_out) {  // folded into the next GEMM: it applies 1 / rms
       inv = 1.f;
-      for (int q = tid; q < a.sumsq_slots; q += 256) a.sumsq_out[q * 32 + b] = q == 0 ? tot : 0.f;
+      for (int q = tid; q < a.sumsq_slots; q += 256) a.sumsq_out[q * kGemmMaxRows + b] = q == 0 ? tot : 0.f;
     }
   }
   for (int i = tid; i < K; i += 256) {
@@ -454,7 +454,8 @@ int gemm_row_groups(int out_rows) {
 const char* check_gemm(const GemmArgs& a) {
   if (!a.w || a.rows <= 0 || a.k <= 0) return "empty matrix";
   if (a.k % 32) return "batched GEMM needs k % 32 == 0";
-  if (a.batch < 1 || a.batch > 32) return "batch must be 1..32";
+  if (a.batch < 1 || a.batch > kGemmMaxRows) return "batch must be 1..64";
+  if (a.impl == kGemmMmaSync && a.batch > 32) return "the mma.sync GEMM takes batch 1..32";
   if (a.epi == kSwiGlu && (a.rows % 2)) return "SwiGLU needs an even row count";
   if (!a.xh || !a.xl || a.ldx < a.k || a.ldx % 8) return "bad activation planes";
   if (a.epi == kSwiGlu ? (!a.yh || !a.yl) : !a.y) return "null output";

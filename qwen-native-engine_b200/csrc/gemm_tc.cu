@@ -1,5 +1,5 @@
 // Batched linear layers on the 5th-generation tensor cores: Y[b] (=, +=, SwiGLU) W X[b] for up
-// to 32 activation rows (batched decode sequences or the tokens of a prompt chunk).
+// to 64 activation rows (batched decode sequences or the tokens of a prompt chunk).
 //
 // Same arithmetic as gemm.cu (the per-token GEMV of kernels/src/shaders.rs:48-250 applied to B
 // rows; the reference's prompt GEMM is batch::gemm, kernels/src/batch.rs:16-99): f16 weights,
@@ -8,7 +8,7 @@
 //
 // B200 design (tcgen05 + TMA + TMEM, one CTA of 4 warps per tile):
 //  * a tile is 128 weight rows (SwiGLU: 64 gate rows and the matching 64 up rows) by the whole
-//    activation batch (N = 16 or 32 columns of the MMA, zero-filled past the batch);
+//    activation batch (N = 16, 32 or 64 columns of the MMA, zero-filled past the batch);
 //  * warp 0 lane 0 streams 64-wide k-blocks of the weight tile and of both activation planes
 //    with TMA (128-byte swizzle, the canonical K-major layout of the MMA operands) into a 6-stage
 //    ring guarded by mbarriers; weight loads of the first stages are issued before waiting on the
@@ -40,7 +40,7 @@ constexpr int kTcStages = 6;
 constexpr int kBK = 64;                 // k per stage: one 128-byte swizzle span of f16
 constexpr int kTileA = 128 * kBK * 2;   // 16 KB of weights per stage
 constexpr int kMaxCluster = 8;
-constexpr int kSumsqLd = 32;  // folded-norm partials: [16-row block][32 columns]
+constexpr int kSumsqLd = kGemmMaxRows;  // folded-norm partials: [16-row block][kGemmMaxRows columns]
 constexpr int kCtaSlots = kNumSms;  // one CTA per SM fits (about 145 KB of shared memory)
 
 struct TcArgs {
@@ -124,6 +124,12 @@ __device__ __forceinline__ void tmem_load_row<32>(uint32_t taddr, float* v) {
   tmem_load_row<16>(taddr + 16, v + 16);
 }
 
+template <>
+__device__ __forceinline__ void tmem_load_row<64>(uint32_t taddr, float* v) {
+  tmem_load_row<32>(taddr, v);
+  tmem_load_row<32>(taddr + 32, v + 32);
+}
+
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -164,7 +170,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   extern __shared__ uint8_t dsm_raw[];
   __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], accb;
   __shared__ uint32_t tmem_slot;
-  __shared__ float inv_s[32];
+  __shared__ float inv_s[kGemmMaxRows];
   constexpr int kTileB = N * kBK * 2;  // one activation plane per stage
   constexpr int kStage = kTileA + 2 * kTileB;
   constexpr int kTmemCols = N < 32 ? 32 : N;
@@ -261,7 +267,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   // consecutive threads take consecutive rows, so each of the 4 output stores is coalesced, and a
   // half-warp covers one 16-row block of one column group (the unit of the folded-norm partials).
   constexpr int kOutTile = SW ? 64 : 128;
-  constexpr int kIt = kOutTile * 8 / kTcThreads;  // work items per thread at most (1 rank, 32 columns)
+  constexpr int kIt = kOutTile * (N / 4) / kTcThreads;  // work items per thread at most (1 rank, N columns)
+  // Residual values prefetched into registers during the MMAs (kIt of them per thread); at
+  // N = 64 that would be 64 more registers, so there the epilogue reads them when it stores.
+  constexpr int kYv = kIt <= 8 ? kIt : 1;
   const int slice = kOutTile / nrank;
   const int o0 = (int)rank * slice;
   const int B = a.batch;
@@ -285,10 +294,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     for (int q = 0; q < a.sumsq_slots; ++q) ss += a.sumsq_in[q * kSumsqLd + b];
     inv_s[b] = rsqrtf(ss / (float)a.norm_k + a.eps);
   }
-  float yv[SW ? 1 : kIt][4];
-  if (!SW && a.epi == kAccumulate) {
+  float yv[SW ? 1 : kYv][4];
+  if (!SW && kYv == kIt && a.epi == kAccumulate) {
 #pragma unroll
-    for (int it = 0; it < (SW ? 1 : kIt); ++it) {
+    for (int it = 0; it < (SW ? 1 : kYv); ++it) {
       int b0, j;
       const bool act = item_of(it, b0, j);
       const int orow = tile * kOutTile + j;
@@ -383,7 +392,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           a.yh[(size_t)b * a.ldy + orow] = __half_as_ushort(hi);
           a.yl[(size_t)b * a.ldy + orow] = __half_as_ushort(lo);
         } else if (a.epi == kAccumulate) {
-          const float hn = yv[SW ? 0 : it][i] + v;
+          const float prev = kYv == kIt ? yv[SW || kYv != kIt ? 0 : it][i] : a.y[(size_t)b * a.ldy + orow];
+          const float hn = prev + v;
           a.y[(size_t)b * a.ldy + orow] = hn;
           if (a.norm_w_out) {
             // producer of a folded RMSNorm: the next GEMM's planes of h * norm_w, and h^2
@@ -547,7 +557,8 @@ bool gemm_tc_available() { return encode_fn() != nullptr; }
 cudaError_t launch_gemm_tc(const GemmArgs& g, cudaStream_t stream, bool pdl) {
   const bool sw = g.epi == kSwiGlu;
   if (g.batch <= 16) return sw ? launch_tc_nsw<16, true>(g, stream, pdl) : launch_tc_nsw<16, false>(g, stream, pdl);
-  return sw ? launch_tc_nsw<32, true>(g, stream, pdl) : launch_tc_nsw<32, false>(g, stream, pdl);
+  if (g.batch <= 32) return sw ? launch_tc_nsw<32, true>(g, stream, pdl) : launch_tc_nsw<32, false>(g, stream, pdl);
+  return sw ? launch_tc_nsw<64, true>(g, stream, pdl) : launch_tc_nsw<64, false>(g, stream, pdl);
 }
 
 }  // namespace qne

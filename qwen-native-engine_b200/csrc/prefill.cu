@@ -1,4 +1,4 @@
-// Batched prompt processing: the n <= 32 tokens of a chunk go through every layer together
+// Batched prompt processing: the n <= 64 tokens of a chunk go through every layer together
 // (Model::prefill_chunk, kernels/src/model.rs:349-372; its per-chunk dispatch list is built at
 // kernels/src/model.rs:222-259 from the kernels of kernels/src/batch.rs). First the embedding
 // prep, then per layer (the RMSNorms are folded into the GEMMs on either side of them):
@@ -10,7 +10,7 @@
 //   | GEMM mixer_out (+= h) | GEMM gate_up (SwiGLU) | GEMM down (+= h);
 // then chunk_finish advances the sequence's control words by n and leaves the last row's hidden
 // state where the B = 1 LM head reads it. The weights stream once per chunk instead of once per
-// token, so a chunk costs about what one batched decode step of 32 sequences costs.
+// token, so a chunk costs about what one batched decode step of as many sequences costs.
 //
 // Numerics follow the per-token kernels: the GDN scan and the key normalization repeat the
 // decode kernels' arithmetic per token; the GEMMs accumulate in f32 from f16 weights and hi/lo
@@ -57,7 +57,7 @@ struct ScanArgs {
   float* tail;          // [3][6144]: the chunk's last three conv inputs, oldest first
 };
 
-constexpr int kScanRows = 32;  // tokens per chunk
+constexpr int kScanRows = 64;  // tokens per chunk
 constexpr int kScanThreads = 512;
 
 struct ScanShared {
@@ -67,9 +67,11 @@ struct ScanShared {
   float g[kScanRows], beta[kScanRows], kq[kScanRows];
 };
 static_assert(kScanRows == PrefillRunner::kRows, "the scan holds one chunk's tokens");
+static_assert(kScanRows <= kGemmMaxRows, "a chunk's rows go through one batched GEMM");
 
 __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_kernel(const __grid_constant__ ScanArgs a) {
-  __shared__ ScanShared sh;
+  extern __shared__ __align__(16) uint8_t scan_smem[];  // one ScanShared (about 71 KB: dynamic)
+  ScanShared& sh = *reinterpret_cast<ScanShared*>(scan_smem);
   const int h = blockIdx.y, t0 = blockIdx.x * kSlice;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int n = a.n;
@@ -279,14 +281,17 @@ PrefillRunner::PrefillRunner(Model* model, Runner* single) : m(model), r(single)
   xnh = static_cast<uint16_t*>(m->alloc((size_t)kRows * c.hidden * 2));
   xnl = static_cast<uint16_t*>(m->alloc((size_t)kRows * c.hidden * 2));
   for (auto* p : {xnh, xnl}) cuda_check(cudaMemset(p, 0, (size_t)kRows * c.hidden * 2), "memset");
-  sumsq = static_cast<float*>(m->alloc((size_t)(c.hidden / 16) * 32 * 4));
-  cuda_check(cudaMemset(sumsq, 0, (size_t)(c.hidden / 16) * 32 * 4), "memset");
+  sumsq = static_cast<float*>(m->alloc((size_t)(c.hidden / 16) * kGemmMaxRows * 4));
+  cuda_check(cudaMemset(sumsq, 0, (size_t)(c.hidden / 16) * kGemmMaxRows * 4), "memset");
   rows = static_cast<SeqCtl*>(m->alloc((size_t)kRows * sizeof(SeqCtl)));
   cuda_check(cudaMemset(rows, 0, (size_t)kRows * sizeof(SeqCtl)), "memset");
   conv_tail = static_cast<float*>(m->alloc((size_t)3 * kConvChannels * 4));
   attn_scratch = m->alloc(attention_scratch_bytes(kRows));
   cuda_check(cudaMemset(attn_scratch, 0, attention_scratch_bytes(kRows)), "memset");
   cuda_check(cudaMallocHost(&pinned, (size_t)kMaxContext * sizeof(SeqCtl)), "cudaMallocHost");
+  cuda_check(cudaFuncSetAttribute(gdn_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)sizeof(ScanShared)),
+             "gdn scan shared memory");
 }
 
 PrefillRunner::~PrefillRunner() {
@@ -394,6 +399,7 @@ void PrefillRunner::record(int n, cudaStream_t s) {
     } else {
       const ScanArgs sa{proj, r->st.conv[i], L.conv_w, r->st.rec[i], L.gdn_params, r->st.ctl, n, raw, conv_tail};
       cudaLaunchConfig_t cfg = make_cfg(dim3(kSlices, kGdnHeads), dim3(kScanThreads), s, true, attr);
+      cfg.dynamicSmemBytes = sizeof(ScanShared);
       count_launch();
       cuda_check(cudaLaunchKernelEx(&cfg, gdn_scan_kernel, sa), "gdn scan launch");
       ++cnt;

@@ -1,4 +1,4 @@
-// Batched prompt processing for the B = 1 sequence: chunks of up to 32 consecutive tokens per
+// Batched prompt processing for the B = 1 sequence: chunks of up to 64 consecutive tokens per
 // pass through tensor-core GEMMs (Model::prefill_chunk, kernels/src/model.rs:349-372).
 #pragma once
 
@@ -12,7 +12,7 @@ namespace qne {
 
 class PrefillRunner {
  public:
-  static constexpr int kRows = 32;  // tokens per chunk (the batched GEMM's batch limit)
+  static constexpr int kRows = 64;  // tokens per chunk (the tensor-core GEMM's batch limit)
 
   // Whether `m` can run chunks: the decoder matrices must be f16 (the batched GEMM's operand).
   static bool supported(const Model& m);
@@ -41,7 +41,7 @@ class PrefillRunner {
   float* raw = nullptr;   // [kRows][2048] mixer output before mixer_out
   uint16_t *x0h = nullptr, *x0l = nullptr, *x1h = nullptr, *x1l = nullptr;  // GEMM operand planes
   uint16_t *xnh = nullptr, *xnl = nullptr;  // planes of h * norm weight (RMSNorm folded into the GEMMs)
-  float* sumsq = nullptr;                   // [hidden / 16][32] partial sums of h^2
+  float* sumsq = nullptr;                   // [hidden / 16][kGemmMaxRows] partial sums of h^2
   SeqCtl* rows = nullptr;    // [kRows] device: (token, position) of each chunk row
   SeqCtl* pinned = nullptr;  // [kMaxContext] host staging of the rows of one call
   void* attn_scratch = nullptr;

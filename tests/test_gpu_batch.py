@@ -18,11 +18,13 @@ def dev(a):
 
 
 @pytest.mark.parametrize("impl", ["tcgen05", "mma_sync"])
-@pytest.mark.parametrize("batch", [1, 3, 8, 13, 16, 17, 32])
+@pytest.mark.parametrize("batch", [1, 3, 8, 13, 16, 17, 32, 33, 50, 64])
 @pytest.mark.parametrize("epilogue,rows,k", [("store", 1024, 1024), ("accumulate", 1024, 3584), ("swiglu", 2 * 3584, 1024),
                                              ("store", 8224, 2048), ("store", 4099, 1024), ("accumulate", 2048, 6144),
                                              ("swiglu", 2 * 6144, 2048), ("store", 1000, 96), ("swiglu", 2 * 200, 4160)])
 def test_gemm_matches_gemv_per_sequence(cuda, impl, batch, epilogue, rows, k):
+    if impl == "mma_sync" and batch > 32:
+        pytest.skip("the mma.sync GEMM takes batch 1..32")
     rng = np.random.default_rng(batch * 7 + rows)
     w = (rng.standard_normal(rows * k) * 0.05).astype(np.float16)
     x = rng.standard_normal((batch, k)).astype(np.float32)
@@ -39,6 +41,21 @@ def test_gemm_matches_gemv_per_sequence(cuda, impl, batch, epilogue, rows, k):
         want = y0[b].copy() if epilogue == "accumulate" else np.zeros(out_rows, np.float32)
         oracle.gemv("f16", w, None, None, rows, k, x[b], want, rc.EPI[epilogue])
         assert rc.rel_err(got[b], want) < 1e-4, b
+
+
+def test_gemm_batch_limits(cuda):
+    """Batches past a kernel's limit are rejected before anything runs: 64 rows on the tensor-core
+    GEMM, 32 on the mma.sync one."""
+    w = dev(np.zeros(256 * 64, np.float16))
+    m = qne.matrix("f16", 256, 64, w)
+    x = dev(np.zeros((65, 64), np.float32))
+    y = dev(np.zeros((65, 256), np.float32))
+    for impl, limit in (("tcgen05", 64), ("mma_sync", 32)):
+        qne.gemm(m, x, limit, y, "store", impl=impl)
+        with pytest.raises(qne.QneError) as e:
+            qne.gemm(m, x, limit + 1, y, "store", impl=impl)
+        assert e.value.name == "EINVAL" and f"1..{limit}" in str(e.value)
+    torch.cuda.synchronize()
 
 
 @pytest.fixture(scope="module")

@@ -1,4 +1,4 @@
-"""Batched prompt processing (qne_prefill_chunk on f16 weights: 32-token chunks through the
+"""Batched prompt processing (qne_prefill_chunk on f16 weights: 64-token chunks through the
 tensor-core GEMMs, the chunked GDN scan, K/V append + causal attention) against the CPU oracle
 and against the per-token path (qne_prefill), on the same random-init weights and token ids.
 
@@ -47,9 +47,9 @@ def steps_after(m, om, tokens, pos):
         logits_close(m.step(int(t), pos + i), om.step(int(t), pos + i))
 
 
-@pytest.mark.parametrize("n", [1, 2, 3, 4, 5, 31, 32, 33, 64, 70, 100])
+@pytest.mark.parametrize("n", [1, 2, 3, 4, 5, 31, 32, 33, 63, 64, 65, 100, 130])
 def test_batched_prefill_matches_oracle(tiny, n):
-    """Ragged chunk sizes (1..32 rows, several chunks): logits, the greedy pick left in the
+    """Ragged chunk sizes (1..64 rows, several chunks): logits, the greedy pick left in the
     control words, and the state the decode steps read afterwards."""
     m, om = tiny
     prompt = synth.prompt_ids(n, 100 + n, VOCAB)
@@ -59,7 +59,7 @@ def test_batched_prefill_matches_oracle(tiny, n):
     m.reset()
     m.prefill_chunk(prompt, 0, True)
     launched = qne.kernel_launches() - launches0
-    chunks = -(-n // 32)
+    chunks = -(-n // qne.PREFILL_CHUNK_TOKENS)
     # embedding prep + per layer (GEMM, mixer, prep, 3 GEMMs) + chunk finish; kv_append per attention layer
     per_chunk = 6 * m.layers + 2 + m.layers // 4
     assert launched == chunks * per_chunk + 1  # + the LM head
