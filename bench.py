@@ -512,8 +512,8 @@ def main():
     torch.cuda.set_stream(stream)
     model.set_stream(stream.cuda_stream)
     prompt = synth.prompt_ids(prompt_len, rank_seed(1, rank))
-    # Batched prompt processing through the public API (qne_prefill_chunk: 64-token chunks on
-    # f16 weights, one token per step on int4), timed on the device. An untimed call first builds
+    # Batched prompt processing through the public API (qne_prefill_chunk: 64-token chunks; int4
+    # matrices decoded to f16 before each GEMM), timed on the device. An untimed call first builds
     # the chunk runner and the launch graphs of the chunk sizes the prompt uses.
     model.reset()
     chunk = qne.PREFILL_CHUNK_TOKENS
@@ -663,8 +663,9 @@ def main():
             "batched": batched,
             "prefill": {"tokens": prompt_len, "ms": round(prefill_ms, 3),
                         "tok_per_s": round(aggregate_rate(world, prompt_len, prefill_ms), 1),
-                        "path": (f"batched: {chunk}-token chunks, tensor-core GEMMs, chunked GDN scan" if prefill_batched
-                                 else "one token per step (int4 weights)"),
+                        "path": (f"batched: {chunk}-token chunks, tensor-core GEMMs, chunked GDN scan"
+                                 + ("" if cfg_info["kind"] == "f16" else ", int4 matrices decoded to f16 per GEMM")
+                                 if prefill_batched else "one token per step"),
                         "weight_gbs": (round(model_weight_bytes * -(-prompt_len // chunk) / (prefill_ms * 1e-3) / 1e9, 1)
                                        if prefill_batched else None)},
         }

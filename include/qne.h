@@ -141,10 +141,11 @@ QNE_API qne_status qne_reset(qne_model* m);
  * afterwards logits hold the prediction after the last id and the greedy pick is stored. */
 QNE_API qne_status qne_prefill(qne_model* m, const uint32_t* ids, uint32_t n);
 /* Model::prefill_chunk, kernels/src/model.rs:349 (prefill_from / prefill_batched are
- * prefill_chunk with finish_logits = 1). Fails when start + n >= QNE_MAX_CONTEXT. With f16
- * decoder matrices the ids run in 64-token chunks (tensor-core GEMMs, chunked GDN scan, causal
- * attention over the appended keys), like the reference's batched prefill list
- * (kernels/src/model.rs:222-259); otherwise one token per step, like qne_prefill. Afterwards the
+ * prefill_chunk with finish_logits = 1). Fails when start + n >= QNE_MAX_CONTEXT. The ids run
+ * in 64-token chunks (tensor-core GEMMs, chunked GDN scan, causal attention over the appended
+ * keys), like the reference's batched prefill list (kernels/src/model.rs:222-259); int4 decoder
+ * matrices are decoded to f16 before each GEMM. Decoder matrices with k % 64 != 0 (not produced
+ * by the converters) run one token per step, like qne_prefill. Afterwards the
  * control words hold (ids[n-1], start + n - 1), or with finish_logits the logits after the last
  * id and (greedy pick, start + n). */
 QNE_API qne_status qne_prefill_chunk(qne_model* m, const uint32_t* ids, uint32_t n, uint32_t start,

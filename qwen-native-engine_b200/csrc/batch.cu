@@ -8,8 +8,10 @@
 //   (+= h) | GEMM gate_up (SwiGLU -> hi/lo) | GEMM down (+= h);  before the first layer the
 //   embedding prep, after the last the GEMM lm_head and the per-sequence greedy pick.
 // The RMSNorms before mixer_in, gate_up and the LM head are folded into the GEMMs on either side
-// (GemmArgs::norm_w_out / sumsq_in), so a step is 6 launches per layer plus 3. All launches of one
-// step are captured once into a CUDA graph (programmatic dependent launch between kernels).
+// (GemmArgs::norm_w_out / sumsq_in), so a step is 6 launches per layer plus 3 (int4 weights: one
+// more launch per GEMM, which decodes the matrix to f16 for it). All launches of one step are
+// captured once into a CUDA graph (programmatic dependent launch between kernels).
+#include <algorithm>
 #include <chrono>
 #include <cstring>
 #include <string>
@@ -35,6 +37,7 @@ class BatchRunner {
   uint16_t *x0h = nullptr, *x0l = nullptr, *x1h = nullptr, *x1l = nullptr;
   uint16_t *xnh = nullptr, *xnl = nullptr;  // planes of h * norm weight (RMSNorm folded into the GEMMs)
   float* sumsq = nullptr;                   // [hidden / 16][kGemmMaxRows] partial sums of h^2
+  uint16_t* wdeq = nullptr;  // int4 models: f16 copy of the matrix the next GEMM reads
   int ldx0 = 0;
   uint32_t* picks = nullptr;
   void* argmax_scratch = nullptr;
@@ -114,6 +117,12 @@ BatchRunner::BatchRunner(Model* model, int batch, uint32_t pool) : m(model), B(b
   cuda_check(cudaMemset(attn_scratch, 0, attention_scratch_bytes(B)), "memset");
   host_pos.assign(B, 0);
   cuda_check(cudaMallocHost(&pinned, (size_t)B * 16 + 64), "cudaMallocHost");
+  size_t deq_elems = 0;  // the largest int4 matrix a step multiplies, decoded to f16 before its GEMM
+  for (const LayerWeights& L : m->layers)
+    for (const Mat* w : {&L.in, &L.out, &L.gate_up, &L.down})
+      if (w->kind != kF16) deq_elems = std::max(deq_elems, (size_t)w->rows * w->k);
+  if (m->lm_head.kind != kF16) deq_elems = std::max(deq_elems, (size_t)m->lm_head.rows * m->lm_head.k);
+  if (deq_elems) wdeq = static_cast<uint16_t*>(m->alloc(deq_elems * 2));
 }
 
 BatchRunner::~BatchRunner() {
@@ -138,9 +147,15 @@ void BatchRunner::record(bool greedy, cudaStream_t s) {
   const int slots = c.hidden / 16;
   auto gemm = [&](const Mat& w, const uint16_t* xh, const uint16_t* xl, int ldx, int epi, float* y, uint16_t* yh,
                   uint16_t* yl, int ldy, const float* norm_out, bool norm_in) {
-    if (w.kind != kF16) throw QneError(kEInval, "batched decode supports f16 weights only");
     GemmArgs g;
     g.w = w.w;
+    if (w.kind != kF16) {  // int4: decode into the f16 scratch first
+      if (w.k % 64) throw QneError(kEInval, "batched decode of int4 matrices needs k % 64 == 0");
+      cuda_check(launch_dequant_f16(w, wdeq, s, true), "dequant launch");
+      ++n;
+      g.w = wdeq;
+      g.w_after_wait = true;
+    }
     g.rows = w.rows;
     g.k = w.k;
     g.batch = B;

@@ -31,6 +31,9 @@ struct GemmArgs {
   int ldy = 0;
   int x_rows = 0;           // rows allocated in xh/xl (0: 8 * ceil(batch / 8))
   int impl = kGemmTensorCore;
+  // The previous kernel of the stream writes w (int4 weights dequantized into a scratch): the
+  // weight tiles are then loaded only after the dependency wait (tensor-core kernel only).
+  bool w_after_wait = false;
   uint32_t* err = nullptr;  // optional: receives kFlagTimeout if a bounded wait gives up
   // RMSNorm folded into the GEMMs on either side of it (tensor-core kernel only). Producer (an
   // accumulating GEMM that updates the residual h): also writes the planes out_xh/out_xl of
@@ -49,6 +52,9 @@ struct GemmArgs {
   float eps = 1e-6f;
 };
 int gemm_row_groups(int out_rows);
+// int4 matrix m (kQ4 or kQ4G64, k % 64 == 0) -> out f16[rows][k], each value the per-token
+// kernels' (float(q) - zp) * scale rounded to f16; loads before the dependency wait, stores after.
+cudaError_t launch_dequant_f16(const Mat& m, uint16_t* out, cudaStream_t stream, bool pdl);
 const char* check_gemm(const GemmArgs& a);
 // impl kGemmTensorCore: tcgen05 + TMA (gemm_tc.cu); kGemmMmaSync: warp-level mma.sync (gemm.cu).
 cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream, bool pdl);

@@ -19,6 +19,8 @@
 //    directly as the hi/lo planes the next GEMM reads.
 #include <math.h>
 
+#include <algorithm>
+
 #include "batch.cuh"
 #include "gemv.cuh"
 
@@ -443,6 +445,44 @@ cudaLaunchConfig_t cfg_of(dim3 grid, dim3 block, cudaStream_t stream, bool pdl, 
   return cfg;
 }
 
+// ------------------------------------------------------------------------------------------
+// int4 matrices (the reference's block-32 layout or group 64) for the batched GEMMs: the matrix
+// is decoded to f16 into a scratch the next GEMM reads (from L2 when the matrix fits). Each thread takes one u32 word, i.e. 8 values of one quantization block, with
+// the per-token kernels' arithmetic (float(q) - zp) * scale, rounded to f16 once. The int4 words
+// are immutable and load before the dependency wait; the stores overwrite what the previous GEMM
+// of the stream read, so they come after it.
+// ------------------------------------------------------------------------------------------
+template <int KIND>
+__global__ void __launch_bounds__(256) dequant_f16_kernel(const Mat m, uint16_t* out) {
+  pdl_launch();
+  const long words = (long)m.rows * (m.k / 8);
+  const long stride = (long)gridDim.x * blockDim.x;
+  bool waited = false;
+  for (long e = (long)blockIdx.x * blockDim.x + threadIdx.x; e < words; e += stride) {
+    const long row = e / (m.k / 8);
+    const int i = (int)(e % (m.k / 8)) * 8;
+    const uint32_t word = __ldg(static_cast<const uint32_t*>(m.w) + e);
+    float scale, zp;
+    if (KIND == kQ4)
+      q4_scale_zp(static_cast<const uint32_t*>(m.s), static_cast<const uint32_t*>(m.z), row, m.k, i / 32, scale, zp);
+    else
+      q4g64_scale_zp(static_cast<const uint16_t*>(m.s), static_cast<const uint16_t*>(m.z), row, m.k, i / 64, scale,
+                     zp);
+    uint32_t h[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t lo = __half_as_ushort(__float2half_rn((nib_f(word, 8 * j) - zp) * scale));
+      const uint32_t hi = __half_as_ushort(__float2half_rn((nib_f(word, 8 * j + 4) - zp) * scale));
+      h[j] = lo | (hi << 16);
+    }
+    if (!waited) {
+      pdl_wait();
+      waited = true;
+    }
+    *reinterpret_cast<uint4*>(out + e * 8) = make_uint4(h[0], h[1], h[2], h[3]);
+  }
+}
+
 }  // namespace
 
 int gemm_row_groups(int out_rows) {
@@ -465,13 +505,27 @@ const char* check_gemm(const GemmArgs& a) {
   if (a.sumsq_in && (a.sumsq_slots < 1 || a.norm_k < 1)) return "a folded-norm consumer needs its partials";
   if ((a.norm_w_out || a.sumsq_in) && (a.impl != kGemmTensorCore || !gemm_tc_available()))
     return "the folded RMSNorm needs the tensor-core GEMM";
+  if (a.w_after_wait && (a.impl != kGemmTensorCore || !gemm_tc_available() || reinterpret_cast<uintptr_t>(a.w) % 16))
+    return "weights written by the previous kernel need the tensor-core GEMM";
   return nullptr;
+}
+
+cudaError_t launch_dequant_f16(const Mat& m, uint16_t* out, cudaStream_t stream, bool pdl) {
+  if ((m.kind != kQ4 && m.kind != kQ4G64) || m.k % 64 || m.rows < 1) return cudaErrorInvalidValue;
+  const long words = (long)m.rows * (m.k / 8);
+  const int grid = (int)std::min<long>((words + 255) / 256, 8L * kNumSms);
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = cfg_of(dim3(grid), dim3(256), stream, pdl, attr);
+  count_launch();
+  return m.kind == kQ4 ? cudaLaunchKernelEx(&cfg, dequant_f16_kernel<kQ4>, m, out)
+                       : cudaLaunchKernelEx(&cfg, dequant_f16_kernel<kQ4G64>, m, out);
 }
 
 cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream, bool pdl) {
   if (a.impl == kGemmTensorCore && gemm_tc_available() && reinterpret_cast<uintptr_t>(a.w) % 16 == 0 &&
       reinterpret_cast<uintptr_t>(a.xh) % 16 == 0 && reinterpret_cast<uintptr_t>(a.xl) % 16 == 0)
     return launch_gemm_tc(a, stream, pdl);
+  if (a.w_after_wait) return cudaErrorInvalidValue;  // the mma.sync kernel prefetches weights early
   return a.epi == kSwiGlu ? launch_sw<true>(a, stream, pdl) : launch_sw<false>(a, stream, pdl);
 }
 

@@ -64,6 +64,7 @@ struct TcArgs {
   const float* sumsq_in;
   int sumsq_slots, norm_k;
   float eps;
+  int w_after_wait;  // weights written by the previous kernel: no weight loads before the wait
 };
 
 __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
@@ -207,7 +208,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   bool ok = true;
   if (warp == 0 && lane == 0 && nkb > 0) {
     // Producer. Weight tiles do not depend on the previous kernel: the first stages' weights go
-    // out before the dependency wait, their activation tiles after it.
+    // out before the dependency wait, their activation tiles after it (unless the previous
+    // kernel wrote the weights, w_after_wait).
     const int r0 = SW ? tile * 64 : tile * 128;
     auto load_a = [&](int i) {
       const uint32_t st = sbase + (uint32_t)((i % kTcStages) * kStage);
@@ -229,8 +231,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tma_load_2d(st + kTileA + kTileB, &txl, kx, 0, bar);
     };
     const int pre = min(kTcStages, nkb);
-    for (int i = 0; i < pre; ++i) load_a(i);
+    if (!a.w_after_wait)
+      for (int i = 0; i < pre; ++i) load_a(i);
     pdl_wait();
+    if (a.w_after_wait)
+      for (int i = 0; i < pre; ++i) load_a(i);
     for (int i = 0; i < pre; ++i) load_b(i);
     for (int i = pre; i < nkb; ++i) {
       if (!mbar_wait(smem_u32(&empty[i % kTcStages]), (uint32_t)((i / kTcStages) + 1) & 1u, a.err)) {
@@ -519,6 +524,7 @@ cudaError_t launch_tc_nsw(const GemmArgs& g, cudaStream_t stream, bool pdl) {
   a.sumsq_slots = g.sumsq_slots;
   a.norm_k = g.norm_k;
   a.eps = g.eps;
+  a.w_after_wait = g.w_after_wait ? 1 : 0;
   const int out_tile = SW ? 64 : 128;
   const int tiles = (a.out_rows + out_tile - 1) / out_tile;
   // Split k over a cluster: the largest power of two whose clusters (one per tile) all fit on

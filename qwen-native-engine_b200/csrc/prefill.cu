@@ -14,7 +14,9 @@
 //
 // Numerics follow the per-token kernels: the GDN scan and the key normalization repeat the
 // decode kernels' arithmetic per token; the GEMMs accumulate in f32 from f16 weights and hi/lo
-// f16 activations (the batched decode GEMM).
+// f16 activations (the batched decode GEMM). int4 decoder matrices are decoded to f16 (one
+// rounding of each dequantized weight) by one more launch before each GEMM.
+#include <algorithm>
 #include <string>
 
 #include "../../include/qne.h"
@@ -262,7 +264,7 @@ cudaLaunchConfig_t make_cfg(dim3 grid, dim3 block, cudaStream_t stream, bool pdl
 bool PrefillRunner::supported(const Model& m) {
   for (const LayerWeights& L : m.layers)
     for (const Mat* w : {&L.in, &L.out, &L.gate_up, &L.down})
-      if (w->kind != kF16 || w->k % 32) return false;
+      if ((w->kind != kF16 && w->kind != kQ4 && w->kind != kQ4G64) || w->k % 64) return false;
   return !m.layers.empty();
 }
 
@@ -289,6 +291,11 @@ PrefillRunner::PrefillRunner(Model* model, Runner* single) : m(model), r(single)
   attn_scratch = m->alloc(attention_scratch_bytes(kRows));
   cuda_check(cudaMemset(attn_scratch, 0, attention_scratch_bytes(kRows)), "memset");
   cuda_check(cudaMallocHost(&pinned, (size_t)kMaxContext * sizeof(SeqCtl)), "cudaMallocHost");
+  size_t deq_elems = 0;  // the largest int4 decoder matrix, decoded to f16 before its GEMM
+  for (const LayerWeights& L : m->layers)
+    for (const Mat* w : {&L.in, &L.out, &L.gate_up, &L.down})
+      if (w->kind != kF16) deq_elems = std::max(deq_elems, (size_t)w->rows * w->k);
+  if (deq_elems) wdeq = static_cast<uint16_t*>(m->alloc(deq_elems * 2));
   cuda_check(cudaFuncSetAttribute(gdn_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)sizeof(ScanShared)),
              "gdn scan shared memory");
@@ -318,6 +325,12 @@ void PrefillRunner::record(int n, cudaStream_t s) {
                   uint16_t* yl, int ldy, const float* norm_out, bool norm_in) {
     GemmArgs g;
     g.w = w.w;
+    if (w.kind != kF16) {  // int4: decode into the f16 scratch first
+      cuda_check(launch_dequant_f16(w, wdeq, s, true), "prefill dequant launch");
+      ++cnt;
+      g.w = wdeq;
+      g.w_after_wait = true;
+    }
     g.rows = w.rows;
     g.k = w.k;
     g.batch = n;

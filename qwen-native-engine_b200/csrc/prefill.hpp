@@ -14,7 +14,8 @@ class PrefillRunner {
  public:
   static constexpr int kRows = 64;  // tokens per chunk (the tensor-core GEMM's batch limit)
 
-  // Whether `m` can run chunks: the decoder matrices must be f16 (the batched GEMM's operand).
+  // Whether `m` can run chunks: decoder matrices f16 (the batched GEMM's operand) or int4 (block
+  // 32 or group 64, decoded to f16 per matrix before its GEMM), k a multiple of 64.
   static bool supported(const Model& m);
 
   PrefillRunner(Model* m, Runner* single);
@@ -46,6 +47,7 @@ class PrefillRunner {
   SeqCtl* pinned = nullptr;  // [kMaxContext] host staging of the rows of one call
   void* attn_scratch = nullptr;
   float* conv_tail = nullptr;  // [3][6144] last conv inputs of a chunk, from the GDN scan to the prep
+  uint16_t* wdeq = nullptr;    // int4 models: f16 copy of the decoder matrix the next GEMM reads
   std::map<int, cudaGraphExec_t> graphs;
   std::map<int, size_t> launches;
 };

@@ -25,7 +25,7 @@ import numpy as np
 MAX_CONTEXT = 4096
 PAGE_TOKENS = 16
 PAGES_PER_SEQ = MAX_CONTEXT // PAGE_TOKENS
-PREFILL_CHUNK_TOKENS = 64  # tokens per batched prefill chunk (f16 weights)
+PREFILL_CHUNK_TOKENS = 64  # tokens per batched prefill chunk
 KIND_F16, KIND_Q4, KIND_Q4G64 = 0, 1, 2
 KINDS = {"f16": KIND_F16, "q4": KIND_Q4, "q4g64": KIND_Q4G64}
 EPI_STORE, EPI_ACCUMULATE, EPI_SWIGLU = 0, 1, 2
@@ -253,7 +253,7 @@ class Model:
 
     @property
     def prefill_batched_supported(self) -> bool:
-        """Whether prefill_chunk runs 64-token batched chunks (f16 weights) on this model."""
+        """Whether prefill_chunk runs 64-token batched chunks on this model (f16 or int4 weights)."""
         return bool(lib.qne_prefill_chunk_batched(self._h))
 
     def prefill_chunk(self, ids, start: int, finish_logits: bool) -> None:

@@ -96,6 +96,44 @@ def test_batched_decode_matches_oracle_per_sequence(tiny):
     bt.close()
 
 
+@pytest.mark.parametrize("kind", ["q4", "q4g64"])
+def test_int4_batched_decode_matches_oracle(cuda, kind):
+    """int4 models (the reference converter's block-32 layout, with an int4 LM head; and group 64
+    with an f16 LM head): every batched GEMM first decodes its matrix to f16 (one more launch per
+    GEMM). Per-sequence logits against the oracle after the prompt, then greedy continuations."""
+    s = synth.build(1024, 3584, layers=4, vocab=8192, kind=kind, embed_kind="q4" if kind == "q4" else "f16",
+                    seed=24)
+    m = qne.Model(s.index_json, s.weights)
+    B, L, steps = 3, 10, 8
+    prompts = np.stack([synth.prompt_ids(L, 400 + b, 8192) for b in range(B)])
+    bt = qne.Batch(m, B)
+    for t in range(L):
+        launches0 = qne.kernel_launches()
+        nxt, lg = bt.step(prompts[:, t], np.full(B, t), want_logits=True)
+        int4_gemms = 4 * m.layers + (1 if kind == "q4" else 0)  # the LM head is int4 only for q4 here
+        assert qne.kernel_launches() - launches0 == 6 * m.layers + 3 + int4_gemms
+    ids = [nxt.copy()]
+    cur = nxt.copy()
+    for i in range(steps):
+        cur = bt.step(cur, np.full(B, L + i))
+        ids.append(cur.copy())
+    ids = np.stack(ids, 1)
+    om = oracle.OracleModel(s.index_json, s.weights, kv_f16=True)
+    for b in range(B):
+        om.reset()
+        want = om.prefill(prompts[b])
+        err = np.abs(lg[b].astype(np.float64) - want).max()
+        assert err <= 2e-2 and rc.rel_err(lg[b], want) <= 1e-3, (b, err)
+        want_ids, margins = om.greedy(want, L, steps + 1)
+        for i, (a, w_) in enumerate(zip(ids[b], want_ids)):
+            if a != w_:
+                assert margins[i] < 4e-2, (b, i, a, w_, margins[i])
+                break
+    om.close()
+    bt.close()
+    m.close()
+
+
 def test_page_table_permutation_is_bit_exact(tiny):
     s, m = tiny
     B, L = 3, 40

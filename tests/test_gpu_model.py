@@ -109,10 +109,8 @@ def test_chunked_prefill_equals_one_pass(tiny):
     m.reset()
     m.prefill_chunk(prompt[:32], 0, False)
     m.prefill_chunk(prompt[32:], 32, True)
-    if kind == "f16":  # batched chunks (tensor-core GEMMs): within the parity tolerance
-        logits_close(m.logits(), a.astype(np.float64))
-    else:  # int4: prefill_chunk runs the per-token kernels, bitwise equal
-        assert np.array_equal(a, m.logits())
+    # batched chunks (tensor-core GEMMs; int4 matrices decoded to f16 first): within the tolerance
+    logits_close(m.logits(), a.astype(np.float64))
     assert m.last_token()[1] == 50
 
 

@@ -1,4 +1,4 @@
-"""Batched prompt processing (qne_prefill_chunk on f16 weights: 64-token chunks through the
+"""Batched prompt processing (qne_prefill_chunk: 64-token chunks through the
 tensor-core GEMMs, the chunked GDN scan, K/V append + causal attention) against the CPU oracle
 and against the per-token path (qne_prefill), on the same random-init weights and token ids.
 
@@ -150,20 +150,43 @@ def test_batched_prefill_long_context_agrees_with_per_token(cuda):
     m.close()
 
 
-def test_int4_weights_fall_back_to_per_token(cuda):
-    """The batched GEMM takes f16 weights; int4 models run prefill_chunk one token per step,
-    bitwise equal to qne_prefill."""
-    s = synth.build(1024, 3584, layers=4, vocab=4096, kind="q4g64", seed=23)
+@pytest.mark.parametrize("kind", ["q4", "q4g64"])
+@pytest.mark.parametrize("n", [20, 64, 100])
+def test_int4_batched_prefill(cuda, kind, n):
+    """int4 decoder matrices (the reference converter's block-32 layout, and group 64): each is
+    decoded to f16 by one more launch before its chunk GEMM. Logits against the oracle and against
+    the per-token path (qne_prefill), the greedy continuation, and the launch count."""
+    s = synth.build(1024, 3584, layers=4, vocab=4096, kind=kind, embed_kind="q4" if kind == "q4" else "f16",
+                    seed=23)
     m = qne.Model(s.index_json, s.weights)
-    prompt = synth.prompt_ids(20, 12, 4096)
+    om = oracle.OracleModel(s.index_json, s.weights, kv_f16=True)
+    assert m.prefill_batched_supported
+    prompt = synth.prompt_ids(n, 12, 4096)
     m.prefill(prompt)
-    a = m.logits().copy()
+    a, ids_a = m.logits().copy(), m.decode(8, 1)
+    m.reset()
+    m.prefill_chunk(prompt, 0, True)  # records the chunk graphs
     m.reset()
     launches0 = qne.kernel_launches()
     m.prefill_chunk(prompt, 0, True)
-    assert qne.kernel_launches() - launches0 == 20 * m.dispatches_per_token() - 19
-    assert np.array_equal(a, m.logits())
+    per_chunk = 6 * m.layers + 2 + m.layers // 4 + 4 * m.layers  # + one decode launch per GEMM
+    assert qne.kernel_launches() - launches0 == -(-n // qne.PREFILL_CHUNK_TOKENS) * per_chunk + 1
+    b = m.logits().copy()
+    want = om.prefill(prompt)
+    logits_close(b, want)
+    logits_close(b, a.astype(np.float64))
+    same_pick(b, want)
+    ids_b = m.decode(8, 1)
+    want_ids, margins = om.greedy(want, n, 8)
+    for i, (x, y) in enumerate(zip(ids_b, want_ids)):
+        if x != y:
+            assert margins[i] < 2 * MAX_ABS, (i, x, y)
+            break
+    if ids_a != ids_b:  # per-token and batched agree unless a near-tie flipped a pick
+        i = next(i for i, (x, y) in enumerate(zip(ids_a, ids_b)) if x != y)
+        assert margins[i] < 2 * MAX_ABS
     m.close()
+    om.close()
 
 
 @pytest.mark.slow

@@ -33,7 +33,7 @@ def _rank(rank, world, port, out):
 
 def test_two_gloo_ranks_agree_on_the_slowest_time():
     world, port = 2, _free_port()
-    with mp.Manager() as mgr:
+    with mp.get_context("spawn").Manager() as mgr:  # no fork: earlier tests leave threads running
         out = mgr.dict()
         mp.spawn(_rank, args=(world, port, out), nprocs=world, join=True)
         res = dict(out)
