@@ -11,8 +11,9 @@
 //    activation batch (N = 16, 32 or 64 columns of the MMA, zero-filled past the batch);
 //  * warp 0 lane 0 streams 64-wide k-blocks of the weight tile and of both activation planes
 //    with TMA (128-byte swizzle, the canonical K-major layout of the MMA operands) into a 6-stage
-//    ring guarded by mbarriers; weight loads of the first stages are issued before waiting on the
-//    previous kernel, whose output the activations are;
+//    ring guarded by mbarriers (3 stages, three CTAs per SM, when the tiles fill more than two
+//    waves, as in the batched LM head); weight loads of the first stages are issued before
+//    waiting on the previous kernel, whose output the activations are;
 //  * warp 1 lane 0 issues tcgen05.mma (M = 128, K = 16, f32 accumulator in tensor memory), two
 //    per k-step (hi and lo planes), and frees each stage with tcgen05.commit;
 //  * split-K runs across the CTAs of a thread-block cluster: every CTA moves its accumulator
@@ -36,7 +37,9 @@ namespace qne {
 namespace {
 
 constexpr int kTcThreads = 128;
-constexpr int kTcStages = 6;
+constexpr int kTcStages = 6;      // ring depth of one CTA per SM (most GEMMs: one wave of tiles)
+constexpr int kTcStagesWide = 3;  // many waves of tiles (the batched LM head): three CTAs per SM,
+                                  // so CTAs' epilogues overlap the others' weight streams
 constexpr int kBK = 64;                 // k per stage: one 128-byte swizzle span of f16
 constexpr int kTileA = 128 * kBK * 2;   // 16 KB of weights per stage
 constexpr int kMaxCluster = 8;
@@ -164,12 +167,12 @@ __device__ __forceinline__ void split_hilo_tc(float x, __half& hi, __half& lo) {
   lo = __float2half_rn(x - __half2float(hi));
 }
 
-template <int N, bool SW>
+template <int N, bool SW, int ST>
 __global__ void __launch_bounds__(kTcThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap txh,
                    const __grid_constant__ CUtensorMap txl, const __grid_constant__ TcArgs a) {
   extern __shared__ uint8_t dsm_raw[];
-  __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], accb;
+  __shared__ __align__(8) uint64_t full[ST], empty[ST], accb;
   __shared__ uint32_t tmem_slot;
   __shared__ float inv_s[kGemmMaxRows];
   constexpr int kTileB = N * kBK * 2;  // one activation plane per stage
@@ -192,7 +195,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   if (tid == 32) {
-    for (int s = 0; s < kTcStages; ++s) {
+    for (int s = 0; s < ST; ++s) {
       mbar_init(smem_u32(&full[s]), 1);
       mbar_init(smem_u32(&empty[s]), 1);
     }
@@ -212,8 +215,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // kernel wrote the weights, w_after_wait).
     const int r0 = SW ? tile * 64 : tile * 128;
     auto load_a = [&](int i) {
-      const uint32_t st = sbase + (uint32_t)((i % kTcStages) * kStage);
-      const uint32_t bar = smem_u32(&full[i % kTcStages]);
+      const uint32_t st = sbase + (uint32_t)((i % ST) * kStage);
+      const uint32_t bar = smem_u32(&full[i % ST]);
       const int kx = (kb0 + i) * kBK;
       mbar_arrive_expect_tx(bar, (uint32_t)kStage);
       if (SW) {
@@ -224,13 +227,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
     };
     auto load_b = [&](int i) {
-      const uint32_t st = sbase + (uint32_t)((i % kTcStages) * kStage);
-      const uint32_t bar = smem_u32(&full[i % kTcStages]);
+      const uint32_t st = sbase + (uint32_t)((i % ST) * kStage);
+      const uint32_t bar = smem_u32(&full[i % ST]);
       const int kx = (kb0 + i) * kBK;
       tma_load_2d(st + kTileA, &txh, kx, 0, bar);
       tma_load_2d(st + kTileA + kTileB, &txl, kx, 0, bar);
     };
-    const int pre = min(kTcStages, nkb);
+    const int pre = min(ST, nkb);
     if (!a.w_after_wait)
       for (int i = 0; i < pre; ++i) load_a(i);
     pdl_wait();
@@ -238,7 +241,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       for (int i = 0; i < pre; ++i) load_a(i);
     for (int i = 0; i < pre; ++i) load_b(i);
     for (int i = pre; i < nkb; ++i) {
-      if (!mbar_wait(smem_u32(&empty[i % kTcStages]), (uint32_t)((i / kTcStages) + 1) & 1u, a.err)) {
+      if (!mbar_wait(smem_u32(&empty[i % ST]), (uint32_t)((i / ST) + 1) & 1u, a.err)) {
         ok = false;
         break;
       }
@@ -249,8 +252,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // MMA issuer: 4 k-steps of 16 per stage, hi and lo planes into one accumulator.
     constexpr uint32_t idesc = instr_desc_f16<N>();
     for (int i = 0; i < nkb; ++i) {
-      const int s = i % kTcStages;
-      if (!mbar_wait(smem_u32(&full[s]), (uint32_t)(i / kTcStages) & 1u, a.err)) {
+      const int s = i % ST;
+      if (!mbar_wait(smem_u32(&full[s]), (uint32_t)(i / ST) & 1u, a.err)) {
         ok = false;
         break;
       }
@@ -295,8 +298,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (a.sumsq_in && tid >= 64 && tid < 64 + B) {
     const int b = tid - 64;
     float ss = 0.f;
-#pragma unroll 8
-    for (int q = 0; q < a.sumsq_slots; ++q) ss += a.sumsq_in[q * kSumsqLd + b];
+    for (int q0 = 0; q0 < a.sumsq_slots; q0 += 32) {  // 32 loads in flight, then the sums in order
+      float v[32];
+#pragma unroll
+      for (int q = 0; q < 32; ++q) v[q] = q0 + q < a.sumsq_slots ? a.sumsq_in[(q0 + q) * kSumsqLd + b] : 0.f;
+#pragma unroll
+      for (int q = 0; q < 32; ++q) ss += v[q];
+    }
     inv_s[b] = rsqrtf(ss / (float)a.norm_k + a.eps);
   }
   float yv[SW ? 1 : kYv][4];
@@ -497,11 +505,11 @@ int max_clusters(K kernel, size_t smem, int ranks) {
   return n;
 }
 
-template <int N, bool SW>
-cudaError_t launch_tc_nsw(const GemmArgs& g, cudaStream_t stream, bool pdl) {
-  auto kernel = gemm_tc_kernel<N, SW>;
+template <int N, bool SW, int ST>
+cudaError_t launch_tc(const GemmArgs& g, cudaStream_t stream, bool pdl) {
+  auto kernel = gemm_tc_kernel<N, SW, ST>;
   constexpr int kStage = kTileA + 2 * N * kBK * 2;
-  const size_t smem = (size_t)kTcStages * kStage + 1024;
+  const size_t smem = (size_t)ST * kStage + 1024;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   TcArgs a;
@@ -554,6 +562,14 @@ cudaError_t launch_tc_nsw(const GemmArgs& g, cudaStream_t stream, bool pdl) {
   cfg.numAttrs = pdl ? 2 : 1;
   count_launch();
   return cudaLaunchKernelEx(&cfg, kernel, tw, txh, txl, a);
+}
+
+template <int N, bool SW>
+cudaError_t launch_tc_nsw(const GemmArgs& g, cudaStream_t stream, bool pdl) {
+  const int out_tile = SW ? 64 : 128;
+  const int tiles = ((SW ? g.rows / 2 : g.rows) + out_tile - 1) / out_tile;
+  if (!SW && tiles > 2 * kCtaSlots) return launch_tc<N, SW, kTcStagesWide>(g, stream, pdl);
+  return launch_tc<N, SW, kTcStages>(g, stream, pdl);
 }
 
 }  // namespace

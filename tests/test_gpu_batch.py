@@ -21,7 +21,8 @@ def dev(a):
 @pytest.mark.parametrize("batch", [1, 3, 8, 13, 16, 17, 32, 33, 50, 64])
 @pytest.mark.parametrize("epilogue,rows,k", [("store", 1024, 1024), ("accumulate", 1024, 3584), ("swiglu", 2 * 3584, 1024),
                                              ("store", 8224, 2048), ("store", 4099, 1024), ("accumulate", 2048, 6144),
-                                             ("swiglu", 2 * 6144, 2048), ("store", 1000, 96), ("swiglu", 2 * 200, 4160)])
+                                             ("swiglu", 2 * 6144, 2048), ("store", 1000, 96), ("swiglu", 2 * 200, 4160),
+                                             ("store", 40000, 1024)])  # > 2 waves of tiles: the 4-stage ring
 def test_gemm_matches_gemv_per_sequence(cuda, impl, batch, epilogue, rows, k):
     if impl == "mma_sync" and batch > 32:
         pytest.skip("the mma.sync GEMM takes batch 1..32")
