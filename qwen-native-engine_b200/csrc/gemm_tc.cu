@@ -14,8 +14,9 @@
 //    ring guarded by mbarriers (3 stages, three CTAs per SM, when the tiles fill more than two
 //    waves, as in the batched LM head); weight loads of the first stages are issued before
 //    waiting on the previous kernel, whose output the activations are;
-//  * warp 1 lane 0 issues tcgen05.mma (M = 128, K = 16, f32 accumulator in tensor memory), two
-//    per k-step (hi and lo planes), and frees each stage with tcgen05.commit;
+//  * warp 1 lane 0 issues tcgen05.mma (M = 128, K = 16, f32 accumulators in tensor memory), one
+//    of width 2N per k-step over the hi and lo tiles together, and frees each stage with
+//    tcgen05.commit;
 //  * split-K runs across the CTAs of a thread-block cluster: every CTA moves its accumulator
 //    from tensor memory to shared memory, and after a cluster barrier each CTA reduces a slice of
 //    the rows over all ranks' shared memory in rank order (deterministic) and applies the
@@ -177,7 +178,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __shared__ float inv_s[kGemmMaxRows];
   constexpr int kTileB = N * kBK * 2;  // one activation plane per stage
   constexpr int kStage = kTileA + 2 * kTileB;
-  constexpr int kTmemCols = N < 32 ? 32 : N;
+  constexpr int kTmemCols = 2 * N < 32 ? 32 : 2 * N;  // accumulator columns: N of hi, then N of lo
   constexpr int kPitch = N + 4;  // partial rows in shared memory: 16-byte aligned, conflict-free v4 stores
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(base);
@@ -249,8 +250,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       load_b(i);
     }
   } else if (warp == 1 && lane == 0 && nkb > 0) {
-    // MMA issuer: 4 k-steps of 16 per stage, hi and lo planes into one accumulator.
-    constexpr uint32_t idesc = instr_desc_f16<N>();
+    // MMA issuer: 4 k-steps of 16 per stage. The hi and lo activation tiles sit back to back in
+    // the stage, which is the layout of one operand of 2N rows: one MMA of width 2N per k-step
+    // (the tensor core's cost here is per instruction, so this halves the MMA time); accumulator
+    // columns [0, N) collect W x_hi and [N, 2N) W x_lo, added in the epilogue.
+    constexpr uint32_t idesc = instr_desc_f16<2 * N>();
     for (int i = 0; i < nkb; ++i) {
       const int s = i % ST;
       if (!mbar_wait(smem_u32(&full[s]), (uint32_t)(i / ST) & 1u, a.err)) {
@@ -263,7 +267,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       for (int kk = 0; kk < kBK / 16; ++kk) {
         const uint64_t ad = smem_desc_sw128(st + kk * 32);
         mma_f16(tmem, ad, smem_desc_sw128(st + kTileA + kk * 32), idesc, (i | kk) != 0);
-        mma_f16(tmem, ad, smem_desc_sw128(st + kTileA + kTileB + kk * 32), idesc, 1u);
       }
       mma_commit(smem_u32(&empty[s]));
     }
@@ -328,7 +331,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (nkb > 0) {
       if (!mbar_wait(smem_u32(&accb), 0u, a.err)) ok = false;
       tc_fence_after();
-      tmem_load_row<N>(tmem + ((uint32_t)(warp * 32) << 16), v);
+      const uint32_t row = tmem + ((uint32_t)(warp * 32) << 16);
+      float u[N];
+      tmem_load_row<N>(row, v);
+      tmem_load_row<N>(row + (uint32_t)N, u);
+#pragma unroll
+      for (int c = 0; c < N; ++c) v[c] += u[c];  // W x_hi + W x_lo
     } else {
 #pragma unroll
       for (int c = 0; c < N; ++c) v[c] = 0.f;
