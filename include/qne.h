@@ -222,10 +222,11 @@ QNE_API const float* qne_logits_device(const qne_model* m);
 /* Batched decode: independent sequences sharing one weight copy                            */
 /* ---------------------------------------------------------------------------------------- */
 
-/* Creates `batch` independent sequences, each with its own GDN states and a page table of
- * QNE_MAX_CONTEXT / QNE_PAGE_TOKENS entries into a shared pool of `pool_pages` pages per
+/* Creates `batch` (1..32) independent sequences, each with its own GDN states and a page table
+ * of QNE_MAX_CONTEXT / QNE_PAGE_TOKENS entries into a shared pool of `pool_pages` pages per
  * attention layer (pool_pages >= batch * 256). The default page table maps sequence b's
- * logical page i to physical page b * 256 + i. */
+ * logical page i to physical page b * 256 + i. f16 and int4 weights (an int4 matrix is decoded
+ * to an f16 scratch, sized for the largest one, before each of its GEMMs). */
 QNE_API qne_status qne_batch_create(qne_model* m, uint32_t batch, uint32_t pool_pages, qne_batch** out);
 QNE_API void qne_batch_free(qne_batch* b);
 /* Replaces the page tables (host, batch x 256 entries, each < pool_pages). */
