@@ -316,11 +316,14 @@ def micro(args):
                                 "us": round(us, 2), "GBs": round(gbs, 1), "frac_of_" + peak_kind: round(gbs / peak, 4),
                                 "bytes": nbytes})
                 keep.clear()
-    if sel & {"all", "gemm"}:
-        # the batched GEMM on the decoder's shapes (2B and 0.8B), B = 32 and 8 activation rows
-        for (rows, K, epi) in ((8224, 2048, "store"), (2048, 2048, "accumulate"), (12288, 2048, "swiglu"),
-                               (2048, 6144, "accumulate"), (8224, 1024, "store"), (1024, 2048, "accumulate"),
-                               (7168, 1024, "swiglu"), (1024, 3584, "accumulate"), (248320, 1024, "store")):
+    if sel & {"all", "gemm", "gemm1"}:
+        # the batched GEMM on the decoder's shapes (2B and 0.8B), B = 32 and 8 activation rows;
+        # gemm1: only the 0.8B gate_up (SwiGLU) GEMM at B = 32 on the tensor-core kernel (ncu)
+        shapes = ((8224, 2048, "store"), (2048, 2048, "accumulate"), (12288, 2048, "swiglu"),
+                  (2048, 6144, "accumulate"), (8224, 1024, "store"), (1024, 2048, "accumulate"),
+                  (7168, 1024, "swiglu"), (1024, 3584, "accumulate"), (248320, 1024, "store"))
+        one = not sel & {"all", "gemm"}
+        for (rows, K, epi) in (((7168, 1024, "swiglu"),) if one else shapes):
             nbytes = rows * K * 2
             copies = max(1, min(16, int(2.5e8 // nbytes) + 1))
             mats = []
@@ -329,10 +332,10 @@ def micro(args):
                 mats.append(qne.matrix("f16", rows, K, w))
                 keep.append(w)
             out_rows = rows // 2 if epi == "swiglu" else rows
-            for B in (32, 8):
+            for B in ((32,) if one else (32, 8)):
                 x = torch.randn(B, K, device="cuda")
                 y = torch.zeros(B, out_rows, device="cuda")
-                for impl in ("tcgen05", "mma_sync"):
+                for impl in (("tcgen05",) if one else ("tcgen05", "mma_sync")):
                     us = timed(lambda i: qne.gemm(mats[i], x, B, y, epi, stream=stream.cuda_stream, impl=impl),
                                copies, max(2, 64 // copies))
                     gbs = nbytes / (us * 1e-6) / 1e9
@@ -452,7 +455,7 @@ def main():
                     help="B=1 workload: benchmark config 1 (0.8B f16), 2 (2B f16, the headline) or 3 (2B int4 g64)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--micro", default="", help="config-5 microbench: all | gemv,gdn,attn; "
-                                                     "step4 = the small decode workload of the ncu captures; "
+                                                     "step4 = the small decode workload of the ncu captures; gemm1 = one batched GEMM shape; "
                                                      "prefill = the last 64-token chunk of the bench prompt")
     ap.add_argument("--no-batched", action="store_true", help="skip the config-4 batched decode run")
     ap.add_argument("--batched-only", action="store_true", help="run only the config-4 batched decode (profiling)")
