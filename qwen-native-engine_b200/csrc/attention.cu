@@ -63,6 +63,8 @@ size_t attention_scratch_bytes(int batch) {
 
 cudaError_t launch_attention(const AttnArgs& a, uint32_t pool_pages, int split_tokens,
                              cudaStream_t stream, bool pdl) {
+  // A split is whole 64-token sub-blocks, and the scratch holds at most kMaxSplits of them.
+  if (split_tokens < kSub || split_tokens % kSub) return cudaErrorInvalidValue;
   KernelArgs ka;
   ka.a = a;
   ka.split = split_tokens;
