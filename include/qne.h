@@ -101,9 +101,19 @@ QNE_API uint64_t qne_kernel_launches(void);
 /* Model::load, kernels/src/model.rs:171. Parses and validates index.json (host, n bytes, not
  * NUL-terminated) against weights (host, weights_len bytes) as Index::validate does
  * (kernels/src/model.rs:51-86), uploads every tensor once per (offset, bytes) pair, and builds
- * the per-token launch graph. The caller may free both host buffers after the call. */
+ * the per-token launch graph. The caller may free both host buffers after the call. Like the
+ * reference, it accepts only the Qwen3.5-0.8B and -2B architectures (24 layers, attention every
+ * 4th, (hidden, intermediate) (1024, 3584) or (2048, 6144), vocab 248320, rope_dim 64, theta 1e7)
+ * and rejects others with QNE_EFORMAT and "unsupported model architecture: these kernels require
+ * Qwen3.5-0.8B or Qwen3.5-2B". Matrices may be q4 (the reference's kind), f16 or q4g64. */
 QNE_API qne_status qne_model_load(const char* index_json, size_t index_len, const void* weights,
                           size_t weights_len, int device, qne_model** out);
+/* qne_model_load with flags (no counterpart in the reference). QNE_LOAD_ANY_SHAPE also accepts
+ * other layer counts (1..256), attention periods, vocabularies and widths (hidden, intermediate:
+ * multiples of 256 up to 8192 / 16384) with the same head geometry, e.g. small test models. */
+#define QNE_LOAD_ANY_SHAPE 1u
+QNE_API qne_status qne_model_load_ex(const char* index_json, size_t index_len, const void* weights,
+                                     size_t weights_len, int device, uint32_t flags, qne_model** out);
 QNE_API void qne_model_free(qne_model* m);
 QNE_API qne_status qne_model_info_get(const qne_model* m, qne_model_info* out);
 /* Runs the model's work on `cuda_stream` (a cudaStream_t of the model's device; NULL = the
@@ -288,8 +298,9 @@ QNE_API qne_status qne_gemm_ex(const qne_matrix* m, const float* x, int batch, f
  * all created at model load): the same kernels, with x's hi/lo planes and the SwiGLU
  * intermediate in one static 2 MiB device array instead of a workspace grown with cudaMalloc.
  * For callers whose device memory is fully planned or who cannot afford an allocation's
- * synchronization. Rejects calls needing more than 2 MiB (2*Bp*k*2 bytes, plus 2*Bp*out_rows*2
- * with SwiGLU; Bp = batch rounded up to 8) with QNE_EINVAL. The first call on a device sets up
+ * synchronization. batch 1..64 and f16 weights with k % 32 == 0, as qne_gemm. Rejects calls needing
+ * more than 2 MiB (2*Bp*k*2 bytes, plus 2*Bp*out_rows*2 with SwiGLU; Bp = batch rounded up to 8)
+ * with QNE_EINVAL. The first call on a device sets up
  * the array's address; make it before any stream capture. One array per device: overlapping
  * calls on one device race; serialize them on one stream. */
 QNE_API qne_status qne_gemm_noalloc(const qne_matrix* m, const float* x, int batch, float* y, int epilogue,

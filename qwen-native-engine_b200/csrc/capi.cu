@@ -65,10 +65,17 @@ uint64_t qne_kernel_launches(void) { return launches_issued(); }
 
 qne_status qne_model_load(const char* index_json, size_t index_len, const void* weights,
                           size_t weights_len, int device, qne_model** out) {
+  return qne_model_load_ex(index_json, index_len, weights, weights_len, device, 0, out);
+}
+
+qne_status qne_model_load_ex(const char* index_json, size_t index_len, const void* weights, size_t weights_len,
+                             int device, uint32_t flags, qne_model** out) {
   if (!out) return fail(QNE_EINVAL, "null output handle");
   *out = nullptr;
+  if (flags & ~(uint32_t)QNE_LOAD_ANY_SHAPE) return fail(QNE_EINVAL, "unknown load flags");
   return guarded([&] {
-    *out = reinterpret_cast<qne_model*>(Model::load(index_json, index_len, weights, weights_len, device));
+    *out = reinterpret_cast<qne_model*>(
+        Model::load(index_json, index_len, weights, weights_len, device, (flags & QNE_LOAD_ANY_SHAPE) != 0));
   });
 }
 

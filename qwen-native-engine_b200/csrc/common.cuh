@@ -22,6 +22,7 @@ constexpr int kHeadDim = 256;
 constexpr int kAttnProj = 5120;     // q, gate (2 x 2048) + k, v (2 x 512)
 constexpr int kRopeHalf = 32;       // rotate-half pairs (i, i + 32), i < 32
 constexpr int kMixerOut = 2048;
+constexpr int kVocab = 248320;     // VOCAB, kernels/src/lib.rs (the two Qwen3.5 sizes)
 // One KV page: [K, V][kv head][token][dim] f16.
 constexpr int kPageElems = 2 * kKvHeads * kPageTokens * kHeadDim;  // 16384 halves = 32 KB
 constexpr int kNumSms = 148;

@@ -14,6 +14,7 @@
 // call per device before any stream capture, so that capture never sees the set-up.
 //
 // Limits and contracts:
+// - batch 1..64 (kGemmMaxRows), as qne_gemm.
 // - A call needs 2 * Bp * k * 2 bytes for the x hi/lo planes (Bp = batch rounded up to 8), plus
 //   2 * Bp * out_rows * 2 bytes with the SwiGLU epilogue; calls needing more than kScratchBytes
 //   are rejected with QNE_EINVAL before anything is launched.
@@ -72,7 +73,7 @@ qne_status qne_gemm_noalloc(const qne_matrix* m, const float* x, int batch, floa
     if (!m || !x || !y) throw QneError(kEInval, "null argument");
     if (m->kind != QNE_KIND_F16) throw QneError(kEInval, "batched GEMM supports f16 weights");
     if (epilogue < 0 || epilogue > 2) throw QneError(kEInval, "unknown epilogue");
-    if (batch < 1 || batch > 32) throw QneError(kEInval, "batch must be 1..32");
+    if (batch < 1 || batch > kGemmMaxRows) throw QneError(kEInval, "batch must be 1..64");
     if (m->k % 32 || m->k <= 0 || m->rows <= 0) throw QneError(kEInval, "batched GEMM needs k % 32 == 0");
     if (epilogue == QNE_EPI_SWIGLU && m->rows % 2) throw QneError(kEInval, "SwiGLU needs an even row count");
     const int Bp = (batch + 7) / 8 * 8;

@@ -93,7 +93,7 @@ Model::~Model() {
 }
 
 Model* Model::load(const char* json, size_t json_len, const void* weights, size_t weights_len,
-                   int device) {
+                   int device, bool any_shape) {
   if (!json || !weights) throw QneError(kEInval, "null index or weights");
   if (device < 0) throw QneError(kEInval, "negative device index");
 
@@ -120,8 +120,17 @@ Model* Model::load(const char* json, size_t json_len, const void* weights, size_
   c.vocab = as_int(num(*cj, "vocab"), "config.vocab");
   c.theta = num(*cj, "rope_theta");
   c.rope_dim = as_int(num(*cj, "rope_dim"), "config.rope_dim");
-  // The kernels need: rotary width 64, hidden and intermediate multiples of 256 (16-byte chunks
-  // per lane of a warp, int4 blocks of 32), fixed head geometry (implied by the matrix shapes).
+  // kernels/src/model.rs:51-55: the reference accepts the two Qwen3.5 sizes only (24 layers,
+  // attention every 4th, (hidden, intermediate) (1024, 3584) or (2048, 6144), vocab 248320, rotary
+  // width 64, theta 1e7), with this message.
+  const bool reference_arch = c.layers == 24 && c.every == 4 &&
+                              ((c.hidden == 1024 && c.inter == 3584) || (c.hidden == 2048 && c.inter == 6144)) &&
+                              c.vocab == kVocab && c.rope_dim == 64 && c.theta == 10000000.0;
+  if (!any_shape && !reference_arch)
+    throw QneError(kEFormat, "unsupported model architecture: these kernels require Qwen3.5-0.8B or Qwen3.5-2B");
+  // With QNE_LOAD_ANY_SHAPE the kernels still need: rotary width 64, hidden and intermediate
+  // multiples of 256 (16-byte chunks per lane of a warp, int4 blocks of 32), fixed head geometry
+  // (implied by the matrix shapes).
   if (c.layers < 1 || c.layers > 256 || c.every < 1 || c.hidden < 256 || c.hidden > 8192 ||
       c.hidden % 256 || c.inter < 256 || c.inter > 16384 || c.inter % 256 || c.vocab < 1 ||
       c.rope_dim != 64 || !(c.theta > 0))

@@ -78,8 +78,12 @@ class PrefillRunner;
 
 class Model {
  public:
+  // any_shape = false (the default of qne_model_load) accepts exactly the architectures the
+  // reference's Index::validate accepts (kernels/src/model.rs:51-55); true also accepts other
+  // layer counts, vocabularies and widths the kernels can run (qne_model_load_ex's
+  // QNE_LOAD_ANY_SHAPE, used by small test models).
   static Model* load(const char* json, size_t json_len, const void* weights, size_t weights_len,
-                     int device);
+                     int device, bool any_shape = false);
   ~Model();
 
   Config cfg;

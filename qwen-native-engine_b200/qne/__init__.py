@@ -10,8 +10,9 @@ Operators (`gemv`, `rmsnorm_gemv`, `dequant_rows`, `argmax`, `gdn_step`, `attent
 `kv_gather`, `embed`) take device tensors (torch is used only for device memory and streams)
 and call the sm_100a kernels directly.
 
-The shared library must exist: importing this module raises if libqne.so is missing, and no
-operation falls back to another implementation.
+The shared library is opened on first use (importing the package loads no native code); the
+first call raises ImportError if libqne.so is missing, and no operation falls back to another
+implementation.
 """
 from __future__ import annotations
 
@@ -75,6 +76,7 @@ def _load_lib() -> C.CDLL:
         "qne_version": (C.c_char_p, []),
         "qne_kernel_launches": (C.c_uint64, []),
         "qne_model_load": (I32, [C.c_char_p, SZ, P, SZ, I32, C.POINTER(P)]),
+        "qne_model_load_ex": (I32, [C.c_char_p, SZ, P, SZ, I32, U32, C.POINTER(P)]),
         "qne_model_free": (None, [P]),
         "qne_model_info_get": (I32, [P, C.POINTER(_Info)]),
         "qne_model_set_stream": (I32, [P, P]),
@@ -140,7 +142,19 @@ def _load_lib() -> C.CDLL:
     return lib
 
 
-lib = _load_lib()
+class _LazyLib:
+    """libqne.so, opened on first use: importing `qne` (for `qne.synth`, say) maps no native code,
+    and the first call of any entry point raises ImportError if the library is not built."""
+
+    _cdll: C.CDLL | None = None
+
+    def __getattr__(self, name: str):
+        if _LazyLib._cdll is None:
+            _LazyLib._cdll = _load_lib()
+        return getattr(_LazyLib._cdll, name)
+
+
+lib = _LazyLib()
 
 
 def _check(status: int) -> None:
@@ -179,10 +193,18 @@ class ModelTiles:
         _check(lib.qne_validate_tiles(b, len(b)))
 
 
-class Model:
-    """A loaded decoder on one GPU (kernels/src/model.rs:147-450)."""
+LOAD_ANY_SHAPE = 1
 
-    def __init__(self, index_json, weights, device: int = 0):
+
+class Model:
+    """A loaded decoder on one GPU (kernels/src/model.rs:147-450).
+
+    Like the reference's Model::load, only the Qwen3.5-0.8B and -2B architectures load; any other
+    raises QneError(EFORMAT, "unsupported model architecture: ..."). `any_shape=True`
+    (qne_model_load_ex with QNE_LOAD_ANY_SHAPE) also accepts smaller layer counts, vocabularies
+    and widths, as the tests' small models need."""
+
+    def __init__(self, index_json, weights, device: int = 0, any_shape: bool = False):
         if isinstance(index_json, str):
             index_json = index_json.encode()
         w = weights
@@ -193,7 +215,11 @@ class Model:
             arr = np.ascontiguousarray(w).view(np.uint8).reshape(-1)
             ptr, n = arr.ctypes.data, arr.nbytes
         h = C.c_void_p()
-        _check(lib.qne_model_load(index_json, len(index_json), C.c_void_p(ptr), n, device, C.byref(h)))
+        if any_shape:
+            _check(lib.qne_model_load_ex(index_json, len(index_json), C.c_void_p(ptr), n, device, LOAD_ANY_SHAPE,
+                                         C.byref(h)))
+        else:
+            _check(lib.qne_model_load(index_json, len(index_json), C.c_void_p(ptr), n, device, C.byref(h)))
         self._h = h
         info = _Info()
         _check(lib.qne_model_info_get(self._h, C.byref(info)))
@@ -210,8 +236,8 @@ class Model:
         self.adapter = lib.qne_adapter(self._h).decode()
 
     @classmethod
-    def load(cls, index_json, weights, device: int = 0) -> "Model":
-        return cls(index_json, weights, device)
+    def load(cls, index_json, weights, device: int = 0, any_shape: bool = False) -> "Model":
+        return cls(index_json, weights, device, any_shape)
 
     def close(self) -> None:
         for ref in getattr(self, "_samplers", []):  # samplers are freed before their model

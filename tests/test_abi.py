@@ -1,5 +1,6 @@
 """The C ABI library loads and exports every entry point include/qne.h declares; host-side
 validation paths answer with status codes and messages (no device needed)."""
+import ctypes as C
 import json
 import re
 from pathlib import Path
@@ -67,10 +68,42 @@ def tiny():
     return synth.build(1024, 3584, layers=4, vocab=512, seed=5)
 
 
-def load_err(index, weights):
+def load_err(index, weights, any_shape=True):
     with pytest.raises(qne.QneError) as e:
-        qne.Model(index, weights)
+        qne.Model(index, weights, any_shape=any_shape)
     return e.value
+
+
+REFERENCE_REJECTS = "unsupported model architecture: these kernels require Qwen3.5-0.8B or Qwen3.5-2B"
+
+
+def test_default_load_accepts_only_the_reference_architectures(tiny):
+    """kernels/src/model.rs:51-55 (Index::validate): 24 layers, attention every 4th, (hidden,
+    intermediate) (1024, 3584) or (2048, 6144), vocab 248320, rope_dim 64, theta 1e7; anything else
+    fails with the reference's message unless QNE_LOAD_ANY_SHAPE is given."""
+    w = tiny.weights
+    err = load_err(tiny.index_json, w, any_shape=False)  # 4 layers, vocab 512
+    assert err.name == "EFORMAT" and str(err).endswith(REFERENCE_REJECTS)
+    base = json.loads(tiny.index_json)
+    ok = {"layers": 24, "full_attention_every": 4, "hidden": 1024, "intermediate": 3584, "vocab": 248320,
+          "rope_theta": 10000000.0, "rope_dim": 64}
+    for size in ({"hidden": 1024, "intermediate": 3584}, {"hidden": 2048, "intermediate": 6144},
+                 {"hidden": 2048, "intermediate": 0}):
+        idx = dict(base, config=dict(ok, **size))
+        # the architecture passes; the tiny file's tensors then fail the size checks
+        e = load_err(json.dumps(idx), w, any_shape=False)
+        assert e.name == "EFORMAT" and "architecture" not in str(e), str(e)
+    for change in ({"layers": 23}, {"full_attention_every": 3}, {"hidden": 1024, "intermediate": 6144},
+                   {"hidden": 2048, "intermediate": 3584}, {"vocab": 248319}, {"rope_dim": 32},
+                   {"rope_theta": 1000000.0}, {"hidden": 4096, "intermediate": 0}):
+        idx = dict(base, config=dict(ok, **change))
+        e = load_err(json.dumps(idx), w, any_shape=False)
+        assert e.name == "EFORMAT" and str(e).endswith(REFERENCE_REJECTS), (change, str(e))
+    with pytest.raises(qne.QneError) as e:
+        h = C.c_void_p()
+        b = tiny.index_json.encode()
+        qne._check(qne.lib.qne_model_load_ex(b, len(b), C.c_void_p(w.ctypes.data), w.nbytes, 0, 6, C.byref(h)))
+    assert e.value.name == "EINVAL" and "flags" in str(e.value)
 
 
 def test_index_validation_rejects_bad_files_before_touching_a_device(tiny):
@@ -102,6 +135,6 @@ def test_index_validation_rejects_bad_files_before_touching_a_device(tiny):
     assert "invalid tensor range" in str(load_err(tiny.index_json, w[: w.nbytes - 4096]))
     # a valid file gets past validation and stops at the device (no GPU in this container)
     try:
-        qne.Model(tiny.index_json, w)
+        qne.Model(tiny.index_json, w, any_shape=True)
     except qne.QneError as e:
         assert e.name in ("ECUDA", "EINVAL")

@@ -62,7 +62,7 @@ def test_gemm_batch_limits(cuda):
 @pytest.fixture(scope="module")
 def tiny(cuda):
     s = synth.build(1024, 3584, layers=4, vocab=8192, kind="f16", seed=21)
-    m = qne.Model(s.index_json, s.weights)
+    m = qne.Model(s.index_json, s.weights, any_shape=True)
     yield s, m
     m.close()
 
@@ -104,7 +104,7 @@ def test_int4_batched_decode_matches_oracle(cuda, kind):
     GEMM). Per-sequence logits against the oracle after the prompt, then greedy continuations."""
     s = synth.build(1024, 3584, layers=4, vocab=8192, kind=kind, embed_kind="q4" if kind == "q4" else "f16",
                     seed=24)
-    m = qne.Model(s.index_json, s.weights)
+    m = qne.Model(s.index_json, s.weights, any_shape=True)
     B, L, steps = 3, 10, 8
     prompts = np.stack([synth.prompt_ids(L, 400 + b, 8192) for b in range(B)])
     bt = qne.Batch(m, B)

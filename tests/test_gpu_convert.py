@@ -15,7 +15,7 @@ VOCAB = 4096
 
 
 def check(index_json, weights, prompt):
-    m = qne.Model(index_json, weights)
+    m = qne.Model(index_json, weights, any_shape=True)
     om = oracle.OracleModel(index_json, weights, kv_f16=True)
     m.prefill(prompt)
     got, want = m.logits(), om.prefill(prompt)

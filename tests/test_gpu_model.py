@@ -51,7 +51,7 @@ def set_path(m, fused):
 def tiny(request, cuda):
     kind, fused = request.param
     s = synth.build(1024, 3584, layers=4, vocab=8192, kind=kind, seed=11)
-    m = qne.Model(s.index_json, s.weights)
+    m = qne.Model(s.index_json, s.weights, any_shape=True)
     set_path(m, fused)
     om = oracle.OracleModel(s.index_json, s.weights, kv_f16=True)
     yield kind, s, m, om
@@ -156,7 +156,7 @@ def test_context_limits_and_errors(tiny):
 
 def test_restore_without_snapshot(cuda):
     s = synth.build(1024, 3584, layers=4, vocab=512, seed=12)
-    m = qne.Model(s.index_json, s.weights)
+    m = qne.Model(s.index_json, s.weights, any_shape=True)
     with pytest.raises(qne.QneError) as e:
         m.restore()
     assert e.value.name == "ENOSNAP"
@@ -171,7 +171,7 @@ def test_fused_and_split_paths_agree(cuda):
     """The two launch paths on one model: logits within the parity tolerance, identical picks,
     and switching paths mid-sequence keeps the state (both read and write the same buffers)."""
     s = synth.build(1024, 3584, layers=8, vocab=8192, seed=13)
-    m = qne.Model(s.index_json, s.weights)
+    m = qne.Model(s.index_json, s.weights, any_shape=True)
     prompt = synth.prompt_ids(70, 6, 8192)
     out = {}
     for fused in (True, False):
@@ -194,7 +194,7 @@ def test_fused_kernels_at_a_long_context(cuda):
     """Attention splits of the fused kernel past one 64-token block and past 8 groups of splits:
     prefill 600 tokens, then compare against the per-operation kernels."""
     s = synth.build(1024, 3584, layers=4, vocab=4096, seed=14)
-    m = qne.Model(s.index_json, s.weights)
+    m = qne.Model(s.index_json, s.weights, any_shape=True)
     prompt = synth.prompt_ids(600, 7, 4096)
     res = []
     for fused in (True, False):
@@ -212,7 +212,7 @@ def test_fused_kernels_at_a_long_context(cuda):
 def test_config1_full_08b_parity(cuda, fused):
     """benchmark config 1: 0.8B-shaped f16 model (seed 0), 128 prompt ids (seed 0), greedy steps."""
     s = synth.build_config(1)
-    m = qne.Model(s.index_json, s.weights)
+    m = qne.Model(s.index_json, s.weights, any_shape=True)
     set_path(m, fused)
     om = oracle.OracleModel(s.index_json, s.weights, kv_f16=True)
     prompt = synth.prompt_ids(128, 0)
@@ -228,7 +228,7 @@ def test_config_2b_short_context_parity(cuda, cfg):
     """benchmark configs 2 (f16) and 3 (int4 g64) at a short context (the full 3968-token prefill on
     the CPU oracle takes too long for a test; attention at 4096 is covered by the operator tests)."""
     s = synth.build_config(cfg)
-    m = qne.Model(s.index_json, s.weights)
+    m = qne.Model(s.index_json, s.weights, any_shape=True)
     if cfg == 2:
         m.set_fused(True)  # the 2B f16 config runs through the fused layer kernels here
     om = oracle.OracleModel(s.index_json, s.weights, kv_f16=True)

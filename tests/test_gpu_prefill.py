@@ -34,7 +34,7 @@ def same_pick(got_logits, want_logits):
 @pytest.fixture(scope="module")
 def tiny(cuda):
     s = synth.build(1024, 3584, layers=4, vocab=VOCAB, kind="f16", seed=21)
-    m = qne.Model(s.index_json, s.weights)
+    m = qne.Model(s.index_json, s.weights, any_shape=True)
     om = oracle.OracleModel(s.index_json, s.weights, kv_f16=True)
     yield m, om
     m.close()
@@ -138,7 +138,7 @@ def test_batched_prefill_long_context_agrees_with_per_token(cuda):
     """600 tokens: attention over many 256-token splits and merge groups per row; batched and
     per-token prefill give logits within the tolerance and the same greedy continuation."""
     s = synth.build(1024, 3584, layers=4, vocab=4096, seed=22)
-    m = qne.Model(s.index_json, s.weights)
+    m = qne.Model(s.index_json, s.weights, any_shape=True)
     prompt = synth.prompt_ids(600, 11, 4096)
     m.prefill(prompt)
     a, ids_a = m.logits().copy(), m.decode(8, 1)
@@ -158,7 +158,7 @@ def test_int4_batched_prefill(cuda, kind, n):
     the per-token path (qne_prefill), the greedy continuation, and the launch count."""
     s = synth.build(1024, 3584, layers=4, vocab=4096, kind=kind, embed_kind="q4" if kind == "q4" else "f16",
                     seed=23)
-    m = qne.Model(s.index_json, s.weights)
+    m = qne.Model(s.index_json, s.weights, any_shape=True)
     om = oracle.OracleModel(s.index_json, s.weights, kv_f16=True)
     assert m.prefill_batched_supported
     prompt = synth.prompt_ids(n, 12, 4096)
@@ -194,7 +194,7 @@ def test_config2_batched_prefill_of_the_bench_prompt(cuda):
     """benchmark config 2 (2B f16): the bench's 3968-token prompt through the batched path and
     through the per-token path: logits within the tolerance, 32 identical greedy tokens."""
     s = synth.build_config(2)
-    m = qne.Model(s.index_json, s.weights)
+    m = qne.Model(s.index_json, s.weights, any_shape=True)
     prompt = synth.prompt_ids(3968, 1)
     m.prefill(prompt)
     a, ids_a = m.logits().copy(), m.decode(32, 1)

@@ -20,7 +20,7 @@ VOCAB = 248320
 @pytest.fixture(scope="module")
 def small(cuda):
     s = synth.build(1024, 3584, layers=4, vocab=512, seed=31)
-    m = qne.Model(s.index_json, s.weights)
+    m = qne.Model(s.index_json, s.weights, any_shape=True)
     yield m
     m.close()
 
@@ -28,7 +28,7 @@ def small(cuda):
 @pytest.fixture(scope="module")
 def full(cuda):
     s = synth.build(1024, 3584, layers=4, vocab=VOCAB, seed=32)
-    m = qne.Model(s.index_json, s.weights)
+    m = qne.Model(s.index_json, s.weights, any_shape=True)
     yield s, m
     m.close()
 
