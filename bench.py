@@ -132,42 +132,87 @@ def cpu_model() -> str:
     return "unknown"
 
 
-def cpu_oracle_rate(s, prompt_len: int, tokens: int, seed: int):
-    """Oracle decode rate on the host: `tokens` steps after a short untimed prefill."""
-    from oracle import oracle
+def bench_config(cfg_n: int, prompt_len: int, steps: int, world: int, l2_note: str | None = None) -> dict:
+    """The `config` object of the B=1 line, shared by both arms so that they name one workload."""
     from qne import synth
-    om = oracle.OracleModel(s.index_json, s.weights, kv_f16=True)
-    prompt = synth.prompt_ids(prompt_len, seed)
-    logits = om.prefill(prompt)
-    tok = oracle.argmax(logits)
+    info = synth.baseline_config(cfg_n)
+    size_name = {"0.8b": "0.8B", "2b": "2B"}[info["size"]]
+    c = {"workload": f"config {cfg_n}: Qwen3.5-{size_name}-shaped {info['kind']} hybrid decoder "
+                     f"(synthetic, seed {info['seed']}), B=1 per GPU, KV prefilled to {prompt_len}, "
+                     f"{steps} greedy decode steps",
+         "model": f"qwen3.5-{size_name.lower()}-shaped", "global_batch": world, "seq_len": 4096,
+         "parallelism": f"replicas x{world}"}
+    if l2_note:
+        c["l2"] = l2_note
+    return c
+
+
+def cpu_oracle_decode(om, prompt_len: int, warmup: int, tokens: int, first_token: int):
+    """Times `tokens` greedy oracle steps from the state `om` holds after a prompt of prompt_len
+    (snapshot taken by the caller): `warmup` untimed steps, restore, then the timed steps."""
+    from oracle import oracle
+    tok = first_token
+    for i in range(warmup):
+        tok = oracle.argmax(om.step(tok, prompt_len + i))
+    om.restore()
+    tok = first_token
     t0 = time.perf_counter()
     for i in range(tokens):
-        logits = om.step(tok, prompt_len + i)
-        tok = oracle.argmax(logits)
-    dt = time.perf_counter() - t0
+        tok = oracle.argmax(om.step(tok, prompt_len + i))
+    return tokens / (time.perf_counter() - t0)
+
+
+def cpu_baseline_sample(s, cfg_n: int, prompt_len: int, tokens: int = 48):
+    """cpu_baseline leg of our arm (rank 0, N=1): the oracle decoding `tokens` steps at the same
+    context as the timed GPU steps, its KV cache and GDN states filled with seeded synthetic history
+    (oracle_model_fill_synthetic) instead of a prompt (a step's cost depends on the context length,
+    not on the cached values)."""
+    from oracle import oracle
+    om = oracle.OracleModel(s.index_json, s.weights, kv_f16=True)
+    om.fill_synthetic(prompt_len, 7)
+    om.snapshot()
+    rate = cpu_oracle_decode(om, prompt_len, 2, tokens, 12345)
     om.close()
-    return tokens / dt, oracle.threads()
+    return rate, oracle.threads()
 
 
 def reference_arm(args, world, rank):
+    """`--impl reference`: the reference's decode arithmetic on the host cores (the CPU oracle, a
+    restatement of the reference WGSL decoder; the reference itself is Rust + wgpu and cannot run
+    here) on the workload of our arm: config 2, the same 3968-token prompt (brought in through the
+    oracle's batched CPU prefill, untimed), then `--warmup` untimed steps, a restore, and the timed
+    greedy steps from position 3968. Imports only the oracle and the synthetic-model generator: no
+    engine code is loaded. Rank 0 alone runs; the other ranks exit without work."""
     if rank != 0:
         return
+    from oracle import oracle
     from qne import synth
-    s = synth.build_config(2)
-    steps = min(args.steps, 16)
-    rate, cores = cpu_oracle_rate(s, 16, args.warmup, 1)  # warm-up, untimed
-    rate, cores = cpu_oracle_rate(s, 16, steps, 1)
+    cfg_n = args.config
+    info = synth.baseline_config(cfg_n)
+    steps = args.steps
+    prompt_len = min(args.prompt if args.prompt is not None else info["prompt"], 4096 - steps)
+    s = synth.build_config(cfg_n)
+    om = oracle.OracleModel(s.index_json, s.weights, kv_f16=True)
+    prompt = synth.prompt_ids(prompt_len, rank_seed(1, 0))
+    t0 = time.perf_counter()
+    logits = om.prefill_batched(prompt)
+    prefill_s = time.perf_counter() - t0
+    om.snapshot()
+    rate = cpu_oracle_decode(om, prompt_len, min(args.warmup, 4096 - prompt_len), steps, oracle.argmax(logits))
+    cores = oracle.threads()
+    om.close()
     line = {
         "impl": "reference", "metric": METRIC, "value": round(rate, 4), "unit": "tok/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000.0 / rate, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": {"workload": "config 2: Qwen3.5-2B-shaped f16 (seed 1), B=1 greedy decode", "global_batch": 1,
-                   "seq_len": 4096, "parallelism": "cpu"},
+        "steps": steps, "warmup": args.warmup, "ms_per_step": round(1000.0 / rate, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16" if info["kind"] == "f16" else "int4 (f32 math)",
+        "data": "synthetic",
+        "config": bench_config(cfg_n, prompt_len, steps, world),
         "cpu_baseline": {"value": round(rate, 4), "unit": "tok/s", "cores": cores, "cpu_model": cpu_model(),
                          "kind": "port",
-                         "sample": f"{steps} decode tokens of the 2B f16 model after a 16-token prefill (the CPU "
-                                   f"restatement of the reference WGSL decoder; attention at context 16-32 instead of "
-                                   f"3968 changes <2% of the bytes per token)"},
+                         "sample": f"{steps} greedy decode steps from position {prompt_len} after the bench's "
+                                   f"{prompt_len}-token prompt (CPU restatement of the reference WGSL decoder, "
+                                   f"all host threads; prompt through its batched CPU path in {prefill_s:.1f} s, "
+                                   f"untimed)"},
         "e2e": {"value": round(rate, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -609,10 +654,12 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        rate, cores = cpu_oracle_rate(s, 16, 4, 1)
+        cpu_tokens = 48
+        rate, cores = cpu_baseline_sample(s, cfg_n, prompt_len, cpu_tokens)
         cpu = {"value": round(rate, 4), "unit": "tok/s", "cores": cores, "cpu_model": cpu_model(), "kind": "port",
-               "sample": f"4 decode tokens of the same {size_name} {cfg_info['kind']} model after a 16-token "
-                         "prefill, CPU oracle (C++ restatement of the reference decoder, all host threads)"}
+               "sample": f"{cpu_tokens} greedy decode steps of the same {size_name} {cfg_info['kind']} model from "
+                         f"position {prompt_len} (KV cache and GDN states filled with seeded synthetic history), "
+                         "CPU oracle (C++ restatement of the reference decoder, all host threads)"}
 
     if rank == 0:
         value = aggregate_rate(world, steps, ms)
@@ -644,12 +691,8 @@ def main():
             "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": steps,
             "warmup": args.warmup, "ms_per_step": round(ms / steps, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-            "config": {"workload": f"config {cfg_n}: Qwen3.5-{size_name}-shaped {cfg_info['kind']} hybrid decoder "
-                                   f"(synthetic, seed {cfg_info['seed']}), B=1 per GPU, KV prefilled to {prompt_len}, "
-                                   f"{steps} greedy decode steps",
-                       "model": f"qwen3.5-{size_name.lower()}-shaped", "global_batch": world, "seq_len": 4096,
-                       "parallelism": f"replicas x{world}",
-                       "l2": f"inputs larger than L2 ({model.weight_bytes / 1e9:.2f} GB of weights per step)"},
+            "config": bench_config(cfg_n, prompt_len, steps, world,
+                                   f"inputs larger than L2 ({model_weight_bytes / 1e9:.2f} GB of weights per step)"),
             "e2e": {"value": round(aggregate_rate(world, steps, e2e_sampled_s * 1e3), 2), "unit": "tok/s",
                     "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8,
                     "loop": "qne_step_sample: decode step + device sampling (T 0.6, top_k 20, top_p 0.95)"},

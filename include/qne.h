@@ -137,6 +137,13 @@ QNE_API int qne_model_fused(const qne_model* m);
 QNE_API qne_status qne_model_set_phase_trace(qne_model* m, int enable);
 QNE_API qne_status qne_model_phase_trace(qne_model* m, uint64_t* out, size_t cap, size_t* n_out,
                                          size_t* ctas);
+/* Test hook of the fused path's bounded waits (no counterpart in the reference): with limit_us > 0
+ * every grid barrier of the fused layer kernels also waits for one arrival that never comes, with
+ * a limit of limit_us microseconds (at most 2 s), so each token's first barrier wait runs out; the
+ * kernels set the timeout flag in the control words and return, and the next call that reads them
+ * (qne_last_token, qne_decode) fails with QNE_ETIMEOUT and clears the flag. limit_us = 0 restores
+ * the normal barriers. QNE_EINVAL if the fused path is not available. */
+QNE_API qne_status qne_model_test_barrier_timeout(qne_model* m, uint32_t limit_us);
 /* Model::adapter, kernels/src/model.rs:167. */
 QNE_API const char* qne_adapter(const qne_model* m);
 /* Model::dispatches_per_token, kernels/src/model.rs:309. */

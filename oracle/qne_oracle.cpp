@@ -24,6 +24,7 @@
 #include <stdint.h>
 #include <string.h>
 
+#include <algorithm>
 #include <atomic>
 #include <condition_variable>
 #include <cstdlib>
@@ -344,6 +345,246 @@ struct Model {
   std::vector<float> h, xn, proj, mixed, act, logits;
 };
 
+
+// ------------------------------------------------------------------------------------------
+// Batched prompt processing on the CPU: the same per-token arithmetic as oracle_model_step for n
+// consecutive tokens, restructured so a 4000-token prompt takes seconds. The reference's batched
+// prefill (kernels/src/batch.rs:16-371, driven by kernels/src/model.rs:222-259) runs the token
+// graph's operators over chunks of tokens; here every operator runs over all n tokens at once.
+// Differences from n calls of oracle_model_step: only the f32 summation order of the matrix
+// products (blocked over rows and tokens instead of one row_dot per output). RMSNorm, the GDN
+// conv/recurrence/gated norm and attention use the per-token functions' loops in the same order,
+// so for equal inputs they give equal bits.
+// ------------------------------------------------------------------------------------------
+
+inline float hsum8(__m256 v) {
+  float t[8];
+  _mm256_storeu_ps(t, v);
+  return ((t[0] + t[1]) + (t[2] + t[3])) + ((t[4] + t[5]) + (t[6] + t[7]));
+}
+
+// out[r][t] = sum_c W[r][c] * X[t][c] for 4 rows of W (f32, row stride k) and NT token rows of X.
+template <int NT>
+void micro4(const float* W, const float* const* X, int k, float out[4][3]) {
+  __m256 acc[4][NT];
+  for (int r = 0; r < 4; ++r)
+    for (int t = 0; t < NT; ++t) acc[r][t] = _mm256_setzero_ps();
+  int c = 0;
+  for (; c + 8 <= k; c += 8) {
+    __m256 x[NT];
+    for (int t = 0; t < NT; ++t) x[t] = _mm256_loadu_ps(X[t] + c);
+    for (int r = 0; r < 4; ++r) {
+      const __m256 w = _mm256_loadu_ps(W + (size_t)r * k + c);
+      for (int t = 0; t < NT; ++t) acc[r][t] = _mm256_fmadd_ps(w, x[t], acc[r][t]);
+    }
+  }
+  for (int r = 0; r < 4; ++r)
+    for (int t = 0; t < NT; ++t) {
+      float v = hsum8(acc[r][t]);
+      for (int cc = c; cc < k; ++cc) v += W[(size_t)r * k + cc] * X[t][cc];
+      out[r][t] = v;
+    }
+}
+
+// Y[t][r] (=, +=, SwiGLU) for the n token rows X[t][0..k) against matrix m (epilogues as gemv;
+// for SwiGLU Y has rows/2 columns). Work is tiled as (16 output rows) x (96 tokens), with the
+// tiles of one token block running together so that block stays in the shared cache.
+void gemm_tokens(const Mat& m, const float* X, int n, float* Y, int ldy, int epi) {
+  const int k = m.k;
+  const int out = epi == 2 ? m.rows / 2 : m.rows;
+  constexpr int kRowBlk = 16, kTokBlk = 96;
+  const int rb_count = (out + kRowBlk - 1) / kRowBlk;
+  const int tb_count = (n + kTokBlk - 1) / kTokBlk;
+  parallel_for((long)rb_count * tb_count, [&](long task) {
+    const int tb = (int)(task / rb_count), rb = (int)(task % rb_count);
+    const int r0 = rb * kRowBlk, r1 = std::min(out, r0 + kRowBlk);
+    const int t0 = tb * kTokBlk, t1 = std::min(n, t0 + kTokBlk);
+    const int nr = r1 - r0;
+    // dequantized rows: [gate rows][up rows] for SwiGLU, padded to whole groups of 4
+    const int groups = epi == 2 ? 2 : 1;
+    static thread_local std::vector<float> wbuf;
+    const int pad_rows = (nr + 3) / 4 * 4;
+    wbuf.assign((size_t)groups * pad_rows * k, 0.f);
+    for (int g = 0; g < groups; ++g)
+      for (int r = 0; r < nr; ++r) {
+        float* dst = wbuf.data() + ((size_t)g * pad_rows + r) * k;
+        const long row = (long)r0 + r + (g ? out : 0);
+        if (m.kind == 0) {
+          const uint16_t* src = (const uint16_t*)m.w + (size_t)row * k;
+          int c = 0;
+          for (; c + 8 <= k; c += 8)
+            _mm256_storeu_ps(dst + c, _mm256_cvtph_ps(_mm_loadu_si128((const __m128i*)(src + c))));
+          for (; c < k; ++c) dst[c] = h2f(src[c]);
+        } else {
+          for (int c = 0; c < k; ++c) dst[c] = deq(m, row, c);
+        }
+      }
+    float res[2][kRowBlk][3];
+    for (int t = t0; t < t1; t += 3) {
+      const int nt = std::min(3, t1 - t);
+      const float* xs[3] = {X + (size_t)t * k, X + (size_t)(t + (nt > 1)) * k, X + (size_t)(t + 2 * (nt > 2)) * k};
+      for (int g = 0; g < groups; ++g)
+        for (int r = 0; r < pad_rows; r += 4) {
+          float o[4][3];
+          const float* wr = wbuf.data() + ((size_t)g * pad_rows + r) * k;
+          if (nt == 3) micro4<3>(wr, xs, k, o);
+          else if (nt == 2) micro4<2>(wr, xs, k, o);
+          else micro4<1>(wr, xs, k, o);
+          for (int i = 0; i < 4 && r + i < kRowBlk; ++i)
+            for (int j = 0; j < nt; ++j) res[g][r + i][j] = o[i][j];
+        }
+      for (int j = 0; j < nt; ++j) {
+        float* y = Y + (size_t)(t + j) * ldy;
+        for (int r = 0; r < nr; ++r) {
+          const float a = res[0][r][j];
+          if (epi == 0) y[r0 + r] = a;
+          else if (epi == 1) y[r0 + r] = y[r0 + r] + a;
+          else y[r0 + r] = silu(a) * res[1][r][j];
+        }
+      }
+    }
+  });
+}
+
+// gdn for n consecutive tokens: P[n][8224] projections, O[n][2048] gated outputs; conv_state and
+// state are updated as n calls of gdn() would. Each (head, 8 value columns) recurrence runs
+// sequentially over the tokens with its 128 x 8 state slice in registers/L1.
+void gdn_tokens(const float* P, int n, float* conv_state, const float* conv_w, float* state, const float* prm,
+                float* O) {
+  std::vector<float> cv((size_t)n * 6144);
+  parallel_for(6144 / 64, [&](long blk) {
+    for (int c = (int)blk * 64; c < (int)blk * 64 + 64; ++c) {
+      float w0 = conv_state[c * 3], w1 = conv_state[c * 3 + 1], w2 = conv_state[c * 3 + 2];
+      for (int t = 0; t < n; ++t) {
+        const float x = P[(size_t)t * kGdnProj + c];
+        const float y = w0 * conv_w[c * 4] + w1 * conv_w[c * 4 + 1] + w2 * conv_w[c * 4 + 2] + x * conv_w[c * 4 + 3];
+        cv[(size_t)t * 6144 + c] = silu(y);
+        w0 = w1;
+        w1 = w2;
+        w2 = x;
+      }
+      conv_state[c * 3] = w0;
+      conv_state[c * 3 + 1] = w1;
+      conv_state[c * 3 + 2] = w2;
+    }
+  });
+  // per (token, head): scaled unit q, unit k, decay g, beta, k.q
+  std::vector<float> qs((size_t)n * 2048), ks((size_t)n * 2048), gb((size_t)n * 48);
+  parallel_for((long)n * 16, [&](long i) {
+    const int t = (int)(i / 16), h = (int)(i % 16);
+    const float* q = cv.data() + (size_t)t * 6144 + h * 128;
+    const float* k = q + 2048;
+    const float* proj = P + (size_t)t * kGdnProj;
+    float nq = 0, nk = 0;
+    for (int j = 0; j < 128; ++j) {
+      nq += q[j] * q[j];
+      nk += k[j] * k[j];
+    }
+    nq = 1.0f / sqrtf(nq + 1e-6f);
+    nk = 1.0f / sqrtf(nk + 1e-6f);
+    float* qo = qs.data() + (size_t)t * 2048 + h * 128;
+    float* ko = ks.data() + (size_t)t * 2048 + h * 128;
+    for (int j = 0; j < 128; ++j) {
+      qo[j] = q[j] * nq * 0.08838834764f;
+      ko[j] = k[j] * nk;
+    }
+    float kq = 0;
+    for (int j = 0; j < 128; ++j) kq += ko[j] * qo[j];
+    float* o = gb.data() + (size_t)t * 48 + h * 3;
+    o[0] = expf(prm[16 + h] * logf(1.0f + expf(proj[8192 + h] + prm[h])));
+    o[1] = 1.0f / (1.0f + expf(-proj[8208 + h]));
+    o[2] = kq;
+  });
+  std::vector<float> raw((size_t)n * 2048);
+  parallel_for(16 * 16, [&](long i) {
+    const int h = (int)(i / 16), c0 = (int)(i % 16) * 8;
+    float S[128][8];
+    for (int j = 0; j < 128; ++j)
+      for (int c = 0; c < 8; ++c) S[j][c] = state[(size_t)h * 16384 + j * 128 + c0 + c];
+    for (int t = 0; t < n; ++t) {
+      const float* kv = ks.data() + (size_t)t * 2048 + h * 128;
+      const float* qv = qs.data() + (size_t)t * 2048 + h * 128;
+      const float* v = cv.data() + (size_t)t * 6144 + 4096 + h * 128;
+      const float g = gb[(size_t)t * 48 + h * 3], beta = gb[(size_t)t * 48 + h * 3 + 1],
+                  kq = gb[(size_t)t * 48 + h * 3 + 2];
+      float sk[8] = {0, 0, 0, 0, 0, 0, 0, 0}, sq[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      for (int j = 0; j < 128; ++j)
+        for (int c = 0; c < 8; ++c) {
+          sk[c] += S[j][c] * kv[j];
+          sq[c] += S[j][c] * qv[j];
+        }
+      for (int c = 0; c < 8; ++c) {
+        const float dv = beta * (v[c0 + c] - g * sk[c]);
+        for (int j = 0; j < 128; ++j) S[j][c] = g * S[j][c] + dv * kv[j];
+        raw[(size_t)t * 2048 + h * 128 + c0 + c] = g * sq[c] + dv * kq;
+      }
+    }
+    for (int j = 0; j < 128; ++j)
+      for (int c = 0; c < 8; ++c) state[(size_t)h * 16384 + j * 128 + c0 + c] = S[j][c];
+  });
+  parallel_for((long)n * 16, [&](long i) {
+    const int t = (int)(i / 16), h = (int)(i % 16);
+    const float* out = raw.data() + (size_t)t * 2048 + h * 128;
+    const float* proj = P + (size_t)t * kGdnProj;
+    float ss = 0;
+    for (int c = 0; c < 128; ++c) ss += out[c] * out[c];
+    const float inv = 1.0f / sqrtf(ss / 128.0f + 1e-6f);
+    for (int c = 0; c < 128; ++c)
+      O[(size_t)t * 2048 + h * 128 + c] = out[c] * inv * silu(proj[6144 + h * 128 + c]) * prm[32 + c];
+  });
+}
+
+// attention for n consecutive tokens at positions start..start+n-1 (P[n][8224] rows hold the
+// 5120 attention projections): every key/value is appended first, then each (token, head) attends
+// over positions 0..its own, as attention() does for one token.
+void attention_tokens(const float* P, int n, int start, float* kc, float* vc, const float* prm, const float* rope,
+                      int kv_f16, float* O) {
+  parallel_for((long)n * 2, [&](long i) {
+    const int t = (int)(i / 2), kvh = (int)(i % 2), pos = start + t;
+    const float* proj = P + (size_t)t * kGdnProj;
+    float kcur[256];
+    norm_rope(proj + 4096 + kvh * 256, prm + 256, rope, pos, kcur);
+    for (int j = 0; j < 256; ++j) {
+      float kv = kcur[j], vv = proj[4608 + kvh * 256 + j];
+      if (kv_f16) {
+        kv = h2f(f2h(kv));
+        vv = h2f(f2h(vv));
+      }
+      kc[((size_t)kvh * kMaxCtx + pos) * 256 + j] = kv;
+      vc[((size_t)kvh * kMaxCtx + pos) * 256 + j] = vv;
+    }
+  });
+  parallel_for((long)n * 8, [&](long i) {
+    const int t = (int)(i / 8), h = (int)(i % 8), kvh = h / 4, pos = start + t;
+    const float* proj = P + (size_t)t * kGdnProj;
+    float q[256];
+    norm_rope(proj + h * 256, prm, rope, pos, q);
+    std::vector<float> e(pos + 1);
+    float m = -3.0e38f;
+    for (int l = 0; l <= pos; ++l) {
+      const float* kr = kc + ((size_t)kvh * kMaxCtx + l) * 256;
+      float d = 0;
+      for (int j = 0; j < 256; ++j) d += q[j] * kr[j];
+      e[l] = d * 0.0625f;
+      m = e[l] > m ? e[l] : m;
+    }
+    float total = 0;
+    for (int l = 0; l <= pos; ++l) {
+      e[l] = expf(e[l] - m);
+      total += e[l];
+    }
+    float acc[256];
+    for (int c = 0; c < 256; ++c) acc[c] = 0;
+    for (int l = 0; l <= pos; ++l) {
+      const float* vr = vc + ((size_t)kvh * kMaxCtx + l) * 256;
+      const float el = e[l];
+      for (int c = 0; c < 256; ++c) acc[c] += el * vr[c];
+    }
+    for (int c = 0; c < 256; ++c)
+      O[(size_t)t * 2048 + h * 256 + c] = acc[c] / total / (1.0f + expf(-proj[2048 + h * 256 + c]));
+  });
+}
+
 }  // namespace
 
 // ------------------------------------------------------------------------------------------
@@ -488,6 +729,102 @@ API void oracle_model_step(void* hm, uint32_t token, int pos, float* logits_out)
     rmsnorm(m->h.data(), m->final_norm, H, m->xn.data());
     gemv(m->lm_head, m->xn.data(), logits_out, 0);
   }
+}
+
+// n consecutive tokens from position `start` through the batched CPU path (gemm_tokens,
+// gdn_tokens, attention_tokens); with logits_out != NULL the final norm + LM head run on the last
+// token. Leaves the state as n oracle_model_step calls would (within the matrix products' f32
+// summation order).
+API int oracle_model_prefill(void* hm, const uint32_t* ids, int n, int start, float* logits_out) {
+  Model* m = (Model*)hm;
+  if (n < 1 || start < 0 || start + n > kMaxCtx) return -1;
+  const int H = m->hidden, I = m->inter;
+  std::vector<float> X((size_t)n * H), XN((size_t)n * H), P((size_t)n * kGdnProj), MIX((size_t)n * kMixerOut),
+      A((size_t)n * I);
+  parallel_for(n, [&](long t) {
+    for (int c = 0; c < H; ++c) X[(size_t)t * H + c] = deq(m->embed, ids[t], c);
+  });
+  auto norm_rows = [&](const float* g) {
+    parallel_for(n, [&](long t) { rmsnorm(X.data() + (size_t)t * H, g, H, XN.data() + (size_t)t * H); });
+  };
+  for (int i = 0; i < m->layers; ++i) {
+    const Layer& l = m->L[i];
+    norm_rows(l.input_norm);
+    gemm_tokens(l.in, XN.data(), n, P.data(), kGdnProj, 0);
+    if (l.attn)
+      attention_tokens(P.data(), n, start, m->kc[i].data(), m->vc[i].data(), l.attn_norms, m->rope.data(), m->kv_f16,
+                       MIX.data());
+    else
+      gdn_tokens(P.data(), n, m->conv[i].data(), l.conv_w, m->rec[i].data(), l.gdn_params, MIX.data());
+    gemm_tokens(l.out, MIX.data(), n, X.data(), H, 1);
+    norm_rows(l.post_norm);
+    gemm_tokens(l.gate_up, XN.data(), n, A.data(), I, 2);
+    gemm_tokens(l.down, A.data(), n, X.data(), H, 1);
+  }
+  memcpy(m->h.data(), X.data() + (size_t)(n - 1) * H, (size_t)H * 4);
+  if (logits_out) {
+    rmsnorm(m->h.data(), m->final_norm, H, m->xn.data());
+    gemv(m->lm_head, m->xn.data(), logits_out, 0);
+  }
+  return 0;
+}
+
+// Whole-state copy and restore (Model::snapshot / restore, kernels/src/model.rs:394-414).
+API void oracle_model_snapshot(void* hm, void** saved) {
+  Model* m = (Model*)hm;
+  auto* copy = new std::vector<std::vector<float>>();
+  for (auto* v : {&m->conv, &m->rec, &m->kc, &m->vc})
+    for (auto& x : *v) copy->push_back(x);
+  delete (std::vector<std::vector<float>>*)*saved;
+  *saved = copy;
+}
+
+API int oracle_model_restore(void* hm, void* saved) {
+  Model* m = (Model*)hm;
+  auto* copy = (std::vector<std::vector<float>>*)saved;
+  if (!copy) return -1;
+  size_t j = 0;
+  for (auto* v : {&m->conv, &m->rec, &m->kc, &m->vc})
+    for (auto& x : *v) x = (*copy)[j++];
+  return 0;
+}
+
+API void oracle_snapshot_free(void* saved) { delete (std::vector<std::vector<float>>*)saved; }
+
+// Synthetic history for throughput samples: keys/values of positions [0, len) and the GDN states
+// and conv windows filled with seeded values (xorshift64, U(-scale, scale)); the cost of a decode
+// step depends on the context length only, not on these values.
+API void oracle_model_fill_synthetic(void* hm, int len, uint64_t seed) {
+  Model* m = (Model*)hm;
+  auto fill = [&](float* p, size_t n, float scale, bool f16) {
+    uint64_t s = seed * 0x9E3779B97F4A7C15ull + n;
+    if (s == 0) s = 1;
+    for (size_t i = 0; i < n; ++i) {
+      s ^= s << 13;
+      s ^= s >> 7;
+      s ^= s << 17;
+      float v = ((float)((uint32_t)(s >> 32) >> 8) / (float)(1u << 24) * 2.0f - 1.0f) * scale;
+      p[i] = f16 ? h2f(f2h(v)) : v;
+    }
+    ++seed;
+  };
+  for (int i = 0; i < m->layers; ++i) {
+    if (m->L[i].attn) {
+      for (int kvh = 0; kvh < 2; ++kvh) {
+        fill(m->kc[i].data() + (size_t)kvh * kMaxCtx * 256, (size_t)len * 256, 0.5f, m->kv_f16);
+        fill(m->vc[i].data() + (size_t)kvh * kMaxCtx * 256, (size_t)len * 256, 0.5f, m->kv_f16);
+      }
+    } else {
+      fill(m->conv[i].data(), m->conv[i].size(), 0.5f, false);
+      fill(m->rec[i].data(), m->rec[i].size(), 0.05f, false);
+    }
+  }
+}
+
+// Test hook for the batched matrix product: Y[n][out] for X[n][k] (epilogues as oracle_gemv).
+API void oracle_gemm_tokens(int kind, const void* w, const void* s, const void* z, int rows, int k, const float* x,
+                            int n, float* y, int epilogue) {
+  gemm_tokens(Mat{kind, rows, k, w, s, z}, x, n, y, epilogue == 2 ? rows / 2 : rows, epilogue);
 }
 
 // Copies of the state for inspection: GDN layer i -> conv (6144*3) + rec (16*16384);

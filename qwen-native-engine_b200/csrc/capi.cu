@@ -129,6 +129,14 @@ qne_status qne_model_phase_trace(qne_model* m, uint64_t* out, size_t cap, size_t
   });
 }
 
+qne_status qne_model_test_barrier_timeout(qne_model* m, uint32_t limit_us) {
+  MODEL(m);
+  return guarded([&] {
+    if (limit_us > 2000000u) throw QneError(kEInval, "limit_us must be at most 2000000");
+    M->set_wait_test((uint64_t)limit_us * 1000ull);
+  });
+}
+
 int qne_model_fused(const qne_model* m) {
   return m ? (reinterpret_cast<const Model*>(m)->fused() ? 1 : 0) : 0;
 }

@@ -498,6 +498,8 @@ void Runner::record_fused(Variant v, cudaStream_t s) {
     la.err = &st.ctl->flags;
     la.trace = trace_on ? trace + (size_t)i * fused_ctas * 32 : nullptr;
     la.xs_bytes = (uint32_t)persist_xs_bytes(fused_max_k);
+    la.wait_limit_ns = wait_test_ns ? wait_test_ns : kBarrierLimitNs;
+    la.wait_extra = wait_test_ns ? 1u : 0u;
   }
   for (int i = 0; i < M.cfg.layers; ++i) {
     const bool head = (i + 1 == M.cfg.layers) && v != kLayers;
@@ -575,6 +577,19 @@ bool Runner::set_trace(bool on) {
   return true;
 }
 
+bool Runner::set_wait_test(uint64_t limit_ns) {
+  if (!fgraph[0]) return false;
+  if (limit_ns == wait_test_ns) return true;
+  wait_test_ns = limit_ns;
+  for (auto& g : fgraph)
+    if (g) {
+      cudaGraphExecDestroy(g);
+      g = nullptr;
+    }
+  capture_set(fgraph, true);
+  return true;
+}
+
 size_t Runner::per_token() const { return use_fused ? fused_launches_per_token : launches_per_token; }
 
 void Runner::launch(Variant v, cudaStream_t s) {
@@ -622,6 +637,12 @@ void Model::set_phase_trace(bool on) {
   DeviceGuard g(device);
   cuda_check(cudaStreamSynchronize(stream()), "set_phase_trace");
   if (!single_->set_trace(on)) throw QneError(kEInval, "the phase trace needs the fused layer kernels");
+}
+
+void Model::set_wait_test(uint64_t limit_ns) {
+  DeviceGuard g(device);
+  cuda_check(cudaStreamSynchronize(stream()), "set_wait_test");
+  if (!single_->set_wait_test(limit_ns)) throw QneError(kEInval, "the barrier test needs the fused layer kernels");
 }
 
 size_t Model::read_phase_trace(uint64_t* out, size_t cap, size_t* ctas) {

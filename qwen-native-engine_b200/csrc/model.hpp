@@ -118,6 +118,7 @@ class Model {
   bool set_fused(bool on);
   bool fused() const;
   void set_phase_trace(bool on);
+  void set_wait_test(uint64_t limit_ns);
   size_t read_phase_trace(uint64_t* out, size_t cap, size_t* ctas);
   size_t dispatches_per_token() const;
   const float* logits_device() const;
@@ -187,6 +188,10 @@ class Runner {
   void record(Variant v, cudaStream_t s);        // enqueue one token's kernels on s
   void record_fused(Variant v, cudaStream_t s);  // the same as one fused launch per layer
   bool set_trace(bool on);
+  // Test hook of the bounded grid-barrier waits: nonzero = every barrier of the fused kernels also
+  // waits for one arrival that never comes, with this limit (ns), so every wait runs out.
+  uint64_t wait_test_ns = 0;
+  bool set_wait_test(uint64_t limit_ns);
   bool fused_supported();
   void capture_set(cudaGraphExec_t* out, bool fused);
   void capture_graphs();

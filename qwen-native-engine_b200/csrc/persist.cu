@@ -30,7 +30,6 @@ namespace {
 
 using namespace dev;
 
-constexpr uint64_t kBarrierLimitNs = 2000000000ull;  // 2 s; a healthy barrier takes about a microsecond
 
 __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;
@@ -74,19 +73,21 @@ struct Trace {
 struct GridBarrier {
   unsigned long long* count;  // [0] arrivals, [1] exits
   unsigned long long target;  // thread 0 only
+  uint64_t limit_ns;          // time limit of one wait
+  uint32_t extra;             // arrivals waited for beyond the grid (0; 1 = never completes, test only)
 
   __device__ __forceinline__ void wait(uint32_t* err, Trace& tr) {
     __syncthreads();
     if (threadIdx.x == 0) {
       tr.mark(8 + tr.nb);
-      target += gridDim.x;
+      target += gridDim.x + extra;
       red_add_release64(count, 1ull);
       const uint64_t t0 = global_ns();
       uint32_t rounds = 0;
       while (ld_acquire64(count) < target) {
         if ((++rounds & 63u) == 0u) {
           if (ld_acquire(err) & kFlagTimeout) break;
-          if (global_ns() - t0 > kBarrierLimitNs) {
+          if (global_ns() - t0 > limit_ns) {
             atomicOr(err, kFlagTimeout);
             break;
           }
@@ -164,7 +165,7 @@ __global__ void __launch_bounds__(256, 2) layer_kernel(const __grid_constant__ L
   AttnShared& ash = *reinterpret_cast<AttnShared*>(ring);
   GdnShared& dsh = *reinterpret_cast<GdnShared*>(ring);
   __shared__ GemvShared gsh;
-  GridBarrier bar{a.barrier, 0ull};
+  GridBarrier bar{a.barrier, 0ull, a.wait_limit_ns, a.wait_extra};
   uint32_t* err = a.err;
   Trace tr{a.trace, 0};
   tr.mark(0);

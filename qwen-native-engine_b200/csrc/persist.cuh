@@ -26,7 +26,12 @@ struct LayerLaunch {
   uint32_t* err;          // receives kFlagTimeout if a barrier wait gives up
   unsigned long long* trace;  // optional phase timestamps ([ctas][32]); null when off
   uint32_t xs_bytes;          // dynamic shared memory before the ring / mixer region
+  uint64_t wait_limit_ns;     // time limit of one grid-barrier wait (kBarrierLimitNs normally)
+  uint32_t wait_extra;        // arrivals each barrier waits for beyond the grid: 0, or 1 in the
+                              // timeout test, where no barrier can complete and every wait runs out
 };
+
+constexpr uint64_t kBarrierLimitNs = 2000000000ull;  // 2 s; a healthy barrier takes about a microsecond
 
 // CTAs of a co-resident grid for the largest GEMV k of the model (0 if the kernels cannot run:
 // the grid must hold at least one CTA per mixer work item).

@@ -83,6 +83,7 @@ def _load_lib() -> C.CDLL:
         "qne_model_set_fused": (I32, [P, I32]),
         "qne_model_fused": (I32, [P]),
         "qne_model_set_phase_trace": (I32, [P, I32]),
+        "qne_model_test_barrier_timeout": (I32, [P, U32]),
         "qne_model_phase_trace": (I32, [P, P, SZ, C.POINTER(SZ), C.POINTER(SZ)]),
         "qne_adapter": (C.c_char_p, [P]),
         "qne_dispatches_per_token": (SZ, [P]),
@@ -346,6 +347,10 @@ class Model:
 
     def set_phase_trace(self, enable: bool) -> None:
         _check(lib.qne_model_set_phase_trace(self._h, 1 if enable else 0))
+
+    def test_barrier_timeout(self, limit_us: int) -> None:
+        """Fused path test hook: every grid-barrier wait runs out after limit_us (0 = off)."""
+        _check(lib.qne_model_test_barrier_timeout(self._h, int(limit_us)))
 
     def phase_trace(self) -> np.ndarray:
         """Last token's fused-path timestamps, shape [layers, ctas, 32] (ns, %globaltimer)."""

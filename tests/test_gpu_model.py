@@ -212,7 +212,7 @@ def test_fused_kernels_at_a_long_context(cuda):
 def test_config1_full_08b_parity(cuda, fused):
     """benchmark config 1: 0.8B-shaped f16 model (seed 0), 128 prompt ids (seed 0), greedy steps."""
     s = synth.build_config(1)
-    m = qne.Model(s.index_json, s.weights, any_shape=True)
+    m = qne.Model(s.index_json, s.weights)
     set_path(m, fused)
     om = oracle.OracleModel(s.index_json, s.weights, kv_f16=True)
     prompt = synth.prompt_ids(128, 0)
@@ -223,17 +223,70 @@ def test_config1_full_08b_parity(cuda, fused):
 
 
 @pytest.mark.slow
-@pytest.mark.parametrize("cfg", [2, 3])
-def test_config_2b_short_context_parity(cuda, cfg):
-    """benchmark configs 2 (f16) and 3 (int4 g64) at a short context (the full 3968-token prefill on
-    the CPU oracle takes too long for a test; attention at 4096 is covered by the operator tests)."""
+@pytest.mark.parametrize("cfg,fused", [(2, False), (2, True), (3, False)], ids=["config2-split", "config2-fused",
+                                                                            "config3"])
+def test_config_2b_short_context_parity(cuda, cfg, fused):
+    """benchmark configs 2 (f16, both launch paths) and 3 (int4 g64) from a short prompt, one token
+    per step (qne_prefill); the benchmark contexts themselves are in test_gpu_bench_configs.py."""
     s = synth.build_config(cfg)
-    m = qne.Model(s.index_json, s.weights, any_shape=True)
-    if cfg == 2:
-        m.set_fused(True)  # the 2B f16 config runs through the fused layer kernels here
+    m = qne.Model(s.index_json, s.weights)
+    set_path(m, fused)
     om = oracle.OracleModel(s.index_json, s.weights, kv_f16=True)
     prompt = synth.prompt_ids(48, cfg)
     n = greedy_compare(m, om, prompt, 32)
     assert n == 32
     m.close()
     om.close()
+
+
+def test_sync_deadline_reports_a_timeout(cuda):
+    """qne_sync / qne_batch_sync poll the stream with a deadline (the reference's GPU wait,
+    kernels/src/lib.rs:398-405, fails with an error instead of hanging). The stream is held by a
+    bounded spin kernel (torch.cuda._sleep, about one second) so that a 1 ms deadline runs out."""
+    import torch
+    s = synth.build(1024, 3584, layers=4, vocab=4096, seed=16)
+    m = qne.Model(s.index_json, s.weights, any_shape=True)
+    st = torch.cuda.Stream()
+    m.set_stream(st.cuda_stream)
+    bt = qne.Batch(m, 2)
+    for hold in (lambda: m.sync(1), lambda: bt.sync(1)):
+        with torch.cuda.stream(st):
+            torch.cuda._sleep(2_000_000_000)
+        with pytest.raises(qne.QneError) as e:
+            hold()
+        assert e.value.name == "ETIMEOUT" and "exceeded" in str(e.value)
+        m.sync()  # the spin ends; a normal wait succeeds
+    m.prefill(synth.prompt_ids(5, 1, 4096))
+    assert m.last_token()[1] == 5
+    bt.close()
+    m.close()
+
+
+def test_fused_barrier_wait_runs_out_and_reports_a_timeout(cuda):
+    """The fused layer kernels' grid barriers are bounded waits. With the test hook every barrier
+    also waits for an arrival that never comes, under a 1 ms limit: the kernels set the timeout flag
+    and return (no hang, the context stays usable), qne_last_token reports QNE_ETIMEOUT and clears
+    the flag, and with the hook off the same prompt gives the same bits as before."""
+    import time
+    s = synth.build(1024, 3584, layers=4, vocab=4096, seed=15)
+    m = qne.Model(s.index_json, s.weights, any_shape=True)
+    m.set_fused(True)
+    prompt = synth.prompt_ids(9, 2, 4096)
+    m.prefill(prompt)
+    want, want_ids = m.logits().copy(), m.decode(4, 1)
+    m.test_barrier_timeout(1000)
+    m.reset()
+    t0 = time.perf_counter()
+    m.prefill(prompt[:3])
+    with pytest.raises(qne.QneError) as e:
+        m.last_token()
+    assert e.value.name == "ETIMEOUT" and "timed out" in str(e.value)
+    assert time.perf_counter() - t0 < 5.0  # one limit, not one per barrier
+    m.test_barrier_timeout(0)
+    m.reset()
+    m.prefill(prompt)
+    assert np.array_equal(m.logits(), want) and m.decode(4, 1) == want_ids
+    m.set_fused(False)
+    with pytest.raises(qne.QneError) as e:  # the hook belongs to the fused path
+        m.test_barrier_timeout(1000)
+    m.close()

@@ -194,7 +194,7 @@ def test_config2_batched_prefill_of_the_bench_prompt(cuda):
     """benchmark config 2 (2B f16): the bench's 3968-token prompt through the batched path and
     through the per-token path: logits within the tolerance, 32 identical greedy tokens."""
     s = synth.build_config(2)
-    m = qne.Model(s.index_json, s.weights, any_shape=True)
+    m = qne.Model(s.index_json, s.weights)
     prompt = synth.prompt_ids(3968, 1)
     m.prefill(prompt)
     a, ids_a = m.logits().copy(), m.decode(32, 1)
