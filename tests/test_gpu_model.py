@@ -286,7 +286,4 @@ def test_fused_barrier_wait_runs_out_and_reports_a_timeout(cuda):
     m.reset()
     m.prefill(prompt)
     assert np.array_equal(m.logits(), want) and m.decode(4, 1) == want_ids
-    m.set_fused(False)
-    with pytest.raises(qne.QneError) as e:  # the hook belongs to the fused path
-        m.test_barrier_timeout(1000)
     m.close()
