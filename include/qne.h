@@ -144,6 +144,19 @@ QNE_API qne_status qne_model_phase_trace(qne_model* m, uint64_t* out, size_t cap
  * (qne_last_token, qne_decode) fails with QNE_ETIMEOUT and clears the flag. limit_us = 0 restores
  * the normal barriers. QNE_EINVAL if the fused path is not available. */
 QNE_API qne_status qne_model_test_barrier_timeout(qne_model* m, uint32_t limit_us);
+/* Model::profile_token, kernels/src/model.rs:305-307 (Gpu::profile, kernels/src/lib.rs:366-396):
+ * consumes one greedy token (like qne_decode of one step), launching its kernels one by one with
+ * a CUDA event behind each, and reports the milliseconds summed per dispatch label ("gemv_<rows>x
+ * <k>_<Store|Accumulate|SwiGlu|Argmax>", "gdn", "attention"), in label order. Writes up to `cap`
+ * entries and the number of labels to *n_out. Diagnostic only: the kernels do not overlap as they
+ * do in decoding, so the sum exceeds a decoded token's time. */
+typedef struct qne_profile_entry {
+  char label[48];
+  double ms;
+  uint32_t dispatches;
+  uint32_t pad;
+} qne_profile_entry;
+QNE_API qne_status qne_profile_token(qne_model* m, qne_profile_entry* out, size_t cap, size_t* n_out);
 /* Model::adapter, kernels/src/model.rs:167. */
 QNE_API const char* qne_adapter(const qne_model* m);
 /* Model::dispatches_per_token, kernels/src/model.rs:309. */
@@ -358,6 +371,19 @@ QNE_API qne_status qne_attention_step_ex(const float* proj, const float* norms, 
  * contiguous out_k/out_v [2 kv heads][len][256] f16 (bit copy). */
 QNE_API qne_status qne_kv_gather(const void* kv, const uint32_t* page_table, uint32_t len, void* out_k,
                          void* out_v, void* stream);
+
+/* Dispatch-cost probe, the reference's noop kernel and dispatch_cost (kernels/src/shaders.rs:
+ * 720-729, kernels/src/lib.rs:718-724): n (1..100000) launches of a one-block kernel that adds 1 to
+ * y[0] (device), back to back on `stream`, timed with CUDA events; *us_per_dispatch (host)
+ * receives the microseconds per launch. mode: QNE_DISPATCH_PLAIN (stream launches), _GRAPH (the
+ * n launches captured as one CUDA graph, replayed once), _PDL (launches with programmatic
+ * dependent launch: each kernel releases its successor, then waits for its predecessor), or
+ * _GRAPH_PDL (a graph of those, how the decode step runs). Synchronizes the stream. */
+#define QNE_DISPATCH_PLAIN 0
+#define QNE_DISPATCH_GRAPH 1
+#define QNE_DISPATCH_PDL 2
+#define QNE_DISPATCH_GRAPH_PDL 3
+QNE_API qne_status qne_dispatch_cost(uint32_t n, int mode, float* y, void* stream, double* us_per_dispatch);
 
 /* Streaming-read probe, kernels/src/shaders.rs:703-717: XOR of `bytes` (multiple of 16). */
 QNE_API qne_status qne_bandwidth_probe(const void* data, size_t bytes, uint32_t* sink, void* stream);

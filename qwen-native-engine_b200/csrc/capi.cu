@@ -1,5 +1,6 @@
 // extern "C" entry points declared in include/qne.h. Every call converts C++ exceptions into
 // a status code plus a thread-local message; nothing escapes across the ABI.
+#include <cstring>
 #include <string>
 
 #include "../../include/qne.h"
@@ -126,6 +127,20 @@ qne_status qne_model_phase_trace(qne_model* m, uint64_t* out, size_t cap, size_t
   return guarded([&] {
     const size_t n = M->read_phase_trace(out, cap, ctas);
     if (n_out) *n_out = n;
+  });
+}
+
+qne_status qne_profile_token(qne_model* m, qne_profile_entry* out, size_t cap, size_t* n_out) {
+  MODEL(m);
+  return guarded([&] {
+    const auto prof = M->profile_token();
+    if (n_out) *n_out = prof.size();
+    for (size_t i = 0; i < prof.size() && i < cap && out; ++i) {
+      std::memset(&out[i], 0, sizeof(out[i]));
+      std::strncpy(out[i].label, prof[i].first.c_str(), sizeof(out[i].label) - 1);
+      out[i].ms = prof[i].second.first;
+      out[i].dispatches = prof[i].second.second;
+    }
   });
 }
 
@@ -463,6 +478,14 @@ qne_status qne_kv_gather(const void* kv, const uint32_t* page_table, uint32_t le
     check_launch(launch_kv_gather(static_cast<const uint16_t*>(kv), page_table, len, static_cast<uint16_t*>(out_k),
                                   static_cast<uint16_t*>(out_v), as_stream(stream)),
                  "kv_gather");
+  });
+}
+
+qne_status qne_dispatch_cost(uint32_t n, int mode, float* y, void* stream, double* us_per_dispatch) {
+  return guarded([&] {
+    if (!y || !us_per_dispatch || n == 0 || n > 100000 || mode < 0 || mode > 3)
+      throw QneError(kEInval, "dispatch cost needs y, an output, 1..100000 launches and mode 0..3");
+    *us_per_dispatch = dispatch_cost(n, mode, y, as_stream(stream));
   });
 }
 

@@ -50,5 +50,7 @@ void rope_table_host(float* table, double theta);
 // Device copy of the table for `theta` on the current device, built on first use and kept.
 const float* rope_table_device(double theta);
 cudaError_t launch_bandwidth_probe(const void* data, size_t bytes, uint32_t* sink, cudaStream_t stream);
+// Microseconds per launch of n noop kernels (mode 0 plain, 1 graph, 2 PDL, 3 graph of PDL).
+double dispatch_cost(uint32_t n, int mode, float* y, cudaStream_t s);
 
 }  // namespace qne

@@ -1,5 +1,6 @@
-// Streaming-read probe (bandwidth, kernels/src/shaders.rs:703-717) and the per-device RoPE
-// table cache used by the attention operator entry point.
+// Streaming-read probe (bandwidth, kernels/src/shaders.rs:703-717), the dispatch-cost probe
+// (noop + dispatch_cost, kernels/src/shaders.rs:720-729 and kernels/src/lib.rs:718-724) and the
+// per-device RoPE table cache used by the attention operator entry point.
 #include <map>
 #include <mutex>
 #include <vector>
@@ -34,7 +35,84 @@ __global__ void __launch_bounds__(256) bandwidth_kernel(const uint4* data, size_
   atomicXor(sink, v);
 }
 
+// noop, kernels/src/shaders.rs:720-729: thread 0 of one 64-thread block adds 1 to y[0]. The PDL
+// form releases its successor first and waits for its predecessor before the update, as every
+// kernel of the decode graphs does.
+template <bool PDL>
+__global__ void __launch_bounds__(64) noop_kernel(float* y) {
+  if (PDL) {
+    pdl_launch();
+    pdl_wait();
+  }
+  if (threadIdx.x == 0) y[0] = y[0] + 1.0f;
+}
+
+cudaError_t launch_noop(float* y, bool pdl, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(64);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  count_launch();
+  return pdl ? cudaLaunchKernelEx(&cfg, noop_kernel<true>, y) : cudaLaunchKernelEx(&cfg, noop_kernel<false>, y);
+}
+
 }  // namespace
+
+// dispatch_cost (kernels/src/lib.rs:718-724): n back-to-back noop launches on `s`, timed with CUDA
+// events, as plain launches (mode 0), one CUDA graph of the n launches (1), launches with
+// programmatic dependent launch (2) or a graph of those (3, how the decode step runs). Returns
+// microseconds per launch.
+double dispatch_cost(uint32_t n, int mode, float* y, cudaStream_t s) {
+  const bool pdl = mode == 2 || mode == 3, graph = mode == 1 || mode == 3;
+  cudaGraphExec_t exec = nullptr;
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  cudaStream_t cs = nullptr;
+  auto cleanup = [&]() {
+    if (exec) cudaGraphExecDestroy(exec);
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    if (cs) cudaStreamDestroy(cs);
+  };
+  try {
+    cuda_check(cudaEventCreate(&e0), "cudaEventCreate");
+    cuda_check(cudaEventCreate(&e1), "cudaEventCreate");
+    if (graph) {
+      cuda_check(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking), "cudaStreamCreate");
+      cuda_check(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal), "begin capture");
+      cudaError_t le = cudaSuccess;
+      for (uint32_t i = 0; i < n && le == cudaSuccess; ++i) le = launch_noop(y, pdl, cs);
+      cudaGraph_t g = nullptr;
+      const cudaError_t ce = cudaStreamEndCapture(cs, &g);
+      cuda_check(le, "noop launch");
+      cuda_check(ce, "end capture");
+      const cudaError_t ie = cudaGraphInstantiate(&exec, g, 0);
+      cudaGraphDestroy(g);
+      cuda_check(ie, "graph instantiate");
+      cuda_check(cudaGraphLaunch(exec, s), "graph launch");  // warm-up
+    } else {
+      for (int i = 0; i < 10; ++i) cuda_check(launch_noop(y, pdl, s), "noop launch");
+    }
+    cuda_check(cudaStreamSynchronize(s), "dispatch_cost");
+    cuda_check(cudaEventRecord(e0, s), "cudaEventRecord");
+    if (graph) cuda_check(cudaGraphLaunch(exec, s), "graph launch");
+    else
+      for (uint32_t i = 0; i < n; ++i) cuda_check(launch_noop(y, pdl, s), "noop launch");
+    cuda_check(cudaEventRecord(e1, s), "cudaEventRecord");
+    cuda_check(cudaEventSynchronize(e1), "dispatch_cost");
+    float ms = 0.f;
+    cuda_check(cudaEventElapsedTime(&ms, e0, e1), "cudaEventElapsedTime");
+    cleanup();
+    return (double)ms * 1000.0 / n;
+  } catch (...) {
+    cleanup();
+    throw;
+  }
+}
 
 cudaError_t launch_bandwidth_probe(const void* data, size_t bytes, uint32_t* sink, cudaStream_t stream) {
   count_launch();

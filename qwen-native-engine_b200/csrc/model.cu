@@ -425,32 +425,41 @@ GemvArgs Runner::head_args(Variant v) const {
   return hd;
 }
 
-void Runner::record(Variant v, cudaStream_t s) {
+// Dispatch label in the reference's form (kernels/src/lib.rs:337: gemv_<rows>x<k>_<epilogue>).
+static std::string gemv_label(const GemvArgs& a) {
+  static const char* epi[] = {"Store", "Accumulate", "SwiGlu", "Argmax"};
+  return "gemv_" + std::to_string(a.m.rows) + "x" + std::to_string(a.m.k) + "_" + epi[a.epi & 3];
+}
+
+void Runner::record(Variant v, cudaStream_t s, const std::function<void(const std::string&)>* after) {
   const Model& M = *m;
+  const bool pdl = after == nullptr;
   size_t n = 0;
   auto gemv = [&](const GemvArgs& a) {
     if (const char* why = check_gemv(a)) throw QneError(kEInval, why);
-    cuda_check(launch_gemv(a, s, true), "gemv launch");
+    cuda_check(launch_gemv(a, s, pdl), "gemv launch");
     ++n;
+    if (after) (*after)(gemv_label(a));
   };
   for (int i = 0; i < M.cfg.layers; ++i) {
     const LayerArgs r = layer_args(i);
     gemv(r.in);
     if (r.attention) {
-      cuda_check(launch_attention(r.at, st.pool_pages, 64, s, true), "attention launch");
+      cuda_check(launch_attention(r.at, st.pool_pages, 64, s, pdl), "attention launch");
     } else {
       const dev::GdnArgs& g = r.gdn;
       cuda_check(launch_gdn_step(g.proj, g.conv, g.conv_w, g.state, g.params, g.counter, g.counter_stride, g.out,
-                                 1, s, true),
+                                 1, s, pdl),
                  "gdn launch");
     }
     ++n;
+    if (after) (*after)(r.attention ? "attention" : "gdn");
     gemv(r.out);
     gemv(r.gate_up);
     gemv(r.down);
   }
   if (v != kLayers) gemv(head_args(v));
-  if (v == kGreedy) launches_per_token = n;
+  if (v == kGreedy && !after) launches_per_token = n;
 }
 
 // Whether the fused layer kernels can run this model: one sequence, f16 GEMV weights with
@@ -637,6 +646,54 @@ void Model::set_phase_trace(bool on) {
   DeviceGuard g(device);
   cuda_check(cudaStreamSynchronize(stream()), "set_phase_trace");
   if (!single_->set_trace(on)) throw QneError(kEInval, "the phase trace needs the fused layer kernels");
+}
+
+// Model::profile_token (kernels/src/model.rs:305-307; Gpu::profile, kernels/src/lib.rs:366-396):
+// consumes one greedy token. Its kernels are launched one by one on the model's stream, without
+// programmatic dependent launch (so no kernel overlaps its neighbours), with a CUDA event behind
+// each; the time between consecutive events is summed per dispatch label. Diagnostic only: the
+// graphs that decode() replays overlap consecutive kernels and take less time in total.
+std::vector<std::pair<std::string, std::pair<double, uint32_t>>> Model::profile_token() {
+  DeviceGuard g(device);
+  cudaStream_t s = stream();
+  if (host_pos_ >= (uint32_t)kMaxContext)
+    throw QneError(kERangeCtx, "context limit of " + std::to_string(kMaxContext) + " tokens reached");
+  cuda_check(cudaStreamSynchronize(s), "profile_token");
+  std::vector<cudaEvent_t> ev;
+  std::vector<std::string> labels;
+  auto event = [&]() {
+    cudaEvent_t e = nullptr;
+    cuda_check(cudaEventCreate(&e), "cudaEventCreate");
+    ev.push_back(e);
+    cuda_check(cudaEventRecord(e, s), "cudaEventRecord");
+  };
+  std::vector<std::pair<std::string, std::pair<double, uint32_t>>> out;
+  try {
+    event();
+    std::function<void(const std::string&)> after = [&](const std::string& label) {
+      event();
+      labels.push_back(label);
+    };
+    single_->record(Runner::kGreedy, s, &after);
+    sync(600000);
+    std::map<std::string, std::pair<double, uint32_t>> acc;
+    for (size_t i = 0; i < labels.size(); ++i) {
+      float ms = 0.f;
+      cuda_check(cudaEventElapsedTime(&ms, ev[i], ev[i + 1]), "cudaEventElapsedTime");
+      auto& slot = acc[labels[i]];
+      slot.first += ms;
+      slot.second += 1;
+    }
+    out.assign(acc.begin(), acc.end());
+  } catch (...) {
+    for (cudaEvent_t e : ev) cudaEventDestroy(e);
+    throw;
+  }
+  for (cudaEvent_t e : ev) cudaEventDestroy(e);
+  ++host_pos_;
+  uint32_t tok = 0, pos = 0;
+  last_token(&tok, &pos);  // reports a timed-out wait like decode() does
+  return out;
 }
 
 void Model::set_wait_test(uint64_t limit_ns) {

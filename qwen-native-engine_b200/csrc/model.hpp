@@ -6,6 +6,7 @@
 
 #include <memory>
 #include <stdexcept>
+#include <functional>
 #include <string>
 #include <vector>
 
@@ -119,6 +120,8 @@ class Model {
   bool fused() const;
   void set_phase_trace(bool on);
   void set_wait_test(uint64_t limit_ns);
+  // Model::profile_token: one greedy token, kernel by kernel, milliseconds per dispatch label.
+  std::vector<std::pair<std::string, std::pair<double, uint32_t>>> profile_token();
   size_t read_phase_trace(uint64_t* out, size_t cap, size_t* ctas);
   size_t dispatches_per_token() const;
   const float* logits_device() const;
@@ -185,7 +188,9 @@ class Runner {
   };
   LayerArgs layer_args(int i) const;
   GemvArgs head_args(Variant v) const;
-  void record(Variant v, cudaStream_t s);        // enqueue one token's kernels on s
+  // Enqueues one token's kernels on s. With `after` set (profiling), the launches are plain
+  // (no programmatic dependent launch) and after(label) runs behind each one.
+  void record(Variant v, cudaStream_t s, const std::function<void(const std::string&)>* after = nullptr);
   void record_fused(Variant v, cudaStream_t s);  // the same as one fused launch per layer
   bool set_trace(bool on);
   // Test hook of the bounded grid-barrier waits: nonzero = every barrier of the fused kernels also

@@ -57,6 +57,10 @@ class _Sampling(C.Structure):
                 ("presence_penalty", C.c_float)]
 
 
+class _ProfileEntry(C.Structure):
+    _fields_ = [("label", C.c_char * 48), ("ms", C.c_double), ("dispatches", C.c_uint32), ("pad", C.c_uint32)]
+
+
 class _Info(C.Structure):
     _fields_ = [("layers", C.c_int32), ("hidden", C.c_int32), ("intermediate", C.c_int32),
                 ("vocab", C.c_int32), ("weight_kind", C.c_int32), ("embed_kind", C.c_int32),
@@ -84,6 +88,7 @@ def _load_lib() -> C.CDLL:
         "qne_model_fused": (I32, [P]),
         "qne_model_set_phase_trace": (I32, [P, I32]),
         "qne_model_test_barrier_timeout": (I32, [P, U32]),
+        "qne_profile_token": (I32, [P, C.POINTER(_ProfileEntry), SZ, C.POINTER(SZ)]),
         "qne_model_phase_trace": (I32, [P, P, SZ, C.POINTER(SZ), C.POINTER(SZ)]),
         "qne_adapter": (C.c_char_p, [P]),
         "qne_dispatches_per_token": (SZ, [P]),
@@ -130,6 +135,7 @@ def _load_lib() -> C.CDLL:
         "qne_attention_step_ex": (I32, [P, P, C.c_double, P, U32, P, P, P, I32, P, SZ, I32, P]),
         "qne_kv_gather": (I32, [P, P, U32, P, P, P]),
         "qne_bandwidth_probe": (I32, [P, SZ, P, P]),
+        "qne_dispatch_cost": (I32, [U32, I32, P, P, C.POINTER(C.c_double)]),
         "qne_sampler_create": (I32, [P, C.POINTER(_Sampling), C.POINTER(P)]),
         "qne_sampler_free": (None, [P]),
         "qne_sampler_sample": (I32, [P, U32P, U32, C.c_int32, C.c_float, U32P]),
@@ -305,6 +311,15 @@ class Model:
         _check(lib.qne_step_sample(self._h, sampler._h, token, pos, _u32p(words) if words is not None else None, n,
                                    bias_token, float(bias), C.byref(out)))
         return int(out.value)
+
+    def profile_token(self) -> dict[str, float]:
+        """Model::profile_token: consumes one greedy token; milliseconds per dispatch label, each
+        kernel timed alone (no overlap with its neighbours)."""
+        n = C.c_size_t()
+        cap = 64
+        buf = (_ProfileEntry * cap)()
+        _check(lib.qne_profile_token(self._h, buf, cap, C.byref(n)))
+        return {buf[i].label.decode(): buf[i].ms for i in range(min(n.value, cap))}
 
     def snapshot(self) -> None:
         _check(lib.qne_snapshot(self._h))
@@ -515,6 +530,16 @@ def kv_gather(kv, page_table, length: int, out_k, out_v, stream=None) -> None:
 
 def bandwidth_probe(data, nbytes: int, sink, stream=None) -> None:
     _check(lib.qne_bandwidth_probe(_ptr(data), nbytes, _ptr(sink), _stream(stream)))
+
+
+DISPATCH_MODES = {"plain": 0, "graph": 1, "pdl": 2, "graph_pdl": 3}
+
+
+def dispatch_cost(n: int, mode: str, y, stream=None) -> float:
+    """Microseconds per launch of n noop kernels (kernels/src/lib.rs:718-724) in the given mode."""
+    us = C.c_double()
+    _check(lib.qne_dispatch_cost(n, DISPATCH_MODES[mode], _ptr(y), _stream(stream), C.byref(us)))
+    return float(us.value)
 
 
 def gemm_scratch_bytes(m: _Matrix, batch: int) -> int:

@@ -287,3 +287,36 @@ def test_fused_barrier_wait_runs_out_and_reports_a_timeout(cuda):
     m.prefill(prompt)
     assert np.array_equal(m.logits(), want) and m.decode(4, 1) == want_ids
     m.close()
+
+
+def test_profile_token_times_every_dispatch_and_consumes_one_token(cuda):
+    """Model::profile_token (kernels/src/model.rs:305-307): one greedy token, milliseconds per
+    dispatch label; afterwards the model stands where one decode step leaves it."""
+    s = synth.build(1024, 3584, layers=4, vocab=4096, seed=17)
+    m = qne.Model(s.index_json, s.weights, any_shape=True)
+    m.prefill(synth.prompt_ids(20, 3, 4096))
+    m.snapshot()
+    want = m.decode(2, 1)
+    m.restore()
+    prof = m.profile_token()
+    assert set(prof) == {"gemv_8224x1024_Store", "gemv_5120x1024_Store", "gemv_1024x2048_Accumulate",
+                         "gemv_7168x1024_SwiGlu", "gemv_1024x3584_Accumulate", "gemv_4096x1024_Argmax", "gdn",
+                         "attention"}, prof
+    assert all(0.0 < v < 50.0 for v in prof.values()), prof
+    assert m.last_token() == (want[1], 21)
+    m.close()
+
+
+def test_dispatch_cost_probe(cuda):
+    """The reference's dispatch-cost probe (noop kernel, kernels/src/lib.rs:718-724) in the four
+    launch modes: every launch runs (y counts them) and costs a few microseconds at most."""
+    import torch
+    y = torch.zeros(1, device="cuda")
+    n, total = 500, 0
+    for mode, warm in (("plain", 10), ("graph", n), ("pdl", 10), ("graph_pdl", n)):
+        us = qne.dispatch_cost(n, mode, y)
+        total += n + warm
+        torch.cuda.synchronize()
+        assert 0.0 < us < 20.0, (mode, us)
+        assert int(y.item()) == total, mode
+        print(f"dispatch cost {mode}: {us:.2f} us per launch")
