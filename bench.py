@@ -132,7 +132,7 @@ def cpu_model() -> str:
     return "unknown"
 
 
-def bench_config(cfg_n: int, prompt_len: int, steps: int, world: int, l2_note: str | None = None) -> dict:
+def bench_config(cfg_n: int, prompt_len: int, steps: int, world: int, weight_file_bytes: int) -> dict:
     """The `config` object of the B=1 line, shared by both arms so that they name one workload."""
     from qne import synth
     info = synth.baseline_config(cfg_n)
@@ -141,9 +141,8 @@ def bench_config(cfg_n: int, prompt_len: int, steps: int, world: int, l2_note: s
                      f"(synthetic, seed {info['seed']}), B=1 per GPU, KV prefilled to {prompt_len}, "
                      f"{steps} greedy decode steps",
          "model": f"qwen3.5-{size_name.lower()}-shaped", "global_batch": world, "seq_len": 4096,
-         "parallelism": f"replicas x{world}"}
-    if l2_note:
-        c["l2"] = l2_note
+         "parallelism": f"replicas x{world}",
+         "l2": f"inputs larger than L2 ({weight_file_bytes / 1e9:.2f} GB of weights read per step)"}
     return c
 
 
@@ -206,7 +205,7 @@ def reference_arm(args, world, rank):
         "steps": steps, "warmup": args.warmup, "ms_per_step": round(1000.0 / rate, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f16" if info["kind"] == "f16" else "int4 (f32 math)",
         "data": "synthetic",
-        "config": bench_config(cfg_n, prompt_len, steps, world),
+        "config": bench_config(cfg_n, prompt_len, steps, world, s.weights.nbytes),
         "cpu_baseline": {"value": round(rate, 4), "unit": "tok/s", "cores": cores, "cpu_model": cpu_model(),
                          "kind": "port",
                          "sample": f"{steps} greedy decode steps from position {prompt_len} after the bench's "
@@ -259,7 +258,7 @@ def profile_step4(args):
     import qne
     from qne import synth
     s = synth.build(2048, 6144, layers=4, vocab=32768, seed=3)
-    m = qne.Model(s.index_json, s.weights)
+    m = qne.Model(s.index_json, s.weights, any_shape=True)
     if args.path != "auto":
         m.set_fused(args.path == "fused")
     m.prefill(synth.prompt_ids(16, 2, 32768))
@@ -691,8 +690,7 @@ def main():
             "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": steps,
             "warmup": args.warmup, "ms_per_step": round(ms / steps, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-            "config": bench_config(cfg_n, prompt_len, steps, world,
-                                   f"inputs larger than L2 ({model_weight_bytes / 1e9:.2f} GB of weights per step)"),
+            "config": bench_config(cfg_n, prompt_len, steps, world, s.weights.nbytes),
             "e2e": {"value": round(aggregate_rate(world, steps, e2e_sampled_s * 1e3), 2), "unit": "tok/s",
                     "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8,
                     "loop": "qne_step_sample: decode step + device sampling (T 0.6, top_k 20, top_p 0.95)"},
