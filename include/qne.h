@@ -129,6 +129,19 @@ QNE_API qne_status qne_model_set_stream(qne_model* m, void* cuda_stream);
 QNE_API qne_status qne_model_set_fused(qne_model* m, int enable);
 /* 1 if the fused layer kernels are in use. */
 QNE_API int qne_model_fused(const qne_model* m);
+/* Launch path of a token (no counterpart in the reference, whose dispatch list is fixed):
+ * QNE_PATH_OPERATIONS = one kernel per operation (qne_model_set_fused(m, 0)), QNE_PATH_LAYERS =
+ * one fused launch per layer (qne_model_set_fused(m, 1)), QNE_PATH_TOKEN = one launch per token:
+ * a kernel with one CTA per SM whose producer warp streams every weight of the token through a
+ * shared-memory ring with bulk copies while the consumer warps run the layers' phases behind
+ * grid barriers. All three compute the same results within the logit tolerance. QNE_PATH_TOKEN
+ * needs one sequence and f16 matrices with k % 256 == 0 and k <= 6144; QNE_EINVAL when a path is
+ * not available. qne_model_path returns the current one. */
+#define QNE_PATH_OPERATIONS 0
+#define QNE_PATH_LAYERS 1
+#define QNE_PATH_TOKEN 2
+QNE_API qne_status qne_model_set_path(qne_model* m, int path);
+QNE_API int qne_model_path(const qne_model* m);
 /* Diagnostics of the fused path (no counterpart in the reference): with enable = 1 every fused
  * launch records, per CTA, %globaltimer stamps at its phase boundaries (slots 0-7), grid-barrier
  * arrivals (8-15) and releases (16-23) into [layer][cta][32] u64 slots, overwritten each token.

@@ -117,6 +117,21 @@ qne_status qne_model_set_fused(qne_model* m, int enable) {
   });
 }
 
+qne_status qne_model_set_path(qne_model* m, int path) {
+  MODEL(m);
+  return guarded([&] {
+    if (path < QNE_PATH_OPERATIONS || path > QNE_PATH_TOKEN) throw QneError(kEInval, "unknown launch path");
+    if (!M->set_path(path))
+      throw QneError(kEInval, path == QNE_PATH_TOKEN
+                                  ? "the token kernel needs one sequence, f16 matrices with k % 256 == 0 and "
+                                    "k <= 6144, and a CTA per SM co-resident"
+                                  : "the fused layer kernels need one sequence, f16 weights with k % 256 == 0 and a "
+                                    "device that co-schedules the grid");
+  });
+}
+
+int qne_model_path(const qne_model* m) { return m ? reinterpret_cast<const Model*>(m)->path() : -1; }
+
 qne_status qne_model_set_phase_trace(qne_model* m, int enable) {
   MODEL(m);
   return guarded([&] { M->set_phase_trace(enable != 0); });

@@ -64,7 +64,15 @@ struct GdnItem {
     for (int jj = 0; jj < 8; ++jj) sv[jj] = S[(size_t)(jg * 8 + jj) * kGdnDim];
   }
 
-  __device__ __forceinline__ void run(const GdnArgs& a, GdnShared& sh) {
+  __device__ __forceinline__ void run(const GdnArgs& a, GdnShared& sh) { run_with(a, sh, BlockSync()); }
+
+  // The item's 256 threads are threads 0..255 of the CTA; `sync` is a barrier over exactly those
+  // (the whole CTA, or a named barrier when other warps of the CTA do other work).
+  struct BlockSync {
+    __device__ __forceinline__ void operator()() const { __syncthreads(); }
+  };
+  template <class Sync>
+  __device__ __forceinline__ void run_with(const GdnArgs& a, GdnShared& sh, Sync sync) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     // Issue every independent load at once: counter, proj, all four ring slots (the slot this
     // step overwrites is read too and discarded, which saves waiting for the counter).
@@ -106,12 +114,12 @@ struct GdnItem {
     // L2 norms: warps 0-3 hold q, warps 4-7 hold k.
     const float ss = warp_sum(val * val);
     if (lane == 0) sh.red[warp] = ss;
-    __syncthreads();
+    sync();
     const float nq = rsqrtf(sh.red[0] + sh.red[1] + sh.red[2] + sh.red[3] + 1e-6f);
     const float nk = rsqrtf(sh.red[4] + sh.red[5] + sh.red[6] + sh.red[7] + 1e-6f);
     if (tid < kGdnDim) sh.qs[i] = val * nq * 0.08838834764f;
     else sh.ks[i] = val * nk;
-    __syncthreads();
+    sync();
     if (warp < 4) {
       const float p = warp_sum(sh.ks[tid] * sh.qs[tid]);
       if (lane == 0) sh.red[warp] = p;  // red[0..3] no longer needed for nq
@@ -127,7 +135,7 @@ struct GdnItem {
     }
     sh.psk[jg][tl] = sk;
     sh.psq[jg][tl] = sq;
-    __syncthreads();
+    sync();
     if (tid < kSlice) {
       float a0 = 0.f, c0 = 0.f;
 #pragma unroll
@@ -139,12 +147,12 @@ struct GdnItem {
       sh.sq_s[tid] = c0;
     }
     if (tid == 0) sh.kq_s = sh.red[0] + sh.red[1] + sh.red[2] + sh.red[3];
-    __syncthreads();
+    sync();
     const float dv = beta * (sh.vs[tl] - g * sh.sk_s[tl]);
 #pragma unroll
     for (int jj = 0; jj < 8; ++jj) S[(size_t)(jg * 8 + jj) * kGdnDim] = g * sv[jj] + dv * sh.ks[jg * 8 + jj];
     if (jg == 0) a.out[(size_t)b * kMixerOut + h * kGdnDim + t0 + tl] = g * sh.sq_s[tl] + dv * sh.kq_s;
-    __syncthreads();  // shared memory is reused by the next item
+    sync();  // shared memory is reused by the next item
   }
 };
 

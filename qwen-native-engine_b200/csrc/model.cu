@@ -345,6 +345,8 @@ Runner::~Runner() {
     if (g) cudaGraphExecDestroy(g);
   for (auto& g : fgraph)
     if (g) cudaGraphExecDestroy(g);
+  for (auto& g : tgraph)
+    if (g) cudaGraphExecDestroy(g);
 }
 
 Runner::LayerArgs Runner::layer_args(int i) const {
@@ -545,11 +547,134 @@ void Runner::capture_set(cudaGraphExec_t* out, bool fused) {
   cudaStreamDestroy(cs);
 }
 
-// Both launch paths are captured; the per-operation graphs are the default (on the 2B config
-// they measure faster than the fused layer kernels), the fused ones are chosen with set_fused.
+// Whether the token kernel can run this model: one sequence, f16 matrices whose shapes the ring
+// slots take (k a multiple of 256 up to 6144), the GDN gated norm on 2048-wide outputs, and a
+// device with a co-resident CTA per SM.
+bool Runner::token_supported() {
+  const Model& M = *m;
+  if (st.batch != 1 || M.cfg.layers < 1) return false;
+  if (M.lm_head.kind != kF16 || !token_gemv_ok(M.lm_head.rows, M.lm_head.k, kArgmax)) return false;
+  if (M.embed.k != M.layers[0].in.k) return false;
+  for (const LayerWeights& L : M.layers) {
+    if (L.in.kind != kF16 || L.out.kind != kF16 || L.gate_up.kind != kF16 || L.down.kind != kF16) return false;
+    if (!token_gemv_ok(L.in.rows, L.in.k, kStore) || !token_gemv_ok(L.out.rows, L.out.k, kAccumulate) ||
+        !token_gemv_ok(L.gate_up.rows, L.gate_up.k, kSwiGlu) || !token_gemv_ok(L.down.rows, L.down.k, kAccumulate))
+      return false;
+    if (L.out.k != kMixerOut) return false;
+  }
+  token_ctas = qne::token_ctas();
+  return token_ctas > 0;
+}
+
+// The token's phases in launch order (kernels/src/model.rs:220-269), with the same buffers and
+// prologues / epilogues as the per-operation graph.
+std::vector<TkPhase> Runner::token_phase_list(Variant v) const {
+  std::vector<TkPhase> ph;
+  auto gemv = [&](const GemvArgs& a) {
+    TkPhase p;
+    p.kind = kTkGemv;
+    p.pro = a.pro;
+    p.epi = a.epi;
+    p.rows = a.m.rows;
+    p.k = a.m.k;
+    p.w = static_cast<const uint16_t*>(a.m.w);
+    p.x = a.x;
+    p.y = a.y;
+    p.norm_w = a.norm_w;
+    p.zgate = a.zgate;
+    ph.push_back(p);
+  };
+  for (int i = 0; i < m->cfg.layers; ++i) {
+    const LayerArgs r = layer_args(i);
+    gemv(r.in);
+    TkPhase mix;
+    if (r.attention) {
+      mix.kind = kTkAttn;
+      mix.at = r.at;
+      mix.pool_pages = st.pool_pages;
+      ph.push_back(mix);
+      mix.kind = kTkMerge;
+      ph.push_back(mix);
+    } else {
+      mix.kind = kTkGdn;
+      mix.gdn = r.gdn;
+      ph.push_back(mix);
+    }
+    gemv(r.out);
+    gemv(r.gate_up);
+    gemv(r.down);
+  }
+  if (v != kLayers) gemv(head_args(v));
+  return ph;
+}
+
+TkArgs Runner::token_args(Variant v) const {
+  TkArgs a;
+  a.phases = token_phases[v];
+  a.nphases = token_nphases[v];
+  a.ctl = st.ctl;
+  a.embed = m->embed;
+  a.h_out = h;
+  argmax_scratch_carve(argmax_scratch, &a.part_val, &a.part_idx, &a.ticket);
+  a.update_token = v == kGreedy ? 1 : 0;
+  a.barrier = reinterpret_cast<unsigned long long*>(barrier);
+  a.err = &st.ctl->flags;
+  a.wait_limit_ns = wait_test_ns ? wait_test_ns : kBarrierLimitNs;
+  a.wait_extra = wait_test_ns ? 1u : 0u;
+  a.attn_part = attn_part;
+  return a;
+}
+
+// Uploads the phase lists once and captures one single-launch graph per variant.
+void Runner::capture_token() {
+  if (!attn_part) attn_part = static_cast<float*>(m->alloc(token_attn_part_floats() * sizeof(float)));
+  for (int v = 0; v < kVariants; ++v) {
+    const std::vector<TkPhase> list = token_phase_list((Variant)v);
+    if (!token_phases[v]) token_phases[v] = static_cast<TkPhase*>(m->alloc(list.size() * sizeof(TkPhase)));
+    cuda_check(cudaMemcpy(token_phases[v], list.data(), list.size() * sizeof(TkPhase), cudaMemcpyHostToDevice),
+               "token phases");
+    token_nphases[v] = (int)list.size();
+  }
+  cudaStream_t cs;
+  cuda_check(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking), "cudaStreamCreate");
+  for (int v = 0; v < kVariants; ++v) {
+    if (tgraph[v]) {
+      cudaGraphExecDestroy(tgraph[v]);
+      tgraph[v] = nullptr;
+    }
+    cuda_check(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal), "begin capture");
+    const cudaError_t le = launch_token(token_args((Variant)v), token_ctas, cs, true);
+    cudaGraph_t g = nullptr;
+    const cudaError_t ce = cudaStreamEndCapture(cs, &g);
+    cudaError_t ie = cudaSuccess;
+    if (le == cudaSuccess && ce == cudaSuccess) ie = cudaGraphInstantiate(&tgraph[v], g, 0);
+    if (g) cudaGraphDestroy(g);
+    if (le != cudaSuccess || ce != cudaSuccess || ie != cudaSuccess) {
+      cudaStreamDestroy(cs);
+      cuda_check(le != cudaSuccess ? le : ce != cudaSuccess ? ce : ie, "token graph");
+    }
+  }
+  cudaStreamDestroy(cs);
+}
+
+// The launch paths are captured once; the per-operation graphs are the default until
+// set_path chooses another.
 void Runner::capture_graphs() {
   capture_set(graph, false);
   use_fused = false;
+  path = kPathOps;
+  if (token_supported()) {
+    try {
+      capture_token();
+    } catch (const QneError&) {
+      for (auto& g : tgraph)
+        if (g) {
+          cudaGraphExecDestroy(g);
+          g = nullptr;
+        }
+      token_ctas = 0;
+    }
+  }
   if (fused_supported()) {
     try {
       capture_set(fgraph, true);
@@ -565,9 +690,14 @@ void Runner::capture_graphs() {
   }
 }
 
-bool Runner::set_fused(bool on) {
-  if (on && !fgraph[0]) return false;
-  use_fused = on;
+bool Runner::set_fused(bool on) { return set_path(on ? kPathLayers : kPathOps); }
+
+bool Runner::set_path(int p) {
+  if (p == kPathLayers && !fgraph[0]) return false;
+  if (p == kPathToken && !tgraph[0]) return false;
+  if (p < kPathOps || p > kPathToken) return false;
+  path = p;
+  use_fused = p == kPathLayers;
   return true;
 }
 
@@ -587,23 +717,30 @@ bool Runner::set_trace(bool on) {
 }
 
 bool Runner::set_wait_test(uint64_t limit_ns) {
-  if (!fgraph[0]) return false;
+  if (!fgraph[0] && !tgraph[0]) return false;
   if (limit_ns == wait_test_ns) return true;
   wait_test_ns = limit_ns;
-  for (auto& g : fgraph)
-    if (g) {
-      cudaGraphExecDestroy(g);
-      g = nullptr;
-    }
-  capture_set(fgraph, true);
+  if (fgraph[0]) {
+    for (auto& g : fgraph)
+      if (g) {
+        cudaGraphExecDestroy(g);
+        g = nullptr;
+      }
+    capture_set(fgraph, true);
+  }
+  if (tgraph[0]) capture_token();
   return true;
 }
 
-size_t Runner::per_token() const { return use_fused ? fused_launches_per_token : launches_per_token; }
+size_t Runner::per_token() const {
+  return path == kPathToken ? 1 : use_fused ? fused_launches_per_token : launches_per_token;
+}
 
 void Runner::launch(Variant v, cudaStream_t s) {
-  cuda_check(cudaGraphLaunch(use_fused ? fgraph[v] : graph[v], s), "graph launch");
-  const size_t n = use_fused ? fused_launches_per_token : (v == kLayers ? launches_per_token - 1 : launches_per_token);
+  cuda_check(cudaGraphLaunch(path == kPathToken ? tgraph[v] : use_fused ? fgraph[v] : graph[v], s), "graph launch");
+  const size_t n = path == kPathToken ? 1
+                   : use_fused        ? fused_launches_per_token
+                                      : (v == kLayers ? launches_per_token - 1 : launches_per_token);
   for (size_t i = 0; i < n; ++i) count_launch();
 }
 
@@ -641,6 +778,14 @@ bool Model::set_fused(bool on) {
 }
 
 bool Model::fused() const { return single_->use_fused; }
+
+bool Model::set_path(int p) {
+  DeviceGuard g(device);
+  cuda_check(cudaStreamSynchronize(stream()), "set_path");
+  return single_->set_path(p);
+}
+
+int Model::path() const { return single_->path; }
 
 void Model::set_phase_trace(bool on) {
   DeviceGuard g(device);

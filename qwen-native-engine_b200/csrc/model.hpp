@@ -15,6 +15,7 @@
 #include "gdn_dev.cuh"
 #include "gemv.cuh"
 #include "persist.cuh"
+#include "token.cuh"
 
 namespace qne {
 
@@ -118,6 +119,8 @@ class Model {
   void set_stream(cudaStream_t s);
   bool set_fused(bool on);
   bool fused() const;
+  bool set_path(int p);  // false if that path cannot run this model
+  int path() const;
   void set_phase_trace(bool on);
   void set_wait_test(uint64_t limit_ns);
   // Model::profile_token: one greedy token, kernel by kernel, milliseconds per dispatch label.
@@ -175,10 +178,24 @@ class Runner {
   enum Variant { kGreedy = 0, kStep = 1, kLayers = 2, kVariants = 3 };
   cudaGraphExec_t graph[kVariants] = {nullptr, nullptr, nullptr};   // one kernel per op
   cudaGraphExec_t fgraph[kVariants] = {nullptr, nullptr, nullptr};  // one fused launch per layer
+  cudaGraphExec_t tgraph[kVariants] = {nullptr, nullptr, nullptr};  // one token-kernel launch
   size_t launches_per_token = 0;
   size_t fused_launches_per_token = 0;
-  bool use_fused = false;
+  // Launch path of a token: kPathOps (one kernel per operation), kPathLayers (one fused launch
+  // per layer), kPathToken (one launch per token).
+  enum Path { kPathOps = 0, kPathLayers = 1, kPathToken = 2 };
+  int path = kPathOps;
+  bool use_fused = false;  // path == kPathLayers
   int fused_ctas = 0, fused_max_k = 0;
+  int token_ctas = 0;                            // 0: the token kernel cannot run this model
+  TkPhase* token_phases[kVariants] = {nullptr, nullptr, nullptr};  // device phase lists
+  int token_nphases[kVariants] = {0, 0, 0};
+  float* attn_part = nullptr;                    // token kernel attention partials
+  bool token_supported();
+  std::vector<TkPhase> token_phase_list(Variant v) const;
+  TkArgs token_args(Variant v) const;
+  void capture_token();
+  bool set_path(int p);
 
   struct LayerArgs {
     bool attention = false;

@@ -1,0 +1,718 @@
+// The token kernel: one launch per B = 1 decode token (the per-token dispatch list of
+// kernels/src/model.rs:220-269 - per layer in-projection, GDN or attention, out-projection,
+// gate_up, down; then final norm + LM head + greedy pick - run as phases of one grid).
+//
+// Why: a decode token is a chain of ~120 dependent steps, and as separate kernels each step pays
+// a launch boundary and its own ramp and tail, during which HBM idles (the per-operation graph
+// measured 1.1 ms per 2B token against 0.58 ms of weight streaming). Here the weight streaming
+// never waits for a dependency:
+//   * one CTA per SM (148), 8 consumer warps + 1 producer warp;
+//   * the producer warp walks the token's GEMV phases in order and bulk-copies (TMA,
+//     cp.async.bulk, no multicast) this CTA's rows of every matrix into a ring of 8 x 24 KB
+//     shared-memory slots, guarded by full/empty mbarriers. Weights depend on nothing, so the
+//     producer runs ahead across phase boundaries until the ring is full: while the consumers
+//     wait at a grid barrier for the previous phase's output, the next phase's first 192 KB per
+//     SM (28 MB over the GPU) are already streaming;
+//   * consumer warp w owns ring slot w and takes every 8th slot of the CTA's sequence. A slot
+//     holds whole rows (2, 3, 6 or 12 by row length; SwiGLU: gate rows then the matching up
+//     rows); the warp dots them with x (staged once per phase in shared memory with its prologue:
+//     copy, RMSNorm, gated GDN RMSNorm, or embedding gather + RMSNorm), reduces across lanes and
+//     applies the epilogue (store, residual add, SwiGLU, greedy-pick candidate);
+//   * phases that read what the previous phase wrote start behind a grid barrier (an arrival
+//     counter; release reduction to arrive, acquire polls, bounded in time with an error flag);
+//   * GDN: one dev::GdnItem (16 value columns of one head) per CTA for CTAs 0..127, its state
+//     slice loaded before the barrier;
+//   * attention: one 64-token split of one KV head per CTA, its K and V rows (f16, through the
+//     page table) loaded into registers before the barrier; q / k RMSNorm + RoPE per warp with
+//     shuffles; scores reduced with one butterfly per warp; per-split (max, sum, 4 x 256 sums)
+//     partials; a merge phase (8 CTAs, one per query head) combines the splits and applies the
+//     output gate. The split holding the current position appends its K/V (rounded to f16).
+// Results match the per-operation kernels within the logit tolerance (f32 accumulation, other
+// summation order).
+#include <math.h>
+
+#include "gemv_dev.cuh"
+#include "tma.cuh"
+#include "token.cuh"
+
+namespace qne {
+namespace {
+
+using namespace dev;
+
+constexpr int kTkConsumerWarps = 8;
+constexpr int kTkConsumers = kTkConsumerWarps * 32;
+constexpr int kTkThreads = kTkConsumers + 32;  // + the producer warp
+constexpr int kTkSlots = kTkConsumerWarps;     // one ring slot per consumer warp
+constexpr uint32_t kTkSlotBytes = 24u << 10;
+constexpr int kTkMaxK = 6144;
+constexpr int kTkSplit = 64;                                       // attention tokens per item
+constexpr int kTkMaxSplits = kMaxContext / kTkSplit;               // 64
+constexpr int kTkPartStride = kQPerKv * kHeadDim + 2 * kQPerKv;    // acc[4][256], m[4], l[4]
+
+struct TkShared {
+  uint8_t ring[kTkSlots][kTkSlotBytes];
+  float xs[kTkMaxK];  // the GEMV input (two planes); scratch of the mixer phases
+  unsigned long long full[kTkSlots];
+  unsigned long long empty[kTkSlots];
+  float red[kTkConsumerWarps];
+  float bval[kTkConsumerWarps];
+  uint32_t bidx[kTkConsumerWarps];
+  float mx[kQPerKv], sm[kQPerKv];
+  uint32_t flag;
+};
+static_assert(sizeof(GdnShared) <= sizeof(float) * kTkMaxK, "GDN scratch aliases xs");
+static_assert((kTkSlotBytes % 128) == 0, "ring slots stay 128-byte aligned");
+
+struct ConsumerBar {
+  __device__ __forceinline__ void operator()() const { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+};
+
+__device__ __forceinline__ unsigned long long tk_now() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ unsigned long long tk_ld_acquire64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint32_t tk_ld_acquire(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void tk_red_release64(unsigned long long* p, unsigned long long v) {
+  asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Grid barrier among the consumer warps of all CTAs (the producer warps never join): the counter
+// is zero at launch, barrier n completes at n * (grid + extra) arrivals, the last CTA to exit
+// clears it. Bounded in time; once any CTA gave up (kFlagTimeout), the others stop waiting.
+struct TkBarrier {
+  unsigned long long* count;
+  unsigned long long target;  // consumer thread 0 only
+  uint64_t limit_ns;
+  uint32_t extra;
+
+  __device__ __forceinline__ void wait(uint32_t* err) {
+    ConsumerBar()();
+    if (threadIdx.x == 0) {
+      target += gridDim.x + extra;
+      __threadfence();
+      tk_red_release64(count, 1ull);
+      const unsigned long long t0 = tk_now();
+      uint32_t rounds = 0;
+      while (tk_ld_acquire64(count) < target) {
+        if ((++rounds & 63u) == 0u) {
+          if (tk_ld_acquire(err) & kFlagTimeout) break;
+          if (tk_now() - t0 > limit_ns) {
+            atomicOr(err, kFlagTimeout);
+            break;
+          }
+        }
+      }
+    }
+    ConsumerBar()();
+  }
+
+  __device__ __forceinline__ void exit() {
+    ConsumerBar()();
+    if (threadIdx.x == 0 && atomicAdd(count + 1, 1ull) == gridDim.x - 1) {
+      count[0] = 0ull;
+      count[1] = 0ull;
+      __threadfence();
+    }
+  }
+};
+
+// This CTA's share of a GEMV phase: output rows [r0, r1), `per` output rows per ring slot (a
+// slot holds R = per rows, or per gate rows then per up rows for SwiGLU; R in {2, 3, 6, 12}).
+struct Geo {
+  int k, out_rows, r0, r1, per, R, nslots;
+  uint32_t rb;  // bytes per row
+  bool sw;
+  __device__ __forceinline__ void init(const TkPhase& p, int cta, int ncta) {
+    sw = p.epi == kSwiGlu;
+    k = p.k;
+    out_rows = sw ? p.rows / 2 : p.rows;
+    rb = (uint32_t)k * 2u;
+    r0 = (int)((long)out_rows * cta / ncta);
+    r1 = (int)((long)out_rows * (cta + 1) / ncta);
+    int cap = (int)(kTkSlotBytes / rb);
+    if (sw) {
+      cap /= 2;
+      per = cap >= 6 ? 6 : cap >= 3 ? 3 : 1;
+      R = 2 * per;
+    } else {
+      per = cap >= 12 ? 12 : cap >= 6 ? 6 : cap >= 3 ? 3 : 2;
+      R = per;
+    }
+    nslots = r1 > r0 ? (r1 - r0 + per - 1) / per : 0;
+  }
+};
+
+// ------------------------------------------------------------------------------------------
+// Producer: lane 0 of the last warp.
+// ------------------------------------------------------------------------------------------
+__device__ __noinline__ void tk_produce(const TkArgs& A, TkShared& sh) {
+  uint32_t g = 0;
+#pragma unroll 1
+  for (int p = 0; p < A.nphases; ++p) {
+    const TkPhase& ph = A.phases[p];
+    if (ph.kind != kTkGemv) continue;
+    Geo geo;
+    geo.init(ph, blockIdx.x, gridDim.x);
+    const uint8_t* W = reinterpret_cast<const uint8_t*>(ph.w);
+#pragma unroll 1
+    for (int i = 0; i < geo.nslots; ++i, ++g) {
+      const int s = (int)(g % kTkSlots);
+      const uint32_t j = g / kTkSlots;
+      mbar_wait(smem_u32(&sh.empty[s]), (j & 1u) ^ 1u, A.err);
+      const int a = geo.r0 + i * geo.per;
+      const int n = min(geo.per, geo.r1 - a);
+      const uint32_t bytes = (uint32_t)n * geo.rb;
+      const uint32_t full = smem_u32(&sh.full[s]);
+      mbar_arrive_expect_tx(full, geo.sw ? 2u * bytes : bytes);
+      bulk_g2s(smem_u32(sh.ring[s]), W + (size_t)a * geo.rb, bytes, full);
+      if (geo.sw)
+        bulk_g2s(smem_u32(sh.ring[s]) + (uint32_t)geo.per * geo.rb, W + (size_t)(geo.out_rows + a) * geo.rb, bytes,
+                 full);
+    }
+  }
+  // Every copy lands before the CTA can exit (bounded; the consumers normally saw them all).
+#pragma unroll 1
+  for (uint32_t s = 0; s < (uint32_t)kTkSlots && s < g; ++s) {
+    const uint32_t fills = (g - s + kTkSlots - 1) / kTkSlots;
+    mbar_wait(smem_u32(&sh.full[s]), (fills - 1u) & 1u, A.err);
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// Consumers
+// ------------------------------------------------------------------------------------------
+
+// Stages x of a GEMV phase as two planes (elements 0-3 and 4-7 of every 8-element chunk), so a
+// lane's 16-byte reads of consecutive chunks are conflict-free, applying the prologue.
+__device__ __forceinline__ void tk_stage(const TkPhase& p, const TkArgs& A, TkShared& sh) {
+  const int k = p.k, tid = threadIdx.x, nc = k / 8;
+  float* xlo = sh.xs;
+  float* xhi = sh.xs + k / 2;
+  float ss = 0.f;
+  uint32_t token = 0;
+  if (p.pro == kProEmbedNorm) {
+    token = A.ctl->token;
+    if (token >= (uint32_t)A.embed.rows) token = (uint32_t)A.embed.rows - 1;
+  }
+#pragma unroll 1
+  for (int c = tid; c < nc; c += kTkConsumers) {
+    float v[8];
+    if (p.pro == kProEmbedNorm) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = deq_elem(A.embed, token, c * 8 + j);
+      if (blockIdx.x == 0) {
+        *reinterpret_cast<float4*>(A.h_out + c * 8) = make_float4(v[0], v[1], v[2], v[3]);
+        *reinterpret_cast<float4*>(A.h_out + c * 8 + 4) = make_float4(v[4], v[5], v[6], v[7]);
+      }
+    } else {
+      const float4 a = __ldcg(reinterpret_cast<const float4*>(p.x + c * 8));
+      const float4 b = __ldcg(reinterpret_cast<const float4*>(p.x + c * 8 + 4));
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+      v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    }
+    float cs = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) cs = fmaf(v[j], v[j], cs);
+    if (p.pro == kProGdnGate) {
+      // k == 2048 and 256 threads: one chunk per thread, 16 consecutive threads per 128-wide head.
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) cs += __shfl_xor_sync(0xffffffffu, cs, o);
+      const float inv = rsqrtf(cs / (float)kGdnDim + 1e-6f);
+      const int d = (c * 8) & (kGdnDim - 1);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = v[j] * inv * silu(__ldcg(p.zgate + c * 8 + j)) * p.norm_w[d + j];
+    }
+    ss += cs;
+    *reinterpret_cast<float4*>(xlo + c * 4) = make_float4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<float4*>(xhi + c * 4) = make_float4(v[4], v[5], v[6], v[7]);
+  }
+  if (p.pro == kProRmsNorm || p.pro == kProEmbedNorm) {
+    if (p.pro == kProEmbedNorm && blockIdx.x == 0 && tid == 0) A.ctl->count += 1;  // conv windows
+    float t = warp_sum(ss);
+    ConsumerBar()();
+    if ((tid & 31) == 0) sh.red[tid >> 5] = t;
+    ConsumerBar()();
+    t = 0.f;
+#pragma unroll
+    for (int w = 0; w < kTkConsumerWarps; ++w) t += sh.red[w];
+    const float inv = rsqrtf(t / (float)k + 1e-6f);
+#pragma unroll 1
+    for (int c = tid; c < nc; c += kTkConsumers) {
+      const float4 w0 = *reinterpret_cast<const float4*>(p.norm_w + c * 8);
+      const float4 w1 = *reinterpret_cast<const float4*>(p.norm_w + c * 8 + 4);
+      float4 lo = *reinterpret_cast<float4*>(xlo + c * 4), hi = *reinterpret_cast<float4*>(xhi + c * 4);
+      lo.x *= inv * w0.x; lo.y *= inv * w0.y; lo.z *= inv * w0.z; lo.w *= inv * w0.w;
+      hi.x *= inv * w1.x; hi.y *= inv * w1.y; hi.z *= inv * w1.z; hi.w *= inv * w1.w;
+      *reinterpret_cast<float4*>(xlo + c * 4) = lo;
+      *reinterpret_cast<float4*>(xhi + c * 4) = hi;
+    }
+  }
+  ConsumerBar()();
+}
+
+// Dot products of the R rows of one ring slot with x; every lane ends with the R sums.
+template <int R>
+__device__ __forceinline__ void tk_dot(const uint8_t* slot, const float* xs, int k, uint32_t rb, int lane,
+                                       float (&acc)[12]) {
+  float a[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) a[r] = 0.f;
+  const float* xlo = xs;
+  const float* xhi = xs + k / 2;
+#pragma unroll 2
+  for (int c = lane; c < k / 8; c += 32) {
+    float xv[8];
+    *reinterpret_cast<float4*>(xv) = *reinterpret_cast<const float4*>(xlo + c * 4);
+    *reinterpret_cast<float4*>(xv + 4) = *reinterpret_cast<const float4*>(xhi + c * 4);
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const uint4 w = *reinterpret_cast<const uint4*>(slot + (size_t)r * rb + (size_t)c * 16);
+      a[r] += dot_f16(w, xv);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < R; ++r) acc[r] = warp_sum(a[r]);
+}
+
+__device__ __noinline__ void tk_gemv(const TkPhase& ph, const TkArgs& A, TkShared& sh, uint32_t& g) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  Geo geo;
+  geo.init(ph, blockIdx.x, gridDim.x);
+  float best_v = -INFINITY;
+  uint32_t best_i = 0xFFFFFFFFu;
+#pragma unroll 1
+  for (int i = 0; i < geo.nslots; ++i) {
+    const uint32_t gi = g + (uint32_t)i;
+    if ((int)(gi % kTkSlots) != warp) continue;
+    const uint32_t j = gi / kTkSlots;
+    mbar_wait(smem_u32(&sh.full[warp]), j & 1u, A.err);
+    float acc[12];
+    const uint8_t* slot = sh.ring[warp];
+    switch (geo.R) {
+      case 2: tk_dot<2>(slot, sh.xs, geo.k, geo.rb, lane, acc); break;
+      case 3: tk_dot<3>(slot, sh.xs, geo.k, geo.rb, lane, acc); break;
+      case 6: tk_dot<6>(slot, sh.xs, geo.k, geo.rb, lane, acc); break;
+      default: tk_dot<12>(slot, sh.xs, geo.k, geo.rb, lane, acc); break;
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(&sh.empty[warp]));
+    const int a = geo.r0 + i * geo.per;
+    const int n = min(geo.per, geo.r1 - a);
+    if (lane == 0) {
+#pragma unroll
+      for (int r = 0; r < 12; ++r) {
+        if (r >= n) break;
+        const int row = a + r;
+        if (geo.sw) {
+          float up = 0.f;
+#pragma unroll
+          for (int u = 0; u < 12; ++u)
+            if (u == geo.per + r) up = acc[u];
+          ph.y[row] = silu(acc[r]) * up;
+        } else if (ph.epi == kAccumulate) {
+          ph.y[row] = __ldcg(ph.y + row) + acc[r];
+        } else {
+          ph.y[row] = acc[r];
+          if (ph.epi == kArgmax && better(acc[r], (uint32_t)row, best_v, best_i) && acc[r] > -INFINITY) {
+            best_v = acc[r];
+            best_i = (uint32_t)row;
+          }
+        }
+      }
+    }
+  }
+  g += (uint32_t)geo.nslots;
+  if (ph.epi != kArgmax) return;
+  // Greedy pick: per-CTA best, then the last CTA reduces across CTAs and updates the control words.
+  if (lane == 0) {
+    sh.bval[warp] = best_v;
+    sh.bidx[warp] = best_i;
+  }
+  ConsumerBar()();
+  if (threadIdx.x == 0) {
+    float v = -INFINITY;
+    uint32_t ix = 0xFFFFFFFFu;
+    for (int w = 0; w < kTkConsumerWarps; ++w)
+      if (better(sh.bval[w], sh.bidx[w], v, ix)) {
+        v = sh.bval[w];
+        ix = sh.bidx[w];
+      }
+    A.part_val[blockIdx.x] = v;
+    A.part_idx[blockIdx.x] = ix;
+    __threadfence();
+    sh.flag = (atomicAdd(A.ticket, 1u) == gridDim.x - 1) ? 1u : 0u;
+  }
+  ConsumerBar()();
+  if (sh.flag && warp == 0) {
+    __threadfence();
+    float v = -INFINITY;
+    uint32_t ix = 0xFFFFFFFFu;
+#pragma unroll 1
+    for (int b = lane; b < (int)gridDim.x; b += 32) {
+      const float bv = __ldcg(A.part_val + b);
+      const uint32_t bi = __ldcg(A.part_idx + b);
+      if (better(bv, bi, v, ix)) {
+        v = bv;
+        ix = bi;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+      const uint32_t oi = __shfl_xor_sync(0xffffffffu, ix, o);
+      if (better(ov, oi, v, ix)) {
+        v = ov;
+        ix = oi;
+      }
+    }
+    if (lane == 0) {
+      if (A.update_token) {
+        A.ctl->token = (ix == 0xFFFFFFFFu) ? 0u : ix;
+        A.ctl->pos += 1;
+      }
+      *A.ticket = 0u;
+    }
+  }
+}
+
+__device__ __forceinline__ void unpack8f(const uint4& w, float* f) {
+  const float2 a = h2f2(w.x), b = h2f2(w.y), c = h2f2(w.z), d = h2f2(w.w);
+  f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y;
+  f[4] = c.x; f[5] = c.y; f[6] = d.x; f[7] = d.y;
+}
+__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
+  return (uint32_t)__half_as_ushort(__float2half_rn(a)) | ((uint32_t)__half_as_ushort(__float2half_rn(b)) << 16);
+}
+
+// RMSNorm (eps 1e-6) of a 256-vector held as 8 dims per lane (dims 8 lane ..), times w, then
+// rotate-half RoPE on dims 0..63 (pairs (i, i + 32): lanes 0-3 pair with lanes 4-7).
+__device__ __forceinline__ void tk_norm_rope(float (&v)[8], const float* w, const float* rope, uint32_t pos,
+                                             int lane) {
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) ss = fmaf(v[j], v[j], ss);
+  const float inv = rsqrtf(warp_sum(ss) / (float)kHeadDim + 1e-6f);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) v[j] = v[j] * inv * w[lane * 8 + j];
+  float other[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) other[j] = __shfl_xor_sync(0xffffffffu, v[j], 4);
+  if (lane < 8) {
+    const int i0 = (lane & 3) * 8;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float c = rope[(size_t)pos * kRopeHalf + i0 + j];
+      const float s = rope[(size_t)kMaxContext * kRopeHalf + (size_t)pos * kRopeHalf + i0 + j];
+      v[j] = lane < 4 ? v[j] * c - other[j] * s : v[j] * c + other[j] * s;
+    }
+  }
+}
+
+// One attention work item: (64-token split, KV head) of the single sequence.
+struct TkAttn {
+  int split, kvh, l0, l1;
+  uint32_t pos;
+  bool valid, owner;
+  uint4 kr[8], vr[8];  // this lane's 8 dims of the warp's 8 tokens' K and V rows
+
+  __device__ __forceinline__ void prefetch(const AttnArgs& a, uint32_t pool_pages, int item) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pos = a.pos[0];
+    if (pos >= (uint32_t)kMaxContext) {
+      if (a.flags && threadIdx.x == 0 && item == 0) atomicOr(a.flags, kFlagPosClamped);
+      pos = kMaxContext - 1;
+    }
+    const int len = (int)pos + 1;
+    const int nsplit = (len + kTkSplit - 1) / kTkSplit;
+    split = item >> 1;
+    kvh = item & 1;
+    valid = split < nsplit;
+    if (!valid) return;
+    l0 = split * kTkSplit;
+    l1 = min(l0 + kTkSplit, len);
+    owner = (int)pos >= l0 && (int)pos < l1;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int t = l0 + warp * 8 + i;
+      kr[i] = make_uint4(0u, 0u, 0u, 0u);
+      vr[i] = make_uint4(0u, 0u, 0u, 0u);
+      if (t < l1 && t != (int)pos) {
+        const uint32_t page = a.page_table[t / kPageTokens];
+        if (page < pool_pages) {
+          kr[i] = ld_stream(kv_row(a.kv, page, 0, kvh, t % kPageTokens) + lane * 8);
+          vr[i] = ld_stream(kv_row(a.kv, page, 1, kvh, t % kPageTokens) + lane * 8);
+        }
+      }
+    }
+  }
+
+  __device__ __forceinline__ void run(const AttnArgs& a, uint32_t pool_pages, TkShared& sh, float* part) {
+    if (!valid) return;  // uniform over the CTA
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const float* pr = a.proj;
+    // q of the 4 heads of this KV head: this lane's 8 dims, normalized, rotated, times 1/16.
+    float q[kQPerKv][8];
+#pragma unroll
+    for (int hh = 0; hh < kQPerKv; ++hh) {
+      const float* src = pr + (kvh * kQPerKv + hh) * kHeadDim + lane * 8;
+      const float4 x0 = __ldcg(reinterpret_cast<const float4*>(src));
+      const float4 x1 = __ldcg(reinterpret_cast<const float4*>(src + 4));
+      q[hh][0] = x0.x; q[hh][1] = x0.y; q[hh][2] = x0.z; q[hh][3] = x0.w;
+      q[hh][4] = x1.x; q[hh][5] = x1.y; q[hh][6] = x1.z; q[hh][7] = x1.w;
+      tk_norm_rope(q[hh], a.norms, a.rope, pos, lane);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) q[hh][j] *= 0.0625f;
+    }
+    // The split holding pos appends the current key (normalized, rotated) and value, rounded
+    // to f16, and uses the rounded values.
+    if (owner && warp == ((int)pos - l0) / 8) {
+      const int io = ((int)pos - l0) % 8;
+      float kc[8], vc[8];
+      const float* ks = pr + 4096 + kvh * kHeadDim + lane * 8;
+      const float* vs = pr + 4608 + kvh * kHeadDim + lane * 8;
+      const float4 k0 = __ldcg(reinterpret_cast<const float4*>(ks)), k1 = __ldcg(reinterpret_cast<const float4*>(ks + 4));
+      const float4 v0 = __ldcg(reinterpret_cast<const float4*>(vs)), v1 = __ldcg(reinterpret_cast<const float4*>(vs + 4));
+      kc[0] = k0.x; kc[1] = k0.y; kc[2] = k0.z; kc[3] = k0.w; kc[4] = k1.x; kc[5] = k1.y; kc[6] = k1.z; kc[7] = k1.w;
+      vc[0] = v0.x; vc[1] = v0.y; vc[2] = v0.z; vc[3] = v0.w; vc[4] = v1.x; vc[5] = v1.y; vc[6] = v1.z; vc[7] = v1.w;
+      tk_norm_rope(kc, a.norms + kHeadDim, a.rope, pos, lane);
+      const uint4 kp = make_uint4(pack_half2(kc[0], kc[1]), pack_half2(kc[2], kc[3]), pack_half2(kc[4], kc[5]),
+                                  pack_half2(kc[6], kc[7]));
+      const uint4 vp = make_uint4(pack_half2(vc[0], vc[1]), pack_half2(vc[2], vc[3]), pack_half2(vc[4], vc[5]),
+                                  pack_half2(vc[6], vc[7]));
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (i == io) {
+          kr[i] = kp;
+          vr[i] = vp;
+        }
+      const uint32_t page = a.page_table[pos / kPageTokens];
+      if (page < pool_pages) {
+        *reinterpret_cast<uint4*>(const_cast<uint16_t*>(kv_row(a.kv, page, 0, kvh, pos % kPageTokens)) + lane) = kp;
+        *reinterpret_cast<uint4*>(const_cast<uint16_t*>(kv_row(a.kv, page, 1, kvh, pos % kPageTokens)) + lane) = vp;
+      }
+    }
+    // Scores of the warp's 8 tokens x 4 heads: lane-local partial dot products, then one
+    // butterfly that leaves the total of (token lane / 4, head lane % 4) in each lane.
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float kf[8];
+      unpack8f(kr[i], kf);
+#pragma unroll
+      for (int hh = 0; hh < kQPerKv; ++hh) {
+        float d = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) d = fmaf(q[hh][j], kf[j], d);
+        v[i * 4 + hh] = d;
+      }
+    }
+#pragma unroll
+    for (int o = 16, half = 16; o >= 1; o >>= 1, half >>= 1) {
+      const bool upper = (lane & o) != 0;
+#pragma unroll
+      for (int e = 0; e < half; ++e) {
+        const float send = upper ? v[e] : v[e + half];
+        const float keep = upper ? v[e + half] : v[e];
+        v[e] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+      }
+    }
+    float* sc = sh.xs;  // [4 heads][64 tokens]
+    {
+      const int i = lane >> 2, hh = lane & 3, t = l0 + warp * 8 + i;
+      sc[hh * kTkSplit + warp * 8 + i] = t < l1 ? v[0] : -INFINITY;
+    }
+    ConsumerBar()();
+    if (warp < kQPerKv) {
+      const float s0 = sc[warp * kTkSplit + lane], s1 = sc[warp * kTkSplit + lane + 32];
+      const float m = warp_max(fmaxf(s0, s1));
+      const float p0 = s0 == -INFINITY ? 0.f : expf(s0 - m), p1 = s1 == -INFINITY ? 0.f : expf(s1 - m);
+      const float l = warp_sum(p0 + p1);
+      sc[warp * kTkSplit + lane] = p0;
+      sc[warp * kTkSplit + lane + 32] = p1;
+      if (lane == 0) {
+        sh.mx[warp] = m;
+        sh.sm[warp] = l;
+      }
+    }
+    ConsumerBar()();
+    float acc[kQPerKv][8];
+#pragma unroll
+    for (int hh = 0; hh < kQPerKv; ++hh)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[hh][j] = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float vf[8];
+      unpack8f(vr[i], vf);
+#pragma unroll
+      for (int hh = 0; hh < kQPerKv; ++hh) {
+        const float p = sc[hh * kTkSplit + warp * 8 + i];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[hh][j] = fmaf(p, vf[j], acc[hh][j]);
+      }
+    }
+    // Sum the 8 warps' accumulators, two heads at a time through shared memory, into the partial.
+    float* buf = sh.xs + kQPerKv * kTkSplit;  // [8 warps][2 heads][256]
+    float* dst = part + (size_t)(kvh * kTkMaxSplits + split) * kTkPartStride;
+#pragma unroll 1
+    for (int hp = 0; hp < 2; ++hp) {
+#pragma unroll
+      for (int hl = 0; hl < 2; ++hl) {
+        float* b = buf + ((size_t)warp * 2 + hl) * kHeadDim + lane * 8;
+        *reinterpret_cast<float4*>(b) = make_float4(acc[2 * hp + hl][0], acc[2 * hp + hl][1], acc[2 * hp + hl][2],
+                                                    acc[2 * hp + hl][3]);
+        *reinterpret_cast<float4*>(b + 4) = make_float4(acc[2 * hp + hl][4], acc[2 * hp + hl][5],
+                                                        acc[2 * hp + hl][6], acc[2 * hp + hl][7]);
+      }
+      ConsumerBar()();
+      {
+        const int hl = tid >> 7, d = (tid & 127) * 2;
+        float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+        for (int w = 0; w < kTkConsumerWarps; ++w) {
+          s0 += buf[((size_t)w * 2 + hl) * kHeadDim + d];
+          s1 += buf[((size_t)w * 2 + hl) * kHeadDim + d + 1];
+        }
+        *reinterpret_cast<float2*>(dst + (2 * hp + hl) * kHeadDim + d) = make_float2(s0, s1);
+      }
+      ConsumerBar()();
+    }
+    if (tid < kQPerKv) {
+      dst[kQPerKv * kHeadDim + tid] = sh.mx[tid];
+      dst[kQPerKv * kHeadDim + kQPerKv + tid] = sh.sm[tid];
+    }
+  }
+};
+
+// Merge of the attention splits for query head h = CTA (0..7), thread = dim: softmax-weighted
+// sum of the splits' partials, divided by the total weight, times sigmoid(gate).
+__device__ __forceinline__ void tk_merge(const AttnArgs& a, const float* part) {
+  const int h = blockIdx.x, d = threadIdx.x;
+  uint32_t pos = a.pos[0];
+  if (pos >= (uint32_t)kMaxContext) pos = kMaxContext - 1;
+  const int nsplit = ((int)pos + kTkSplit) / kTkSplit;
+  const int kvh = h / kQPerKv, hh = h % kQPerKv;
+  const float* base = part + (size_t)kvh * kTkMaxSplits * kTkPartStride;
+  float M = -INFINITY;
+#pragma unroll 1
+  for (int s = 0; s < nsplit; ++s) M = fmaxf(M, __ldcg(base + (size_t)s * kTkPartStride + kQPerKv * kHeadDim + hh));
+  float L = 0.f, o = 0.f;
+#pragma unroll 4
+  for (int s = 0; s < nsplit; ++s) {
+    const float* ps = base + (size_t)s * kTkPartStride;
+    const float w = expf(__ldcg(ps + kQPerKv * kHeadDim + hh) - M);
+    L = fmaf(w, __ldcg(ps + kQPerKv * kHeadDim + kQPerKv + hh), L);
+    o = fmaf(w, __ldcg(ps + hh * kHeadDim + d), o);
+  }
+  const float gate = __ldcg(a.proj + 2048 + h * kHeadDim + d);
+  a.out[h * kHeadDim + d] = o / L / (1.0f + expf(-gate));
+}
+
+__device__ __noinline__ void tk_consume(const TkArgs& A, TkShared& sh) {
+  TkBarrier bar{A.barrier, 0ull, A.wait_limit_ns, A.wait_extra};
+  uint32_t g = 0;
+  pdl_wait();  // the previous token's control words and states are complete
+#pragma unroll 1
+  for (int p = 0; p < A.nphases; ++p) {
+    const TkPhase& ph = A.phases[p];
+    if (ph.kind == kTkGemv) {
+      if (p > 0) bar.wait(A.err);
+      tk_stage(ph, A, sh);
+      tk_gemv(ph, A, sh, g);
+    } else if (ph.kind == kTkGdn) {
+      const bool mine = (int)blockIdx.x < kGdnItemsPerSeq;
+      GdnItem it;
+      if (mine) it.prefetch(ph.gdn, blockIdx.x);  // the state slice, before the barrier
+      bar.wait(A.err);
+      if (mine) it.run_with(ph.gdn, *reinterpret_cast<GdnShared*>(sh.xs), ConsumerBar());
+    } else if (ph.kind == kTkAttn) {
+      TkAttn it;
+      const uint32_t pool = ph.pool_pages;
+      it.valid = false;
+      if ((int)blockIdx.x < kTkMaxSplits * kKvHeads) it.prefetch(ph.at, pool, blockIdx.x);
+      bar.wait(A.err);
+      it.run(ph.at, pool, sh, A.attn_part);
+    } else {  // kTkMerge
+      bar.wait(A.err);
+      if ((int)blockIdx.x < kAttnHeads) tk_merge(ph.at, A.attn_part);
+    }
+  }
+  bar.exit();
+}
+
+__global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_constant__ TkArgs A) {
+  extern __shared__ __align__(128) uint8_t tk_smem[];
+  TkShared& sh = *reinterpret_cast<TkShared*>(tk_smem);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTkSlots; ++s) {
+      mbar_init(smem_u32(&sh.full[s]), 1);
+      mbar_init(smem_u32(&sh.empty[s]), 1);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  pdl_launch();
+  if ((threadIdx.x >> 5) == kTkConsumerWarps) {
+    if ((threadIdx.x & 31) == 0) tk_produce(A, sh);
+    return;
+  }
+  tk_consume(A, sh);
+}
+
+}  // namespace
+
+size_t token_attn_part_floats() { return (size_t)kKvHeads * kTkMaxSplits * kTkPartStride; }
+
+bool token_gemv_ok(int rows, int k, int epi) {
+  if (k < 256 || k > kTkMaxK || k % 256 || rows < 1) return false;
+  if (epi == kSwiGlu && (rows % 2 || (size_t)4 * k > kTkSlotBytes)) return false;
+  return true;
+}
+
+int token_ctas() {
+  int dev = 0, sms = 0, per_sm = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  const int smem = (int)sizeof(TkShared);
+  if (cudaFuncSetAttribute(token_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, token_kernel, kTkThreads, smem) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  // One CTA per SM, all co-resident (the grid barriers need it); the mixers need a CTA per item.
+  if (per_sm < 1 || sms < kTkMaxSplits * kKvHeads || sms < kGdnItemsPerSeq || sms > kMaxGrid) return 0;
+  return sms;
+}
+
+cudaError_t launch_token(const TkArgs& args, int ctas, cudaStream_t stream, bool pdl) {
+  const int smem = (int)sizeof(TkShared);
+  cudaError_t e = cudaFuncSetAttribute(token_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ctas);
+  cfg.blockDim = dim3(kTkThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  count_launch();
+  return cudaLaunchKernelEx(&cfg, token_kernel, args);
+}
+
+}  // namespace qne

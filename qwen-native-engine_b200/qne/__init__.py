@@ -86,6 +86,8 @@ def _load_lib() -> C.CDLL:
         "qne_model_set_stream": (I32, [P, P]),
         "qne_model_set_fused": (I32, [P, I32]),
         "qne_model_fused": (I32, [P]),
+        "qne_model_set_path": (I32, [P, I32]),
+        "qne_model_path": (I32, [P]),
         "qne_model_set_phase_trace": (I32, [P, I32]),
         "qne_model_test_barrier_timeout": (I32, [P, U32]),
         "qne_profile_token": (I32, [P, C.POINTER(_ProfileEntry), SZ, C.POINTER(SZ)]),
@@ -359,6 +361,18 @@ class Model:
     @property
     def fused(self) -> bool:
         return bool(lib.qne_model_fused(self._h))
+
+    PATHS = {"operations": 0, "layers": 1, "token": 2}
+
+    def set_path(self, path: str) -> None:
+        """Launch path of a token: "operations" (one kernel per operation), "layers" (one fused
+        launch per layer) or "token" (one launch per token)."""
+        _check(lib.qne_model_set_path(self._h, self.PATHS[path]))
+
+    @property
+    def path(self) -> str:
+        n = int(lib.qne_model_path(self._h))
+        return {v: k for k, v in self.PATHS.items()}[n]
 
     def set_phase_trace(self, enable: bool) -> None:
         _check(lib.qne_model_set_phase_trace(self._h, 1 if enable else 0))
