@@ -156,7 +156,7 @@ struct Geo {
 // ------------------------------------------------------------------------------------------
 // Producer: lane 0 of the last warp.
 // ------------------------------------------------------------------------------------------
-__device__ __noinline__ void tk_produce(const TkArgs& A, TkShared& sh) {
+__device__ __forceinline__ void tk_produce(const TkArgs& A, TkShared& sh) {
   uint32_t g = 0;
 #pragma unroll 1
   for (int p = 0; p < A.nphases; ++p) {
@@ -264,13 +264,14 @@ __device__ __forceinline__ void tk_stage(const TkPhase& p, const TkArgs& A, TkSh
 // Dot products of the R rows of one ring slot with x; every lane ends with the R sums.
 template <int R>
 __device__ __forceinline__ void tk_dot(const uint8_t* slot, const float* xs, int k, uint32_t rb, int lane,
-                                       float (&acc)[12]) {
+                                       float (&acc)[R]) {
   float a[R];
 #pragma unroll
   for (int r = 0; r < R; ++r) a[r] = 0.f;
   const float* xlo = xs;
   const float* xhi = xs + k / 2;
-#pragma unroll 2
+  constexpr int U = R >= 6 ? 1 : 4;  // R (or 4 R) independent 16-byte loads per iteration
+#pragma unroll U
   for (int c = lane; c < k / 8; c += 32) {
     float xv[8];
     *reinterpret_cast<float4*>(xv) = *reinterpret_cast<const float4*>(xlo + c * 4);
@@ -285,51 +286,66 @@ __device__ __forceinline__ void tk_dot(const uint8_t* slot, const float* xs, int
   for (int r = 0; r < R; ++r) acc[r] = warp_sum(a[r]);
 }
 
-__device__ __noinline__ void tk_gemv(const TkPhase& ph, const TkArgs& A, TkShared& sh, uint32_t& g) {
+// The warp's slots of one GEMV phase (every 8th of the CTA's sequence), R rows per slot: wait for
+// the slot, dot, release the slot to the producer, apply the epilogue (lane 0). For SwiGLU the
+// slot's rows are per = R / 2 gate rows, then the matching up rows.
+template <int R, bool SW>
+__device__ __forceinline__ void tk_slots(const TkPhase& ph, const Geo& geo, const TkArgs& A, TkShared& sh, uint32_t g,
+                                         float& best_v, uint32_t& best_i) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  Geo geo;
-  geo.init(ph, blockIdx.x, gridDim.x);
-  float best_v = -INFINITY;
-  uint32_t best_i = 0xFFFFFFFFu;
+  constexpr int OUT = SW ? R / 2 : R;
 #pragma unroll 1
   for (int i = 0; i < geo.nslots; ++i) {
     const uint32_t gi = g + (uint32_t)i;
     if ((int)(gi % kTkSlots) != warp) continue;
     const uint32_t j = gi / kTkSlots;
     mbar_wait(smem_u32(&sh.full[warp]), j & 1u, A.err);
-    float acc[12];
-    const uint8_t* slot = sh.ring[warp];
-    switch (geo.R) {
-      case 2: tk_dot<2>(slot, sh.xs, geo.k, geo.rb, lane, acc); break;
-      case 3: tk_dot<3>(slot, sh.xs, geo.k, geo.rb, lane, acc); break;
-      case 6: tk_dot<6>(slot, sh.xs, geo.k, geo.rb, lane, acc); break;
-      default: tk_dot<12>(slot, sh.xs, geo.k, geo.rb, lane, acc); break;
-    }
+    float acc[R];
+    tk_dot<R>(sh.ring[warp], sh.xs, geo.k, geo.rb, lane, acc);
     __syncwarp();
     if (lane == 0) mbar_arrive(smem_u32(&sh.empty[warp]));
     const int a = geo.r0 + i * geo.per;
     const int n = min(geo.per, geo.r1 - a);
     if (lane == 0) {
 #pragma unroll
-      for (int r = 0; r < 12; ++r) {
-        if (r >= n) break;
-        const int row = a + r;
-        if (geo.sw) {
-          float up = 0.f;
-#pragma unroll
-          for (int u = 0; u < 12; ++u)
-            if (u == geo.per + r) up = acc[u];
-          ph.y[row] = silu(acc[r]) * up;
-        } else if (ph.epi == kAccumulate) {
-          ph.y[row] = __ldcg(ph.y + row) + acc[r];
-        } else {
-          ph.y[row] = acc[r];
-          if (ph.epi == kArgmax && better(acc[r], (uint32_t)row, best_v, best_i) && acc[r] > -INFINITY) {
-            best_v = acc[r];
-            best_i = (uint32_t)row;
+      for (int r = 0; r < OUT; ++r) {
+        if (r < n) {
+          const int row = a + r;
+          if (SW) {
+            ph.y[row] = silu(acc[r]) * acc[OUT + r];
+          } else if (ph.epi == kAccumulate) {
+            ph.y[row] = __ldcg(ph.y + row) + acc[r];
+          } else {
+            ph.y[row] = acc[r];
+            if (ph.epi == kArgmax && acc[r] > -INFINITY && better(acc[r], (uint32_t)row, best_v, best_i)) {
+              best_v = acc[r];
+              best_i = (uint32_t)row;
+            }
           }
         }
       }
+    }
+  }
+}
+
+__device__ __forceinline__ void tk_gemv(const TkPhase& ph, const TkArgs& A, TkShared& sh, uint32_t& g) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  Geo geo;
+  geo.init(ph, blockIdx.x, gridDim.x);
+  float best_v = -INFINITY;
+  uint32_t best_i = 0xFFFFFFFFu;
+  if (geo.sw) {
+    switch (geo.R) {
+      case 2: tk_slots<2, true>(ph, geo, A, sh, g, best_v, best_i); break;
+      case 6: tk_slots<6, true>(ph, geo, A, sh, g, best_v, best_i); break;
+      default: tk_slots<12, true>(ph, geo, A, sh, g, best_v, best_i); break;
+    }
+  } else {
+    switch (geo.R) {
+      case 2: tk_slots<2, false>(ph, geo, A, sh, g, best_v, best_i); break;
+      case 3: tk_slots<3, false>(ph, geo, A, sh, g, best_v, best_i); break;
+      case 6: tk_slots<6, false>(ph, geo, A, sh, g, best_v, best_i); break;
+      default: tk_slots<12, false>(ph, geo, A, sh, g, best_v, best_i); break;
     }
   }
   g += (uint32_t)geo.nslots;
@@ -442,17 +458,30 @@ struct TkAttn {
     l0 = split * kTkSplit;
     l1 = min(l0 + kTkSplit, len);
     owner = (int)pos >= l0 && (int)pos < l1;
+    // K rows before the barrier; V rows (needed only for the weighted sum) once the scores are
+    // done, so that K and V are never both live in registers.
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int t = l0 + warp * 8 + i;
       kr[i] = make_uint4(0u, 0u, 0u, 0u);
+      if (t < l1 && t != (int)pos) {
+        const uint32_t page = a.page_table[t / kPageTokens];
+        if (page < pool_pages) kr[i] = ld_stream(kv_row(a.kv, page, 0, kvh, t % kPageTokens) + lane * 8);
+      }
+    }
+  }
+
+  // V rows of the warp's tokens (the current token's, when this split appends it, is written by
+  // run() after this).
+  __device__ __forceinline__ void load_v(const AttnArgs& a, uint32_t pool_pages) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int t = l0 + warp * 8 + i;
       vr[i] = make_uint4(0u, 0u, 0u, 0u);
       if (t < l1 && t != (int)pos) {
         const uint32_t page = a.page_table[t / kPageTokens];
-        if (page < pool_pages) {
-          kr[i] = ld_stream(kv_row(a.kv, page, 0, kvh, t % kPageTokens) + lane * 8);
-          vr[i] = ld_stream(kv_row(a.kv, page, 1, kvh, t % kPageTokens) + lane * 8);
-        }
+        if (page < pool_pages) vr[i] = ld_stream(kv_row(a.kv, page, 1, kvh, t % kPageTokens) + lane * 8);
       }
     }
   }
@@ -461,21 +490,9 @@ struct TkAttn {
     if (!valid) return;  // uniform over the CTA
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const float* pr = a.proj;
-    // q of the 4 heads of this KV head: this lane's 8 dims, normalized, rotated, times 1/16.
-    float q[kQPerKv][8];
-#pragma unroll
-    for (int hh = 0; hh < kQPerKv; ++hh) {
-      const float* src = pr + (kvh * kQPerKv + hh) * kHeadDim + lane * 8;
-      const float4 x0 = __ldcg(reinterpret_cast<const float4*>(src));
-      const float4 x1 = __ldcg(reinterpret_cast<const float4*>(src + 4));
-      q[hh][0] = x0.x; q[hh][1] = x0.y; q[hh][2] = x0.z; q[hh][3] = x0.w;
-      q[hh][4] = x1.x; q[hh][5] = x1.y; q[hh][6] = x1.z; q[hh][7] = x1.w;
-      tk_norm_rope(q[hh], a.norms, a.rope, pos, lane);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) q[hh][j] *= 0.0625f;
-    }
     // The split holding pos appends the current key (normalized, rotated) and value, rounded
     // to f16, and uses the rounded values.
+    uint4 vp = make_uint4(0u, 0u, 0u, 0u);  // the appended value (owner warp)
     if (owner && warp == ((int)pos - l0) / 8) {
       const int io = ((int)pos - l0) % 8;
       float kc[8], vc[8];
@@ -488,49 +505,76 @@ struct TkAttn {
       tk_norm_rope(kc, a.norms + kHeadDim, a.rope, pos, lane);
       const uint4 kp = make_uint4(pack_half2(kc[0], kc[1]), pack_half2(kc[2], kc[3]), pack_half2(kc[4], kc[5]),
                                   pack_half2(kc[6], kc[7]));
-      const uint4 vp = make_uint4(pack_half2(vc[0], vc[1]), pack_half2(vc[2], vc[3]), pack_half2(vc[4], vc[5]),
-                                  pack_half2(vc[6], vc[7]));
+      vp = make_uint4(pack_half2(vc[0], vc[1]), pack_half2(vc[2], vc[3]), pack_half2(vc[4], vc[5]),
+                      pack_half2(vc[6], vc[7]));
 #pragma unroll
       for (int i = 0; i < 8; ++i)
-        if (i == io) {
-          kr[i] = kp;
-          vr[i] = vp;
-        }
-      const uint32_t page = a.page_table[pos / kPageTokens];
-      if (page < pool_pages) {
-        *reinterpret_cast<uint4*>(const_cast<uint16_t*>(kv_row(a.kv, page, 0, kvh, pos % kPageTokens)) + lane) = kp;
-        *reinterpret_cast<uint4*>(const_cast<uint16_t*>(kv_row(a.kv, page, 1, kvh, pos % kPageTokens)) + lane) = vp;
+        if (i == io) kr[i] = kp;
+      const uint32_t pg = a.page_table[pos / kPageTokens];
+      if (pg < pool_pages) {
+        *reinterpret_cast<uint4*>(const_cast<uint16_t*>(kv_row(a.kv, pg, 0, kvh, pos % kPageTokens)) + lane) = kp;
+        *reinterpret_cast<uint4*>(const_cast<uint16_t*>(kv_row(a.kv, pg, 1, kvh, pos % kPageTokens)) + lane) = vp;
       }
     }
-    // Scores of the warp's 8 tokens x 4 heads: lane-local partial dot products, then one
-    // butterfly that leaves the total of (token lane / 4, head lane % 4) in each lane.
-    float v[32];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      float kf[8];
-      unpack8f(kr[i], kf);
-#pragma unroll
-      for (int hh = 0; hh < kQPerKv; ++hh) {
-        float d = 0.f;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) d = fmaf(q[hh][j], kf[j], d);
-        v[i * 4 + hh] = d;
-      }
-    }
-#pragma unroll
-    for (int o = 16, half = 16; o >= 1; o >>= 1, half >>= 1) {
-      const bool upper = (lane & o) != 0;
-#pragma unroll
-      for (int e = 0; e < half; ++e) {
-        const float send = upper ? v[e] : v[e + half];
-        const float keep = upper ? v[e + half] : v[e];
-        v[e] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-      }
-    }
+    // Scores, two query heads at a time: q of the pair (this lane's 8 dims: RMSNorm, RoPE, times
+    // 1/16), lane-local partial dot products of 4 tokens x 2 heads, then a butterfly over lanes
+    // (offsets 16, 8, 4 halve the values a lane holds; offsets 2, 1 complete the sums), which
+    // leaves the total of pair lane / 4 (token 4 half + lane / 8, head 2 pair + (lane / 4) % 2)
+    // in each group of 4 lanes.
     float* sc = sh.xs;  // [4 heads][64 tokens]
-    {
-      const int i = lane >> 2, hh = lane & 3, t = l0 + warp * 8 + i;
-      sc[hh * kTkSplit + warp * 8 + i] = t < l1 ? v[0] : -INFINITY;
+#pragma unroll 1
+    for (int hp = 0; hp < 2; ++hp) {
+      float q[2][8];
+#pragma unroll
+      for (int hl = 0; hl < 2; ++hl) {
+        const float* src = pr + (kvh * kQPerKv + 2 * hp + hl) * kHeadDim + lane * 8;
+        const float4 x0 = __ldcg(reinterpret_cast<const float4*>(src));
+        const float4 x1 = __ldcg(reinterpret_cast<const float4*>(src + 4));
+        q[hl][0] = x0.x; q[hl][1] = x0.y; q[hl][2] = x0.z; q[hl][3] = x0.w;
+        q[hl][4] = x1.x; q[hl][5] = x1.y; q[hl][6] = x1.z; q[hl][7] = x1.w;
+        tk_norm_rope(q[hl], a.norms, a.rope, pos, lane);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) q[hl][j] *= 0.0625f;
+      }
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float kf[8];
+          unpack8f(kr[hf * 4 + i], kf);
+#pragma unroll
+          for (int hl = 0; hl < 2; ++hl) {
+            float d = 0.f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) d = fmaf(q[hl][j], kf[j], d);
+            v[i * 2 + hl] = d;
+          }
+        }
+#pragma unroll
+        for (int o = 16, half = 4; o >= 4; o >>= 1, half >>= 1) {
+          const bool upper = (lane & o) != 0;
+#pragma unroll
+          for (int e = 0; e < half; ++e) {
+            const float send = upper ? v[e] : v[e + half];
+            const float keep = upper ? v[e + half] : v[e];
+            v[e] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+          }
+        }
+        v[0] += __shfl_xor_sync(0xffffffffu, v[0], 2);
+        v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
+        if ((lane & 3) == 0) {
+          const int e = lane >> 2, i = hf * 4 + (e >> 1), hh = 2 * hp + (e & 1), t = l0 + warp * 8 + i;
+          sc[hh * kTkSplit + warp * 8 + i] = t < l1 ? v[0] : -INFINITY;
+        }
+      }
+    }
+    load_v(a, pool_pages);
+    if (owner && warp == ((int)pos - l0) / 8) {
+      const int io = ((int)pos - l0) % 8;
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (i == io) vr[i] = vp;
     }
     ConsumerBar()();
     if (warp < kQPerKv) {
@@ -546,34 +590,33 @@ struct TkAttn {
       }
     }
     ConsumerBar()();
-    float acc[kQPerKv][8];
-#pragma unroll
-    for (int hh = 0; hh < kQPerKv; ++hh)
-#pragma unroll
-      for (int j = 0; j < 8; ++j) acc[hh][j] = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      float vf[8];
-      unpack8f(vr[i], vf);
-#pragma unroll
-      for (int hh = 0; hh < kQPerKv; ++hh) {
-        const float p = sc[hh * kTkSplit + warp * 8 + i];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[hh][j] = fmaf(p, vf[j], acc[hh][j]);
-      }
-    }
-    // Sum the 8 warps' accumulators, two heads at a time through shared memory, into the partial.
+    // Weighted sums of V, two heads at a time: per lane 2 heads x 8 dims over the warp's 8 tokens,
+    // then the 8 warps' sums through shared memory into this split's partial.
     float* buf = sh.xs + kQPerKv * kTkSplit;  // [8 warps][2 heads][256]
     float* dst = part + (size_t)(kvh * kTkMaxSplits + split) * kTkPartStride;
 #pragma unroll 1
     for (int hp = 0; hp < 2; ++hp) {
+      float acc[2][8];
+#pragma unroll
+      for (int hl = 0; hl < 2; ++hl)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[hl][j] = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float vf[8];
+        unpack8f(vr[i], vf);
+#pragma unroll
+        for (int hl = 0; hl < 2; ++hl) {
+          const float p = sc[(2 * hp + hl) * kTkSplit + warp * 8 + i];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[hl][j] = fmaf(p, vf[j], acc[hl][j]);
+        }
+      }
 #pragma unroll
       for (int hl = 0; hl < 2; ++hl) {
         float* b = buf + ((size_t)warp * 2 + hl) * kHeadDim + lane * 8;
-        *reinterpret_cast<float4*>(b) = make_float4(acc[2 * hp + hl][0], acc[2 * hp + hl][1], acc[2 * hp + hl][2],
-                                                    acc[2 * hp + hl][3]);
-        *reinterpret_cast<float4*>(b + 4) = make_float4(acc[2 * hp + hl][4], acc[2 * hp + hl][5],
-                                                        acc[2 * hp + hl][6], acc[2 * hp + hl][7]);
+        *reinterpret_cast<float4*>(b) = make_float4(acc[hl][0], acc[hl][1], acc[hl][2], acc[hl][3]);
+        *reinterpret_cast<float4*>(b + 4) = make_float4(acc[hl][4], acc[hl][5], acc[hl][6], acc[hl][7]);
       }
       ConsumerBar()();
       {
@@ -619,7 +662,7 @@ __device__ __forceinline__ void tk_merge(const AttnArgs& a, const float* part) {
   a.out[h * kHeadDim + d] = o / L / (1.0f + expf(-gate));
 }
 
-__device__ __noinline__ void tk_consume(const TkArgs& A, TkShared& sh) {
+__device__ __forceinline__ void tk_consume(const TkArgs& A, TkShared& sh) {
   TkBarrier bar{A.barrier, 0ull, A.wait_limit_ns, A.wait_extra};
   uint32_t g = 0;
   pdl_wait();  // the previous token's control words and states are complete
