@@ -52,7 +52,6 @@ def test_bench_prompt_and_decode_match_the_oracle(cuda, cfg, steps):
     info = synth.baseline_config(cfg)
     s = synth.build_config(cfg)
     m = qne.Model(s.index_json, s.weights)  # the reference architecture loads without opt-in
-    assert not m.fused  # the default per-operation path, which bench.py times
     om = oracle.OracleModel(s.index_json, s.weights, kv_f16=True)
     n = info["prompt"]
     prompt = synth.prompt_ids(n, 1 if cfg == 2 else cfg)  # bench.py's prompt for config 2
@@ -63,20 +62,27 @@ def test_bench_prompt_and_decode_match_the_oracle(cuda, cfg, steps):
     print(f"config {cfg}: logits after the prompt max-abs {err:.3g} rel {rel:.3g}, top-5 overlap {top5}/5")
     m.snapshot()
     om.snapshot()
-    ids = m.decode(steps, 1)
     want_ids, margins = om.greedy(want, n, steps)
-    same = streams_agree(ids, want_ids, margins, f"config {cfg} greedy")
-    print(f"config {cfg}: {same}/{steps} greedy tokens identical")
-    assert same >= steps // 2
-    # per-token logits on the same path at the longest contexts
-    m.restore()
-    om.restore()
-    tok = oracle.argmax(want)
-    for i in range(4):
-        g = m.step(tok, n + i)
-        w = om.step(tok, n + i)
-        logits_close(g, w, f"config {cfg} step at position {n + i}")
-        tok = oracle.argmax(w)
+    # every launch path the model offers (the token kernel needs f16 weights), the default first
+    paths = [m.path] + [p for p in ("operations", "token") if p != m.path and (p != "token" or cfg == 2)]
+    for path in paths:
+        m.set_path(path)
+        m.restore()
+        ids = m.decode(steps, 1)
+        same = streams_agree(ids, want_ids, margins, f"config {cfg} greedy ({path})")
+        print(f"config {cfg} ({path}): {same}/{steps} greedy tokens identical")
+        assert same >= steps // 2
+    # per-token logits on each path at the longest contexts
+    for path in paths:
+        m.set_path(path)
+        m.restore()
+        om.restore()
+        tok = oracle.argmax(want)
+        for i in range(4):
+            g = m.step(tok, n + i)
+            w = om.step(tok, n + i)
+            logits_close(g, w, f"config {cfg} step at position {n + i} ({path})")
+            tok = oracle.argmax(w)
     m.close()
     om.close()
 

@@ -38,16 +38,21 @@ def greedy_compare(model, om, prompt, steps):
     return steps
 
 
-def set_path(m, fused):
-    """fused=True selects the fused layer kernels (f16 weights on a B200; an error if they are not
-    available); False the per-operation kernels (the default)."""
-    m.set_fused(fused)
-    assert m.fused == fused
-    assert m.dispatches_per_token() == (m.layers if fused else 5 * m.layers + 1)
+DISPATCHES = {"operations": lambda layers: 5 * layers + 1, "layers": lambda layers: layers, "token": lambda layers: 1}
 
 
-@pytest.fixture(scope="module", params=[("f16", True), ("f16", False), ("q4g64", False), ("q4", False)],
-                ids=["f16-fused", "f16-split", "q4g64", "q4"])
+def set_path(m, path):
+    """Launch path: "operations" (one kernel per operation, the default), "layers" (one fused launch
+    per layer) or "token" (one launch per token); an error if it is not available (f16 weights on a
+    B200 for the last two)."""
+    m.set_path(path)
+    assert m.path == path and m.fused == (path == "layers")
+    assert m.dispatches_per_token() == DISPATCHES[path](m.layers)
+
+
+@pytest.fixture(scope="module", params=[("f16", "layers"), ("f16", "operations"), ("f16", "token"),
+                                        ("q4g64", "operations"), ("q4", "operations")],
+                ids=["f16-fused", "f16-split", "f16-token", "q4g64", "q4"])
 def tiny(request, cuda):
     kind, fused = request.param
     s = synth.build(1024, 3584, layers=4, vocab=8192, kind=kind, seed=11)
@@ -163,30 +168,35 @@ def test_restore_without_snapshot(cuda):
     assert not m.fused and m.dispatches_per_token() == 4 * 5 + 1  # per-operation path by default
     m.set_fused(True)
     assert m.dispatches_per_token() == 4  # one fused launch per layer
+    m.set_path("token")
+    assert m.dispatches_per_token() == 1 and not m.fused  # one launch per token
     assert "B200" in m.adapter or "sm_10" in m.adapter
     m.close()
 
 
-def test_fused_and_split_paths_agree(cuda):
-    """The two launch paths on one model: logits within the parity tolerance, identical picks,
-    and switching paths mid-sequence keeps the state (both read and write the same buffers)."""
+def test_launch_paths_agree(cuda):
+    """The three launch paths on one model: logits within the parity tolerance, identical picks,
+    and switching paths mid-sequence keeps the state (all read and write the same buffers)."""
     s = synth.build(1024, 3584, layers=8, vocab=8192, seed=13)
     m = qne.Model(s.index_json, s.weights, any_shape=True)
     prompt = synth.prompt_ids(70, 6, 8192)
     out = {}
-    for fused in (True, False):
-        m.set_fused(fused)
+    for path in ("layers", "operations", "token"):
+        set_path(m, path)
         m.reset()
         m.prefill(prompt)
-        out[fused] = (m.logits().copy(), m.decode(12, 1))
-    logits_close(out[True][0], out[False][0].astype(np.float64))
-    assert out[True][1] == out[False][1]
+        out[path] = (m.logits().copy(), m.decode(12, 1))
+    for path in ("layers", "token"):
+        logits_close(out[path][0], out["operations"][0].astype(np.float64))
+        assert out[path][1] == out["operations"][1]
     m.set_fused(True)
     m.reset()
     m.prefill(prompt[:40])
+    m.set_path("token")
+    m.prefill(prompt[40:55])
     m.set_fused(False)
-    m.prefill_chunk(prompt[40:], 40, True)
-    logits_close(m.logits(), out[False][0].astype(np.float64))
+    m.prefill_chunk(prompt[55:], 55, True)
+    logits_close(m.logits(), out["operations"][0].astype(np.float64))
     m.close()
 
 
@@ -197,18 +207,19 @@ def test_fused_kernels_at_a_long_context(cuda):
     m = qne.Model(s.index_json, s.weights, any_shape=True)
     prompt = synth.prompt_ids(600, 7, 4096)
     res = []
-    for fused in (True, False):
-        m.set_fused(fused)
+    for path in ("layers", "token", "operations"):
+        set_path(m, path)
         m.reset()
         m.prefill(prompt)
         res.append((m.logits().copy(), m.decode(6, 1)))
-    logits_close(res[0][0], res[1][0].astype(np.float64))
-    assert res[0][1] == res[1][1]
+    for r in res[:2]:
+        logits_close(r[0], res[2][0].astype(np.float64))
+        assert r[1] == res[2][1]
     m.close()
 
 
 @pytest.mark.slow
-@pytest.mark.parametrize("fused", [True, False], ids=["fused", "split"])
+@pytest.mark.parametrize("fused", ["layers", "operations", "token"], ids=["fused", "split", "token"])
 def test_config1_full_08b_parity(cuda, fused):
     """benchmark config 1: 0.8B-shaped f16 model (seed 0), 128 prompt ids (seed 0), greedy steps."""
     s = synth.build_config(1)
@@ -223,8 +234,8 @@ def test_config1_full_08b_parity(cuda, fused):
 
 
 @pytest.mark.slow
-@pytest.mark.parametrize("cfg,fused", [(2, False), (2, True), (3, False)], ids=["config2-split", "config2-fused",
-                                                                            "config3"])
+@pytest.mark.parametrize("cfg,fused", [(2, "operations"), (2, "layers"), (2, "token"), (3, "operations")],
+                         ids=["config2-split", "config2-fused", "config2-token", "config3"])
 def test_config_2b_short_context_parity(cuda, cfg, fused):
     """benchmark configs 2 (f16, both launch paths) and 3 (int4 g64) from a short prompt, one token
     per step (qne_prefill); the benchmark contexts themselves are in test_gpu_bench_configs.py."""
@@ -262,15 +273,17 @@ def test_sync_deadline_reports_a_timeout(cuda):
     m.close()
 
 
-def test_fused_barrier_wait_runs_out_and_reports_a_timeout(cuda):
-    """The fused layer kernels' grid barriers are bounded waits. With the test hook every barrier
-    also waits for an arrival that never comes, under a 1 ms limit: the kernels set the timeout flag
-    and return (no hang, the context stays usable), qne_last_token reports QNE_ETIMEOUT and clears
-    the flag, and with the hook off the same prompt gives the same bits as before."""
+@pytest.mark.parametrize("path", ["layers", "token"])
+def test_barrier_wait_runs_out_and_reports_a_timeout(cuda, path):
+    """The grid barriers of the fused layer kernels and of the token kernel are bounded waits. With
+    the test hook every barrier also waits for an arrival that never comes, under a 1 ms limit: the
+    kernels set the timeout flag and return (no hang, the context stays usable), qne_last_token
+    reports QNE_ETIMEOUT and clears the flag, and with the hook off the same prompt gives the same
+    bits as before."""
     import time
     s = synth.build(1024, 3584, layers=4, vocab=4096, seed=15)
     m = qne.Model(s.index_json, s.weights, any_shape=True)
-    m.set_fused(True)
+    set_path(m, path)
     prompt = synth.prompt_ids(9, 2, 4096)
     m.prefill(prompt)
     want, want_ids = m.logits().copy(), m.decode(4, 1)
