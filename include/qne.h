@@ -131,10 +131,11 @@ QNE_API qne_status qne_model_set_fused(qne_model* m, int enable);
 QNE_API int qne_model_fused(const qne_model* m);
 /* Launch path of a token (no counterpart in the reference, whose dispatch list is fixed):
  * QNE_PATH_OPERATIONS = one kernel per operation (qne_model_set_fused(m, 0)), QNE_PATH_LAYERS =
- * one fused launch per layer (qne_model_set_fused(m, 1)), QNE_PATH_TOKEN = one launch per token:
- * a kernel with one CTA per SM whose producer warp streams every weight of the token through a
- * shared-memory ring with bulk copies while the consumer warps run the layers' phases behind
- * grid barriers. All three compute the same results within the logit tolerance. QNE_PATH_TOKEN
+ * one fused launch per layer (qne_model_set_fused(m, 1)), QNE_PATH_TOKEN = the token kernel: one
+ * launch per stretch of layers between attention mixers (a kernel with one CTA per SM whose
+ * producer warp streams every weight of the stretch through a shared-memory ring with bulk copies
+ * while the consumer warps run the layers' phases behind grid barriers), the attention mixers as
+ * their own kernel in between (13 launches per token for 24 layers). All three compute the same results within the logit tolerance. QNE_PATH_TOKEN
  * needs one sequence and f16 matrices with k % 256 == 0 and k <= 6144; QNE_EINVAL when a path is
  * not available. qne_model_path returns the current one. */
 #define QNE_PATH_OPERATIONS 0

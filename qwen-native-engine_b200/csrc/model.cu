@@ -567,9 +567,11 @@ bool Runner::token_supported() {
 }
 
 // The token's phases in launch order (kernels/src/model.rs:220-269), with the same buffers and
-// prologues / epilogues as the per-operation graph.
-std::vector<TkPhase> Runner::token_phase_list(Variant v) const {
+// prologues / epilogues as the per-operation graph, cut into launches at the attention mixers.
+std::vector<TkPhase> Runner::token_phase_list(Variant v, std::vector<TokenSeg>& segs) const {
   std::vector<TkPhase> ph;
+  segs.clear();
+  segs.push_back(TokenSeg{});
   auto gemv = [&](const GemvArgs& a) {
     TkPhase p;
     p.kind = kTkGemv;
@@ -587,15 +589,14 @@ std::vector<TkPhase> Runner::token_phase_list(Variant v) const {
   for (int i = 0; i < m->cfg.layers; ++i) {
     const LayerArgs r = layer_args(i);
     gemv(r.in);
-    TkPhase mix;
     if (r.attention) {
-      mix.kind = kTkAttn;
-      mix.at = r.at;
-      mix.pool_pages = st.pool_pages;
-      ph.push_back(mix);
-      mix.kind = kTkMerge;
-      ph.push_back(mix);
+      segs.back().count = (int)ph.size() - segs.back().first;
+      segs.back().attn_layer = i;
+      TokenSeg next;
+      next.first = (int)ph.size();
+      segs.push_back(next);
     } else {
+      TkPhase mix;
       mix.kind = kTkGdn;
       mix.gdn = r.gdn;
       ph.push_back(mix);
@@ -605,13 +606,14 @@ std::vector<TkPhase> Runner::token_phase_list(Variant v) const {
     gemv(r.down);
   }
   if (v != kLayers) gemv(head_args(v));
+  segs.back().count = (int)ph.size() - segs.back().first;
   return ph;
 }
 
-TkArgs Runner::token_args(Variant v) const {
+TkArgs Runner::token_args(Variant v, const TokenSeg& seg) const {
   TkArgs a;
-  a.phases = token_phases[v];
-  a.nphases = token_nphases[v];
+  a.phases = token_phases[v] + seg.first;
+  a.nphases = seg.count;
   a.ctl = st.ctl;
   a.embed = m->embed;
   a.h_out = h;
@@ -621,19 +623,17 @@ TkArgs Runner::token_args(Variant v) const {
   a.err = &st.ctl->flags;
   a.wait_limit_ns = wait_test_ns ? wait_test_ns : kBarrierLimitNs;
   a.wait_extra = wait_test_ns ? 1u : 0u;
-  a.attn_part = attn_part;
   return a;
 }
 
-// Uploads the phase lists once and captures one single-launch graph per variant.
+// Uploads the phase lists once and captures one graph per variant: the token-kernel launches and,
+// between them, the attention kernels, chained by programmatic dependent launch.
 void Runner::capture_token() {
-  if (!attn_part) attn_part = static_cast<float*>(m->alloc(token_attn_part_floats() * sizeof(float)));
   for (int v = 0; v < kVariants; ++v) {
-    const std::vector<TkPhase> list = token_phase_list((Variant)v);
+    const std::vector<TkPhase> list = token_phase_list((Variant)v, token_segs[v]);
     if (!token_phases[v]) token_phases[v] = static_cast<TkPhase*>(m->alloc(list.size() * sizeof(TkPhase)));
     cuda_check(cudaMemcpy(token_phases[v], list.data(), list.size() * sizeof(TkPhase), cudaMemcpyHostToDevice),
                "token phases");
-    token_nphases[v] = (int)list.size();
   }
   cudaStream_t cs;
   cuda_check(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking), "cudaStreamCreate");
@@ -643,7 +643,19 @@ void Runner::capture_token() {
       tgraph[v] = nullptr;
     }
     cuda_check(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal), "begin capture");
-    const cudaError_t le = launch_token(token_args((Variant)v), token_ctas, cs, true);
+    cudaError_t le = cudaSuccess;
+    size_t launches = 0;
+    for (const TokenSeg& seg : token_segs[v]) {
+      if (le == cudaSuccess && seg.count > 0) {
+        le = launch_token(token_args((Variant)v, seg), token_ctas, cs, true);
+        ++launches;
+      }
+      if (le == cudaSuccess && seg.attn_layer >= 0) {
+        le = launch_attention(layer_args(seg.attn_layer).at, st.pool_pages, 64, cs, true);
+        ++launches;
+      }
+    }
+    token_launches[v] = launches;
     cudaGraph_t g = nullptr;
     const cudaError_t ce = cudaStreamEndCapture(cs, &g);
     cudaError_t ie = cudaSuccess;
@@ -733,12 +745,12 @@ bool Runner::set_wait_test(uint64_t limit_ns) {
 }
 
 size_t Runner::per_token() const {
-  return path == kPathToken ? 1 : use_fused ? fused_launches_per_token : launches_per_token;
+  return path == kPathToken ? token_launches[kGreedy] : use_fused ? fused_launches_per_token : launches_per_token;
 }
 
 void Runner::launch(Variant v, cudaStream_t s) {
   cuda_check(cudaGraphLaunch(path == kPathToken ? tgraph[v] : use_fused ? fgraph[v] : graph[v], s), "graph launch");
-  const size_t n = path == kPathToken ? 1
+  const size_t n = path == kPathToken ? token_launches[v]
                    : use_fused        ? fused_launches_per_token
                                       : (v == kLayers ? launches_per_token - 1 : launches_per_token);
   for (size_t i = 0; i < n; ++i) count_launch();

@@ -189,11 +189,16 @@ class Runner {
   int fused_ctas = 0, fused_max_k = 0;
   int token_ctas = 0;                            // 0: the token kernel cannot run this model
   TkPhase* token_phases[kVariants] = {nullptr, nullptr, nullptr};  // device phase lists
-  int token_nphases[kVariants] = {0, 0, 0};
-  float* attn_part = nullptr;                    // token kernel attention partials
+  size_t token_launches[kVariants] = {0, 0, 0};  // launches of one token, per variant
+  // One token-kernel launch: phases [first, first + count) of the variant's list, followed by the
+  // attention mixer of layer attn_layer (-1: none, the last launch of a token).
+  struct TokenSeg {
+    int first = 0, count = 0, attn_layer = -1;
+  };
+  std::vector<TokenSeg> token_segs[kVariants];
   bool token_supported();
-  std::vector<TkPhase> token_phase_list(Variant v) const;
-  TkArgs token_args(Variant v) const;
+  std::vector<TkPhase> token_phase_list(Variant v, std::vector<TokenSeg>& segs) const;
+  TkArgs token_args(Variant v, const TokenSeg& seg) const;
   void capture_token();
   bool set_path(int p);
 

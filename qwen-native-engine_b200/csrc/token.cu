@@ -1,18 +1,19 @@
-// The token kernel: one launch per B = 1 decode token (the per-token dispatch list of
-// kernels/src/model.rs:220-269 - per layer in-projection, GDN or attention, out-projection,
-// gate_up, down; then final norm + LM head + greedy pick - run as phases of one grid).
+// The token kernel: the per-token dispatch list of kernels/src/model.rs:220-269 (per layer
+// in-projection, GDN, out-projection, gate_up, down; then final norm + LM head + greedy pick) run
+// as phases of one grid, between the attention layers.
 //
 // Why: a decode token is a chain of ~120 dependent steps, and as separate kernels each step pays
 // a launch boundary and its own ramp and tail, during which HBM idles (the per-operation graph
 // measured 1.1 ms per 2B token against 0.58 ms of weight streaming). Here the weight streaming
-// never waits for a dependency:
+// does not wait for the dependencies:
 //   * one CTA per SM (148), 8 consumer warps + 1 producer warp;
-//   * the producer warp walks the token's GEMV phases in order and bulk-copies (TMA,
+//   * the producer warp walks the launch's GEMV phases in order and bulk-copies (TMA,
 //     cp.async.bulk, no multicast) this CTA's rows of every matrix into a ring of 8 x 24 KB
 //     shared-memory slots, guarded by full/empty mbarriers. Weights depend on nothing, so the
 //     producer runs ahead across phase boundaries until the ring is full: while the consumers
 //     wait at a grid barrier for the previous phase's output, the next phase's first 192 KB per
-//     SM (28 MB over the GPU) are already streaming;
+//     SM (28 MB over the GPU) are already streaming. It starts before the launch's dependency
+//     wait, so a launch's first weights stream while the kernel before it finishes;
 //   * consumer warp w owns ring slot w and takes every 8th slot of the CTA's sequence. A slot
 //     holds whole rows (2, 3, 6 or 12 by row length; SwiGLU: gate rows then the matching up
 //     rows); the warp dots them with x (staged once per phase in shared memory with its prologue:
@@ -21,14 +22,11 @@
 //   * phases that read what the previous phase wrote start behind a grid barrier (an arrival
 //     counter; release reduction to arrive, acquire polls, bounded in time with an error flag);
 //   * GDN: one dev::GdnItem (16 value columns of one head) per CTA for CTAs 0..127, its state
-//     slice loaded before the barrier;
-//   * attention: one 64-token split of one KV head per CTA, its K and V rows (f16, through the
-//     page table) loaded into registers before the barrier; q / k RMSNorm + RoPE per warp with
-//     shuffles; scores reduced with one butterfly per warp; per-split (max, sum, 4 x 256 sums)
-//     partials; a merge phase (8 CTAs, one per query head) combines the splits and applies the
-//     output gate. The split holding the current position appends its K/V (rounded to f16).
-// Results match the per-operation kernels within the logit tolerance (f32 accumulation, other
-// summation order).
+//     slice loaded before the barrier.
+// A token is one launch per stretch of layers between attention mixers; each attention layer's
+// mixer is the paged attention kernel (attention.cu) between two such launches, chained by
+// programmatic dependent launch. Results match the per-operation kernels within the logit
+// tolerance (f32 accumulation, other summation order).
 #include <math.h>
 
 #include "gemv_dev.cuh"
@@ -46,9 +44,6 @@ constexpr int kTkThreads = kTkConsumers + 32;  // + the producer warp
 constexpr int kTkSlots = kTkConsumerWarps;     // one ring slot per consumer warp
 constexpr uint32_t kTkSlotBytes = 24u << 10;
 constexpr int kTkMaxK = 6144;
-constexpr int kTkSplit = 64;                                       // attention tokens per item
-constexpr int kTkMaxSplits = kMaxContext / kTkSplit;               // 64
-constexpr int kTkPartStride = kQPerKv * kHeadDim + 2 * kQPerKv;    // acc[4][256], m[4], l[4]
 
 struct TkShared {
   uint8_t ring[kTkSlots][kTkSlotBytes];
@@ -58,7 +53,6 @@ struct TkShared {
   float red[kTkConsumerWarps];
   float bval[kTkConsumerWarps];
   uint32_t bidx[kTkConsumerWarps];
-  float mx[kQPerKv], sm[kQPerKv];
   uint32_t flag;
 };
 static_assert(sizeof(GdnShared) <= sizeof(float) * kTkMaxK, "GDN scratch aliases xs");
@@ -402,266 +396,6 @@ __device__ __forceinline__ void tk_gemv(const TkPhase& ph, const TkArgs& A, TkSh
   }
 }
 
-__device__ __forceinline__ void unpack8f(const uint4& w, float* f) {
-  const float2 a = h2f2(w.x), b = h2f2(w.y), c = h2f2(w.z), d = h2f2(w.w);
-  f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y;
-  f[4] = c.x; f[5] = c.y; f[6] = d.x; f[7] = d.y;
-}
-__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
-  return (uint32_t)__half_as_ushort(__float2half_rn(a)) | ((uint32_t)__half_as_ushort(__float2half_rn(b)) << 16);
-}
-
-// RMSNorm (eps 1e-6) of a 256-vector held as 8 dims per lane (dims 8 lane ..), times w, then
-// rotate-half RoPE on dims 0..63 (pairs (i, i + 32): lanes 0-3 pair with lanes 4-7).
-__device__ __forceinline__ void tk_norm_rope(float (&v)[8], const float* w, const float* rope, uint32_t pos,
-                                             int lane) {
-  float ss = 0.f;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) ss = fmaf(v[j], v[j], ss);
-  const float inv = rsqrtf(warp_sum(ss) / (float)kHeadDim + 1e-6f);
-#pragma unroll
-  for (int j = 0; j < 8; ++j) v[j] = v[j] * inv * w[lane * 8 + j];
-  float other[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) other[j] = __shfl_xor_sync(0xffffffffu, v[j], 4);
-  if (lane < 8) {
-    const int i0 = (lane & 3) * 8;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float c = rope[(size_t)pos * kRopeHalf + i0 + j];
-      const float s = rope[(size_t)kMaxContext * kRopeHalf + (size_t)pos * kRopeHalf + i0 + j];
-      v[j] = lane < 4 ? v[j] * c - other[j] * s : v[j] * c + other[j] * s;
-    }
-  }
-}
-
-// One attention work item: (64-token split, KV head) of the single sequence.
-struct TkAttn {
-  int split, kvh, l0, l1;
-  uint32_t pos;
-  bool valid, owner;
-  uint4 kr[8], vr[8];  // this lane's 8 dims of the warp's 8 tokens' K and V rows
-
-  __device__ __forceinline__ void prefetch(const AttnArgs& a, uint32_t pool_pages, int item) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    pos = a.pos[0];
-    if (pos >= (uint32_t)kMaxContext) {
-      if (a.flags && threadIdx.x == 0 && item == 0) atomicOr(a.flags, kFlagPosClamped);
-      pos = kMaxContext - 1;
-    }
-    const int len = (int)pos + 1;
-    const int nsplit = (len + kTkSplit - 1) / kTkSplit;
-    split = item >> 1;
-    kvh = item & 1;
-    valid = split < nsplit;
-    if (!valid) return;
-    l0 = split * kTkSplit;
-    l1 = min(l0 + kTkSplit, len);
-    owner = (int)pos >= l0 && (int)pos < l1;
-    // K rows before the barrier; V rows (needed only for the weighted sum) once the scores are
-    // done, so that K and V are never both live in registers.
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int t = l0 + warp * 8 + i;
-      kr[i] = make_uint4(0u, 0u, 0u, 0u);
-      if (t < l1 && t != (int)pos) {
-        const uint32_t page = a.page_table[t / kPageTokens];
-        if (page < pool_pages) kr[i] = ld_stream(kv_row(a.kv, page, 0, kvh, t % kPageTokens) + lane * 8);
-      }
-    }
-  }
-
-  // V rows of the warp's tokens (the current token's, when this split appends it, is written by
-  // run() after this).
-  __device__ __forceinline__ void load_v(const AttnArgs& a, uint32_t pool_pages) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int t = l0 + warp * 8 + i;
-      vr[i] = make_uint4(0u, 0u, 0u, 0u);
-      if (t < l1 && t != (int)pos) {
-        const uint32_t page = a.page_table[t / kPageTokens];
-        if (page < pool_pages) vr[i] = ld_stream(kv_row(a.kv, page, 1, kvh, t % kPageTokens) + lane * 8);
-      }
-    }
-  }
-
-  __device__ __forceinline__ void run(const AttnArgs& a, uint32_t pool_pages, TkShared& sh, float* part) {
-    if (!valid) return;  // uniform over the CTA
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const float* pr = a.proj;
-    // The split holding pos appends the current key (normalized, rotated) and value, rounded
-    // to f16, and uses the rounded values.
-    uint4 vp = make_uint4(0u, 0u, 0u, 0u);  // the appended value (owner warp)
-    if (owner && warp == ((int)pos - l0) / 8) {
-      const int io = ((int)pos - l0) % 8;
-      float kc[8], vc[8];
-      const float* ks = pr + 4096 + kvh * kHeadDim + lane * 8;
-      const float* vs = pr + 4608 + kvh * kHeadDim + lane * 8;
-      const float4 k0 = __ldcg(reinterpret_cast<const float4*>(ks)), k1 = __ldcg(reinterpret_cast<const float4*>(ks + 4));
-      const float4 v0 = __ldcg(reinterpret_cast<const float4*>(vs)), v1 = __ldcg(reinterpret_cast<const float4*>(vs + 4));
-      kc[0] = k0.x; kc[1] = k0.y; kc[2] = k0.z; kc[3] = k0.w; kc[4] = k1.x; kc[5] = k1.y; kc[6] = k1.z; kc[7] = k1.w;
-      vc[0] = v0.x; vc[1] = v0.y; vc[2] = v0.z; vc[3] = v0.w; vc[4] = v1.x; vc[5] = v1.y; vc[6] = v1.z; vc[7] = v1.w;
-      tk_norm_rope(kc, a.norms + kHeadDim, a.rope, pos, lane);
-      const uint4 kp = make_uint4(pack_half2(kc[0], kc[1]), pack_half2(kc[2], kc[3]), pack_half2(kc[4], kc[5]),
-                                  pack_half2(kc[6], kc[7]));
-      vp = make_uint4(pack_half2(vc[0], vc[1]), pack_half2(vc[2], vc[3]), pack_half2(vc[4], vc[5]),
-                      pack_half2(vc[6], vc[7]));
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-        if (i == io) kr[i] = kp;
-      const uint32_t pg = a.page_table[pos / kPageTokens];
-      if (pg < pool_pages) {
-        *reinterpret_cast<uint4*>(const_cast<uint16_t*>(kv_row(a.kv, pg, 0, kvh, pos % kPageTokens)) + lane) = kp;
-        *reinterpret_cast<uint4*>(const_cast<uint16_t*>(kv_row(a.kv, pg, 1, kvh, pos % kPageTokens)) + lane) = vp;
-      }
-    }
-    // Scores, two query heads at a time: q of the pair (this lane's 8 dims: RMSNorm, RoPE, times
-    // 1/16), lane-local partial dot products of 4 tokens x 2 heads, then a butterfly over lanes
-    // (offsets 16, 8, 4 halve the values a lane holds; offsets 2, 1 complete the sums), which
-    // leaves the total of pair lane / 4 (token 4 half + lane / 8, head 2 pair + (lane / 4) % 2)
-    // in each group of 4 lanes.
-    float* sc = sh.xs;  // [4 heads][64 tokens]
-#pragma unroll 1
-    for (int hp = 0; hp < 2; ++hp) {
-      float q[2][8];
-#pragma unroll
-      for (int hl = 0; hl < 2; ++hl) {
-        const float* src = pr + (kvh * kQPerKv + 2 * hp + hl) * kHeadDim + lane * 8;
-        const float4 x0 = __ldcg(reinterpret_cast<const float4*>(src));
-        const float4 x1 = __ldcg(reinterpret_cast<const float4*>(src + 4));
-        q[hl][0] = x0.x; q[hl][1] = x0.y; q[hl][2] = x0.z; q[hl][3] = x0.w;
-        q[hl][4] = x1.x; q[hl][5] = x1.y; q[hl][6] = x1.z; q[hl][7] = x1.w;
-        tk_norm_rope(q[hl], a.norms, a.rope, pos, lane);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) q[hl][j] *= 0.0625f;
-      }
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        float v[8];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          float kf[8];
-          unpack8f(kr[hf * 4 + i], kf);
-#pragma unroll
-          for (int hl = 0; hl < 2; ++hl) {
-            float d = 0.f;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) d = fmaf(q[hl][j], kf[j], d);
-            v[i * 2 + hl] = d;
-          }
-        }
-#pragma unroll
-        for (int o = 16, half = 4; o >= 4; o >>= 1, half >>= 1) {
-          const bool upper = (lane & o) != 0;
-#pragma unroll
-          for (int e = 0; e < half; ++e) {
-            const float send = upper ? v[e] : v[e + half];
-            const float keep = upper ? v[e + half] : v[e];
-            v[e] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-          }
-        }
-        v[0] += __shfl_xor_sync(0xffffffffu, v[0], 2);
-        v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
-        if ((lane & 3) == 0) {
-          const int e = lane >> 2, i = hf * 4 + (e >> 1), hh = 2 * hp + (e & 1), t = l0 + warp * 8 + i;
-          sc[hh * kTkSplit + warp * 8 + i] = t < l1 ? v[0] : -INFINITY;
-        }
-      }
-    }
-    load_v(a, pool_pages);
-    if (owner && warp == ((int)pos - l0) / 8) {
-      const int io = ((int)pos - l0) % 8;
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-        if (i == io) vr[i] = vp;
-    }
-    ConsumerBar()();
-    if (warp < kQPerKv) {
-      const float s0 = sc[warp * kTkSplit + lane], s1 = sc[warp * kTkSplit + lane + 32];
-      const float m = warp_max(fmaxf(s0, s1));
-      const float p0 = s0 == -INFINITY ? 0.f : expf(s0 - m), p1 = s1 == -INFINITY ? 0.f : expf(s1 - m);
-      const float l = warp_sum(p0 + p1);
-      sc[warp * kTkSplit + lane] = p0;
-      sc[warp * kTkSplit + lane + 32] = p1;
-      if (lane == 0) {
-        sh.mx[warp] = m;
-        sh.sm[warp] = l;
-      }
-    }
-    ConsumerBar()();
-    // Weighted sums of V, two heads at a time: per lane 2 heads x 8 dims over the warp's 8 tokens,
-    // then the 8 warps' sums through shared memory into this split's partial.
-    float* buf = sh.xs + kQPerKv * kTkSplit;  // [8 warps][2 heads][256]
-    float* dst = part + (size_t)(kvh * kTkMaxSplits + split) * kTkPartStride;
-#pragma unroll 1
-    for (int hp = 0; hp < 2; ++hp) {
-      float acc[2][8];
-#pragma unroll
-      for (int hl = 0; hl < 2; ++hl)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[hl][j] = 0.f;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        float vf[8];
-        unpack8f(vr[i], vf);
-#pragma unroll
-        for (int hl = 0; hl < 2; ++hl) {
-          const float p = sc[(2 * hp + hl) * kTkSplit + warp * 8 + i];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) acc[hl][j] = fmaf(p, vf[j], acc[hl][j]);
-        }
-      }
-#pragma unroll
-      for (int hl = 0; hl < 2; ++hl) {
-        float* b = buf + ((size_t)warp * 2 + hl) * kHeadDim + lane * 8;
-        *reinterpret_cast<float4*>(b) = make_float4(acc[hl][0], acc[hl][1], acc[hl][2], acc[hl][3]);
-        *reinterpret_cast<float4*>(b + 4) = make_float4(acc[hl][4], acc[hl][5], acc[hl][6], acc[hl][7]);
-      }
-      ConsumerBar()();
-      {
-        const int hl = tid >> 7, d = (tid & 127) * 2;
-        float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-        for (int w = 0; w < kTkConsumerWarps; ++w) {
-          s0 += buf[((size_t)w * 2 + hl) * kHeadDim + d];
-          s1 += buf[((size_t)w * 2 + hl) * kHeadDim + d + 1];
-        }
-        *reinterpret_cast<float2*>(dst + (2 * hp + hl) * kHeadDim + d) = make_float2(s0, s1);
-      }
-      ConsumerBar()();
-    }
-    if (tid < kQPerKv) {
-      dst[kQPerKv * kHeadDim + tid] = sh.mx[tid];
-      dst[kQPerKv * kHeadDim + kQPerKv + tid] = sh.sm[tid];
-    }
-  }
-};
-
-// Merge of the attention splits for query head h = CTA (0..7), thread = dim: softmax-weighted
-// sum of the splits' partials, divided by the total weight, times sigmoid(gate).
-__device__ __forceinline__ void tk_merge(const AttnArgs& a, const float* part) {
-  const int h = blockIdx.x, d = threadIdx.x;
-  uint32_t pos = a.pos[0];
-  if (pos >= (uint32_t)kMaxContext) pos = kMaxContext - 1;
-  const int nsplit = ((int)pos + kTkSplit) / kTkSplit;
-  const int kvh = h / kQPerKv, hh = h % kQPerKv;
-  const float* base = part + (size_t)kvh * kTkMaxSplits * kTkPartStride;
-  float M = -INFINITY;
-#pragma unroll 1
-  for (int s = 0; s < nsplit; ++s) M = fmaxf(M, __ldcg(base + (size_t)s * kTkPartStride + kQPerKv * kHeadDim + hh));
-  float L = 0.f, o = 0.f;
-#pragma unroll 4
-  for (int s = 0; s < nsplit; ++s) {
-    const float* ps = base + (size_t)s * kTkPartStride;
-    const float w = expf(__ldcg(ps + kQPerKv * kHeadDim + hh) - M);
-    L = fmaf(w, __ldcg(ps + kQPerKv * kHeadDim + kQPerKv + hh), L);
-    o = fmaf(w, __ldcg(ps + hh * kHeadDim + d), o);
-  }
-  const float gate = __ldcg(a.proj + 2048 + h * kHeadDim + d);
-  a.out[h * kHeadDim + d] = o / L / (1.0f + expf(-gate));
-}
-
 __device__ __forceinline__ void tk_consume(const TkArgs& A, TkShared& sh) {
   TkBarrier bar{A.barrier, 0ull, A.wait_limit_ns, A.wait_extra};
   uint32_t g = 0;
@@ -679,16 +413,6 @@ __device__ __forceinline__ void tk_consume(const TkArgs& A, TkShared& sh) {
       if (mine) it.prefetch(ph.gdn, blockIdx.x);  // the state slice, before the barrier
       bar.wait(A.err);
       if (mine) it.run_with(ph.gdn, *reinterpret_cast<GdnShared*>(sh.xs), ConsumerBar());
-    } else if (ph.kind == kTkAttn) {
-      TkAttn it;
-      const uint32_t pool = ph.pool_pages;
-      it.valid = false;
-      if ((int)blockIdx.x < kTkMaxSplits * kKvHeads) it.prefetch(ph.at, pool, blockIdx.x);
-      bar.wait(A.err);
-      it.run(ph.at, pool, sh, A.attn_part);
-    } else {  // kTkMerge
-      bar.wait(A.err);
-      if ((int)blockIdx.x < kAttnHeads) tk_merge(ph.at, A.attn_part);
     }
   }
   bar.exit();
@@ -715,8 +439,6 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
 
 }  // namespace
 
-size_t token_attn_part_floats() { return (size_t)kKvHeads * kTkMaxSplits * kTkPartStride; }
-
 bool token_gemv_ok(int rows, int k, int epi) {
   if (k < 256 || k > kTkMaxK || k % 256 || rows < 1) return false;
   if (epi == kSwiGlu && (rows % 2 || (size_t)4 * k > kTkSlotBytes)) return false;
@@ -735,8 +457,8 @@ int token_ctas() {
     cudaGetLastError();
     return 0;
   }
-  // One CTA per SM, all co-resident (the grid barriers need it); the mixers need a CTA per item.
-  if (per_sm < 1 || sms < kTkMaxSplits * kKvHeads || sms < kGdnItemsPerSeq || sms > kMaxGrid) return 0;
+  // One CTA per SM, all co-resident (the grid barriers need it); the GDN phase needs a CTA per item.
+  if (per_sm < 1 || sms < kGdnItemsPerSeq || sms > kMaxGrid) return 0;
   return sms;
 }
 

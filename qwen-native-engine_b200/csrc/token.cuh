@@ -1,6 +1,7 @@
-// Host interface of the token kernel: one launch runs a whole B = 1 decode token (every layer's
-// GEMVs, GDN / attention mixers and the LM head) on one CTA per SM, with a bulk-copy producer
-// warp per CTA streaming all of the token's weights through a shared-memory ring.
+// Host interface of the token kernel: one launch runs a stretch of a B = 1 decode token (the
+// GEMVs and GDN mixers of the layers between two attention mixers, and the LM head) on one CTA
+// per SM, with a bulk-copy producer warp per CTA streaming the stretch's weights through a
+// shared-memory ring.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -13,10 +14,10 @@
 
 namespace qne {
 
-// Phase kinds of a token, in launch order per layer: GEMV (in-projection), GDN or attention
-// partials (+ attention merge), GEMV (out-projection), GEMV (gate_up), GEMV (down); then the LM
-// head GEMV with the greedy pick.
-enum TkKind : int { kTkGemv = 0, kTkGdn = 1, kTkAttn = 2, kTkMerge = 3 };
+// Phase kinds, in launch order per layer: GEMV (in-projection), GDN (attention layers end a
+// launch after their in-projection), GEMV (out-projection), GEMV (gate_up), GEMV (down); then the
+// LM head GEMV with the greedy pick.
+enum TkKind : int { kTkGemv = 0, kTkGdn = 1 };
 
 struct TkPhase {
   int kind = kTkGemv;
@@ -29,9 +30,6 @@ struct TkPhase {
   const float* zgate = nullptr;   // kProGdnGate: z vector [2048]
   // GDN mixer.
   dev::GdnArgs gdn{};
-  // Attention partials and merge (proj, norms, rope, kv, page table, pos, flags, out).
-  AttnArgs at;
-  uint32_t pool_pages = 0;  // pages of the KV pool (bounds the page-table entries)
 };
 
 struct TkArgs {
@@ -48,12 +46,10 @@ struct TkArgs {
   uint32_t* err = nullptr;          // receives kFlagTimeout if a bounded wait gives up
   uint64_t wait_limit_ns = 0;       // one grid-barrier wait
   uint32_t wait_extra = 0;          // arrivals a barrier waits for beyond the grid (timeout test)
-  float* attn_part = nullptr;       // attention partials, token_attn_part_floats() floats
 };
 
 // CTAs of the token kernel on this device (one per SM), or 0 if it cannot run here.
 int token_ctas();
-size_t token_attn_part_floats();
 // Whether a GEMV of this shape can run in the token kernel (f16, 16-byte rows, k <= 6144).
 bool token_gemv_ok(int rows, int k, int epi);
 cudaError_t launch_token(const TkArgs& args, int ctas, cudaStream_t stream, bool pdl);
