@@ -81,21 +81,29 @@ __device__ __forceinline__ void tk_red_release64(unsigned long long* p, unsigned
   asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
-// Grid barrier among the consumer warps of all CTAs (the producer warps never join): the counter
-// is zero at launch, barrier n completes at n * (grid + extra) arrivals, the last CTA to exit
-// clears it. Bounded in time; once any CTA gave up (kFlagTimeout), the others stop waiting.
+// Grid barrier among the consumer warps of all CTAs (the producer warps never join), split into
+// arrive (right after a phase's last write) and wait (before the next phase's first read), so the
+// next phase's prefetch loads go out in between without delaying the arrival. The counter is zero
+// at launch, barrier n completes at n * (grid + extra) arrivals, the last CTA to exit clears it.
+// The consumer barrier orders the CTA's writes before thread 0's release reduction, which
+// publishes them; the acquire polls make the other CTAs' writes visible. Bounded in time; once any
+// CTA gave up (kFlagTimeout), the others stop waiting.
 struct TkBarrier {
   unsigned long long* count;
   unsigned long long target;  // consumer thread 0 only
   uint64_t limit_ns;
   uint32_t extra;
 
-  __device__ __forceinline__ void wait(uint32_t* err) {
+  __device__ __forceinline__ void arrive() {
     ConsumerBar()();
     if (threadIdx.x == 0) {
       target += gridDim.x + extra;
-      __threadfence();
       tk_red_release64(count, 1ull);
+    }
+  }
+
+  __device__ __forceinline__ void wait(uint32_t* err) {
+    if (threadIdx.x == 0) {
       const unsigned long long t0 = tk_now();
       uint32_t rounds = 0;
       while (tk_ld_acquire64(count) < target) {
@@ -123,6 +131,8 @@ struct TkBarrier {
 
 // This CTA's share of a GEMV phase: output rows [r0, r1), `per` output rows per ring slot (a
 // slot holds R = per rows, or per gate rows then per up rows for SwiGLU; R in {2, 3, 6, 12}).
+// `per` is the smallest size that still spreads the CTA's rows over all 8 consumer warps (many
+// small slots when a matrix has few rows), up to what a 24 KB slot holds.
 struct Geo {
   int k, out_rows, r0, r1, per, R, nslots;
   uint32_t rb;  // bytes per row
@@ -134,13 +144,18 @@ struct Geo {
     rb = (uint32_t)k * 2u;
     r0 = (int)((long)out_rows * cta / ncta);
     r1 = (int)((long)out_rows * (cta + 1) / ncta);
+    const int want = (r1 - r0 + kTkSlots - 1) / kTkSlots;  // rows per warp if every warp gets one slot
     int cap = (int)(kTkSlotBytes / rb);
     if (sw) {
       cap /= 2;
-      per = cap >= 6 ? 6 : cap >= 3 ? 3 : 1;
+      const int mx = cap >= 6 ? 6 : cap >= 3 ? 3 : 1;
+      per = want <= 1 ? 1 : want <= 3 ? 3 : 6;
+      if (per > mx) per = mx;
       R = 2 * per;
     } else {
-      per = cap >= 12 ? 12 : cap >= 6 ? 6 : cap >= 3 ? 3 : 2;
+      const int mx = cap >= 12 ? 12 : cap >= 6 ? 6 : cap >= 3 ? 3 : 2;
+      per = want <= 2 ? 2 : want <= 3 ? 3 : want <= 6 ? 6 : 12;
+      if (per > mx) per = mx;
       R = per;
     }
     nslots = r1 > r0 ? (r1 - r0 + per - 1) / per : 0;
@@ -187,20 +202,56 @@ __device__ __forceinline__ void tk_produce(const TkArgs& A, TkShared& sh) {
 // Consumers
 // ------------------------------------------------------------------------------------------
 
+constexpr int kTkMaxChunks = kTkMaxK / 8 / kTkConsumers;  // 8-element chunks of x per thread (3)
+
+// Prologue operands that do not depend on the previous phase (the norm weight, and for the gated
+// GDN norm the gate z, written two phases earlier), loaded before the grid barrier.
+struct TkPre {
+  float w[kTkMaxChunks][8];
+  float z[kTkMaxChunks][8];
+};
+
+__device__ __forceinline__ void ld8(float* d, const float* s) {
+  const float4 a = __ldcg(reinterpret_cast<const float4*>(s));
+  const float4 b = __ldcg(reinterpret_cast<const float4*>(s + 4));
+  d[0] = a.x; d[1] = a.y; d[2] = a.z; d[3] = a.w;
+  d[4] = b.x; d[5] = b.y; d[6] = b.z; d[7] = b.w;
+}
+
+__device__ __forceinline__ void tk_prefetch(const TkPhase& p, TkPre& pre) {
+  const int nc = p.k / 8;
+#pragma unroll
+  for (int i = 0; i < kTkMaxChunks; ++i) {
+    const int c = threadIdx.x + i * kTkConsumers;
+    if (c < nc) {
+      if (p.pro == kProRmsNorm || p.pro == kProEmbedNorm) ld8(pre.w[i], p.norm_w + c * 8);
+      if (p.pro == kProGdnGate) {
+        ld8(pre.z[i], p.zgate + c * 8);
+        ld8(pre.w[i], p.norm_w + ((c * 8) & (kGdnDim - 1)));
+      }
+    }
+  }
+}
+
 // Stages x of a GEMV phase as two planes (elements 0-3 and 4-7 of every 8-element chunk), so a
-// lane's 16-byte reads of consecutive chunks are conflict-free, applying the prologue.
-__device__ __forceinline__ void tk_stage(const TkPhase& p, const TkArgs& A, TkShared& sh) {
+// lane's 16-byte reads of consecutive chunks are conflict-free, applying the prologue. RMSNorm is
+// folded: the planes hold x * norm_w and the returned factor rsqrt(mean(x^2) + eps) scales the
+// dot products in the epilogue (1 for the other prologues). One consumer barrier.
+__device__ __forceinline__ float tk_stage(const TkPhase& p, const TkArgs& A, TkShared& sh, const TkPre& pre) {
   const int k = p.k, tid = threadIdx.x, nc = k / 8;
   float* xlo = sh.xs;
   float* xhi = sh.xs + k / 2;
+  const bool norm = p.pro == kProRmsNorm || p.pro == kProEmbedNorm;
   float ss = 0.f;
   uint32_t token = 0;
   if (p.pro == kProEmbedNorm) {
     token = A.ctl->token;
     if (token >= (uint32_t)A.embed.rows) token = (uint32_t)A.embed.rows - 1;
   }
-#pragma unroll 1
-  for (int c = tid; c < nc; c += kTkConsumers) {
+#pragma unroll
+  for (int i = 0; i < kTkMaxChunks; ++i) {
+    const int c = tid + i * kTkConsumers;
+    if (c >= nc) break;
     float v[8];
     if (p.pro == kProEmbedNorm) {
 #pragma unroll
@@ -210,49 +261,37 @@ __device__ __forceinline__ void tk_stage(const TkPhase& p, const TkArgs& A, TkSh
         *reinterpret_cast<float4*>(A.h_out + c * 8 + 4) = make_float4(v[4], v[5], v[6], v[7]);
       }
     } else {
-      const float4 a = __ldcg(reinterpret_cast<const float4*>(p.x + c * 8));
-      const float4 b = __ldcg(reinterpret_cast<const float4*>(p.x + c * 8 + 4));
-      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-      v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+      ld8(v, p.x + c * 8);
     }
     float cs = 0.f;
 #pragma unroll
     for (int j = 0; j < 8; ++j) cs = fmaf(v[j], v[j], cs);
-    if (p.pro == kProGdnGate) {
+    ss += cs;
+    if (norm) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] *= pre.w[i][j];
+    } else if (p.pro == kProGdnGate) {
       // k == 2048 and 256 threads: one chunk per thread, 16 consecutive threads per 128-wide head.
 #pragma unroll
       for (int o = 8; o > 0; o >>= 1) cs += __shfl_xor_sync(0xffffffffu, cs, o);
       const float inv = rsqrtf(cs / (float)kGdnDim + 1e-6f);
-      const int d = (c * 8) & (kGdnDim - 1);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = v[j] * inv * silu(__ldcg(p.zgate + c * 8 + j)) * p.norm_w[d + j];
+      for (int j = 0; j < 8; ++j) v[j] = v[j] * inv * silu(pre.z[i][j]) * pre.w[i][j];
     }
-    ss += cs;
     *reinterpret_cast<float4*>(xlo + c * 4) = make_float4(v[0], v[1], v[2], v[3]);
     *reinterpret_cast<float4*>(xhi + c * 4) = make_float4(v[4], v[5], v[6], v[7]);
   }
-  if (p.pro == kProRmsNorm || p.pro == kProEmbedNorm) {
-    if (p.pro == kProEmbedNorm && blockIdx.x == 0 && tid == 0) A.ctl->count += 1;  // conv windows
-    float t = warp_sum(ss);
-    ConsumerBar()();
+  if (p.pro == kProEmbedNorm && blockIdx.x == 0 && tid == 0) A.ctl->count += 1;  // conv windows
+  if (norm) {
+    const float t = warp_sum(ss);
     if ((tid & 31) == 0) sh.red[tid >> 5] = t;
-    ConsumerBar()();
-    t = 0.f;
-#pragma unroll
-    for (int w = 0; w < kTkConsumerWarps; ++w) t += sh.red[w];
-    const float inv = rsqrtf(t / (float)k + 1e-6f);
-#pragma unroll 1
-    for (int c = tid; c < nc; c += kTkConsumers) {
-      const float4 w0 = *reinterpret_cast<const float4*>(p.norm_w + c * 8);
-      const float4 w1 = *reinterpret_cast<const float4*>(p.norm_w + c * 8 + 4);
-      float4 lo = *reinterpret_cast<float4*>(xlo + c * 4), hi = *reinterpret_cast<float4*>(xhi + c * 4);
-      lo.x *= inv * w0.x; lo.y *= inv * w0.y; lo.z *= inv * w0.z; lo.w *= inv * w0.w;
-      hi.x *= inv * w1.x; hi.y *= inv * w1.y; hi.z *= inv * w1.z; hi.w *= inv * w1.w;
-      *reinterpret_cast<float4*>(xlo + c * 4) = lo;
-      *reinterpret_cast<float4*>(xhi + c * 4) = hi;
-    }
   }
   ConsumerBar()();
+  if (!norm) return 1.f;
+  float t = 0.f;
+#pragma unroll
+  for (int w = 0; w < kTkConsumerWarps; ++w) t += sh.red[w];
+  return rsqrtf(t / (float)k + 1e-6f);
 }
 
 // Dot products of the R rows of one ring slot with x; every lane ends with the R sums.
@@ -264,7 +303,7 @@ __device__ __forceinline__ void tk_dot(const uint8_t* slot, const float* xs, int
   for (int r = 0; r < R; ++r) a[r] = 0.f;
   const float* xlo = xs;
   const float* xhi = xs + k / 2;
-  constexpr int U = R >= 6 ? 1 : 4;  // R (or 4 R) independent 16-byte loads per iteration
+  constexpr int U = R >= 6 ? 2 : 4;  // 2 R (or 4 R) independent 16-byte loads in flight
 #pragma unroll U
   for (int c = lane; c < k / 8; c += 32) {
     float xv[8];
@@ -280,12 +319,22 @@ __device__ __forceinline__ void tk_dot(const uint8_t* slot, const float* xs, int
   for (int r = 0; r < R; ++r) acc[r] = warp_sum(a[r]);
 }
 
+template <int N>
+__device__ __forceinline__ float pick(const float (&v)[N], int i) {
+  float r = 0.f;
+#pragma unroll
+  for (int j = 0; j < N; ++j)
+    if (j == i) r = v[j];
+  return r;
+}
+
 // The warp's slots of one GEMV phase (every 8th of the CTA's sequence), R rows per slot: wait for
-// the slot, dot, release the slot to the producer, apply the epilogue (lane 0). For SwiGLU the
-// slot's rows are per = R / 2 gate rows, then the matching up rows.
+// the slot, dot, release the slot to the producer; lane r applies the epilogue to output row r of
+// the slot (the residual it adds is loaded before the dot). For SwiGLU the slot's rows are
+// per = R / 2 gate rows, then the matching up rows. Each lane keeps its best greedy-pick candidate.
 template <int R, bool SW>
 __device__ __forceinline__ void tk_slots(const TkPhase& ph, const Geo& geo, const TkArgs& A, TkShared& sh, uint32_t g,
-                                         float& best_v, uint32_t& best_i) {
+                                         float inv, float& best_v, uint32_t& best_i) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int OUT = SW ? R / 2 : R;
 #pragma unroll 1
@@ -293,36 +342,33 @@ __device__ __forceinline__ void tk_slots(const TkPhase& ph, const Geo& geo, cons
     const uint32_t gi = g + (uint32_t)i;
     if ((int)(gi % kTkSlots) != warp) continue;
     const uint32_t j = gi / kTkSlots;
+    const int a = geo.r0 + i * geo.per;
+    const int n = min(geo.per, geo.r1 - a);
+    const float resid = (ph.epi == kAccumulate && lane < n) ? __ldcg(ph.y + a + lane) : 0.f;
     mbar_wait(smem_u32(&sh.full[warp]), j & 1u, A.err);
     float acc[R];
     tk_dot<R>(sh.ring[warp], sh.xs, geo.k, geo.rb, lane, acc);
     __syncwarp();
     if (lane == 0) mbar_arrive(smem_u32(&sh.empty[warp]));
-    const int a = geo.r0 + i * geo.per;
-    const int n = min(geo.per, geo.r1 - a);
-    if (lane == 0) {
-#pragma unroll
-      for (int r = 0; r < OUT; ++r) {
-        if (r < n) {
-          const int row = a + r;
-          if (SW) {
-            ph.y[row] = silu(acc[r]) * acc[OUT + r];
-          } else if (ph.epi == kAccumulate) {
-            ph.y[row] = __ldcg(ph.y + row) + acc[r];
-          } else {
-            ph.y[row] = acc[r];
-            if (ph.epi == kArgmax && acc[r] > -INFINITY && better(acc[r], (uint32_t)row, best_v, best_i)) {
-              best_v = acc[r];
-              best_i = (uint32_t)row;
-            }
-          }
+    if (lane < n) {
+      const int row = a + lane;
+      const float v = pick<R>(acc, lane) * inv;
+      if (SW) {
+        ph.y[row] = silu(v) * (pick<R>(acc, OUT + lane) * inv);
+      } else if (ph.epi == kAccumulate) {
+        ph.y[row] = resid + v;
+      } else {
+        ph.y[row] = v;
+        if (ph.epi == kArgmax && v > -INFINITY && better(v, (uint32_t)row, best_v, best_i)) {
+          best_v = v;
+          best_i = (uint32_t)row;
         }
       }
     }
   }
 }
 
-__device__ __forceinline__ void tk_gemv(const TkPhase& ph, const TkArgs& A, TkShared& sh, uint32_t& g) {
+__device__ __forceinline__ void tk_gemv(const TkPhase& ph, const TkArgs& A, TkShared& sh, uint32_t& g, float inv) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   Geo geo;
   geo.init(ph, blockIdx.x, gridDim.x);
@@ -330,21 +376,31 @@ __device__ __forceinline__ void tk_gemv(const TkPhase& ph, const TkArgs& A, TkSh
   uint32_t best_i = 0xFFFFFFFFu;
   if (geo.sw) {
     switch (geo.R) {
-      case 2: tk_slots<2, true>(ph, geo, A, sh, g, best_v, best_i); break;
-      case 6: tk_slots<6, true>(ph, geo, A, sh, g, best_v, best_i); break;
-      default: tk_slots<12, true>(ph, geo, A, sh, g, best_v, best_i); break;
+      case 2: tk_slots<2, true>(ph, geo, A, sh, g, inv, best_v, best_i); break;
+      case 6: tk_slots<6, true>(ph, geo, A, sh, g, inv, best_v, best_i); break;
+      default: tk_slots<12, true>(ph, geo, A, sh, g, inv, best_v, best_i); break;
     }
   } else {
     switch (geo.R) {
-      case 2: tk_slots<2, false>(ph, geo, A, sh, g, best_v, best_i); break;
-      case 3: tk_slots<3, false>(ph, geo, A, sh, g, best_v, best_i); break;
-      case 6: tk_slots<6, false>(ph, geo, A, sh, g, best_v, best_i); break;
-      default: tk_slots<12, false>(ph, geo, A, sh, g, best_v, best_i); break;
+      case 2: tk_slots<2, false>(ph, geo, A, sh, g, inv, best_v, best_i); break;
+      case 3: tk_slots<3, false>(ph, geo, A, sh, g, inv, best_v, best_i); break;
+      case 6: tk_slots<6, false>(ph, geo, A, sh, g, inv, best_v, best_i); break;
+      default: tk_slots<12, false>(ph, geo, A, sh, g, inv, best_v, best_i); break;
     }
   }
   g += (uint32_t)geo.nslots;
   if (ph.epi != kArgmax) return;
-  // Greedy pick: per-CTA best, then the last CTA reduces across CTAs and updates the control words.
+  // Greedy pick: warp best, CTA best, then the last CTA reduces across CTAs and updates the
+  // control words.
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best_v, o);
+    const uint32_t oi = __shfl_xor_sync(0xffffffffu, best_i, o);
+    if (better(ov, oi, best_v, best_i)) {
+      best_v = ov;
+      best_i = oi;
+    }
+  }
   if (lane == 0) {
     sh.bval[warp] = best_v;
     sh.bidx[warp] = best_i;
@@ -404,9 +460,11 @@ __device__ __forceinline__ void tk_consume(const TkArgs& A, TkShared& sh) {
   for (int p = 0; p < A.nphases; ++p) {
     const TkPhase& ph = A.phases[p];
     if (ph.kind == kTkGemv) {
+      TkPre pre;
+      tk_prefetch(ph, pre);
       if (p > 0) bar.wait(A.err);
-      tk_stage(ph, A, sh);
-      tk_gemv(ph, A, sh, g);
+      const float inv = tk_stage(ph, A, sh, pre);
+      tk_gemv(ph, A, sh, g, inv);
     } else if (ph.kind == kTkGdn) {
       const bool mine = (int)blockIdx.x < kGdnItemsPerSeq;
       GdnItem it;
@@ -414,6 +472,7 @@ __device__ __forceinline__ void tk_consume(const TkArgs& A, TkShared& sh) {
       bar.wait(A.err);
       if (mine) it.run_with(ph.gdn, *reinterpret_cast<GdnShared*>(sh.xs), ConsumerBar());
     }
+    if (p + 1 < A.nphases) bar.arrive();
   }
   bar.exit();
 }
