@@ -566,18 +566,13 @@ bool Runner::token_supported() {
   return token_ctas > 0;
 }
 
-// The token's phases in launch order (kernels/src/model.rs:220-269), with the same weights,
-// prologues and epilogues as the per-operation graph, cut into launches at the attention mixers.
-// Vectors passed between phases of one launch go through the tagged buffers; each phase's tag
-// index is its position in the token (tout), and a reader expects the index of the phase that last
-// wrote what it reads (tin, tres, tz). The attention in-projection (the last phase of a launch)
-// writes plain floats for the attention kernel, whose output the next launch reads as plain floats.
+// The token's phases in launch order (kernels/src/model.rs:220-269), with the same buffers and
+// prologues / epilogues as the per-operation graph, cut into launches at the attention mixers.
 std::vector<TkPhase> Runner::token_phase_list(Variant v, std::vector<TokenSeg>& segs) const {
   std::vector<TkPhase> ph;
   segs.clear();
   segs.push_back(TokenSeg{});
-  int h_q = -1;  // phase that last wrote the tagged h
-  auto gemv = [&](const GemvArgs& a) -> TkPhase& {
+  auto gemv = [&](const GemvArgs& a) {
     TkPhase p;
     p.kind = kTkGemv;
     p.pro = a.pro;
@@ -589,69 +584,28 @@ std::vector<TkPhase> Runner::token_phase_list(Variant v, std::vector<TokenSeg>& 
     p.y = a.y;
     p.norm_w = a.norm_w;
     p.zgate = a.zgate;
-    p.tout = (int)ph.size();
     ph.push_back(p);
-    return ph.back();
   };
   for (int i = 0; i < m->cfg.layers; ++i) {
     const LayerArgs r = layer_args(i);
-    TkPhase& in = gemv(r.in);
-    const int in_q = in.tout;
-    if (i == 0) {
-      in.ht = th;  // the embedding row starts the residual stream
-      h_q = in_q;
-    } else {
-      in.xt = th;
-      in.tin = h_q;
-    }
+    gemv(r.in);
     if (r.attention) {
-      in.yt = nullptr;  // plain proj for the attention kernel
       segs.back().count = (int)ph.size() - segs.back().first;
       segs.back().attn_layer = i;
       TokenSeg next;
       next.first = (int)ph.size();
       segs.push_back(next);
     } else {
-      in.yt = tproj;
       TkPhase mix;
       mix.kind = kTkGdn;
       mix.gdn = r.gdn;
-      mix.xt = tproj;
-      mix.tin = in_q;
-      mix.yt = traw;
-      mix.tout = (int)ph.size();
       ph.push_back(mix);
     }
-    const int mix_q = (int)ph.size() - 1;
-    TkPhase& out = gemv(r.out);
-    if (!r.attention) {
-      out.xt = traw;
-      out.tin = mix_q;
-      out.zt = tproj + 6144;
-      out.tz = in_q;
-    }
-    out.rt = th;
-    out.tres = h_q;
-    out.yt = th;
-    h_q = out.tout;
-    TkPhase& gu = gemv(r.gate_up);
-    gu.xt = th;
-    gu.tin = h_q;
-    gu.yt = tact;
-    const int gu_q = gu.tout;
-    TkPhase& dn = gemv(r.down);
-    dn.xt = tact;
-    dn.tin = gu_q;
-    dn.rt = th;
-    dn.tres = h_q;
-    dn.yt = th;
-    h_q = dn.tout;
+    gemv(r.out);
+    gemv(r.gate_up);
+    gemv(r.down);
   }
-  if (v != kLayers) {
-    TkPhase& hd = gemv(head_args(v));
-    hd.xt = th;
-    hd.tin = h_q;
-  }
+  if (v != kLayers) gemv(head_args(v));
   segs.back().count = (int)ph.size() - segs.back().first;
   return ph;
 }
@@ -660,8 +614,6 @@ TkArgs Runner::token_args(Variant v, const TokenSeg& seg) const {
   TkArgs a;
   a.phases = token_phases[v] + seg.first;
   a.nphases = seg.count;
-  a.epoch = tepoch;
-  a.last_of_token = &seg == &token_segs[v].back() ? 1 : 0;
   a.ctl = st.ctl;
   a.embed = m->embed;
   a.h_out = h;
@@ -677,20 +629,6 @@ TkArgs Runner::token_args(Variant v, const TokenSeg& seg) const {
 // Uploads the phase lists once and captures one graph per variant: the token-kernel launches and,
 // between them, the attention kernels, chained by programmatic dependent launch.
 void Runner::capture_token() {
-  if (!th) {
-    const Config& c = m->cfg;
-    th = static_cast<unsigned long long*>(m->alloc((size_t)c.hidden * 8));
-    tproj = static_cast<unsigned long long*>(m->alloc((size_t)kGdnProj * 8));
-    traw = static_cast<unsigned long long*>(m->alloc((size_t)kMixerOut * 8));
-    tact = static_cast<unsigned long long*>(m->alloc((size_t)c.inter * 8));
-    tepoch = static_cast<uint32_t*>(m->alloc(256));
-    // tag 0 is never expected (the phase byte of every expected tag is at least 1)
-    cuda_check(cudaMemset(tepoch, 0, 256), "token buffers");
-    cuda_check(cudaMemset(th, 0, (size_t)c.hidden * 8), "token buffers");
-    cuda_check(cudaMemset(tproj, 0, (size_t)kGdnProj * 8), "token buffers");
-    cuda_check(cudaMemset(traw, 0, (size_t)kMixerOut * 8), "token buffers");
-    cuda_check(cudaMemset(tact, 0, (size_t)c.inter * 8), "token buffers");
-  }
   for (int v = 0; v < kVariants; ++v) {
     const std::vector<TkPhase> list = token_phase_list((Variant)v, token_segs[v]);
     if (!token_phases[v]) token_phases[v] = static_cast<TkPhase*>(m->alloc(list.size() * sizeof(TkPhase)));

@@ -190,10 +190,6 @@ class Runner {
   int token_ctas = 0;                            // 0: the token kernel cannot run this model
   TkPhase* token_phases[kVariants] = {nullptr, nullptr, nullptr};  // device phase lists
   size_t token_launches[kVariants] = {0, 0, 0};  // launches of one token, per variant
-  // Tagged copies of the vectors passed between the token kernel's phases ({f32, tag} words) and
-  // the tag epoch: h[hidden], proj[8224], raw[2048], act[intermediate], epoch.
-  unsigned long long *th = nullptr, *tproj = nullptr, *traw = nullptr, *tact = nullptr;
-  uint32_t* tepoch = nullptr;
   // One token-kernel launch: phases [first, first + count) of the variant's list, followed by the
   // attention mixer of layer attn_layer (-1: none, the last launch of a token).
   struct TokenSeg {

@@ -19,14 +19,10 @@
 //     rows); the warp dots them with x (staged once per phase in shared memory with its prologue:
 //     copy, RMSNorm, gated GDN RMSNorm, or embedding gather + RMSNorm), reduces across lanes and
 //     applies the epilogue (store, residual add, SwiGLU, greedy-pick candidate);
-//   * no grid barrier separates the phases: the vectors they pass (residual stream, projection,
-//     GDN output, SwiGLU activations) are tagged words {f32 value, tag of the writing phase}
-//     stored with single 8-byte stores, and a reader polls the words it needs until they carry
-//     the expected tag (bounded in time, with an error flag). A phase transition then costs one
-//     store and one load through L2 instead of a fence, a barrier round trip and a reload, which
-//     matters because the producers keep L2 and HBM saturated;
-//   * GDN: one work item (16 value columns of one head, the arithmetic of dev::GdnItem) per CTA
-//     for CTAs 0..127, its state slice loaded before the item's inputs are polled.
+//   * phases that read what the previous phase wrote start behind a grid barrier (an arrival
+//     counter; release reduction to arrive, acquire polls, bounded in time with an error flag);
+//   * GDN: one dev::GdnItem (16 value columns of one head) per CTA for CTAs 0..127, its state
+//     slice loaded before the barrier.
 // A token is one launch per stretch of layers between attention mixers; each attention layer's
 // mixer is the paged attention kernel (attention.cu) between two such launches, chained by
 // programmatic dependent launch. Results match the per-operation kernels within the logit
@@ -71,63 +67,67 @@ __device__ __forceinline__ unsigned long long tk_now() {
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
 }
+__device__ __forceinline__ unsigned long long tk_ld_acquire64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
 __device__ __forceinline__ uint32_t tk_ld_acquire(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-
-// Tagged words: {f32 value, tag}, written with one 8-byte store (single-copy atomic) and read
-// with L2-coherent loads, so a reader sees a value and its tag together.
-__device__ __forceinline__ unsigned long long ld_tag(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_tag(unsigned long long* p, float v, uint32_t tag) {
-  const unsigned long long w = ((unsigned long long)tag << 32) | __float_as_uint(v);
-  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+__device__ __forceinline__ void tk_red_release64(unsigned long long* p, unsigned long long v) {
+  asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
-// Per-launch tag state of a consumer thread.
-struct TkTags {
-  uint32_t epoch;
-  uint32_t flip;  // nonzero in the timeout test: no expected tag is ever written
-  __device__ __forceinline__ uint32_t of(int q) const { return (epoch << 8) | (uint32_t)(q + 1); }
-  __device__ __forceinline__ uint32_t want(int q) const { return of(q) ^ flip; }
-};
+// Grid barrier among the consumer warps of all CTAs (the producer warps never join), split into
+// arrive (right after a phase's last write) and wait (before the next phase's first read), so the
+// next phase's prefetch loads go out in between without delaying the arrival. The counter is zero
+// at launch, barrier n completes at n * (grid + extra) arrivals, the last CTA to exit clears it.
+// The consumer barrier orders the CTA's writes before thread 0's release reduction, which
+// publishes them; the acquire polls make the other CTAs' writes visible. Bounded in time; once any
+// CTA gave up (kFlagTimeout), the others stop waiting.
+struct TkBarrier {
+  unsigned long long* count;
+  unsigned long long target;  // consumer thread 0 only
+  uint64_t limit_ns;
+  uint32_t extra;
 
-// N tagged words from p that must carry `tag`: loads them, then reloads the ones that do not
-// until all do. Bounded in time (wait_limit_ns from the first miss); after a timeout, or once any
-// CTA has flagged one, it returns what it has and the error flag stays set.
-template <int N>
-__device__ __forceinline__ void poll_n(const unsigned long long* p, uint32_t tag, float* out, const TkArgs& A) {
-  unsigned long long w[N];
-#pragma unroll
-  for (int j = 0; j < N; ++j) w[j] = ld_tag(p + j);
-  unsigned long long t0 = 0;
-  uint32_t rounds = 0;
-#pragma unroll 1
-  for (;;) {
-    bool ok = true;
-#pragma unroll
-    for (int j = 0; j < N; ++j) ok = ok && (uint32_t)(w[j] >> 32) == tag;
-    if (ok) break;
-    if (rounds == 0) t0 = tk_now();
-    if ((++rounds & 15u) == 0u) {
-      if (tk_ld_acquire(A.err) & kFlagTimeout) break;
-      if (tk_now() - t0 > A.wait_limit_ns) {
-        atomicOr(A.err, kFlagTimeout);
-        break;
+  __device__ __forceinline__ void arrive() {
+    ConsumerBar()();
+    if (threadIdx.x == 0) {
+      target += gridDim.x + extra;
+      tk_red_release64(count, 1ull);
+    }
+  }
+
+  __device__ __forceinline__ void wait(uint32_t* err) {
+    if (threadIdx.x == 0) {
+      const unsigned long long t0 = tk_now();
+      uint32_t rounds = 0;
+      while (tk_ld_acquire64(count) < target) {
+        if ((++rounds & 63u) == 0u) {
+          if (tk_ld_acquire(err) & kFlagTimeout) break;
+          if (tk_now() - t0 > limit_ns) {
+            atomicOr(err, kFlagTimeout);
+            break;
+          }
+        }
       }
     }
-#pragma unroll
-    for (int j = 0; j < N; ++j)
-      if ((uint32_t)(w[j] >> 32) != tag) w[j] = ld_tag(p + j);
+    ConsumerBar()();
   }
-#pragma unroll
-  for (int j = 0; j < N; ++j) out[j] = __uint_as_float((uint32_t)w[j]);
-}
+
+  __device__ __forceinline__ void exit() {
+    ConsumerBar()();
+    if (threadIdx.x == 0 && atomicAdd(count + 1, 1ull) == gridDim.x - 1) {
+      count[0] = 0ull;
+      count[1] = 0ull;
+      __threadfence();
+    }
+  }
+};
 
 // This CTA's share of a GEMV phase: output rows [r0, r1), `per` output rows per ring slot (a
 // slot holds R = per rows, or per gate rows then per up rows for SwiGLU; R in {2, 3, 6, 12}).
@@ -204,15 +204,16 @@ __device__ __forceinline__ void tk_produce(const TkArgs& A, TkShared& sh) {
 
 constexpr int kTkMaxChunks = kTkMaxK / 8 / kTkConsumers;  // 8-element chunks of x per thread (3)
 
-// Prologue operands that do not depend on earlier phases: the norm weight (constant), loaded
-// before x.
+// Prologue operands that do not depend on the previous phase (the norm weight, and for the gated
+// GDN norm the gate z, written two phases earlier), loaded before the grid barrier.
 struct TkPre {
   float w[kTkMaxChunks][8];
+  float z[kTkMaxChunks][8];
 };
 
 __device__ __forceinline__ void ld8(float* d, const float* s) {
-  const float4 a = __ldg(reinterpret_cast<const float4*>(s));
-  const float4 b = __ldg(reinterpret_cast<const float4*>(s + 4));
+  const float4 a = __ldcg(reinterpret_cast<const float4*>(s));
+  const float4 b = __ldcg(reinterpret_cast<const float4*>(s + 4));
   d[0] = a.x; d[1] = a.y; d[2] = a.z; d[3] = a.w;
   d[4] = b.x; d[5] = b.y; d[6] = b.z; d[7] = b.w;
 }
@@ -224,19 +225,19 @@ __device__ __forceinline__ void tk_prefetch(const TkPhase& p, TkPre& pre) {
     const int c = threadIdx.x + i * kTkConsumers;
     if (c < nc) {
       if (p.pro == kProRmsNorm || p.pro == kProEmbedNorm) ld8(pre.w[i], p.norm_w + c * 8);
-      if (p.pro == kProGdnGate) ld8(pre.w[i], p.norm_w + ((c * 8) & (kGdnDim - 1)));
+      if (p.pro == kProGdnGate) {
+        ld8(pre.z[i], p.zgate + c * 8);
+        ld8(pre.w[i], p.norm_w + ((c * 8) & (kGdnDim - 1)));
+      }
     }
   }
 }
 
 // Stages x of a GEMV phase as two planes (elements 0-3 and 4-7 of every 8-element chunk), so a
-// lane's 16-byte reads of consecutive chunks are conflict-free, applying the prologue. x (and z)
-// are polled from tagged words when the previous phases wrote them in this launch, else read as
-// plain floats. RMSNorm is folded: the planes hold x * norm_w and the returned factor
-// rsqrt(mean(x^2) + eps) scales the dot products in the epilogue (1 for the other prologues).
-// Starts and ends with a consumer barrier (the planes are shared with the previous phase's dot).
-__device__ __forceinline__ float tk_stage(const TkPhase& p, const TkArgs& A, TkShared& sh, const TkPre& pre,
-                                          const TkTags& tg) {
+// lane's 16-byte reads of consecutive chunks are conflict-free, applying the prologue. RMSNorm is
+// folded: the planes hold x * norm_w and the returned factor rsqrt(mean(x^2) + eps) scales the
+// dot products in the epilogue (1 for the other prologues). One consumer barrier.
+__device__ __forceinline__ float tk_stage(const TkPhase& p, const TkArgs& A, TkShared& sh, const TkPre& pre) {
   const int k = p.k, tid = threadIdx.x, nc = k / 8;
   float* xlo = sh.xs;
   float* xhi = sh.xs + k / 2;
@@ -247,51 +248,40 @@ __device__ __forceinline__ float tk_stage(const TkPhase& p, const TkArgs& A, TkS
     token = A.ctl->token;
     if (token >= (uint32_t)A.embed.rows) token = (uint32_t)A.embed.rows - 1;
   }
-  float v[kTkMaxChunks][8];
 #pragma unroll
   for (int i = 0; i < kTkMaxChunks; ++i) {
     const int c = tid + i * kTkConsumers;
-    if (c < nc) {
-      if (p.pro == kProEmbedNorm) {
+    if (c >= nc) break;
+    float v[8];
+    if (p.pro == kProEmbedNorm) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[i][j] = deq_elem(A.embed, token, c * 8 + j);
-        if (blockIdx.x == 0) {
-#pragma unroll
-          for (int j = 0; j < 8; ++j) st_tag(p.ht + c * 8 + j, v[i][j], tg.of(p.tout));
-        }
-      } else if (p.xt) {
-        poll_n<8>(p.xt + c * 8, tg.want(p.tin), v[i], A);
-      } else {
-        ld8(v[i], p.x + c * 8);
+      for (int j = 0; j < 8; ++j) v[j] = deq_elem(A.embed, token, c * 8 + j);
+      if (blockIdx.x == 0) {
+        *reinterpret_cast<float4*>(A.h_out + c * 8) = make_float4(v[0], v[1], v[2], v[3]);
+        *reinterpret_cast<float4*>(A.h_out + c * 8 + 4) = make_float4(v[4], v[5], v[6], v[7]);
       }
+    } else {
+      ld8(v, p.x + c * 8);
     }
-  }
-  ConsumerBar()();  // the previous phase's dot products are done with the planes
+    float cs = 0.f;
 #pragma unroll
-  for (int i = 0; i < kTkMaxChunks; ++i) {
-    const int c = tid + i * kTkConsumers;
-    if (c < nc) {
-      float cs = 0.f;
+    for (int j = 0; j < 8; ++j) cs = fmaf(v[j], v[j], cs);
+    ss += cs;
+    if (norm) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) cs = fmaf(v[i][j], v[i][j], cs);
-      ss += cs;
-      if (norm) {
+      for (int j = 0; j < 8; ++j) v[j] *= pre.w[i][j];
+    } else if (p.pro == kProGdnGate) {
+      // k == 2048 and 256 threads: one chunk per thread, 16 consecutive threads per 128-wide head.
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[i][j] *= pre.w[i][j];
-      } else if (p.pro == kProGdnGate) {
-        // k == 2048 and 256 threads: one chunk per thread, 16 consecutive threads per 128-wide head.
-        float z[8];
-        poll_n<8>(p.zt + c * 8, tg.want(p.tz), z, A);
+      for (int o = 8; o > 0; o >>= 1) cs += __shfl_xor_sync(0xffffffffu, cs, o);
+      const float inv = rsqrtf(cs / (float)kGdnDim + 1e-6f);
 #pragma unroll
-        for (int o = 8; o > 0; o >>= 1) cs += __shfl_xor_sync(0xffffffffu, cs, o);
-        const float inv = rsqrtf(cs / (float)kGdnDim + 1e-6f);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[i][j] = v[i][j] * inv * silu(z[j]) * pre.w[i][j];
-      }
-      *reinterpret_cast<float4*>(xlo + c * 4) = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
-      *reinterpret_cast<float4*>(xhi + c * 4) = make_float4(v[i][4], v[i][5], v[i][6], v[i][7]);
+      for (int j = 0; j < 8; ++j) v[j] = v[j] * inv * silu(pre.z[i][j]) * pre.w[i][j];
     }
+    *reinterpret_cast<float4*>(xlo + c * 4) = make_float4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<float4*>(xhi + c * 4) = make_float4(v[4], v[5], v[6], v[7]);
   }
+  if (p.pro == kProEmbedNorm && blockIdx.x == 0 && tid == 0) A.ctl->count += 1;  // conv windows
   if (norm) {
     const float t = warp_sum(ss);
     if ((tid & 31) == 0) sh.red[tid >> 5] = t;
@@ -340,11 +330,11 @@ __device__ __forceinline__ float pick(const float (&v)[N], int i) {
 
 // The warp's slots of one GEMV phase (every 8th of the CTA's sequence), R rows per slot: wait for
 // the slot, dot, release the slot to the producer; lane r applies the epilogue to output row r of
-// the slot (the residual it adds is polled before the dot). For SwiGLU the slot's rows are
+// the slot (the residual it adds is loaded before the dot). For SwiGLU the slot's rows are
 // per = R / 2 gate rows, then the matching up rows. Each lane keeps its best greedy-pick candidate.
 template <int R, bool SW>
 __device__ __forceinline__ void tk_slots(const TkPhase& ph, const Geo& geo, const TkArgs& A, TkShared& sh, uint32_t g,
-                                         float inv, const TkTags& tg, float& best_v, uint32_t& best_i) {
+                                         float inv, float& best_v, uint32_t& best_i) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int OUT = SW ? R / 2 : R;
 #pragma unroll 1
@@ -354,11 +344,7 @@ __device__ __forceinline__ void tk_slots(const TkPhase& ph, const Geo& geo, cons
     const uint32_t j = gi / kTkSlots;
     const int a = geo.r0 + i * geo.per;
     const int n = min(geo.per, geo.r1 - a);
-    float resid = 0.f;
-    if (ph.epi == kAccumulate && lane < n) {
-      if (ph.rt) poll_n<1>(ph.rt + a + lane, tg.want(ph.tres), &resid, A);
-      else resid = __ldcg(ph.y + a + lane);
-    }
+    const float resid = (ph.epi == kAccumulate && lane < n) ? __ldcg(ph.y + a + lane) : 0.f;
     mbar_wait(smem_u32(&sh.full[warp]), j & 1u, A.err);
     float acc[R];
     tk_dot<R>(sh.ring[warp], sh.xs, geo.k, geo.rb, lane, acc);
@@ -367,22 +353,22 @@ __device__ __forceinline__ void tk_slots(const TkPhase& ph, const Geo& geo, cons
     if (lane < n) {
       const int row = a + lane;
       const float v = pick<R>(acc, lane) * inv;
-      float out;
-      if (SW) out = silu(v) * (pick<R>(acc, OUT + lane) * inv);
-      else if (ph.epi == kAccumulate) out = resid + v;
-      else out = v;
-      if (ph.yt) st_tag(ph.yt + row, out, tg.of(ph.tout));
-      else ph.y[row] = out;
-      if (ph.epi == kArgmax && v > -INFINITY && better(v, (uint32_t)row, best_v, best_i)) {
-        best_v = v;
-        best_i = (uint32_t)row;
+      if (SW) {
+        ph.y[row] = silu(v) * (pick<R>(acc, OUT + lane) * inv);
+      } else if (ph.epi == kAccumulate) {
+        ph.y[row] = resid + v;
+      } else {
+        ph.y[row] = v;
+        if (ph.epi == kArgmax && v > -INFINITY && better(v, (uint32_t)row, best_v, best_i)) {
+          best_v = v;
+          best_i = (uint32_t)row;
+        }
       }
     }
   }
 }
 
-__device__ __forceinline__ void tk_gemv(const TkPhase& ph, const TkArgs& A, TkShared& sh, uint32_t& g, float inv,
-                                        const TkTags& tg) {
+__device__ __forceinline__ void tk_gemv(const TkPhase& ph, const TkArgs& A, TkShared& sh, uint32_t& g, float inv) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   Geo geo;
   geo.init(ph, blockIdx.x, gridDim.x);
@@ -390,16 +376,16 @@ __device__ __forceinline__ void tk_gemv(const TkPhase& ph, const TkArgs& A, TkSh
   uint32_t best_i = 0xFFFFFFFFu;
   if (geo.sw) {
     switch (geo.R) {
-      case 2: tk_slots<2, true>(ph, geo, A, sh, g, inv, tg, best_v, best_i); break;
-      case 6: tk_slots<6, true>(ph, geo, A, sh, g, inv, tg, best_v, best_i); break;
-      default: tk_slots<12, true>(ph, geo, A, sh, g, inv, tg, best_v, best_i); break;
+      case 2: tk_slots<2, true>(ph, geo, A, sh, g, inv, best_v, best_i); break;
+      case 6: tk_slots<6, true>(ph, geo, A, sh, g, inv, best_v, best_i); break;
+      default: tk_slots<12, true>(ph, geo, A, sh, g, inv, best_v, best_i); break;
     }
   } else {
     switch (geo.R) {
-      case 2: tk_slots<2, false>(ph, geo, A, sh, g, inv, tg, best_v, best_i); break;
-      case 3: tk_slots<3, false>(ph, geo, A, sh, g, inv, tg, best_v, best_i); break;
-      case 6: tk_slots<6, false>(ph, geo, A, sh, g, inv, tg, best_v, best_i); break;
-      default: tk_slots<12, false>(ph, geo, A, sh, g, inv, tg, best_v, best_i); break;
+      case 2: tk_slots<2, false>(ph, geo, A, sh, g, inv, best_v, best_i); break;
+      case 3: tk_slots<3, false>(ph, geo, A, sh, g, inv, best_v, best_i); break;
+      case 6: tk_slots<6, false>(ph, geo, A, sh, g, inv, best_v, best_i); break;
+      default: tk_slots<12, false>(ph, geo, A, sh, g, inv, best_v, best_i); break;
     }
   }
   g += (uint32_t)geo.nslots;
@@ -466,148 +452,29 @@ __device__ __forceinline__ void tk_gemv(const TkPhase& ph, const TkArgs& A, TkSh
   }
 }
 
-// The GDN step of one work item (16 value columns of one head; gdn, kernels/src/shaders.rs:
-// 445-520, as dev::GdnItem) with the head's q, k, v, a, b polled from the tagged projection and the
-// output written tagged. `cnt` counts the tokens including this one (ring slot (cnt - 1) % 4 takes
-// this step's conv input).
-struct TkGdn {
-  int s, h, t0, jg, tl;
-  float* S;
-  float sv[8];
-
-  __device__ __forceinline__ void prefetch(const GdnArgs& a, int item) {
-    s = item % kSlices;
-    h = item / kSlices;
-    const int tid = threadIdx.x;
-    t0 = s * kSlice;
-    jg = tid >> 4;
-    tl = tid & 15;  // state slice: column t0 + tl, rows jg*8 .. jg*8+7
-    S = a.state + (size_t)h * kGdnDim * kGdnDim + t0 + tl;
-#pragma unroll
-    for (int jj = 0; jj < 8; ++jj) sv[jj] = S[(size_t)(jg * 8 + jj) * kGdnDim];
-  }
-
-  __device__ __forceinline__ void run(const TkPhase& ph, uint32_t cnt, GdnShared& sh, const TkArgs& A,
-                                      const TkTags& tg) {
-    const GdnArgs& a = ph.gdn;
-    const uint32_t tin = tg.want(ph.tin);
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    float* ring = a.conv;
-    const int i = tid & (kGdnDim - 1);
-    const int ch = (tid < kGdnDim ? 0 : 2048) + h * kGdnDim + i;
-    const float4 w = *reinterpret_cast<const float4*>(a.conv_w + (size_t)ch * 4);
-    float rv[4];
-#pragma unroll
-    for (int r = 0; r < 4; ++r) rv[r] = ring[r * kConvChannels + ch];
-    const int cv = 4096 + h * kGdnDim + t0 + (tid & (kSlice - 1));
-    float vrv[4] = {0.f, 0.f, 0.f, 0.f};
-    float4 vw = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (tid < kSlice) {
-      vw = *reinterpret_cast<const float4*>(a.conv_w + (size_t)cv * 4);
-#pragma unroll
-      for (int r = 0; r < 4; ++r) vrv[r] = ring[r * kConvChannels + cv];
-    }
-    float x, vx = 0.f, ab[2];
-    poll_n<1>(ph.xt + ch, tin, &x, A);
-    if (tid < kSlice) poll_n<1>(ph.xt + cv, tin, &vx, A);
-    poll_n<1>(ph.xt + 8192 + h, tin, &ab[0], A);
-    poll_n<1>(ph.xt + 8208 + h, tin, &ab[1], A);
-    const int slot_new = (int)((cnt - 1u) & 3u);
-    const int s2 = (int)((cnt - 2u) & 3u);  // previous input
-    const int s1 = (int)((cnt - 3u) & 3u);
-    const int s0 = (int)((cnt - 4u) & 3u);  // oldest input of the window
-    float val;
-    {
-      const float y = sel4(rv, s0) * w.x + sel4(rv, s1) * w.y + sel4(rv, s2) * w.z + x * w.w;
-      val = silu(y);
-      if (i >= t0 && i < t0 + kSlice) ring[slot_new * kConvChannels + ch] = x;
-    }
-    if (tid < kSlice) {
-      const float y = sel4(vrv, s0) * vw.x + sel4(vrv, s1) * vw.y + sel4(vrv, s2) * vw.z + vx * vw.w;
-      sh.vs[tid] = silu(y);
-      ring[slot_new * kConvChannels + cv] = vx;
-    }
-    // L2 norms: warps 0-3 hold q, warps 4-7 hold k.
-    const float ss = warp_sum(val * val);
-    if (lane == 0) sh.red[warp] = ss;
-    ConsumerBar()();
-    const float nq = rsqrtf(sh.red[0] + sh.red[1] + sh.red[2] + sh.red[3] + 1e-6f);
-    const float nk = rsqrtf(sh.red[4] + sh.red[5] + sh.red[6] + sh.red[7] + 1e-6f);
-    if (tid < kGdnDim) sh.qs[i] = val * nq * 0.08838834764f;
-    else sh.ks[i] = val * nk;
-    ConsumerBar()();
-    if (warp < 4) {
-      const float pq = warp_sum(sh.ks[tid] * sh.qs[tid]);
-      if (lane == 0) sh.red[warp] = pq;
-    }
-    const float g = expf(a.params[16 + h] * logf(1.0f + expf(ab[0] + a.params[h])));
-    const float beta = 1.0f / (1.0f + expf(-ab[1]));
-    float sk = 0.f, sq = 0.f;
-#pragma unroll
-    for (int jj = 0; jj < 8; ++jj) {
-      sk = fmaf(sv[jj], sh.ks[jg * 8 + jj], sk);
-      sq = fmaf(sv[jj], sh.qs[jg * 8 + jj], sq);
-    }
-    sh.psk[jg][tl] = sk;
-    sh.psq[jg][tl] = sq;
-    ConsumerBar()();
-    if (tid < kSlice) {
-      float a0 = 0.f, c0 = 0.f;
-#pragma unroll
-      for (int r = 0; r < 16; ++r) {
-        a0 += sh.psk[r][tid];
-        c0 += sh.psq[r][tid];
-      }
-      sh.sk_s[tid] = a0;
-      sh.sq_s[tid] = c0;
-    }
-    if (tid == 0) sh.kq_s = sh.red[0] + sh.red[1] + sh.red[2] + sh.red[3];
-    ConsumerBar()();
-    const float dv = beta * (sh.vs[tl] - g * sh.sk_s[tl]);
-#pragma unroll
-    for (int jj = 0; jj < 8; ++jj) S[(size_t)(jg * 8 + jj) * kGdnDim] = g * sv[jj] + dv * sh.ks[jg * 8 + jj];
-    if (jg == 0) st_tag(ph.yt + h * kGdnDim + t0 + tl, g * sh.sq_s[tl] + dv * sh.kq_s, tg.of(ph.tout));
-  }
-};
-
 __device__ __forceinline__ void tk_consume(const TkArgs& A, TkShared& sh) {
+  TkBarrier bar{A.barrier, 0ull, A.wait_limit_ns, A.wait_extra};
   uint32_t g = 0;
-  pdl_wait();  // the previous launch's outputs, control words and states are complete
-  TkTags tg;
-  tg.epoch = *A.epoch;
-  tg.flip = A.wait_extra ? 0x80u : 0u;
-  const uint32_t cnt = A.ctl->count + 1u;  // this token's conv ring counter
+  pdl_wait();  // the previous token's control words and states are complete
 #pragma unroll 1
   for (int p = 0; p < A.nphases; ++p) {
     const TkPhase& ph = A.phases[p];
     if (ph.kind == kTkGemv) {
       TkPre pre;
       tk_prefetch(ph, pre);
-      const float inv = tk_stage(ph, A, sh, pre, tg);
-      tk_gemv(ph, A, sh, g, inv, tg);
+      if (p > 0) bar.wait(A.err);
+      const float inv = tk_stage(ph, A, sh, pre);
+      tk_gemv(ph, A, sh, g, inv);
     } else if (ph.kind == kTkGdn) {
       const bool mine = (int)blockIdx.x < kGdnItemsPerSeq;
-      TkGdn it;
-      if (mine) it.prefetch(ph.gdn, blockIdx.x);
-      ConsumerBar()();  // the previous phase's dot products are done with the shared scratch
-      if (mine) it.run(ph, cnt, *reinterpret_cast<GdnShared*>(sh.xs), A, tg);
+      GdnItem it;
+      if (mine) it.prefetch(ph.gdn, blockIdx.x);  // the state slice, before the barrier
+      bar.wait(A.err);
+      if (mine) it.run_with(ph.gdn, *reinterpret_cast<GdnShared*>(sh.xs), ConsumerBar());
     }
+    if (p + 1 < A.nphases) bar.arrive();
   }
-  // The last CTA to finish a token's last launch advances the tag epoch and the conv counter (no
-  // CTA of this launch reads either after it started; the next launch reads them after its
-  // dependency wait). It also clears the exit counter for the next launch.
-  ConsumerBar()();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    if (atomicAdd(A.barrier + 1, 1ull) == gridDim.x - 1) {
-      if (A.last_of_token) {
-        *A.epoch += 1u;
-        A.ctl->count += 1u;
-      }
-      A.barrier[1] = 0ull;
-      __threadfence();
-    }
-  }
+  bar.exit();
 }
 
 __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_constant__ TkArgs A) {

@@ -30,27 +30,12 @@ struct TkPhase {
   const float* zgate = nullptr;   // kProGdnGate: z vector [2048]
   // GDN mixer.
   dev::GdnArgs gdn{};
-  // Vectors passed between phases of one token are tagged (flag in data): 8-byte words, the f32
-  // value in the low half and tag(q) = (epoch << 8) | (q + 1) in the high half, q the global
-  // index of the writing phase within the token. A reader polls the words until they carry the
-  // tag it expects, so no grid barrier separates the phases. Null pointers / -1: plain floats.
-  const unsigned long long* xt = nullptr;  // tagged input (x of the prologue; GDN: proj)
-  int tin = -1;                            // phase whose tag the input carries
-  unsigned long long* yt = nullptr;        // tagged output (GDN: raw)
-  int tout = -1;                           // this phase's global index (tag of its outputs)
-  const unsigned long long* rt = nullptr;  // accumulate epilogue: tagged residual (h)
-  int tres = -1;
-  const unsigned long long* zt = nullptr;  // gated GDN norm: tagged z
-  int tz = -1;
-  unsigned long long* ht = nullptr;        // embedding prologue: tagged h receives the row
 };
 
 struct TkArgs {
   const TkPhase* phases = nullptr;  // device array
   int nphases = 0;
   SeqCtl* ctl = nullptr;
-  uint32_t* epoch = nullptr;        // token counter of the tags, advanced after a token's last launch
-  int last_of_token = 0;            // this launch ends the token: advance epoch and ctl->count
   Mat embed;                        // layer-0 prologue: embedding row of ctl->token
   float* h_out = nullptr;           // receives the embedding row (the residual stream)
   float* part_val = nullptr;        // greedy pick: per-CTA best value / index, ticket
