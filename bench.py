@@ -430,6 +430,54 @@ def micro(args):
         print(json.dumps(line), flush=True)
 
 
+def other_config_run(torch, qne, synth, cfg_n: int, rank: int, world: int, barrier, max_over_ranks, warmup: int):
+    """benchmark configs 1 (0.8B f16, 128-token prompt, 128 greedy steps) and 3 (2B int4 group-64,
+    1024-token prompt, 256 steps) on each rank's own replica, on the default launch path: the prompt
+    through qne_prefill_chunk, `warmup` untimed steps, a restore, then the config's steps timed with
+    CUDA events (max over ranks). Returns the sub-object of the JSON line (rank 0) or None."""
+    info = synth.baseline_config(cfg_n)
+    s = synth.build_config(cfg_n)
+    model = qne.Model(s.index_json, s.weights, device=torch.cuda.current_device())
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    model.set_stream(stream.cuda_stream)
+    steps, prompt_len = info["steps"], info["prompt"]
+    model.prefill_chunk(synth.prompt_ids(prompt_len, rank_seed(cfg_n, rank)), 0, True)
+    model.snapshot()
+    model.sync()
+    if warmup:
+        model.decode_async(warmup)
+        model.sync()
+    model.restore()
+    model.sync()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda._sleep(20_000_000)
+    e0.record(stream)
+    model.decode_async(steps)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    kv_bytes = 2048 * (model.layers // 4) * (prompt_len + steps / 2)
+    state_bytes = (model.layers - model.layers // 4) * (2 * 16 * 128 * 128 * 4 + 2 * 4 * 6144 * 4)
+    tok_bytes = model.weight_bytes + kv_bytes + state_bytes + model.vocab * 4
+    path = model.path
+    model.close()
+    if rank != 0:
+        return None
+    peak, kind = peaks()
+    tps = aggregate_rate(world, steps, ms)
+    gbs = tok_bytes / (ms / steps * 1e-3) / 1e9
+    size_name = {"0.8b": "0.8B", "2b": "2B"}[info["size"]]
+    return {"workload": f"config {cfg_n}: Qwen3.5-{size_name}-shaped {info['kind']} hybrid decoder (synthetic, seed "
+                        f"{info['seed']}), B=1 per GPU, {prompt_len}-token prompt, {steps} greedy decode steps",
+            "value": round(tps, 2), "unit": "tok/s", "n_gpus": world, "ms_per_step": round(ms / steps, 4),
+            "launch_path": path, "bytes_per_token": int(tok_bytes),
+            "step_roofline": {"achieved_gbs": round(gbs, 1), "peak": peak, "frac": round(gbs / peak, 4),
+                              "peak_source": kind}}
+
+
 def batched_run(torch, qne, synth, rank: int, world: int, barrier, max_over_ranks, warmup: int,
                 steps: int = 64, batch: int = 32):
     """benchmark config 4: Qwen3.5-0.8B-shaped f16 (seed 3), `batch` independent sequences per GPU
@@ -502,6 +550,7 @@ def main():
                                                      "step4 = the small decode workload of the ncu captures; gemm1 = one batched GEMM shape; "
                                                      "prefill = the last 64-token chunk of the bench prompt")
     ap.add_argument("--no-batched", action="store_true", help="skip the config-4 batched decode run")
+    ap.add_argument("--no-other-configs", action="store_true", help="skip the config-1 and config-3 decode runs")
     ap.add_argument("--batched-only", action="store_true", help="run only the config-4 batched decode (profiling)")
     ap.add_argument("--batched-steps", type=int, default=64)
     ap.add_argument("--path", default="auto", choices=["auto", "fused", "split"],
@@ -639,6 +688,29 @@ def main():
     e2e_sampled_s = max_over_ranks(time.perf_counter() - t0)
     sampler.close()
 
+    # the other launch paths on the same state and steps (informational; `value` is the default path)
+    paths = {model.path: round(aggregate_rate(world, steps, ms), 2)}
+    for other_path in ("token", "layers"):
+        if other_path == model.path:
+            continue
+        default_path = model.path
+        try:
+            model.set_path(other_path)
+        except qne.QneError:
+            continue
+        model.restore()
+        model.sync()
+        barrier()
+        torch.cuda.synchronize()
+        q0, q1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(20_000_000)
+        q0.record(stream)
+        model.decode_async(steps)
+        q1.record(stream)
+        torch.cuda.synchronize()
+        paths[other_path] = round(aggregate_rate(world, steps, max_over_ranks(q0.elapsed_time(q1))), 2)
+        model.set_path(default_path)
+
     # the dominant kernel, timed live
     gemv_ms, gemv_bytes = time_gemv_family(model, torch)
     peak, peak_kind = peaks()
@@ -650,6 +722,11 @@ def main():
     batched = None
     if not args.no_batched:
         batched = batched_run(torch, qne, synth, rank, world, barrier, max_over_ranks, args.warmup, args.batched_steps)
+    others = {}
+    if not args.no_other_configs and cfg_n == 2:
+        for other in (1, 3):
+            others[f"config{other}"] = other_config_run(torch, qne, synth, other, rank, world, barrier, max_over_ranks,
+                                                        args.warmup)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -702,9 +779,11 @@ def main():
                               "frac": round(tok_bytes * value / world / 1e9 / peak, 4)},
             "gpu_launches": int(launches),
             "dispatches_per_token": dispatches,
+            "launch_paths_tok_s": paths,
             "clocks": clk,
             "cpu_baseline": cpu,
             "batched": batched,
+            **others,
             "prefill": {"tokens": prompt_len, "ms": round(prefill_ms, 3),
                         "tok_per_s": round(aggregate_rate(world, prompt_len, prefill_ms), 1),
                         "path": (f"batched: {chunk}-token chunks, tensor-core GEMMs, chunked GDN scan"
