@@ -196,7 +196,8 @@ def test_launch_paths_agree(cuda):
     m.reset()
     m.prefill(prompt[:40])
     m.set_path("token")
-    m.prefill(prompt[40:55])
+    for i in range(40, 55):  # one token per step on the token kernel (Model::step)
+        m.step(int(prompt[i]), i)
     m.set_fused(False)
     m.prefill_chunk(prompt[55:], 55, True)
     logits_close(m.logits(), out["operations"][0].astype(np.float64))
