@@ -306,7 +306,8 @@ QNE_API qne_status qne_gemv(const qne_matrix* m, const float* x, float* y, int e
  * rows dealt over all warps; int4: the warp's whole share of weights, scales and zero points
  * loaded into registers before the dependency wait, k <= 8192 (4096 with SwiGLU), else the
  * tensor-core kernel), 1 = row-group register streaming, 2 = bulk-copy (TMA) shared-memory ring
- * (f16, k % 512 == 0), 3 = tensor-core int4 kernel (int4, k % 256 == 0). ctas_per_sm (1 or 2)
+ * with a producer warp per CTA (f16, k % 256 == 0, k <= 6144, k <= 4096 for SwiGLU),
+ * 3 = tensor-core int4 kernel (int4, k % 256 == 0). ctas_per_sm (1 or 2)
  * sizes the grid of variant 1. */
 QNE_API qne_status qne_gemv_ex(const qne_matrix* m, const float* x, float* y, int epilogue, int variant,
                                int ctas_per_sm, void* stream);

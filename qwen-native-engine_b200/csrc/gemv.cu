@@ -35,201 +35,328 @@ namespace {
 // ------------------------------------------------------------------------------------------
 // f16 GEMV streamed by the bulk-copy (TMA) unit.
 //
-// A CTA owns a contiguous range of output rows. Its rows are cut into groups (16 physical rows:
-// 16 plain rows, or 8 gate + 8 up rows for SwiGLU) and each group into 512-element segments;
-// one stage = one group x one segment = 16 KB in shared memory, and a ring of kStagesT stages
-// is kept in flight by one producer thread issuing 1 KB bulk copies (one per row) that complete
-// on the stage's mbarrier. The producer starts before the programmatic-launch wait: weights do
-// not depend on the previous kernel, so up to 80 KB per CTA is already arriving while the
-// previous kernel finishes. Eight consumer warps stage x, then each takes two row slots of every
-// stage (x is read once from shared memory for both), accumulates in f32 across the segments of
-// its rows, and releases the stage.
+// A CTA owns a contiguous range of output rows [r0, r1), so its share of the matrix is one
+// contiguous byte range (two for SwiGLU: its gate rows and its up rows). The range is cut into
+// pieces of `per` whole rows (SwiGLU: per gate rows, then the per matching up rows), at most
+// 16 KB, and one producer thread bulk-copies the pieces in order into a ring of shared-memory
+// slots (one or two copies per piece, completing on the slot's mbarrier). Consumer warp w owns
+// slot w and takes every NS-th piece (NS = the slot count, 5 or 6 by k; the other consumer warps
+// only stage x): wait for the slot, dot its rows with x (staged once in shared memory as two
+// planes), release the slot, and lane r applies the epilogue to output row r of the piece. A
+// slot has one consumer, so a warp waits on a slot's fills in order and a parity wait cannot
+// mistake an earlier, not yet completed fill for the one it wants. The producer starts before the programmatic-launch wait, since weights depend on
+// nothing: the first ring's worth of weights (~90 KB per SM) streams while the previous kernel
+// finishes. A CTA takes at most ~110 KB of shared memory and 32 K registers, so the next GEMV's
+// CTA fits beside it on the same SM and starts streaming as early.
 // ------------------------------------------------------------------------------------------
-constexpr int kSegE = 512;                 // elements per row segment
-constexpr int kSegB = kSegE * 2;           // bytes per row segment
-constexpr int kSlots = 16;                 // physical rows per stage
-constexpr int kStageB = kSlots * kSegB;    // 16 KB
-constexpr int kStagesT = 5;                // 80 KB ring
-constexpr int kConsumers = 8;
-constexpr int kThreadsT = (kConsumers + 1) * 32;
+constexpr int kRingConsumers = 8;
+constexpr int kThreadsT = (kRingConsumers + 1) * 32;
+constexpr uint32_t kPieceB = 16u << 10;    // ring slot
+constexpr int kMaxSlots = 8;  // at most one slot per consumer warp
+constexpr size_t kRingSmemCap = 110u << 10;  // per CTA: two CTAs share an SM
+constexpr int kRingHead = 256;               // barriers and reduction scratch before the ring
+constexpr int kRingMaxK = 6144;
 
-// Ring depth for a given k: 5 stages, 4 when x (and its planes) would keep two CTAs per SM
-// (the running kernel and the next one's early-streaming CTA) from fitting.
-__host__ __device__ inline int tma_stages(int k) { return k <= 4096 ? kStagesT : kStagesT - 1; }
-__host__ __device__ inline size_t tma_smem_bytes(int k) {
-  return 128 + (size_t)tma_stages(k) * kStageB + (size_t)k * 8;  // barriers, ring, x, x planes
+// Ring slots for a given k: what fits beside the x planes (k floats) under the per-CTA cap.
+__host__ __device__ inline int ring_slots(int k) {
+  const size_t left = kRingSmemCap - kRingHead - (size_t)k * 4;
+  const int s = (int)(left / kPieceB);
+  return s > kMaxSlots ? kMaxSlots : s;
+}
+__host__ __device__ inline size_t ring_smem_bytes(int k) {
+  return kRingHead + (size_t)ring_slots(k) * kPieceB + (size_t)k * 4;
+}
+
+struct RingHead {
+  unsigned long long full[kMaxSlots];
+  unsigned long long empty[kMaxSlots];
+  float red[kRingConsumers];
+  float bval[kRingConsumers];
+  uint32_t bidx[kRingConsumers];
+  uint32_t is_last;
+};
+static_assert(sizeof(RingHead) <= kRingHead, "ring header fits its reserved bytes");
+
+// This CTA's rows and their cut into pieces. `per` is the largest power of two (up to 8 rows, 4
+// for SwiGLU) that a slot holds and that still gives every slot's warp a piece when the CTA has
+// few rows.
+struct RingGeo {
+  int out_rows, r0, r1, per, R, npieces;
+  uint32_t rb;
+  __host__ __device__ void init(int rows, int k, bool sw, int cta, int ncta, int nslots) {
+    out_rows = sw ? rows / 2 : rows;
+    rb = (uint32_t)k * 2u;
+    r0 = (int)((long)out_rows * cta / ncta);
+    r1 = (int)((long)out_rows * (cta + 1) / ncta);
+    const int cap = (int)(kPieceB / (sw ? 2u * rb : rb));
+    const int want = (r1 - r0 + nslots - 1) / nslots;
+    const int mx = sw ? 4 : 8;
+    per = 1;
+    while (per * 2 <= cap && per * 2 <= want && per * 2 <= mx) per *= 2;
+    R = sw ? 2 * per : per;
+    npieces = r1 > r0 ? (r1 - r0 + per - 1) / per : 0;
+  }
+};
+
+// Stages x for the consumer warps as two planes (elements 0-3 and 4-7 of every 8-element
+// chunk; a lane's 16-byte reads of consecutive chunks are then conflict-free) with the prologue
+// applied. RMSNorm is folded: the planes hold x * norm_w and the returned factor
+// rsqrt(mean(x^2) + eps) scales the dot products in the epilogue (1 for the other prologues).
+// `nw` holds this thread's chunk of the norm weight, loaded before the dependency wait.
+template <int PRO>
+__device__ __forceinline__ float ring_stage(const GemvArgs& a, float* xs, RingHead& hd, const float (&nw)[8]) {
+  const int k = a.m.k, tid = threadIdx.x, nc = k / 8;
+  float* xlo = xs;
+  float* xhi = xs + k / 2;
+  constexpr bool kNorm = PRO == kProRmsNorm || PRO == kProEmbedNorm;
+  float ss = 0.f;
+  if (PRO == kProCopy) {
+#pragma unroll 1
+    for (int c = tid; c < nc; c += kRingConsumers * 32) {
+      *reinterpret_cast<float4*>(xlo + c * 4) = __ldcg(reinterpret_cast<const float4*>(a.x + c * 8));
+      *reinterpret_cast<float4*>(xhi + c * 4) = __ldcg(reinterpret_cast<const float4*>(a.x + c * 8 + 4));
+    }
+  } else {
+    // Norm prologues run on k <= 2048: one chunk per thread at most.
+    const int c = tid;
+    if (c < nc) {
+      float v[8];
+      if (PRO == kProEmbedNorm) {
+        uint32_t token = a.ctl->token;
+        if (token >= (uint32_t)a.embed.rows) token = (uint32_t)a.embed.rows - 1;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = deq_elem(a.embed, token, c * 8 + j);
+        if (blockIdx.x == 0) {
+          *reinterpret_cast<float4*>(a.h_out + c * 8) = make_float4(v[0], v[1], v[2], v[3]);
+          *reinterpret_cast<float4*>(a.h_out + c * 8 + 4) = make_float4(v[4], v[5], v[6], v[7]);
+        }
+      } else {
+        const float4 p = __ldcg(reinterpret_cast<const float4*>(a.x + c * 8));
+        const float4 q = __ldcg(reinterpret_cast<const float4*>(a.x + c * 8 + 4));
+        v[0] = p.x; v[1] = p.y; v[2] = p.z; v[3] = p.w;
+        v[4] = q.x; v[5] = q.y; v[6] = q.z; v[7] = q.w;
+      }
+      float cs = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) cs = fmaf(v[j], v[j], cs);
+      ss = cs;
+      if (kNorm) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] *= nw[j];
+      } else if (PRO == kProGdnGate) {
+        // k == 2048 and 256 threads: one chunk per thread, 16 consecutive threads per 128-wide head.
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) cs += __shfl_xor_sync(0xffffffffu, cs, o);
+        const float inv = rsqrtf(cs / (float)kGdnDim + a.eps);
+        const float4 z0 = __ldcg(reinterpret_cast<const float4*>(a.zgate + c * 8));
+        const float4 z1 = __ldcg(reinterpret_cast<const float4*>(a.zgate + c * 8 + 4));
+        const float z[8] = {z0.x, z0.y, z0.z, z0.w, z1.x, z1.y, z1.z, z1.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = v[j] * inv * silu(z[j]) * nw[j];
+      }
+      *reinterpret_cast<float4*>(xlo + c * 4) = make_float4(v[0], v[1], v[2], v[3]);
+      *reinterpret_cast<float4*>(xhi + c * 4) = make_float4(v[4], v[5], v[6], v[7]);
+    }
+    if (PRO == kProEmbedNorm && blockIdx.x == 0 && tid == 0) a.ctl->count += 1;  // conv windows
+    if (kNorm) {
+      const float t = warp_sum(ss);
+      if ((tid & 31) == 0) hd.red[tid >> 5] = t;
+    }
+  }
+  ConsumerSync()();
+  if (!kNorm) return 1.f;
+  float t = 0.f;
+#pragma unroll
+  for (int w = 0; w < kRingConsumers; ++w) t += hd.red[w];
+  return rsqrtf(t / (float)k + a.eps);
+}
+
+// Dot products of the R rows of one piece with x; every lane ends with the R sums.
+template <int R>
+__device__ __forceinline__ void ring_dot(const uint8_t* piece, const float* xs, int k, uint32_t rb, int lane,
+                                         float (&acc)[R]) {
+  float s[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) s[r] = 0.f;
+  const float* xlo = xs;
+  const float* xhi = xs + k / 2;
+  constexpr int U = R >= 4 ? 2 : 4;
+#pragma unroll U
+  for (int c = lane; c < k / 8; c += 32) {
+    float xv[8];
+    *reinterpret_cast<float4*>(xv) = *reinterpret_cast<const float4*>(xlo + c * 4);
+    *reinterpret_cast<float4*>(xv + 4) = *reinterpret_cast<const float4*>(xhi + c * 4);
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+      s[r] += dot_f16(*reinterpret_cast<const uint4*>(piece + (size_t)r * rb + (size_t)c * 16), xv);
+  }
+#pragma unroll
+  for (int r = 0; r < R; ++r) acc[r] = warp_sum(s[r]);
+}
+
+template <int N>
+__device__ __forceinline__ float ring_pick(const float (&v)[N], int i) {
+  float r = 0.f;
+#pragma unroll
+  for (int j = 0; j < N; ++j)
+    if (j == i) r = v[j];
+  return r;
+}
+
+__device__ __forceinline__ bool ring_better(float v, uint32_t i, float bv, uint32_t bi) {
+  return i != 0xFFFFFFFFu && (bi == 0xFFFFFFFFu || v > bv || (v == bv && i < bi));
+}
+
+// The pieces of consumer warp w < NS (w, w + NS, ...: every fill of slot w), R rows each.
+template <int EPI, int R>
+__device__ __forceinline__ void ring_consume(const GemvArgs& a, const RingGeo& geo, uint8_t* ring, int NS,
+                                             const float* xs, RingHead& hd, float inv, float& best_v,
+                                             uint32_t& best_i) {
+  constexpr bool SW = (EPI == kSwiGlu);
+  constexpr int OUT = SW ? R / 2 : R;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int k = a.m.k;
+#pragma unroll 1
+  for (int j = warp; j < geo.npieces; j += NS) {
+    const int slot = warp;
+    const int row0 = geo.r0 + j * geo.per;
+    const int n = min(geo.per, geo.r1 - row0);
+    const float resid = (EPI == kAccumulate && lane < n) ? __ldcg(a.y + row0 + lane) : 0.f;
+    if (!mbar_wait(smem_u32(&hd.full[slot]), (uint32_t)(j / NS) & 1u, a.err)) return;
+    float acc[R];
+    ring_dot<R>(ring + (size_t)slot * kPieceB, xs, k, geo.rb, lane, acc);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(&hd.empty[slot]));
+    if (lane < n) {
+      const int row = row0 + lane;
+      const float v = ring_pick<R>(acc, lane) * inv;
+      if (SW) {
+        a.y[row] = silu(v) * (ring_pick<R>(acc, OUT + lane) * inv);
+      } else if (EPI == kAccumulate) {
+        a.y[row] = resid + v;
+      } else {
+        a.y[row] = v;
+        if (EPI == kArgmax && v > -INFINITY && ring_better(v, (uint32_t)row, best_v, best_i)) {
+          best_v = v;
+          best_i = (uint32_t)row;
+        }
+      }
+    }
+  }
 }
 
 template <int PRO, int EPI>
 __global__ void __launch_bounds__(kThreadsT, 2) gemv_tma_kernel(const GemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw);
-  uint64_t* empty = full + kStagesT;  // barrier slots for the deepest ring
-  uint8_t* ring = smem_raw + 128;
-  const int NS = tma_stages(a.m.k);
-  float* xs = reinterpret_cast<float*>(ring + (size_t)NS * kStageB);
-  __shared__ float red[8];
-  __shared__ float bval[8];
-  __shared__ uint32_t bidx[8];
-  __shared__ uint32_t is_last;
-
-  constexpr bool SW = (EPI == kSwiGlu);
-  constexpr int GROUP_OUT = SW ? kSlots / 2 : kSlots;  // output rows per group
+  RingHead& hd = *reinterpret_cast<RingHead*>(smem_raw);
+  uint8_t* ring = smem_raw + kRingHead;
   const int k = a.m.k;
-  const int nseg = k / kSegE;
-  const int out_rows = SW ? a.m.rows / 2 : a.m.rows;
-  const long half = SW ? a.m.rows / 2 : 0;
-  const size_t rb = (size_t)k * 2;
-  const long r0 = (long)blockIdx.x * out_rows / gridDim.x;
-  const long r1 = (long)(blockIdx.x + 1) * out_rows / gridDim.x;
-  const int ngroups = (int)((r1 - r0 + GROUP_OUT - 1) / GROUP_OUT);
-  const int nstages = ngroups * nseg;
-  const uint8_t* W = static_cast<const uint8_t*>(a.m.w);
+  const int NS = ring_slots(k);
+  float* xs = reinterpret_cast<float*>(ring + (size_t)NS * kPieceB);
+  constexpr bool SW = (EPI == kSwiGlu);
+  RingGeo geo;
+  geo.init(a.m.rows, k, SW, blockIdx.x, gridDim.x, NS);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < NS; ++i) {
-      mbar_init(smem_u32(full + i), 1);
-      mbar_init(smem_u32(empty + i), kConsumers);
+      mbar_init(smem_u32(&hd.full[i]), 1);
+      mbar_init(smem_u32(&hd.empty[i]), 1);
     }
     fence_barrier_init();
   }
   __syncthreads();
   pdl_launch();
 
-  if (warp == kConsumers) {
-    // ---------------- producer ----------------
-    // lane 0 arms the stage's barrier with the byte count, then lanes 0..15 issue one row
-    // segment each (gate and up segments for SwiGLU), so a stage costs one issue round.
-    for (int q = 0; q < nstages; ++q) {
-      const int slot = q % NS;
-      bool ok = true;
-      if (q >= NS) {
-        if (lane == 0) ok = mbar_wait(smem_u32(empty + slot), ((q / NS) - 1) & 1, a.err);
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-      }
-      if (!ok) break;
-      const int grp = q / nseg, sg = q % nseg;
-      const long gr0 = r0 + (long)grp * GROUP_OUT;
-      const int valid = (int)min((long)GROUP_OUT, r1 - gr0);
-      const uint32_t fb = smem_u32(full + slot);
-      if (lane == 0) mbar_arrive_expect_tx(fb, (uint32_t)(valid * (SW ? 2 : 1)) * kSegB);
-      __syncwarp();
-      const uint32_t dst = smem_u32(ring + (size_t)slot * kStageB);
-      if (lane < valid) {
-        if (SW) {
-          bulk_g2s(dst + (2 * lane) * kSegB, W + (size_t)(gr0 + lane) * rb + (size_t)sg * kSegB, kSegB, fb);
-          bulk_g2s(dst + (2 * lane + 1) * kSegB, W + (size_t)(half + gr0 + lane) * rb + (size_t)sg * kSegB, kSegB, fb);
-        } else {
-          bulk_g2s(dst + lane * kSegB, W + (size_t)(gr0 + lane) * rb + (size_t)sg * kSegB, kSegB, fb);
-        }
-      }
+  if (warp == kRingConsumers) {
+    // ---------------- producer: lane 0 ----------------
+    if (lane != 0) return;
+    const uint8_t* W = static_cast<const uint8_t*>(a.m.w);
+    int issued = 0;
+#pragma unroll 1
+    for (int j = 0; j < geo.npieces; ++j, ++issued) {
+      const int slot = j % NS;
+      if (j >= NS && !mbar_wait(smem_u32(&hd.empty[slot]), (uint32_t)(j / NS - 1) & 1u, a.err)) break;
+      const int row0 = geo.r0 + j * geo.per;
+      const int n = min(geo.per, geo.r1 - row0);
+      const uint32_t bytes = (uint32_t)n * geo.rb;
+      const uint32_t fb = smem_u32(&hd.full[slot]);
+      const uint32_t dst = smem_u32(ring + (size_t)slot * kPieceB);
+      mbar_arrive_expect_tx(fb, SW ? 2u * bytes : bytes);
+      bulk_g2s(dst, W + (size_t)row0 * geo.rb, bytes, fb);
+      if (SW) bulk_g2s(dst + (uint32_t)geo.per * geo.rb, W + (size_t)(geo.out_rows + row0) * geo.rb, bytes, fb);
+    }
+    // Every copy lands before the CTA exits (bounded; normally the consumers saw them all).
+#pragma unroll 1
+    for (int s = 0; s < NS && s < issued; ++s) {
+      const int fills = (issued - s + NS - 1) / NS;
+      mbar_wait(smem_u32(&hd.full[s]), (uint32_t)(fills - 1) & 1u, a.err);
     }
     return;
   }
 
   // ---------------- consumers ----------------
-  pdl_wait();
-  stage_x<PRO>(a, xs, red, ConsumerSync());
-  // Repack x as two planes (elements 0-3 and 4-7 of every 8-element chunk) so that a warp's
-  // 16-byte loads of consecutive chunks hit consecutive addresses (no bank conflicts).
-  float* xp = xs + k;  // [2][k/2]
-  for (int c = threadIdx.x; c < k / 8; c += 256) {
-    const float4 lo4 = *reinterpret_cast<const float4*>(xs + c * 8);
-    const float4 hi4 = *reinterpret_cast<const float4*>(xs + c * 8 + 4);
-    *reinterpret_cast<float4*>(xp + c * 4) = lo4;
-    *reinterpret_cast<float4*>(xp + k / 2 + c * 4) = hi4;
+  float nw[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) nw[j] = 1.f;
+  if (PRO != kProCopy && threadIdx.x < k / 8) {
+    // The norm weight depends on nothing: load it before the dependency wait.
+    const float* src = (PRO == kProGdnGate) ? a.norm_w + ((threadIdx.x * 8) & (kGdnDim - 1)) : a.norm_w + threadIdx.x * 8;
+    const float4 p = __ldg(reinterpret_cast<const float4*>(src));
+    const float4 q = __ldg(reinterpret_cast<const float4*>(src + 4));
+    nw[0] = p.x; nw[1] = p.y; nw[2] = p.z; nw[3] = p.w;
+    nw[4] = q.x; nw[5] = q.y; nw[6] = q.z; nw[7] = q.w;
   }
-  ConsumerSync()();
+  pdl_wait();
+  const float inv = ring_stage<PRO>(a, xs, hd, nw);
 
   float best_v = -INFINITY;
   uint32_t best_i = 0xFFFFFFFFu;
-  float acc0 = 0.f, acc1 = 0.f;
-  bool ok = true;
-  for (int q = 0; q < nstages && ok; ++q) {
-    const int slot = q % NS;
-    ok = mbar_wait(smem_u32(full + slot), (q / NS) & 1, a.err);
-    if (!ok) break;
-    const int grp = q / nseg, sg = q % nseg;
-    const long gr0 = r0 + (long)grp * GROUP_OUT;
-    const uint8_t* st = ring + (size_t)slot * kStageB;
-    // row slots 2w and 2w+1 of this stage
-    const int s0 = 2 * warp, s1 = 2 * warp + 1;
-    const long o0 = SW ? gr0 + warp : gr0 + s0;  // output row of slot s0
-    const long o1 = SW ? o0 : gr0 + s1;
-    const bool v0 = o0 < r1, v1 = o1 < r1;
-    const float* xlo = xp + sg * (kSegE / 2);
-    const float* xhi = xp + k / 2 + sg * (kSegE / 2);
-#pragma unroll
-    for (int m = 0; m < kSegE / 256; ++m) {
-      const int c = lane + 32 * m;
-      float xv[8];
-      *reinterpret_cast<float4*>(xv) = *reinterpret_cast<const float4*>(xlo + c * 4);
-      *reinterpret_cast<float4*>(xv + 4) = *reinterpret_cast<const float4*>(xhi + c * 4);
-      if (v0) acc0 += dot_f16(*reinterpret_cast<const uint4*>(st + s0 * kSegB + c * 16), xv);
-      if (v1) acc1 += dot_f16(*reinterpret_cast<const uint4*>(st + s1 * kSegB + c * 16), xv);
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(smem_u32(empty + slot));
-    if (sg == nseg - 1) {
-      const float t0 = warp_sum(acc0), t1 = warp_sum(acc1);
-      acc0 = acc1 = 0.f;
-      if (SW) {
-        if (v0 && lane == 0) a.y[o0] = silu(t0) * t1;
-      } else {
-        if (EPI == kArgmax) {
-          if (v0 && t0 > -INFINITY && (t0 > best_v || (t0 == best_v && (uint32_t)o0 < best_i))) {
-            best_v = t0;
-            best_i = (uint32_t)o0;
-          }
-          if (v1 && t1 > -INFINITY && (t1 > best_v || (t1 == best_v && (uint32_t)o1 < best_i))) {
-            best_v = t1;
-            best_i = (uint32_t)o1;
-          }
-        }
-        if (lane == 0) {
-          if (EPI == kAccumulate) {
-            if (v0) a.y[o0] += t0;
-            if (v1) a.y[o1] += t1;
-          } else {
-            if (v0) a.y[o0] = t0;
-            if (v1) a.y[o1] = t1;
-          }
-        }
-      }
-    }
+  if (warp < NS) switch (geo.R) {
+    case 1: ring_consume<EPI, 1>(a, geo, ring, NS, xs, hd, inv, best_v, best_i); break;
+    case 2: ring_consume<EPI, 2>(a, geo, ring, NS, xs, hd, inv, best_v, best_i); break;
+    case 4: ring_consume<EPI, 4>(a, geo, ring, NS, xs, hd, inv, best_v, best_i); break;
+    default: ring_consume<EPI, 8>(a, geo, ring, NS, xs, hd, inv, best_v, best_i); break;
   }
 
   if (EPI == kArgmax) {
+    // Greedy pick: warp best, CTA best, then the last CTA reduces across CTAs.
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best_v, o);
+      const uint32_t oi = __shfl_xor_sync(0xffffffffu, best_i, o);
+      if (ring_better(ov, oi, best_v, best_i)) {
+        best_v = ov;
+        best_i = oi;
+      }
+    }
     if (lane == 0) {
-      bval[warp] = best_v;
-      bidx[warp] = best_i;
+      hd.bval[warp] = best_v;
+      hd.bidx[warp] = best_i;
     }
     ConsumerSync()();
     if (threadIdx.x == 0) {
       float v = -INFINITY;
       uint32_t ix = 0xFFFFFFFFu;
-      for (int w = 0; w < kConsumers; ++w) {
-        if (bidx[w] != 0xFFFFFFFFu && (ix == 0xFFFFFFFFu || bval[w] > v || (bval[w] == v && bidx[w] < ix))) {
-          v = bval[w];
-          ix = bidx[w];
+      for (int w = 0; w < kRingConsumers; ++w)
+        if (ring_better(hd.bval[w], hd.bidx[w], v, ix)) {
+          v = hd.bval[w];
+          ix = hd.bidx[w];
         }
-      }
       a.part_val[blockIdx.x] = v;
       a.part_idx[blockIdx.x] = ix;
       __threadfence();
-      const uint32_t t = atomicAdd(a.ticket, 1u);
-      is_last = (t == gridDim.x - 1) ? 1u : 0u;
+      hd.is_last = (atomicAdd(a.ticket, 1u) == gridDim.x - 1) ? 1u : 0u;
     }
     ConsumerSync()();
-    if (is_last && warp == 0) {
+    if (hd.is_last && warp == 0) {
       __threadfence();
       float v = -INFINITY;
       uint32_t ix = 0xFFFFFFFFu;
       for (int b = lane; b < (int)gridDim.x; b += 32) {
         const float bv = __ldcg(a.part_val + b);
         const uint32_t bi = __ldcg(a.part_idx + b);
-        if (bi != 0xFFFFFFFFu && (ix == 0xFFFFFFFFu || bv > v || (bv == v && bi < ix))) {
+        if (ring_better(bv, bi, v, ix)) {
           v = bv;
           ix = bi;
         }
@@ -238,7 +365,7 @@ __global__ void __launch_bounds__(kThreadsT, 2) gemv_tma_kernel(const GemvArgs a
       for (int o = 16; o > 0; o >>= 1) {
         const float ov = __shfl_xor_sync(0xffffffffu, v, o);
         const uint32_t oi = __shfl_xor_sync(0xffffffffu, ix, o);
-        if (oi != 0xFFFFFFFFu && (ix == 0xFFFFFFFFu || ov > v || (ov == v && oi < ix))) {
+        if (ring_better(ov, oi, v, ix)) {
           v = ov;
           ix = oi;
         }
@@ -912,16 +1039,24 @@ cudaError_t launch_q4_mma(GemvArgs a, cudaStream_t stream, bool pdl) {
   return launch_ex(kernel, dim3(grid), dim3(kThreads), smem, stream, pdl, a);
 }
 
+// Whether the bulk-copy kernel takes this shape: a piece slot holds a row (SwiGLU: a gate and an
+// up row), x fits beside the ring, and the norm prologues stage one chunk per consumer thread.
+bool ring_fits(const GemvArgs& a) {
+  const int k = a.m.k;
+  if (a.m.kind != kF16 || k % 256 || k > kRingMaxK) return false;
+  if (a.epi == kSwiGlu && 4 * k > (int)kPieceB) return false;
+  if (a.pro != kProCopy && k > 8 * kRingConsumers * 32) return false;
+  return true;
+}
+
 template <int PRO, int EPI>
 cudaError_t launch_tma(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   auto kernel = gemv_tma_kernel<PRO, EPI>;
-  const size_t smem = tma_smem_bytes(a.m.k);
+  const size_t smem = ring_smem_bytes(a.m.k);
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const int out_rows = (EPI == kSwiGlu) ? a.m.rows / 2 : a.m.rows;
-  const int per_group = (EPI == kSwiGlu) ? kSlots / 2 : kSlots;
-  int grid = (out_rows + per_group - 1) / per_group;
-  if (grid > kNumSms) grid = kNumSms;
+  int grid = out_rows < kNumSms ? out_rows : kNumSms;  // one CTA per SM, at least a row each
   if (grid < 1) grid = 1;
   return launch_ex(kernel, dim3(grid), dim3(kThreadsT), smem, stream, pdl, a);
 }
@@ -930,7 +1065,7 @@ template <int KIND>
 cudaError_t launch_kind(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   // Variant 2 (bulk-copy ring) on request; auto picks the register-streamed kernel, which
   // measures faster on B200 for every decode shape.
-  if (KIND == kF16 && a.variant == 2 && a.m.k % kSegE == 0) {
+  if (KIND == kF16 && a.variant == 2 && ring_fits(a)) {
 #define QNE_TCOMBO(P, E) \
     if (a.pro == P && a.epi == E) return launch_tma<P, E>(a, stream, pdl);
     QNE_TCOMBO(kProCopy, kStore)
@@ -1018,7 +1153,8 @@ const char* check_gemv(const GemvArgs& a) {
   const Mat& m = a.m;
   if (a.variant < 0 || a.variant > 3) return "unknown GEMV variant";
   if (a.variant == 3 && (m.kind == kF16 || m.k % 256)) return "the tensor-core GEMV needs int4 weights and k % 256 == 0";
-  if (a.variant == 2 && (m.kind != kF16 || m.k % 512)) return "the bulk-copy GEMV needs f16 weights and k % 512 == 0";
+  if (a.variant == 2 && !ring_fits(a))
+    return "the bulk-copy GEMV needs f16 weights, k % 256 == 0 and k <= 6144 (4096 with SwiGLU, 2048 with a norm prologue)";
   if (!m.w || m.rows <= 0 || m.k <= 0) return "matrix has no data or an empty shape";
   if (m.kind == kF16) {
     if (m.k % 256) return "f16 GEMV needs k % 256 == 0";

@@ -127,6 +127,33 @@ def test_gemv_epilogues_and_tails(cuda, kind, epilogue, rows, k):
     assert rc.rel_err(got, want) < 1e-4
 
 
+@pytest.mark.parametrize("variant", [1, 2])
+@pytest.mark.parametrize("epilogue", ["store", "accumulate", "swiglu"])
+@pytest.mark.parametrize("rows,k", [(12288, 2048), (2048, 6144), (2 * 3584, 1024), (300, 6144), (2, 256), (16, 256)])
+def test_gemv_variants_match_the_oracle(cuda, variant, epilogue, rows, k):
+    """The selectable f16 kernels (1: the older register kernel, 2: the bulk-copy ring with one
+    producer warp per CTA) compute what the default kernel computes, tails and pieces included."""
+    if epilogue == "swiglu" and 4 * k > 16384 and variant == 2:
+        pytest.skip("a SwiGLU row pair of this width does not fit a ring slot")
+    rng = np.random.default_rng(rows * 7 + k)
+    mat = make_matrix("f16", rows, k, rng)
+    x = rng.standard_normal(k).astype(np.float32)
+    out_rows = rows // 2 if epilogue == "swiglu" else rows
+    y0 = rng.standard_normal(out_rows).astype(np.float32) if epilogue == "accumulate" else None
+    m = devmat("f16", rows, k, mat["w"])
+    y = dev(y0 if y0 is not None else np.zeros(out_rows, np.float32))
+    qne.gemv_ex(m, dev(x), y, epilogue, variant)
+    want = oracle_gemv("f16", mat, rows, k, x, epilogue, y0)
+    assert rc.rel_err(host(y), want) < 1e-4
+
+
+def test_gemv_ring_variant_rejects_wide_rows(cuda):
+    m = devmat("f16", 64, 8192, np.zeros(64 * 8192, np.float16))
+    with pytest.raises(qne.QneError) as e:
+        qne.gemv_ex(m, dev(np.zeros(8192, np.float32)), dev(np.zeros(64, np.float32)), "store", 2)
+    assert e.value.name == "EINVAL"
+
+
 @pytest.mark.parametrize("kind", ["f16", "q4g64", "q4"])
 def test_rmsnorm_prologue(cuda, kind):
     rng = np.random.default_rng(11)
