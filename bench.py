@@ -351,7 +351,7 @@ def micro(args):
                         keep.extend([w, sc, zp])
                 x = torch.randn(K, device="cuda")
                 y = torch.empty(N, device="cuda")
-                variants = [(0, 2), (1, 1), (2, 2)] if kind == "f16" else [(0, 2), (1, 1)]
+                variants = [(0, 2), (1, 1), (2, 2)] if kind == "f16" else [(0, 2), (1, 1), (4, 2)]
                 for var, cps in variants:
                     us = timed(lambda i: qne.gemv_ex(mats[i], x, y, "store", var, cps, stream=stream.cuda_stream),
                                copies, max(2, 64 // copies))

@@ -303,11 +303,12 @@ QNE_API qne_status qne_batch_sync(qne_batch* b, uint32_t timeout_ms);
 QNE_API qne_status qne_gemv(const qne_matrix* m, const float* x, float* y, int epilogue, void* stream);
 /* qne_gemv with an explicit kernel variant (the counterpart of the reference's per-matrix Tile
  * choice, kernels/src/lib.rs:39-64): 0 = automatic (f16: pipelined register streaming with
- * rows dealt over all warps; int4: the warp's whole share of weights, scales and zero points
- * loaded into registers before the dependency wait, k <= 8192 (4096 with SwiGLU), else the
- * tensor-core kernel), 1 = row-group register streaming, 2 = bulk-copy (TMA) shared-memory ring
- * with a producer warp per CTA (f16, k % 256 == 0, k <= 6144, k <= 4096 for SwiGLU),
- * 3 = tensor-core int4 kernel (int4, k % 256 == 0). ctas_per_sm (1 or 2)
+ * rows dealt over all warps; int4: the tensor-core kernel when k % 128 == 0, else the register
+ * pipeline), 1 = row-group register streaming, 2 = bulk-copy (TMA) shared-memory ring with a
+ * producer warp per CTA (f16, k % 256 == 0, k <= 6144, k <= 4096 for SwiGLU), 3 = tensor-core
+ * int4 kernel (int4, k % 128 == 0: mma.sync on nibbles widened in registers, the warp's share of
+ * weights, scales and zero points loaded before the dependency wait), 4 = int4 register pipeline
+ * (CUDA-core dot products, k % 256 == 0, k <= 8192, 4096 with SwiGLU). ctas_per_sm (1 or 2)
  * sizes the grid of variant 1. */
 QNE_API qne_status qne_gemv_ex(const qne_matrix* m, const float* x, float* y, int epilogue, int variant,
                                int ctas_per_sm, void* stream);

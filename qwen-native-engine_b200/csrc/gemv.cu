@@ -398,16 +398,26 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_pipe_kernel(const GemvArgs a
 // ------------------------------------------------------------------------------------------
 // int4 GEMV on the tensor cores (B = 1).
 //
-// A warp owns 16 weight rows (plus the 16 matching up rows for SwiGLU) and a slice of k. In
-// every 32-wide k step lane (g, t) loads one 32-bit word (8 nibbles, k = 32s + 8t .. +7) of rows
-// g and g + 8; (w >> 4i) & 0x000F000F | 0x64006400 turns nibbles i and i + 4 into the f16 pair
-// (1024 + n_i, 1024 + n_{i+4}), and subtracting 1024 leaves the exact integers. Two
-// mma.m16n8k16 per step multiply them with x, fed as column 0 = f16(x) and column 1 =
-// f16(x - f16(x)) (columns 2-7 zero); the k order inside a step is permuted identically for
-// weights and x. One step never crosses a quantization block, so after each block lane t = 0
-// (which holds columns 0 and 1) applies scale * (sum_k n_k x_k - zp * sum_k x_k) in f32.
-// Warps of a CTA split k when the matrix has few rows; partial sums meet in shared memory.
+// A warp owns a tile of 16 weight rows (plus the 16 matching up rows for SwiGLU) and a slice of
+// k cut into 128-wide segments (64 bytes of a row). For every segment lane (g, t) holds one
+// 16-byte load of rows g and g + 8: nibbles k = 128S + 32t .. +31, i.e. lane t's own
+// quantization block (block-32) or half of one (group-64). The warp's whole slice (up to 6
+// segments, 2-3 for SwiGLU), with each block's scale and zero-point words, is loaded into
+// registers before the wait on the previous kernel. (w >> 4i) & 0x000F000F | 0x64006400 turns
+// nibbles i and i + 4 into the f16 pair (1024 + n_i, 1024 + n_{i+4}); subtracting 1024 leaves the
+// exact integers. Each word of a lane feeds two mma.m16n8k16 (A slots 2t, 2t + 1, 2t + 8, 2t + 9
+// of lane t are its own nibbles, so no data moves between lanes; the k order inside an MMA is
+// permuted identically for weights and x). The 8 MMA columns keep the blocks apart: column
+// 2b + 0 / 1 carries f16(x) / f16(x - f16(x)) of the k values in block b of the segment and zero
+// elsewhere, so lane t ends each segment holding block t's exact sum_k n_k x_k for rows g and
+// g + 8 (columns 2t, 2t + 1), and applies scale * (sum - zp * sum_k x_k) in f32. Warps of a CTA
+// split k when the matrix has few rows; partial sums meet in shared memory.
 // ------------------------------------------------------------------------------------------
+constexpr int kQtSeg = 128;  // k per segment
+// Segments a warp holds in registers (block-32 SwiGLU keeps two: its scale and zero-point words
+// do not fit three within 128 registers).
+__host__ __device__ constexpr int qt_batch(int kind, bool swiglu) { return swiglu ? (kind == kQ4 ? 2 : 3) : 6; }
+
 __device__ __forceinline__ uint32_t nib_pair_f16(uint32_t w, int i) {
   uint32_t r;
   asm("lop3.b32 %0, %1, 0x000F000F, 0x64006400, 0xEA;" : "=r"(r) : "r"(w >> (4 * i)));  // (a & b) | c
@@ -442,14 +452,15 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4pipe_kernel(const GemvArgs
 
 template <int KIND, int PRO, int EPI>
 __global__ void __launch_bounds__(kThreads, 2) gemv_q4_mma_kernel(const GemvArgs a) {
-  extern __shared__ __align__(16) float xs[];  // [k] x, then [2][k/8] uint4 pair planes, then [k/32] block sums
-  __shared__ float red[kWarps];
-  __shared__ float bval[kWarps];
-  __shared__ uint32_t bidx[kWarps];
-  __shared__ uint32_t is_last;
+  // [k] x (f32), then the hi and lo f16 pair planes ([2][k / 8] uint4), then [k / QB] block sums
+  extern __shared__ __align__(16) float xs[];
+  __shared__ GemvShared sh;
   __shared__ float part[kWarps][2][16];
 
   constexpr bool SW = (EPI == kSwiGlu);
+  constexpr int PH = SW ? 2 : 1;
+  constexpr int PF = qt_batch(KIND, SW);       // segments held in registers per batch
+  constexpr int QB = (KIND == kQ4) ? 32 : 64;  // values per quantization block
   const int k = a.m.k;
   const int out_rows = SW ? a.m.rows / 2 : a.m.rows;
   const long half = SW ? a.m.rows / 2 : 0;
@@ -458,29 +469,66 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4_mma_kernel(const GemvArgs
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int rg = warp % RG, kg = warp / RG;
-  const int steps = k / 32;
-  const int blk_steps = (KIND == kQ4) ? 1 : 2;  // k32 steps per quantization block
-  // k slices of the warps cut at quantization-block boundaries
-  const int nblk = steps / blk_steps;
-  const int s0 = (kg * nblk / KG) * blk_steps, s1 = ((kg + 1) * nblk / KG) * blk_steps;
-  const uint32_t* W = static_cast<const uint32_t*>(a.m.w);
-  const size_t wpr = (size_t)k / 8;  // words per row
+  const int nseg = k / kQtSeg;
+  const int s0 = kg * nseg / KG, s1 = (kg + 1) * nseg / KG;
+  const uint8_t* W = static_cast<const uint8_t*>(a.m.w);
+  const size_t rb = (size_t)k / 2;
+  // Lane t's quantization block within a segment (block-32: t; group-64: t / 2, lanes 0-1 hold
+  // the two groups' sums) and whether it feeds x to the MMA: column g carries block g / 2,
+  // hi (g even) or lo (g odd).
+  const int qblk = (KIND == kQ4) ? t : (t >> 1);
+  const bool feeds = (g >> 1) == qblk;
+  const bool sums = (KIND == kQ4) || t < 2;
+
+  uint4 w[PF][PH][2];        // [segment][gate / up][row g, row g + 8]: 32 nibbles each
+  uint32_t sq[PF][PH][2];    // scale word of lane t's block
+  uint32_t zq[PF][PH][2];    // zero-point word of lane t's block
+
+  // Loads segments [sb, min(sb + PF, s1)) of tile `tile` (rows clamped into the matrix).
+  auto load = [&](int tile, int sb) {
+    const long rA = min((long)tile * 16 + g, (long)out_rows - 1);
+    const long rB = min((long)tile * 16 + g + 8, (long)out_rows - 1);
+#pragma unroll
+    for (int i = 0; i < PF; ++i) {
+      const int S = sb + i;
+#pragma unroll
+      for (int p = 0; p < PH; ++p)
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          w[i][p][r] = make_uint4(0u, 0u, 0u, 0u);
+          sq[i][p][r] = 0u;
+          zq[i][p][r] = 0u;
+        }
+      if (S >= s1) continue;
+#pragma unroll
+      for (int p = 0; p < PH; ++p)
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const long row = (r ? rB : rA) + (p ? half : 0);
+          w[i][p][r] = ld_stream(W + (size_t)row * rb + (size_t)S * (kQtSeg / 2) + (size_t)t * 16);
+          if (sums) {
+            if (KIND == kQ4) {  // f16 scale pair per 64 values, 8 zero-point nibbles per 256
+              sq[i][p][r] = __ldg(static_cast<const uint32_t*>(a.m.s) + row * (k / 64) + 2 * S + (t >> 1));
+              zq[i][p][r] = __ldg(static_cast<const uint32_t*>(a.m.z) + row * (k / 256) + (S >> 1));
+            } else {            // f16 scale and f16 zero point per 64 values
+              sq[i][p][r] = __ldg(static_cast<const uint16_t*>(a.m.s) + row * (k / 64) + 2 * S + t);
+              zq[i][p][r] = __ldg(static_cast<const uint16_t*>(a.m.z) + row * (k / 64) + 2 * S + t);
+            }
+          }
+        }
+    }
+  };
 
   pdl_launch();
-  if (warp == 0) {
-    // warm L2 with the first rows of this CTA while the previous kernel finishes
-    const long r0 = (long)blockIdx.x * RG * 16;
-    const long r1 = min(r0 + (long)RG * 16, (long)out_rows);
-    prefetch_rows(reinterpret_cast<const uint8_t*>(W), wpr * 4, r0, r1, kPrefetchBytes, lane);
-    if (SW) prefetch_rows(reinterpret_cast<const uint8_t*>(W), wpr * 4, half + r0, half + r1, kPrefetchBytes, lane);
-  }
+  const int first = blockIdx.x * RG + rg;
+  if (first < tiles) load(first, s0);  // weights depend on nothing: before the dependency wait
   pdl_wait();
-  stage_x<PRO>(a, xs, red);
-  // pair planes: for every 8-element group G, (x0,x4),(x1,x5),(x2,x6),(x3,x7) as f16x2, hi and lo
-  uint4* xq = reinterpret_cast<uint4*>(xs + k);
-  float* xsum = xs + k + k;  // after 2 * (k/8) uint4 = k floats
-  for (int G = threadIdx.x; G < k / 8; G += kThreads) {
-    const float* x8 = xs + G * 8;
+
+  stage_x<PRO>(a, xs, sh.red);
+  uint4* xq = reinterpret_cast<uint4*>(xs + k);  // [2][k / 8]: hi plane, then lo plane
+  float* xsum = xs + 2 * k;
+  for (int c = threadIdx.x; c < k / 8; c += kThreads) {
+    const float* x8 = xs + c * 8;
     uint32_t hw[4], lw[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -489,195 +537,132 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4_mma_kernel(const GemvArgs
       hw[i] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
       lw[i] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
     }
-    xq[G] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-    xq[k / 8 + G] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    xq[c] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    xq[k / 8 + c] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
   }
-  for (int b = threadIdx.x; b < k / 32; b += kThreads) {
+  for (int b = threadIdx.x; b < k / QB; b += kThreads) {
     float sum = 0.f;
-    for (int i = 0; i < 32; ++i) sum += xs[b * 32 + i];
+    for (int i = 0; i < QB; ++i) sum += xs[b * QB + i];
     xsum[b] = sum;
   }
   __syncthreads();
+  const uint2* xplane = reinterpret_cast<const uint2*>(xq + (g & 1) * (k / 8));
 
   float best_v = -INFINITY;
   uint32_t best_i = 0xFFFFFFFFu;
-  constexpr int U = SW ? 4 : 8;  // k32 steps loaded ahead
-  // CTA-uniform loop (every warp runs the same iterations: the k-group reduction synchronizes)
+  bool loaded = true;
+  // CTA-uniform loop (every warp runs the same iterations: the k-slice reduction synchronizes)
   for (int base = blockIdx.x * RG; base < tiles; base += gridDim.x * RG) {
     const int tile = base + rg;
     const bool tile_ok = tile < tiles;
-    const long rA = min((long)tile * 16 + g, (long)out_rows - 1);
-    const long rB = min((long)tile * 16 + g + 8, (long)out_rows - 1);
-    const uint32_t* wA = W + rA * wpr;
-    const uint32_t* wB = W + rB * wpr;
-    const uint32_t* uA = W + (half + rA) * wpr;
-    const uint32_t* uB = W + (half + rB) * wpr;
-    float totA = 0.f, totB = 0.f, utA = 0.f, utB = 0.f;
-    float c[4] = {0.f, 0.f, 0.f, 0.f}, cu[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int sb = s0; sb < s1; sb += U) {
-      uint32_t wa[U], wb[U], ua[U], ub[U];
+    float tot[PH][2];
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int s = sb + u;
-        const bool ok = s < s1;
-        wa[u] = ok ? __ldg(wA + s * 4 + t) : 0u;
-        wb[u] = ok ? __ldg(wB + s * 4 + t) : 0u;
-        if (SW) {
-          ua[u] = ok ? __ldg(uA + s * 4 + t) : 0u;
-          ub[u] = ok ? __ldg(uB + s * 4 + t) : 0u;
-        }
-      }
+    for (int p = 0; p < PH; ++p) tot[p][0] = tot[p][1] = 0.f;
+    for (int sb = s0; sb < s1; sb += PF) {
+      if (!loaded && tile_ok) load(tile, sb);
+      loaded = false;
+      if (!tile_ok) continue;
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int s = sb + u;
-        if (s >= s1) break;
-        uint4 xb = make_uint4(0u, 0u, 0u, 0u);
-        if (g < 2) xb = xq[(size_t)g * (k / 8) + s * 4 + t];
-        mma_f16(c, nib_pair_f16(wa[u], 0), nib_pair_f16(wb[u], 0), nib_pair_f16(wa[u], 1), nib_pair_f16(wb[u], 1),
-                xb.x, xb.y);
-        mma_f16(c, nib_pair_f16(wa[u], 2), nib_pair_f16(wb[u], 2), nib_pair_f16(wa[u], 3), nib_pair_f16(wb[u], 3),
-                xb.z, xb.w);
-        if (SW) {
-          mma_f16(cu, nib_pair_f16(ua[u], 0), nib_pair_f16(ub[u], 0), nib_pair_f16(ua[u], 1), nib_pair_f16(ub[u], 1),
-                  xb.x, xb.y);
-          mma_f16(cu, nib_pair_f16(ua[u], 2), nib_pair_f16(ub[u], 2), nib_pair_f16(ua[u], 3), nib_pair_f16(ub[u], 3),
-                  xb.z, xb.w);
-        }
-        if ((s + 1) % blk_steps == 0) {
-          if (t == 0) {
-            const int blk = s / blk_steps;  // quantization block (q4: 32 values, q4g64: 64 values)
-            const float xsb = (KIND == kQ4) ? xsum[s] : xsum[s - 1] + xsum[s];
-            float sa, za, sb2, zb;
-            if (KIND == kQ4) {
-              q4_scale_zp((const uint32_t*)a.m.s, (const uint32_t*)a.m.z, rA, k, blk, sa, za);
-              q4_scale_zp((const uint32_t*)a.m.s, (const uint32_t*)a.m.z, rB, k, blk, sb2, zb);
-            } else {
-              q4g64_scale_zp((const uint16_t*)a.m.s, (const uint16_t*)a.m.z, rA, k, blk, sa, za);
-              q4g64_scale_zp((const uint16_t*)a.m.s, (const uint16_t*)a.m.z, rB, k, blk, sb2, zb);
-            }
-            totA = fmaf(sa, (c[0] + c[1]) - za * xsb, totA);
-            totB = fmaf(sb2, (c[2] + c[3]) - zb * xsb, totB);
-            if (SW) {
-              float su, zu, sv, zv;
-              if (KIND == kQ4) {
-                q4_scale_zp((const uint32_t*)a.m.s, (const uint32_t*)a.m.z, half + rA, k, blk, su, zu);
-                q4_scale_zp((const uint32_t*)a.m.s, (const uint32_t*)a.m.z, half + rB, k, blk, sv, zv);
-              } else {
-                q4g64_scale_zp((const uint16_t*)a.m.s, (const uint16_t*)a.m.z, half + rA, k, blk, su, zu);
-                q4g64_scale_zp((const uint16_t*)a.m.s, (const uint16_t*)a.m.z, half + rB, k, blk, sv, zv);
-              }
-              utA = fmaf(su, (cu[0] + cu[1]) - zu * xsb, utA);
-              utB = fmaf(sv, (cu[2] + cu[3]) - zv * xsb, utB);
+      for (int i = 0; i < PF; ++i) {
+        const int S = sb + i;
+        if (S >= s1) break;
+        float c[PH][4];
+#pragma unroll
+        for (int p = 0; p < PH; ++p) c[p][0] = c[p][1] = c[p][2] = c[p][3] = 0.f;
+#pragma unroll
+        for (int wd = 0; wd < 4; ++wd) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            // x of chunk (segment S, block t, word wd): elements 2h, 2h + 4 and 2h + 1, 2h + 5
+            uint2 xb = make_uint2(0u, 0u);
+            if (feeds) xb = xplane[(size_t)(S * 16 + t * 4 + wd) * 2 + h];
+#pragma unroll
+            for (int p = 0; p < PH; ++p) {
+              const uint32_t wa = (&w[i][p][0].x)[wd], wb = (&w[i][p][1].x)[wd];
+              mma_f16(c[p], nib_pair_f16(wa, 2 * h), nib_pair_f16(wb, 2 * h), nib_pair_f16(wa, 2 * h + 1),
+                      nib_pair_f16(wb, 2 * h + 1), xb.x, xb.y);
             }
           }
-          c[0] = c[1] = c[2] = c[3] = 0.f;
-          if (SW) cu[0] = cu[1] = cu[2] = cu[3] = 0.f;
+        }
+        if (sums) {
+          // lane t holds columns 2t (hi) and 2t + 1 (lo): block qblk of the segment, rows g, g + 8
+          const int blk = (KIND == kQ4) ? 4 * S + t : 2 * S + t;
+          const float xsb = xsum[blk];
+#pragma unroll
+          for (int p = 0; p < PH; ++p)
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+              float scale, zp;
+              if (KIND == kQ4) {
+                scale = h2f((uint16_t)((t & 1) ? (sq[i][p][r] >> 16) : (sq[i][p][r] & 0xFFFFu)));
+                zp = (float)((zq[i][p][r] >> (4 * (4 * (S & 1) + t))) & 15u);
+              } else {
+                scale = h2f((uint16_t)sq[i][p][r]);
+                zp = h2f((uint16_t)zq[i][p][r]);
+              }
+              tot[p][r] = fmaf(scale, (c[p][2 * r] + c[p][2 * r + 1]) - zp * xsb, tot[p][r]);
+            }
         }
       }
     }
-    // k-groups meet in shared memory; lane (g, 0) of the row group holds rows g and g + 8
+    // blocks of the quad, then the k-slices of the CTA's warps (shared memory)
+#pragma unroll
+    for (int p = 0; p < PH; ++p)
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        tot[p][r] += __shfl_xor_sync(0xffffffffu, tot[p][r], 1);
+        tot[p][r] += __shfl_xor_sync(0xffffffffu, tot[p][r], 2);
+      }
     if (KG > 1) {
       __syncthreads();
       if (t == 0) {
-        part[warp][0][g] = totA;
-        part[warp][0][g + 8] = totB;
-        part[warp][1][g] = utA;
-        part[warp][1][g + 8] = utB;
+#pragma unroll
+        for (int p = 0; p < PH; ++p) {
+          part[warp][p][g] = tot[p][0];
+          part[warp][p][g + 8] = tot[p][1];
+        }
       }
       __syncthreads();
       if (kg == 0 && t == 0) {
-        for (int q = 1; q < KG; ++q) {
-          totA += part[rg + q * RG][0][g];
-          totB += part[rg + q * RG][0][g + 8];
-          utA += part[rg + q * RG][1][g];
-          utB += part[rg + q * RG][1][g + 8];
-        }
+        for (int q = 1; q < KG; ++q)
+#pragma unroll
+          for (int p = 0; p < PH; ++p) {
+            tot[p][0] += part[rg + q * RG][p][g];
+            tot[p][1] += part[rg + q * RG][p][g + 8];
+          }
       }
     }
     if (tile_ok && kg == 0 && t == 0) {
-      const long oa = (long)tile * 16 + g, ob = oa + 8;
-      float va = totA, vb = totB;
-      if (SW) {
-        va = silu(totA) * utA;
-        vb = silu(totB) * utB;
-      }
-      if (oa < out_rows) {
-        if (EPI == kAccumulate) a.y[oa] += va;
-        else a.y[oa] = va;
-        if (EPI == kArgmax && va > -INFINITY && (va > best_v || (va == best_v && (uint32_t)oa < best_i))) {
-          best_v = va;
-          best_i = (uint32_t)oa;
-        }
-      }
-      if (ob < out_rows) {
-        if (EPI == kAccumulate) a.y[ob] += vb;
-        else a.y[ob] = vb;
-        if (EPI == kArgmax && vb > -INFINITY && (vb > best_v || (vb == best_v && (uint32_t)ob < best_i))) {
-          best_v = vb;
-          best_i = (uint32_t)ob;
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const long o = (long)tile * 16 + g + 8 * r;
+        if (o >= out_rows) continue;
+        const float v = SW ? silu(tot[0][r]) * tot[PH - 1][r] : tot[0][r];
+        if (EPI == kAccumulate) a.y[o] += v;
+        else a.y[o] = v;
+        if (EPI == kArgmax && v > -INFINITY && better(v, (uint32_t)o, best_v, best_i)) {
+          best_v = v;
+          best_i = (uint32_t)o;
         }
       }
     }
   }
   if (EPI == kArgmax) {
-    // lanes without rows hold no candidate; reduce the warp, then the CTA, then the grid
+    // lanes without rows hold no candidate; reduce the warp, then the CTA and the grid
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       const float ov = __shfl_xor_sync(0xffffffffu, best_v, o);
       const uint32_t oi = __shfl_xor_sync(0xffffffffu, best_i, o);
-      if (oi != 0xFFFFFFFFu && (best_i == 0xFFFFFFFFu || ov > best_v || (ov == best_v && oi < best_i))) {
+      if (better(ov, oi, best_v, best_i)) {
         best_v = ov;
         best_i = oi;
       }
     }
     if (lane == 0) {
-      bval[warp] = best_v;
-      bidx[warp] = best_i;
+      sh.bval[warp] = best_v;
+      sh.bidx[warp] = best_i;
     }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      float v = -INFINITY;
-      uint32_t ix = 0xFFFFFFFFu;
-      for (int w = 0; w < kWarps; ++w)
-        if (bidx[w] != 0xFFFFFFFFu && (ix == 0xFFFFFFFFu || bval[w] > v || (bval[w] == v && bidx[w] < ix))) {
-          v = bval[w];
-          ix = bidx[w];
-        }
-      a.part_val[blockIdx.x] = v;
-      a.part_idx[blockIdx.x] = ix;
-      __threadfence();
-      is_last = (atomicAdd(a.ticket, 1u) == gridDim.x - 1) ? 1u : 0u;
-    }
-    __syncthreads();
-    if (is_last && warp == 0) {
-      __threadfence();
-      float v = -INFINITY;
-      uint32_t ix = 0xFFFFFFFFu;
-      for (int b = lane; b < (int)gridDim.x; b += 32) {
-        const float bv = __ldcg(a.part_val + b);
-        const uint32_t bi = __ldcg(a.part_idx + b);
-        if (bi != 0xFFFFFFFFu && (ix == 0xFFFFFFFFu || bv > v || (bv == v && bi < ix))) {
-          v = bv;
-          ix = bi;
-        }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, v, o);
-        const uint32_t oi = __shfl_xor_sync(0xffffffffu, ix, o);
-        if (oi != 0xFFFFFFFFu && (ix == 0xFFFFFFFFu || ov > v || (ov == v && oi < ix))) {
-          v = ov;
-          ix = oi;
-        }
-      }
-      if (lane == 0) {
-        if (a.update_token) {
-          a.ctl->token = (ix == 0xFFFFFFFFu) ? 0u : ix;
-          a.ctl->pos += 1;
-        }
-        *a.ticket = 0u;
-      }
-    }
+    argmax_finish(a, blockIdx.x, gridDim.x, sh);
   }
 }
 
@@ -1029,9 +1014,22 @@ cudaError_t launch_q4_mma(GemvArgs a, cudaStream_t stream, bool pdl) {
   }
   const int out_rows = (EPI == kSwiGlu) ? a.m.rows / 2 : a.m.rows;
   const int tiles = (out_rows + 15) / 16;
+  const int nseg = k / kQtSeg;
+  const int pf = qt_batch(KIND, EPI == kSwiGlu);
   const int max_grid = 2 * kNumSms;
-  int rg = 8;
-  while (rg > 1 && (tiles + rg - 1) / rg < max_grid) rg /= 2;
+  // k-slices per tile: of the splits that keep every warp's slice within one register batch and
+  // the grid within two CTAs per SM, the one with the most CTAs; 8 when none does (the CTAs
+  // then loop over tiles and batches).
+  int kg = 8;
+  long most = -1;
+  for (int q = 1; q <= kWarps; q *= 2) {
+    const long ctas = (tiles + kWarps / q - 1) / (kWarps / q);
+    if ((nseg + q - 1) / q <= pf && ctas <= max_grid && ctas > most) {
+      most = ctas;
+      kg = q;
+    }
+  }
+  const int rg = kWarps / kg;
   a.row_groups = rg;
   int grid = (tiles + rg - 1) / rg;
   if (grid > max_grid) grid = max_grid;
@@ -1094,7 +1092,9 @@ cudaError_t launch_kind(const GemvArgs& a, cudaStream_t stream, bool pdl) {
 #undef QNE_PCOMBO
   }
   if constexpr (KIND != kF16) {
-    if (a.variant == 0 && q4pipe_fits(a)) {
+    // int4: the tensor-core kernel by default (k % 128 == 0), the register pipeline on request
+    // (variant 4) or for the other widths.
+    if ((a.variant == 4 || (a.variant == 0 && a.m.k % kQtSeg)) && q4pipe_fits(a)) {
 #define QNE_Q4P(P, E) \
     if (a.pro == P && a.epi == E) return launch_q4pipe<KIND, P, E>(a, stream, pdl);
       QNE_Q4P(kProCopy, kStore)
@@ -1109,7 +1109,7 @@ cudaError_t launch_kind(const GemvArgs& a, cudaStream_t stream, bool pdl) {
 #undef QNE_Q4P
     }
   }
-  if (KIND != kF16 && (a.variant == 0 || a.variant == 3) && a.m.k % 256 == 0) {
+  if (KIND != kF16 && (a.variant == 0 || a.variant == 3) && a.m.k % kQtSeg == 0) {
 #define QNE_QCOMBO(P, E) \
     if (a.pro == P && a.epi == E) return launch_q4_mma<KIND, P, E>(a, stream, pdl);
     QNE_QCOMBO(kProCopy, kStore)
@@ -1151,8 +1151,10 @@ void argmax_scratch_carve(void* scratch, float** part_val, uint32_t** part_idx, 
 
 const char* check_gemv(const GemvArgs& a) {
   const Mat& m = a.m;
-  if (a.variant < 0 || a.variant > 3) return "unknown GEMV variant";
-  if (a.variant == 3 && (m.kind == kF16 || m.k % 256)) return "the tensor-core GEMV needs int4 weights and k % 256 == 0";
+  if (a.variant < 0 || a.variant > 4) return "unknown GEMV variant";
+  if (a.variant == 4 && (m.kind == kF16 || !q4pipe_fits(a)))
+    return "the int4 register pipeline needs int4 weights, k % 256 == 0 and k <= 8192 (4096 with SwiGLU)";
+  if (a.variant == 3 && (m.kind == kF16 || m.k % kQtSeg)) return "the tensor-core GEMV needs int4 weights and k % 128 == 0";
   if (a.variant == 2 && !ring_fits(a))
     return "the bulk-copy GEMV needs f16 weights, k % 256 == 0 and k <= 6144 (4096 with SwiGLU, 2048 with a norm prologue)";
   if (!m.w || m.rows <= 0 || m.k <= 0) return "matrix has no data or an empty shape";

@@ -488,7 +488,8 @@ def gemv(m: _Matrix, x, y, epilogue="store", stream=None) -> None:
 
 
 def gemv_ex(m: _Matrix, x, y, epilogue="store", variant: int = 0, ctas_per_sm: int = 2, stream=None) -> None:
-    """gemv with an explicit kernel variant (0 auto, 1 register-streamed, 2 bulk-copy ring)."""
+    """gemv with an explicit kernel variant (0 auto, 1 row-group register streaming, 2 bulk-copy
+    ring, 3 tensor-core int4, 4 int4 register pipeline)."""
     epi = EPILOGUES[epilogue] if isinstance(epilogue, str) else int(epilogue)
     _check(lib.qne_gemv_ex(C.byref(m), _ptr(x), _ptr(y), epi, variant, ctas_per_sm, _stream(stream)))
 

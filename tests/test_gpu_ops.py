@@ -147,6 +147,29 @@ def test_gemv_variants_match_the_oracle(cuda, variant, epilogue, rows, k):
     assert rc.rel_err(host(y), want) < 1e-4
 
 
+@pytest.mark.parametrize("variant", [3, 4])
+@pytest.mark.parametrize("kind", ["q4g64", "q4"])
+@pytest.mark.parametrize("epilogue", ["store", "accumulate", "swiglu"])
+@pytest.mark.parametrize("rows,k", [(12288, 2048), (2048, 6144), (2 * 3584, 1024), (1024, 3584), (8224, 2048),
+                                    (300, 6144), (74, 1024), (2, 256), (16, 256)])
+def test_gemv_int4_variants(cuda, variant, kind, epilogue, rows, k):
+    """Variant 3 (tensor-core int4: per-block MMA columns, slices held in registers, the default)
+    and variant 4 (the CUDA-core register pipeline) against the oracle: random zero points,
+    partial last tiles and every k-slice split the launcher picks."""
+    if variant == 4 and epilogue == "swiglu" and k > 4096:
+        pytest.skip("the register pipeline holds a SwiGLU row pair of at most 4096 values")
+    rng = np.random.default_rng(rows * 3 + k)
+    mat = make_matrix(kind, rows, k, rng, zp_random=True)
+    x = rng.standard_normal(k).astype(np.float32)
+    out_rows = rows // 2 if epilogue == "swiglu" else rows
+    y0 = rng.standard_normal(out_rows).astype(np.float32) if epilogue == "accumulate" else None
+    m = devmat(kind, rows, k, mat["w"], mat["s"], mat["z"])
+    y = dev(y0 if y0 is not None else np.zeros(out_rows, np.float32))
+    qne.gemv_ex(m, dev(x), y, epilogue, variant)
+    want = oracle_gemv(kind, mat, rows, k, x, epilogue, y0)
+    assert rc.rel_err(host(y), want) < 1e-4
+
+
 def test_gemv_ring_variant_rejects_wide_rows(cuda):
     m = devmat("f16", 64, 8192, np.zeros(64 * 8192, np.float16))
     with pytest.raises(qne.QneError) as e:
