@@ -389,7 +389,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_pipe_kernel(const GemvArgs a
   Pipe<PRO, EPI> p;
   p.init(a, blockIdx.x, gridDim.x);
   pdl_launch();
-  p.prefetch();
+  p.prefetch(a);
   pdl_wait();
   p.run(a, xs, sh);
   if (EPI == kArgmax) argmax_finish(a, blockIdx.x, gridDim.x, sh);
@@ -452,7 +452,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4pipe_kernel(const GemvArgs
 
 template <int KIND, int PRO, int EPI>
 __global__ void __launch_bounds__(kThreads, 2) gemv_q4_mma_kernel(const GemvArgs a) {
-  // [k] x (f32), then the hi and lo f16 pair planes ([2][k / 8] uint4), then [k / QB] block sums
+  // the hi and lo f16 pair planes of x ([2][k / 8] uint4), then [k / QB] block sums
   extern __shared__ __align__(16) float xs[];
   __shared__ GemvShared sh;
   __shared__ float part[kWarps][2][16];
@@ -522,30 +522,14 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4_mma_kernel(const GemvArgs
   pdl_launch();
   const int first = blockIdx.x * RG + rg;
   if (first < tiles) load(first, s0);  // weights depend on nothing: before the dependency wait
+  float nw[8];
+  pre_norm<PRO>(a, nw);
   pdl_wait();
 
-  stage_x<PRO>(a, xs, sh.red);
-  uint4* xq = reinterpret_cast<uint4*>(xs + k);  // [2][k / 8]: hi plane, then lo plane
-  float* xsum = xs + 2 * k;
-  for (int c = threadIdx.x; c < k / 8; c += kThreads) {
-    const float* x8 = xs + c * 8;
-    uint32_t hw[4], lw[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const __half h0 = __float2half_rn(x8[i]), h1 = __float2half_rn(x8[i + 4]);
-      const __half l0 = __float2half_rn(x8[i] - __half2float(h0)), l1 = __float2half_rn(x8[i + 4] - __half2float(h1));
-      hw[i] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
-      lw[i] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
-    }
-    xq[c] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-    xq[k / 8 + c] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-  }
-  for (int b = threadIdx.x; b < k / QB; b += kThreads) {
-    float sum = 0.f;
-    for (int i = 0; i < QB; ++i) sum += xs[b * QB + i];
-    xsum[b] = sum;
-  }
-  __syncthreads();
+  // x (prologue applied, RMSNorm folded into `inv`) as hi / lo f16 pair planes and block sums
+  uint4* xq = reinterpret_cast<uint4*>(xs);  // [2][k / 8]: hi plane, then lo plane
+  float* xsum = xs + k;
+  const float inv = stage_fold<PRO, 1>(a, xq, sh.red, nw, CtaSync(), xsum, QB / 8);
   const uint2* xplane = reinterpret_cast<const uint2*>(xq + (g & 1) * (k / 8));
 
   float best_v = -INFINITY;
@@ -637,7 +621,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4_mma_kernel(const GemvArgs
       for (int r = 0; r < 2; ++r) {
         const long o = (long)tile * 16 + g + 8 * r;
         if (o >= out_rows) continue;
-        const float v = SW ? silu(tot[0][r]) * tot[PH - 1][r] : tot[0][r];
+        const float v = SW ? silu(tot[0][r] * inv) * (tot[PH - 1][r] * inv) : tot[0][r] * inv;
         if (EPI == kAccumulate) a.y[o] += v;
         else a.y[o] = v;
         if (EPI == kArgmax && v > -INFINITY && better(v, (uint32_t)o, best_v, best_i)) {
@@ -969,7 +953,7 @@ cudaError_t launch_nr(const GemvArgs& a, cudaStream_t stream, bool pdl) {
 template <int PRO, int EPI>
 cudaError_t launch_pipe(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   auto kernel = gemv_pipe_kernel<PRO, EPI>;
-  const size_t smem = (size_t)a.m.k * 2 * sizeof(float);
+  const size_t smem = (size_t)a.m.k * sizeof(float);  // the two planes of x
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
@@ -1007,7 +991,7 @@ template <int KIND, int PRO, int EPI>
 cudaError_t launch_q4_mma(GemvArgs a, cudaStream_t stream, bool pdl) {
   auto kernel = gemv_q4_mma_kernel<KIND, PRO, EPI>;
   const int k = a.m.k;
-  const size_t smem = ((size_t)2 * k + k / 32) * sizeof(float);
+  const size_t smem = ((size_t)k + k / 32) * sizeof(float);  // pair planes, block sums
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;

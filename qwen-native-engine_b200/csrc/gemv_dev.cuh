@@ -145,6 +145,151 @@ __device__ __forceinline__ void stage_x(const GemvArgs& a, float* xs, float* red
 }
 
 // ------------------------------------------------------------------------------------------
+// One-pass staging (the default kernels). The prologue operand that depends on nothing (the
+// norm weight) is loaded into registers before the dependency wait (pre_norm); after the wait
+// every thread loads its chunks of x at once, applies the prologue and writes the layout the
+// streaming loop reads, so a GEMV pays one round trip to L2 and one barrier between its release
+// and its first dot product. RMSNorm is folded: the staged values are x * norm_w and the
+// returned factor rsqrt(mean(x^2) + eps) scales the dot products in the epilogue (1 for the
+// other prologues, which are applied in full).
+// ------------------------------------------------------------------------------------------
+constexpr int kStageChunks = 3;  // 8-element chunks per thread loaded together (k <= 6144)
+
+// The norm weight of this thread's first chunk (chunk c = threadIdx.x; the gated GDN norm
+// repeats its 128 weights per head).
+template <int PRO>
+__device__ __forceinline__ void pre_norm(const GemvArgs& a, float (&nw)[8]) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) nw[j] = 1.f;
+  if (PRO == kProCopy || (int)threadIdx.x >= a.m.k / 8) return;
+  const float* src = (PRO == kProGdnGate) ? a.norm_w + ((threadIdx.x * 8) & (kGdnDim - 1)) : a.norm_w + threadIdx.x * 8;
+  const float4 p = __ldg(reinterpret_cast<const float4*>(src));
+  const float4 q = __ldg(reinterpret_cast<const float4*>(src + 4));
+  nw[0] = p.x; nw[1] = p.y; nw[2] = p.z; nw[3] = p.w;
+  nw[4] = q.x; nw[5] = q.y; nw[6] = q.z; nw[7] = q.w;
+}
+
+__device__ __forceinline__ void ldcg8(float (&v)[8], const float* s) {
+  const float4 p = __ldcg(reinterpret_cast<const float4*>(s));
+  const float4 q = __ldcg(reinterpret_cast<const float4*>(s + 4));
+  v[0] = p.x; v[1] = p.y; v[2] = p.z; v[3] = p.w;
+  v[4] = q.x; v[5] = q.y; v[6] = q.z; v[7] = q.w;
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+  return (uint32_t)__half_as_ushort(__float2half_rn(lo)) | ((uint32_t)__half_as_ushort(__float2half_rn(hi)) << 16);
+}
+
+// Stages x (prologue applied, RMSNorm folded) in one pass and returns the folded factor.
+// OUT = 0: f32 planes, xp[4c ..] = elements 0-3 and xp[k/2 + 4c ..] = elements 4-7 of chunk c.
+// OUT = 1: f16 pair planes for the int4 tensor-core kernel, uint4 hi[c] = (v0,v4),(v1,v5),
+// (v2,v6),(v3,v7) as f16x2 of f16(v), lo[c] the same of f16(v - f16(v)), lo at hi + k/8; and
+// when csum is set, the sums of every `group` consecutive chunks (one quantization block).
+// Norm prologues need k <= 8 * kThreads (one chunk per thread; the gated norm k == 2048).
+template <int PRO, int OUT, typename Sync>
+__device__ __forceinline__ float stage_fold(const GemvArgs& a, void* planes, float* red, const float (&nw)[8],
+                                            Sync sync, float* csum = nullptr, int group = 1) {
+  const int k = a.m.k, nc = k / 8, tid = threadIdx.x;
+  constexpr bool kNorm = PRO == kProRmsNorm || PRO == kProEmbedNorm;
+  // chunks per thread and round: the norm prologues stage k <= 2048 (one chunk per thread)
+  constexpr int NCH = PRO == kProCopy ? kStageChunks : 1;
+  uint32_t token = 0;
+  if (PRO == kProEmbedNorm) {
+    token = a.ctl->token;
+    if (token >= (uint32_t)a.embed.rows) token = (uint32_t)a.embed.rows - 1;
+  }
+  float ss = 0.f;
+#pragma unroll 1
+  for (int c0 = 0; c0 < nc; c0 += kThreads * NCH) {
+    float v[NCH][8];
+    // every load of this round first
+#pragma unroll
+    for (int i = 0; i < NCH; ++i) {
+      const int c = c0 + tid + i * kThreads;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
+      if (c < nc) {
+        if (PRO == kProEmbedNorm) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[i][j] = deq_elem(a.embed, token, c * 8 + j);
+        } else {
+          ldcg8(v[i], a.x + c * 8);
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < NCH; ++i) {
+      const int c = c0 + tid + i * kThreads;
+      const bool in = c < nc;
+      if (PRO == kProEmbedNorm && in && blockIdx.x == 0) {
+        *reinterpret_cast<float4*>(a.h_out + c * 8) = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
+        *reinterpret_cast<float4*>(a.h_out + c * 8 + 4) = make_float4(v[i][4], v[i][5], v[i][6], v[i][7]);
+      }
+      float cs = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) cs = fmaf(v[i][j], v[i][j], cs);
+      if (kNorm) {
+        ss += cs;
+        float w[8];
+        if (c0 == 0 && i == 0) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) w[j] = nw[j];
+        } else if (in) {
+          ldcg8(w, a.norm_w + c * 8);
+        }
+        if (in) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[i][j] *= w[j];
+        }
+      } else if (PRO == kProGdnGate) {
+        // k == 2048: one chunk per thread, 16 consecutive threads per 128-wide head
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) cs += __shfl_xor_sync(0xffffffffu, cs, o);
+        const float inv = rsqrtf(cs / (float)kGdnDim + a.eps);
+        float z[8];
+        ldcg8(z, a.zgate + c * 8);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] = v[i][j] * inv * silu(z[j]) * nw[j];
+      }
+      if (OUT == 0) {
+        if (in) {
+          float* xp = static_cast<float*>(planes);
+          *reinterpret_cast<float4*>(xp + c * 4) = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
+          *reinterpret_cast<float4*>(xp + k / 2 + c * 4) = make_float4(v[i][4], v[i][5], v[i][6], v[i][7]);
+        }
+      } else {
+        if (in) {
+          uint4* xq = static_cast<uint4*>(planes);
+          float lo[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) lo[j] = v[i][j] - __half2float(__float2half_rn(v[i][j]));
+          xq[c] = make_uint4(pack_h2(v[i][0], v[i][4]), pack_h2(v[i][1], v[i][5]), pack_h2(v[i][2], v[i][6]),
+                             pack_h2(v[i][3], v[i][7]));
+          xq[nc + c] = make_uint4(pack_h2(lo[0], lo[4]), pack_h2(lo[1], lo[5]), pack_h2(lo[2], lo[6]), pack_h2(lo[3], lo[7]));
+        }
+        if (csum) {
+          // chunks of one block sit in consecutive lanes (c0 and i * kThreads are multiples of 32)
+          float s = ((v[i][0] + v[i][1]) + (v[i][2] + v[i][3])) + ((v[i][4] + v[i][5]) + (v[i][6] + v[i][7]));
+          for (int o = 1; o < group; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+          if (in && (c % group) == 0) csum[c / group] = s;
+        }
+      }
+    }
+  }
+  if (PRO == kProEmbedNorm && blockIdx.x == 0 && tid == 0) a.ctl->count += 1;  // conv windows
+  if (kNorm) {
+    const float t = warp_sum(ss);
+    if ((tid & 31) == 0) red[tid >> 5] = t;
+  }
+  sync();
+  if (!kNorm) return 1.f;
+  float t = 0.f;
+#pragma unroll
+  for (int w = 0; w < kThreads / 32; ++w) t += red[w];
+  return rsqrtf(t / (float)k + a.eps);
+}
+
+// ------------------------------------------------------------------------------------------
 // Chunk dot products: 16 bytes of one row against the matching slice of x in shared memory.
 // ------------------------------------------------------------------------------------------
 __device__ __forceinline__ float dot_f16(const uint4& w, const float* x) {
@@ -201,6 +346,7 @@ struct Pipe {
   size_t rb;
   const uint8_t* W;
   uint4 cur[R][CPL];
+  float normw[8];  // norm weight of this thread's chunk of x, loaded before the dependency wait
 
   __device__ __forceinline__ void init(const GemvArgs& a, int cta, int ncta) {
     k = a.m.k;
@@ -231,23 +377,20 @@ struct Pipe {
     }
   }
 
-  // First unit into registers. (A bulk L2 prefetch of the warp's next rows here was measured
-  // and makes the decode step slower: it competes with the demand stream instead of filling gaps.)
-  __device__ __forceinline__ void prefetch() {
+  // First unit into registers, and the norm weight of the prologue. (A bulk L2 prefetch of the
+  // warp's next rows here was measured and makes the decode step slower: it competes with the
+  // demand stream instead of filling gaps.)
+  __device__ __forceinline__ void prefetch(const GemvArgs& a) {
     if (units > 0) load(cur, 0);
+    pre_norm<PRO>(a, normw);
   }
 
-  // Stages x (prologue), then streams every unit. For kArgmax the lane-0 best candidate of each
-  // warp lands in sh.bval / sh.bidx.
+  // Stages x (prologue, one pass), then streams every unit. For kArgmax the lane-0 best
+  // candidate of each warp lands in sh.bval / sh.bidx.
   __device__ __forceinline__ void run(const GemvArgs& a, float* xs, GemvShared& sh) {
     const int warp = threadIdx.x >> 5;
-    stage_x<PRO>(a, xs, sh.red);
-    float* xp = xs + k;  // planes: elements 0-3 and 4-7 of every 8-element chunk
-    for (int c = threadIdx.x; c < k / 8; c += kThreads) {
-      *reinterpret_cast<float4*>(xp + c * 4) = *reinterpret_cast<const float4*>(xs + c * 8);
-      *reinterpret_cast<float4*>(xp + k / 2 + c * 4) = *reinterpret_cast<const float4*>(xs + c * 8 + 4);
-    }
-    __syncthreads();
+    float* xp = xs;  // planes: elements 0-3 and 4-7 of every 8-element chunk
+    const float inv = stage_fold<PRO, 0>(a, xp, sh.red, normw, CtaSync());
     float best_v = -INFINITY;
     uint32_t best_i = 0xFFFFFFFFu;
     float acc[R];
@@ -275,7 +418,7 @@ struct Pipe {
         float v[R];
 #pragma unroll
         for (int rr = 0; rr < R; ++rr) {
-          v[rr] = warp_sum(acc[rr]);
+          v[rr] = warp_sum(acc[rr]) * inv;
           acc[rr] = 0.f;
         }
         if (EPI == kArgmax && v[0] > -INFINITY && (v[0] > best_v || (v[0] == best_v && (uint32_t)row < best_i))) {
