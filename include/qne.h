@@ -317,7 +317,10 @@ QNE_API qne_status qne_gemv_ex(const qne_matrix* m, const float* x, float* y, in
 QNE_API qne_status qne_rmsnorm_gemv(const qne_matrix* m, const float* h, const float* norm_w, float eps,
                             float* y, int epilogue, void* stream);
 /* Batched GEMV/GEMM over `batch` (1..64) f32 vectors x[batch][k] -> y[batch][out_rows]. Uses the
- * tensor cores for batch >= 2. `scratch` must hold qne_gemm_scratch_bytes(m, batch) bytes. */
+ * tensor cores for batch >= 2. `scratch` must hold qne_gemm_scratch_bytes(m, batch) bytes.
+ * f16, block-32 int4 (k % 256 == 0) and group-64 int4 (k % 64 == 0) weights; int4 nibbles are
+ * widened to f16 ((q - zp) * scale, rounded once, the value the per-token kernels multiply) in
+ * shared memory between the tensor-memory-accelerator load and the MMA. */
 QNE_API size_t qne_gemm_scratch_bytes(const qne_matrix* m, int batch);
 QNE_API qne_status qne_gemm(const qne_matrix* m, const float* x, int batch, float* y, int epilogue,
                     void* scratch, size_t scratch_bytes, void* stream);

@@ -149,17 +149,25 @@ void BatchRunner::record(bool greedy, cudaStream_t s) {
                   uint16_t* yl, int ldy, const float* norm_out, bool norm_in) {
     GemmArgs g;
     g.w = w.w;
-    if (w.kind != kF16) {  // int4: decode into the f16 scratch first
-      if (w.k % 64) throw QneError(kEInval, "batched decode of int4 matrices needs k % 64 == 0");
-      cuda_check(launch_dequant_f16(w, wdeq, s, true), "dequant launch");
-      ++n;
-      g.w = wdeq;
-      g.w_after_wait = true;
-    }
     g.rows = w.rows;
     g.k = w.k;
     g.batch = B;
     g.epi = epi;
+    if (w.kind != kF16) {
+      // int4: widened to f16 inside the GEMM, or (the many-wave LM head) decoded into the f16
+      // scratch first
+      g.wkind = w.kind;
+      g.ws = w.s;
+      g.wz = w.z;
+      if (!gemm_int4_direct(g)) {
+        if (w.k % 64) throw QneError(kEInval, "batched decode of int4 matrices needs k % 64 == 0");
+        cuda_check(launch_dequant_f16(w, wdeq, s, true), "dequant launch");
+        ++n;
+        g.wkind = kF16;
+        g.w = wdeq;
+        g.w_after_wait = true;
+      }
+    }
     g.row_groups = gemm_row_groups(epi == kSwiGlu ? w.rows / 2 : w.rows);
     g.xh = xh;
     g.xl = xl;
@@ -496,7 +504,8 @@ qne_status qne_gemm_ex(const qne_matrix* m, const float* x, int batch, float* y,
   return bguard([&] {
     if (impl != QNE_GEMM_TENSOR_CORE && impl != QNE_GEMM_MMA_SYNC) throw QneError(kEInval, "unknown GEMM kernel");
     if (!m || !x || !y) throw QneError(kEInval, "null argument");
-    if (m->kind != QNE_KIND_F16) throw QneError(kEInval, "batched GEMM supports f16 weights");
+    if (m->kind != QNE_KIND_F16 && impl != QNE_GEMM_TENSOR_CORE)
+      throw QneError(kEInval, "int4 weights need the tensor-core GEMM");
     if (epilogue < 0 || epilogue > 2) throw QneError(kEInval, "unknown epilogue");
     if (batch < 1 || batch > (impl == QNE_GEMM_MMA_SYNC ? 32 : kGemmMaxRows))
       throw QneError(kEInval, impl == QNE_GEMM_MMA_SYNC ? "batch must be 1..32" : "batch must be 1..64");
@@ -534,6 +543,11 @@ qne_status qne_gemm_ex(const qne_matrix* m, const float* x, int batch, float* y,
     cuda_check(launch_prep(p, batch, s, false), "gemm prep");
     GemmArgs g;
     g.w = m->w;
+    if (m->kind != QNE_KIND_F16) {  // QNE_KIND_* are the engine's weight kinds
+      g.wkind = m->kind;
+      g.ws = m->s;
+      g.wz = m->z;
+    }
     g.rows = m->rows;
     g.k = m->k;
     g.batch = batch;

@@ -17,6 +17,11 @@ constexpr int kGemmMaxRows = 64;
 // Y[b][row] for b < batch: W [rows][k] f16 times the activation planes xh/xl [>= 8*ceil(batch/8)][ldx].
 struct GemmArgs {
   const void* w = nullptr;
+  // Weight kind: kF16 (w = f16 [rows][k]), or kQ4 / kQ4G64 (w = packed nibbles, ws / wz = scales
+  // and zero points in the layouts of Mat; tensor-core kernel, see gemm_int4_direct).
+  int wkind = kF16;
+  const void* ws = nullptr;
+  const void* wz = nullptr;
   int rows = 0;  // physical rows (SwiGLU: gate rows then up rows)
   int k = 0;
   int batch = 1;
@@ -58,6 +63,9 @@ cudaError_t launch_dequant_f16(const Mat& m, uint16_t* out, cudaStream_t stream,
 const char* check_gemm(const GemmArgs& a);
 // impl kGemmTensorCore: tcgen05 + TMA (gemm_tc.cu); kGemmMmaSync: warp-level mma.sync (gemm.cu).
 cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream, bool pdl);
+// Whether the tensor-core GEMM takes these int4 weights directly (nibbles widened to f16 in
+// shared memory). Otherwise callers decode the matrix into an f16 scratch (launch_dequant_f16).
+bool gemm_int4_direct(const GemmArgs& a);
 bool gemm_tc_available();
 cudaError_t launch_gemm_tc(const GemmArgs& a, cudaStream_t stream, bool pdl);
 

@@ -507,6 +507,8 @@ const char* check_gemm(const GemmArgs& a) {
     return "the folded RMSNorm needs the tensor-core GEMM";
   if (a.w_after_wait && (a.impl != kGemmTensorCore || !gemm_tc_available() || reinterpret_cast<uintptr_t>(a.w) % 16))
     return "weights written by the previous kernel need the tensor-core GEMM";
+  if (a.wkind != kF16 && !gemm_int4_direct(a))
+    return "int4 weights need the tensor-core GEMM, k % 64 == 0 (block-32: k % 256), scales and zero points";
   return nullptr;
 }
 
@@ -522,6 +524,7 @@ cudaError_t launch_dequant_f16(const Mat& m, uint16_t* out, cudaStream_t stream,
 }
 
 cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream, bool pdl) {
+  if (a.wkind != kF16) return gemm_int4_direct(a) ? launch_gemm_tc(a, stream, pdl) : cudaErrorInvalidValue;
   if (a.impl == kGemmTensorCore && gemm_tc_available() && reinterpret_cast<uintptr_t>(a.w) % 16 == 0 &&
       reinterpret_cast<uintptr_t>(a.xh) % 16 == 0 && reinterpret_cast<uintptr_t>(a.xl) % 16 == 0)
     return launch_gemm_tc(a, stream, pdl);

@@ -69,6 +69,12 @@ struct TcArgs {
   int sumsq_slots, norm_k;
   float eps;
   int w_after_wait;  // weights written by the previous kernel: no weight loads before the wait
+  // int4 weights (kernel instances with Q != kF16): the packed nibbles come through `tw`, the
+  // scales and zero points are read directly.
+  int rows;       // physical rows
+  int k;
+  const void* ws;
+  const void* wz;
 };
 
 __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
@@ -163,21 +169,52 @@ __device__ __forceinline__ float4 ld_cluster_v4(uint32_t addr) {
   return v;
 }
 
+// f16x2 helpers of the int4 converters (round to nearest, subnormals kept).
+__device__ __forceinline__ uint32_t hsub2_u(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t hmul2_u(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t hfma2_u(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ uint32_t prmt_u(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+// Nibbles i and i + 4 of w as the f16 pair (1024 + n_i, 1024 + n_{i+4}).
+__device__ __forceinline__ uint32_t nib_pair_1024(uint32_t w, int i) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, 0x000F000F, 0x64006400, 0xEA;" : "=r"(r) : "r"(w >> (4 * i)));  // (a & b) | c
+  return r;
+}
+
 __device__ __forceinline__ void split_hilo_tc(float x, __half& hi, __half& lo) {
   hi = __float2half_rn(x);
   lo = __float2half_rn(x - __half2float(hi));
 }
 
-template <int N, bool SW, int ST>
-__global__ void __launch_bounds__(kTcThreads, 1)
+template <int N, bool SW, int ST, int Q>
+__global__ void __launch_bounds__(Q != kF16 ? 2 * kTcThreads : kTcThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap txh,
                    const __grid_constant__ CUtensorMap txl, const __grid_constant__ TcArgs a) {
   extern __shared__ uint8_t dsm_raw[];
-  __shared__ __align__(8) uint64_t full[ST], empty[ST], accb;
+  constexpr bool kQ = Q != kF16;  // int4 weights, widened to f16 in shared memory
+  __shared__ __align__(8) uint64_t full[ST], empty[ST], accb, rawf[kQ ? ST : 1], conv[kQ ? ST : 1];
   __shared__ uint32_t tmem_slot;
   __shared__ float inv_s[kGemmMaxRows];
   constexpr int kTileB = N * kBK * 2;  // one activation plane per stage
-  constexpr int kStage = kTileA + 2 * kTileB;
+  constexpr int kLoadF16 = kTileA + 2 * kTileB;  // bytes of one stage's TMA loads (f16 weights)
+  constexpr int kRaw = kQ ? 128 * kBK / 2 : 0;   // int4: the stage's packed nibbles (4 KB)
+  constexpr int kStage = kTileA + 2 * kTileB + kRaw;
   constexpr int kTmemCols = 2 * N < 32 ? 32 : 2 * N;  // accumulator columns: N of hi, then N of lo
   constexpr int kPitch = N + 4;  // partial rows in shared memory: 16-byte aligned, conflict-free v4 stores
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
@@ -199,6 +236,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     for (int s = 0; s < ST; ++s) {
       mbar_init(smem_u32(&full[s]), 1);
       mbar_init(smem_u32(&empty[s]), 1);
+      if (kQ) {
+        mbar_init(smem_u32(&rawf[s]), 1);
+        mbar_init(smem_u32(&conv[s]), 4);  // one arrival per converter warp
+      }
     }
     mbar_init(smem_u32(&accb), 1);
     fence_barrier_init();
@@ -217,9 +258,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int r0 = SW ? tile * 64 : tile * 128;
     auto load_a = [&](int i) {
       const uint32_t st = sbase + (uint32_t)((i % ST) * kStage);
-      const uint32_t bar = smem_u32(&full[i % ST]);
       const int kx = (kb0 + i) * kBK;
-      mbar_arrive_expect_tx(bar, (uint32_t)kStage);
+      if (kQ) {
+        // packed nibbles: 32 bytes of every row of the tile, into the stage's raw area
+        const uint32_t bar = smem_u32(&rawf[i % ST]);
+        const uint32_t raw = st + (uint32_t)(kTileA + 2 * kTileB);
+        mbar_arrive_expect_tx(bar, (uint32_t)kRaw);
+        if (SW) {
+          tma_load_2d(raw, &tw, kx / 2, r0, bar);
+          tma_load_2d(raw + kRaw / 2, &tw, kx / 2, a.half + r0, bar);
+        } else {
+          tma_load_2d(raw, &tw, kx / 2, r0, bar);
+        }
+        return;
+      }
+      const uint32_t bar = smem_u32(&full[i % ST]);
+      mbar_arrive_expect_tx(bar, (uint32_t)kLoadF16);
       if (SW) {
         tma_load_2d(st, &tw, kx, r0, bar);
         tma_load_2d(st + kTileA / 2, &tw, kx, a.half + r0, bar);
@@ -231,6 +285,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const uint32_t st = sbase + (uint32_t)((i % ST) * kStage);
       const uint32_t bar = smem_u32(&full[i % ST]);
       const int kx = (kb0 + i) * kBK;
+      if (kQ) mbar_arrive_expect_tx(bar, (uint32_t)(2 * kTileB));
       tma_load_2d(st + kTileA, &txh, kx, 0, bar);
       tma_load_2d(st + kTileA + kTileB, &txl, kx, 0, bar);
     };
@@ -257,7 +312,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     constexpr uint32_t idesc = instr_desc_f16<2 * N>();
     for (int i = 0; i < nkb; ++i) {
       const int s = i % ST;
-      if (!mbar_wait(smem_u32(&full[s]), (uint32_t)(i / ST) & 1u, a.err)) {
+      if (!mbar_wait(smem_u32(&full[s]), (uint32_t)(i / ST) & 1u, a.err) ||
+          (kQ && !mbar_wait(smem_u32(&conv[s]), (uint32_t)(i / ST) & 1u, a.err))) {
         ok = false;
         break;
       }
@@ -271,6 +327,96 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mma_commit(smem_u32(&empty[s]));
     }
     mma_commit(smem_u32(&accb));
+  } else if (kQ && warp >= 4 && nkb > 0) {
+    // Converters (warps 4-7, int4 instances only): thread t widens row t of every stage's weight
+    // tile into the 128-byte-swizzled K-major layout the MMA reads (16-byte chunk c of row r at
+    // c ^ (r % 8)). The row's scales and zero points of a stage are loaded four stages ahead.
+    const int t = tid - 128;
+    const int r0 = SW ? tile * 64 : tile * 128;
+    long prow[1];
+    {
+      const int ar = t;
+      const long phys = SW ? (ar < 64 ? (long)r0 + ar : (long)a.half + r0 + ar - 64) : (long)r0 + ar;
+      prow[0] = phys < a.rows ? phys : (long)a.rows - 1;  // rows past the matrix: read as zero, never stored
+    }
+    uint32_t sq[4][1], zq[4][1];
+    auto load_sz = [&](int i, uint32_t (&sv)[1], uint32_t (&zv)[1]) {
+#pragma unroll
+      for (int rr = 0; rr < 1; ++rr) {
+        sv[rr] = 0u;
+        zv[rr] = 0u;
+        if (i < nkb) {
+          const int kb = kb0 + i;
+          if (Q == kQ4) {  // f16 scale pair per 64 values, 8 zero-point nibbles per 256
+            sv[rr] = __ldg(static_cast<const uint32_t*>(a.ws) + prow[rr] * (a.k / 64) + kb);
+            zv[rr] = __ldg(static_cast<const uint32_t*>(a.wz) + prow[rr] * (a.k / 256) + kb / 4);
+          } else {         // f16 scale and zero point per 64 values
+            sv[rr] = __ldg(static_cast<const uint16_t*>(a.ws) + prow[rr] * (a.k / 64) + kb);
+            zv[rr] = __ldg(static_cast<const uint16_t*>(a.wz) + prow[rr] * (a.k / 64) + kb);
+          }
+        }
+      }
+    };
+#pragma unroll
+    for (int j = 0; j < 4; ++j) load_sz(j, sq[j], zq[j]);
+    for (int i0 = 0; i0 < nkb && ok; i0 += 4) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int i = i0 + j;
+        if (i >= nkb || !ok) break;  // uniform across the two converter warps
+        const int s = i % ST;
+        if (!mbar_wait(smem_u32(&rawf[s]), (uint32_t)(i / ST) & 1u, a.err)) {
+          ok = false;
+          break;
+        }
+        uint8_t* A = base + (size_t)s * kStage;
+        const uint8_t* raw = A + kTileA + 2 * kTileB;
+        const int kb = kb0 + i;
+#pragma unroll
+        for (int rr = 0; rr < 1; ++rr) {
+          const int ar = t;
+          const uint4 w0 = *reinterpret_cast<const uint4*>(raw + ar * 32);
+          const uint4 w1 = *reinterpret_cast<const uint4*>(raw + ar * 32 + 16);
+          const uint32_t wd[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+          // Per block (words 0-3 and 4-7: one block-32 block each, one group-64 group), f16x2
+          // constants. Block-32 (integer zero point): (1024 + q) - (1024 + zp) is the exact
+          // integer q - zp and one f16x2 multiply rounds (q - zp) * scale once, the value the
+          // per-token kernels use. Group-64 (f16 zero point): q * scale + f16(-zp * scale) in one
+          // f16x2 fma (within an f16 unit of the f32 form).
+          uint32_t ca[2], cb[2];
+          if (Q == kQ4) {
+            const uint32_t z0 = (zq[j][rr] >> (4 * (2 * (kb & 3)))) & 15u, z1 = (zq[j][rr] >> (4 * (2 * (kb & 3) + 1))) & 15u;
+            ca[0] = 0x64006400u | z0 | (z0 << 16);
+            ca[1] = 0x64006400u | z1 | (z1 << 16);
+            cb[0] = prmt_u(sq[j][rr], sq[j][rr], 0x1010u);  // scale of block 2kb in both halves
+            cb[1] = prmt_u(sq[j][rr], sq[j][rr], 0x3232u);  // block 2kb + 1
+          } else {
+            const uint32_t sh = sq[j][rr] & 0xFFFFu;
+            const uint32_t cz = __half_as_ushort(__float2half_rn(-h2f((uint16_t)zq[j][rr]) * h2f((uint16_t)sh)));
+            ca[0] = ca[1] = cz | (cz << 16);
+            cb[0] = cb[1] = sh | (sh << 16);
+          }
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            uint32_t v[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const uint32_t p = nib_pair_1024(wd[c], e);  // (1024 + n_e, 1024 + n_{e+4})
+              v[e] = Q == kQ4 ? hmul2_u(hsub2_u(p, ca[c >> 2]), cb[c >> 2])
+                              : hfma2_u(hsub2_u(p, 0x64006400u), cb[c >> 2], ca[c >> 2]);
+            }
+            // v[e] = (value e, value e + 4): back to the natural order (0,1) (2,3) (4,5) (6,7)
+            *reinterpret_cast<uint4*>(A + ar * 128 + ((c ^ (ar & 7)) << 4)) =
+                make_uint4(prmt_u(v[0], v[1], 0x5410u), prmt_u(v[2], v[3], 0x5410u), prmt_u(v[0], v[1], 0x7632u),
+                           prmt_u(v[2], v[3], 0x7632u));
+          }
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> the MMA's operand reads
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&conv[s]));
+        load_sz(i + 4, sq[j], zq[j]);
+      }
+    }
   }
   __syncwarp();
 
@@ -291,7 +437,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int e = it * kTcThreads + tid;
     b0 = (e / slice) * 4;
     j = o0 + e % slice;
-    return e < total;
+    return tid < kTcThreads && e < total;  // the converter warps of the int4 instances hold no items
   };
 
   // What depends only on the previous kernel is fetched while the MMAs run: the consumer's 1/rms
@@ -326,7 +472,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   // Accumulator -> shared memory (the stage ring is free once accb fired: every MMA completed,
   // so every TMA load it consumed had landed). Thread t holds row t of the tile.
   float* part = reinterpret_cast<float*>(base);
-  {
+  if (warp < 4) {  // the tile's 128 accumulator lanes (the int4 converter warps hold none)
     float v[N];
     if (nkb > 0) {
       if (!mbar_wait(smem_u32(&accb), 0u, a.err)) ok = false;
@@ -482,9 +628,24 @@ bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, 
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 2-D byte tensor [outer][inner] (int4 weights: the packed nibbles of a row), no swizzle; box =
+// 32 bytes (one 64-value k-block) x box_outer rows.
+bool make_map_u8(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                 uint32_t box_outer) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {(cuuint32_t)(kBK / 2), box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // Clusters of `ranks` CTAs that can be resident at once (cached per device, kernel and size).
 template <typename K>
-int max_clusters(K kernel, size_t smem, int ranks) {
+int max_clusters(K kernel, size_t smem, int ranks, int threads) {
   static std::mutex mu;
   static std::map<std::tuple<int, const void*, int>, int> cache;
   int dev = 0;
@@ -495,7 +656,7 @@ int max_clusters(K kernel, size_t smem, int ranks) {
   if (it != cache.end()) return it->second;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(ranks, 1);
-  cfg.blockDim = dim3(kTcThreads);
+  cfg.blockDim = dim3(threads);
   cfg.dynamicSmemBytes = smem;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -513,10 +674,10 @@ int max_clusters(K kernel, size_t smem, int ranks) {
   return n;
 }
 
-template <int N, bool SW, int ST>
+template <int N, bool SW, int ST, int Q>
 cudaError_t launch_tc(const GemmArgs& g, cudaStream_t stream, bool pdl) {
-  auto kernel = gemm_tc_kernel<N, SW, ST>;
-  constexpr int kStage = kTileA + 2 * N * kBK * 2;
+  auto kernel = gemm_tc_kernel<N, SW, ST, Q>;
+  constexpr int kStage = kTileA + 2 * N * kBK * 2 + (Q != kF16 ? 128 * kBK / 2 : 0);
   const size_t smem = (size_t)ST * kStage + 1024;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
@@ -541,22 +702,30 @@ cudaError_t launch_tc(const GemmArgs& g, cudaStream_t stream, bool pdl) {
   a.norm_k = g.norm_k;
   a.eps = g.eps;
   a.w_after_wait = g.w_after_wait ? 1 : 0;
+  a.rows = g.rows;
+  a.k = g.k;
+  a.ws = g.ws;
+  a.wz = g.wz;
   const int out_tile = SW ? 64 : 128;
   const int tiles = (a.out_rows + out_tile - 1) / out_tile;
   // Split k over a cluster: the largest power of two whose clusters (one per tile) all fit on
   // the device at once, with every rank at two k-blocks or more.
   int ranks = 1;
-  while (ranks < kMaxCluster && a.kblocks >= ranks * 4 && tiles <= max_clusters(kernel, smem, ranks * 2)) ranks *= 2;
+  constexpr int kThreadsLaunch = Q != kF16 ? 2 * kTcThreads : kTcThreads;  // int4: + 4 converter warps
+  while (ranks < kMaxCluster && a.kblocks >= ranks * 4 && tiles <= max_clusters(kernel, smem, ranks * 2, kThreadsLaunch))
+    ranks *= 2;
   a.kb_per_rank = (a.kblocks + ranks - 1) / ranks;
   const int x_rows = g.x_rows > 0 ? g.x_rows : (g.batch + 7) / 8 * 8;
   CUtensorMap tw, txh, txl;
-  if (!make_map(&tw, g.w, (uint64_t)g.k, (uint64_t)g.rows, (uint64_t)g.k * 2, SW ? 64 : 128) ||
+  const bool wmap = Q != kF16 ? make_map_u8(&tw, g.w, (uint64_t)g.k / 2, (uint64_t)g.rows, (uint64_t)g.k / 2, SW ? 64 : 128)
+                              : make_map(&tw, g.w, (uint64_t)g.k, (uint64_t)g.rows, (uint64_t)g.k * 2, SW ? 64 : 128);
+  if (!wmap ||
       !make_map(&txh, g.xh, (uint64_t)g.k, (uint64_t)x_rows, (uint64_t)g.ldx * 2, N) ||
       !make_map(&txl, g.xl, (uint64_t)g.k, (uint64_t)x_rows, (uint64_t)g.ldx * 2, N))
     return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(ranks, tiles);
-  cfg.blockDim = dim3(kTcThreads);
+  cfg.blockDim = dim3(kThreadsLaunch);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
@@ -576,13 +745,26 @@ template <int N, bool SW>
 cudaError_t launch_tc_nsw(const GemmArgs& g, cudaStream_t stream, bool pdl) {
   const int out_tile = SW ? 64 : 128;
   const int tiles = ((SW ? g.rows / 2 : g.rows) + out_tile - 1) / out_tile;
-  if (!SW && tiles > 2 * kCtaSlots) return launch_tc<N, SW, kTcStagesWide>(g, stream, pdl);
-  return launch_tc<N, SW, kTcStages>(g, stream, pdl);
+  if (g.wkind == kQ4) return launch_tc<N, SW, kTcStages, kQ4>(g, stream, pdl);
+  if (g.wkind == kQ4G64) return launch_tc<N, SW, kTcStages, kQ4G64>(g, stream, pdl);
+  if (!SW && tiles > 2 * kCtaSlots) return launch_tc<N, SW, kTcStagesWide, kF16>(g, stream, pdl);
+  return launch_tc<N, SW, kTcStages, kF16>(g, stream, pdl);
 }
 
 }  // namespace
 
 bool gemm_tc_available() { return encode_fn() != nullptr; }
+
+bool gemm_int4_direct(const GemmArgs& g) {
+  if (g.wkind != kQ4 && g.wkind != kQ4G64) return false;
+  if (g.impl != kGemmTensorCore || !gemm_tc_available() || g.w_after_wait || !g.ws || !g.wz) return false;
+  if (g.k % (g.wkind == kQ4 ? 256 : 64) || g.batch < 1 || g.batch > kGemmMaxRows) return false;
+  if (reinterpret_cast<uintptr_t>(g.w) % 16 || (size_t)g.k / 2 % 16) return false;
+  // the many-wave case (the batched LM head) keeps the f16 route: it runs three CTAs per SM
+  const bool sw = g.epi == kSwiGlu;
+  const int tiles = ((sw ? g.rows / 2 : g.rows) + (sw ? 63 : 127)) / (sw ? 64 : 128);
+  return sw || tiles <= 2 * kCtaSlots;
+}
 
 cudaError_t launch_gemm_tc(const GemmArgs& g, cudaStream_t stream, bool pdl) {
   const bool sw = g.epi == kSwiGlu;

@@ -325,16 +325,24 @@ void PrefillRunner::record(int n, cudaStream_t s) {
                   uint16_t* yl, int ldy, const float* norm_out, bool norm_in) {
     GemmArgs g;
     g.w = w.w;
-    if (w.kind != kF16) {  // int4: decode into the f16 scratch first
-      cuda_check(launch_dequant_f16(w, wdeq, s, true), "prefill dequant launch");
-      ++cnt;
-      g.w = wdeq;
-      g.w_after_wait = true;
-    }
     g.rows = w.rows;
     g.k = w.k;
     g.batch = n;
     g.epi = epi;
+    if (w.kind != kF16) {
+      // int4: widened to f16 inside the GEMM, or (the many-wave LM head) decoded into the f16
+      // scratch first
+      g.wkind = w.kind;
+      g.ws = w.s;
+      g.wz = w.z;
+      if (!gemm_int4_direct(g)) {
+        cuda_check(launch_dequant_f16(w, wdeq, s, true), "prefill dequant launch");
+        ++cnt;
+        g.wkind = kF16;
+        g.w = wdeq;
+        g.w_after_wait = true;
+      }
+    }
     g.row_groups = gemm_row_groups(epi == kSwiGlu ? w.rows / 2 : w.rows);
     g.xh = xh;
     g.xl = xl;

@@ -100,8 +100,9 @@ def test_batched_decode_matches_oracle_per_sequence(tiny):
 @pytest.mark.parametrize("kind", ["q4", "q4g64"])
 def test_int4_batched_decode_matches_oracle(cuda, kind):
     """int4 models (the reference converter's block-32 layout, with an int4 LM head; and group 64
-    with an f16 LM head): every batched GEMM first decodes its matrix to f16 (one more launch per
-    GEMM). Per-sequence logits against the oracle after the prompt, then greedy continuations."""
+    with an f16 LM head): every batched GEMM widens its nibbles to f16 in shared memory, so a step
+    launches what an f16 step launches. Per-sequence logits against the oracle after the prompt,
+    then greedy continuations."""
     s = synth.build(1024, 3584, layers=4, vocab=8192, kind=kind, embed_kind="q4" if kind == "q4" else "f16",
                     seed=24)
     m = qne.Model(s.index_json, s.weights, any_shape=True)
@@ -111,8 +112,7 @@ def test_int4_batched_decode_matches_oracle(cuda, kind):
     for t in range(L):
         launches0 = qne.kernel_launches()
         nxt, lg = bt.step(prompts[:, t], np.full(B, t), want_logits=True)
-        int4_gemms = 4 * m.layers + (1 if kind == "q4" else 0)  # the LM head is int4 only for q4 here
-        assert qne.kernel_launches() - launches0 == 6 * m.layers + 3 + int4_gemms
+        assert qne.kernel_launches() - launches0 == 6 * m.layers + 3  # no decode-to-f16 launches
     ids = [nxt.copy()]
     cur = nxt.copy()
     for i in range(steps):
@@ -195,3 +195,51 @@ def test_context_limit_and_bad_tables(tiny):
     bt.close()
     with pytest.raises(qne.QneError):
         qne.Batch(m, 33)
+
+
+def _int4_matrix(kind, rows, k, rng):
+    w = rng.integers(0, 1 << 32, rows * k // 8, dtype=np.uint64).astype(np.uint32)
+    if kind == "q4":
+        s = np.abs(rng.standard_normal(rows * k // 32) * 0.01).astype(np.float16)
+        z = rng.integers(0, 1 << 32, rows * k // 256, dtype=np.uint64).astype(np.uint32)
+    else:
+        s = np.abs(rng.standard_normal(rows * k // 64) * 0.01).astype(np.float16)
+        z = rng.uniform(0, 15, rows * k // 64).astype(np.float16)
+    return w, s, z
+
+
+@pytest.mark.parametrize("kind", ["q4g64", "q4"])
+@pytest.mark.parametrize("batch", [1, 5, 16, 32, 33, 64])
+@pytest.mark.parametrize("epilogue,rows,k", [("store", 8224, 1024), ("accumulate", 1024, 3584), ("swiglu", 2 * 3584, 1024),
+                                             ("swiglu", 2 * 6144, 2048), ("accumulate", 2048, 6144), ("store", 300, 256)])
+def test_int4_gemm_widens_nibbles_in_shared_memory(cuda, kind, batch, epilogue, rows, k):
+    """The tensor-core GEMM on int4 weights (nibbles widened to f16 between the TMA load and the
+    MMA, random zero points, partial tiles, split k) against the oracle's per-sequence GEMV."""
+    rng = np.random.default_rng(batch * 11 + rows + k)
+    w, s, z = _int4_matrix(kind, rows, k, rng)
+    x = rng.standard_normal((batch, k)).astype(np.float32)
+    out_rows = rows // 2 if epilogue == "swiglu" else rows
+    y0 = rng.standard_normal((batch, out_rows)).astype(np.float32)
+    wd, sd, zd = dev(w.view(np.int32)), dev(s), dev(z.view(np.int32) if kind == "q4" else z)
+    m = qne.matrix(kind, rows, k, wd, sd, zd)
+    yd = dev(y0 if epilogue == "accumulate" else np.zeros((batch, out_rows), np.float32))
+    qne.gemm(m, dev(x), batch, yd, epilogue, impl="tcgen05")
+    torch.cuda.synchronize()
+    got = yd.cpu().numpy()
+    for b in range(batch):
+        want = y0[b].copy() if epilogue == "accumulate" else np.zeros(out_rows, np.float32)
+        oracle.gemv(kind, w, s, z, rows, k, x[b], want, rc.EPI[epilogue])
+        # the GEMM multiplies the f16-rounded dequantized weights (one rounding per weight)
+        assert rc.rel_err(got[b], want) < 2e-3, b
+
+
+def test_int4_gemm_rejects_the_mma_sync_kernel(cuda):
+    rng = np.random.default_rng(1)
+    w, s, z = _int4_matrix("q4g64", 256, 256, rng)
+    m = qne.matrix("q4g64", 256, 256, dev(w.view(np.int32)), dev(s), dev(z))
+    x = dev(np.zeros((4, 256), np.float32))
+    y = dev(np.zeros((4, 256), np.float32))
+    with pytest.raises(qne.QneError) as e:
+        qne.gemm(m, x, 4, y, "store", impl="mma_sync")
+    assert e.value.name == "EINVAL"
+    torch.cuda.synchronize()

@@ -153,9 +153,10 @@ def test_batched_prefill_long_context_agrees_with_per_token(cuda):
 @pytest.mark.parametrize("kind", ["q4", "q4g64"])
 @pytest.mark.parametrize("n", [20, 64, 100])
 def test_int4_batched_prefill(cuda, kind, n):
-    """int4 decoder matrices (the reference converter's block-32 layout, and group 64): each is
-    decoded to f16 by one more launch before its chunk GEMM. Logits against the oracle and against
-    the per-token path (qne_prefill), the greedy continuation, and the launch count."""
+    """int4 decoder matrices (the reference converter's block-32 layout, and group 64): the chunk
+    GEMMs widen the nibbles to f16 in shared memory (no decode launches). Logits against the
+    oracle and against the per-token path (qne_prefill), the greedy continuation, and the launch
+    count."""
     s = synth.build(1024, 3584, layers=4, vocab=4096, kind=kind, embed_kind="q4" if kind == "q4" else "f16",
                     seed=23)
     m = qne.Model(s.index_json, s.weights, any_shape=True)
@@ -169,7 +170,7 @@ def test_int4_batched_prefill(cuda, kind, n):
     m.reset()
     launches0 = qne.kernel_launches()
     m.prefill_chunk(prompt, 0, True)
-    per_chunk = 6 * m.layers + 2 + m.layers // 4 + 4 * m.layers  # + one decode launch per GEMM
+    per_chunk = 6 * m.layers + 2 + m.layers // 4  # as for f16 weights
     assert qne.kernel_launches() - launches0 == -(-n // qne.PREFILL_CHUNK_TOKENS) * per_chunk + 1
     b = m.logits().copy()
     want = om.prefill(prompt)
