@@ -442,7 +442,17 @@ def other_config_run(torch, qne, synth, cfg_n: int, rank: int, world: int, barri
     torch.cuda.set_stream(stream)
     model.set_stream(stream.cuda_stream)
     steps, prompt_len = info["steps"], info["prompt"]
-    model.prefill_chunk(synth.prompt_ids(prompt_len, rank_seed(cfg_n, rank)), 0, True)
+    prompt = synth.prompt_ids(prompt_len, rank_seed(cfg_n, rank))
+    model.prefill_chunk(prompt, 0, True)  # records the chunk graphs
+    # the prompt itself, timed (batched chunks; for int4 the tensor-core GEMMs widen the nibbles)
+    model.reset()
+    model.sync()
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record(stream)
+    model.prefill_chunk(prompt, 0, True)
+    p1.record(stream)
+    torch.cuda.synchronize()
+    prefill_ms = max_over_ranks(p0.elapsed_time(p1))
     model.snapshot()
     model.sync()
     if warmup:
@@ -475,7 +485,9 @@ def other_config_run(torch, qne, synth, cfg_n: int, rank: int, world: int, barri
             "value": round(tps, 2), "unit": "tok/s", "n_gpus": world, "ms_per_step": round(ms / steps, 4),
             "launch_path": path, "bytes_per_token": int(tok_bytes),
             "step_roofline": {"achieved_gbs": round(gbs, 1), "peak": peak, "frac": round(gbs / peak, 4),
-                              "peak_source": kind}}
+                              "peak_source": kind},
+            "prefill": {"tokens": prompt_len, "ms": round(prefill_ms, 2),
+                        "tok_per_s": round(world * prompt_len / (prefill_ms * 1e-3), 1)}}
 
 
 def batched_run(torch, qne, synth, rank: int, world: int, barrier, max_over_ranks, warmup: int,
