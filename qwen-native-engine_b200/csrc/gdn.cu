@@ -27,7 +27,11 @@ namespace {
 
 using namespace dev;
 
-__global__ void __launch_bounds__(256) gdn_step_kernel(const GdnArgs a) {
+// kPre: the constant operands are loaded before the dependency wait (one sequence: 128 CTAs, one
+// wave, latency-bound); with many sequences the kernel keeps the smaller register footprint, so
+// more CTAs stay resident per SM.
+template <bool kPre>
+__global__ void __launch_bounds__(256, kPre ? 1 : 6) gdn_step_kernel(const GdnArgs a) {
   __shared__ GdnShared sh;
   const int item = (blockIdx.z * kGdnHeads + blockIdx.y) * kSlices + blockIdx.x;
   GdnItem it;
@@ -35,6 +39,7 @@ __global__ void __launch_bounds__(256) gdn_step_kernel(const GdnArgs a) {
   // Programmatic launch only guarantees that the previous kernel has started: warm L2 with the
   // state slice, read it after the wait.
   it.warm_l2(a, item);
+  if (kPre) it.preload(a, item);
   pdl_wait();
   it.prefetch(a, item);
   it.run(a, sh);
@@ -76,7 +81,7 @@ cudaError_t launch_gdn_step(const float* proj, float* conv, const float* conv_w,
   cudaLaunchConfig_t cfg = make_cfg(dim3(dev::kSlices, kGdnHeads, batch), dim3(256), stream, pdl, attr);
   count_launch();
   const GdnArgs a{proj, conv, conv_w, state, params, counter, counter_stride, out_raw};
-  return cudaLaunchKernelEx(&cfg, gdn_step_kernel, a);
+  return batch == 1 ? cudaLaunchKernelEx(&cfg, gdn_step_kernel<true>, a) : cudaLaunchKernelEx(&cfg, gdn_step_kernel<false>, a);
 }
 
 cudaError_t launch_gdn_gate(const float* raw, const float* proj, const float* norm_w, float* out,

@@ -43,12 +43,38 @@ struct GdnItem {
   int s, h, b, t0, jg, tl;
   float* S;
   float sv[8];
+  // Operands that depend on nothing (conv weights of this thread's channels, the head's decay
+  // parameters), loaded by preload() before the dependency wait; run_with loads them itself when
+  // preload() was not called.
+  bool pre = false;
+  float4 cw, cvw;
+  float pA, pDt;
 
   // L2 warm-up of the item's state rows: a hint only, safe before any dependency wait.
   __device__ __forceinline__ void warm_l2(const GdnArgs& a, int item) const {
     const int ss = item % kSlices, hh = (item / kSlices) % kGdnHeads, bb = item / kGdnItemsPerSeq;
     const float* base = a.state + ((size_t)bb * kGdnHeads + hh) * kGdnDim * kGdnDim + ss * kSlice;
     if (threadIdx.x < kGdnDim) asm volatile("prefetch.global.L2 [%0];" ::"l"(base + (size_t)threadIdx.x * kGdnDim));
+  }
+
+  // Constant operands into registers and the item's conv window slots into L2 (a hint): safe
+  // before any dependency wait.
+  __device__ __forceinline__ void preload(const GdnArgs& a, int item) {
+    const int ss = item % kSlices, hh = (item / kSlices) % kGdnHeads, bb = item / kGdnItemsPerSeq;
+    const int tid = threadIdx.x;
+    const int ch = (tid < kGdnDim ? 0 : 2048) + hh * kGdnDim + (tid & (kGdnDim - 1));
+    const int cv = 4096 + hh * kGdnDim + ss * kSlice + (tid & (kSlice - 1));
+    cw = __ldg(reinterpret_cast<const float4*>(a.conv_w + (size_t)ch * 4));
+    cvw = tid < kSlice ? __ldg(reinterpret_cast<const float4*>(a.conv_w + (size_t)cv * 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    pA = __ldg(a.params + 16 + hh);
+    pDt = __ldg(a.params + hh);
+    const float* ring = a.conv + (size_t)bb * kConvSlots * kConvChannels;
+#pragma unroll
+    for (int r = 0; r < kConvSlots; ++r) {
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(ring + r * kConvChannels + ch));
+      if (tid < kSlice) asm volatile("prefetch.global.L2 [%0];" ::"l"(ring + r * kConvChannels + cv));
+    }
+    pre = true;
   }
 
   __device__ __forceinline__ void prefetch(const GdnArgs& a, int item) {
@@ -82,7 +108,9 @@ struct GdnItem {
     const int i = tid & (kGdnDim - 1);
     const int ch = (tid < kGdnDim ? 0 : 2048) + h * kGdnDim + i;
     const float x = pr[ch];
-    const float4 w = *reinterpret_cast<const float4*>(a.conv_w + (size_t)ch * 4);
+    // the decay and write-strength inputs of the head, with the other step inputs (one round trip)
+    const float ga = pr[8192 + h], gb = pr[8208 + h];
+    const float4 w = pre ? cw : *reinterpret_cast<const float4*>(a.conv_w + (size_t)ch * 4);
     float rv[4];
 #pragma unroll
     for (int r = 0; r < 4; ++r) rv[r] = ring[r * kConvChannels + ch];
@@ -91,7 +119,7 @@ struct GdnItem {
     const int cv = 4096 + h * kGdnDim + t0 + (tid & (kSlice - 1));
     if (tid < kSlice) {
       vx = pr[cv];
-      vw = *reinterpret_cast<const float4*>(a.conv_w + (size_t)cv * 4);
+      vw = pre ? cvw : *reinterpret_cast<const float4*>(a.conv_w + (size_t)cv * 4);
 #pragma unroll
       for (int r = 0; r < 4; ++r) vrv[r] = ring[r * kConvChannels + cv];
     }
@@ -111,6 +139,10 @@ struct GdnItem {
       sh.vs[tid] = silu(y);
       ring[slot_new * kConvChannels + cv] = vx;
     }
+    // Decay and write strength (their transcendental latency overlaps the barriers below).
+    const float pa = pre ? pA : a.params[16 + h], pd = pre ? pDt : a.params[h];
+    const float g = expf(pa * logf(1.0f + expf(ga + pd)));
+    const float beta = 1.0f / (1.0f + expf(-gb));
     // L2 norms: warps 0-3 hold q, warps 4-7 hold k.
     const float ss = warp_sum(val * val);
     if (lane == 0) sh.red[warp] = ss;
@@ -124,9 +156,6 @@ struct GdnItem {
       const float p = warp_sum(sh.ks[tid] * sh.qs[tid]);
       if (lane == 0) sh.red[warp] = p;  // red[0..3] no longer needed for nq
     }
-    // Decay and write strength.
-    const float g = expf(a.params[16 + h] * logf(1.0f + expf(pr[8192 + h] + a.params[h])));
-    const float beta = 1.0f / (1.0f + expf(-pr[8208 + h]));
     float sk = 0.f, sq = 0.f;
 #pragma unroll
     for (int jj = 0; jj < 8; ++jj) {
