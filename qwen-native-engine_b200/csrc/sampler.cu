@@ -124,11 +124,25 @@ __device__ uint32_t select_kth_largest(const uint32_t (&key)[N], const bool (&va
   return prefix;
 }
 
+template <int THREADS>
+__device__ uint32_t block_count(uint32_t v, uint32_t* red) {
+  v = __reduce_add_sync(0xffffffffu, v);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  uint32_t s = 0;
+#pragma unroll
+  for (int w = 0; w < THREADS / 32; ++w) s += red[w];
+  __syncthreads();
+  return s;
+}
+
 // Keeps the top `k` of the items (ties at the threshold by lower index): returns per item whether
-// it is kept. n_valid = number of valid items in the block.
+// it is kept. n_valid = number of valid items in the block. When every item equal to the k-th
+// largest key belongs to the top k (no tie crosses the threshold: the usual case), the second
+// selection that orders the tied items by index is skipped.
 template <int N, int THREADS>
 __device__ void keep_top_k(const uint32_t (&key)[N], const uint32_t (&idx)[N], const bool (&valid)[N], uint32_t k,
-                           uint32_t n_valid, bool (&keep)[N], uint32_t* hist, uint32_t* bc) {
+                           uint32_t n_valid, bool (&keep)[N], uint32_t* hist, uint32_t* bc, uint32_t* red) {
   if (n_valid <= k) {
 #pragma unroll
     for (int j = 0; j < N; ++j) keep[j] = valid[j];
@@ -136,6 +150,14 @@ __device__ void keep_top_k(const uint32_t (&key)[N], const uint32_t (&idx)[N], c
   }
   uint32_t ties = 0;
   const uint32_t T = select_kth_largest<N, THREADS>(key, valid, k, hist, bc, ties);
+  uint32_t ne = 0;
+#pragma unroll
+  for (int j = 0; j < N; ++j) ne += (valid[j] && key[j] == T) ? 1u : 0u;
+  if (block_count<THREADS>(ne, red) == ties) {
+#pragma unroll
+    for (int j = 0; j < N; ++j) keep[j] = valid[j] && key[j] >= T;
+    return;
+  }
   // among the items equal to T, the `ties` lowest indices: the ties-th largest of ~index
   uint32_t nidx[N];
   bool tie[N];
@@ -148,18 +170,6 @@ __device__ void keep_top_k(const uint32_t (&key)[N], const uint32_t (&idx)[N], c
   const uint32_t TI = select_kth_largest<N, THREADS>(nidx, tie, ties, hist, bc, dummy);
 #pragma unroll
   for (int j = 0; j < N; ++j) keep[j] = valid[j] && (key[j] > T || (key[j] == T && nidx[j] >= TI));
-}
-
-template <int THREADS>
-__device__ uint32_t block_count(uint32_t v, uint32_t* red) {
-  v = __reduce_add_sync(0xffffffffu, v);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
-  __syncthreads();
-  uint32_t s = 0;
-#pragma unroll
-  for (int w = 0; w < THREADS / 32; ++w) s += red[w];
-  __syncthreads();
-  return s;
 }
 
 __global__ void __launch_bounds__(kCandThreads) sample_candidates_kernel(const SampleArgs a) {
@@ -229,7 +239,7 @@ __global__ void __launch_bounds__(kCandThreads) sample_candidates_kernel(const S
   for (int j = 0; j < N; ++j) nv += valid[j] ? 1u : 0u;
   const uint32_t n_valid = block_count<kCandThreads>(nv, red);
   bool keep[N];
-  keep_top_k<N, kCandThreads>(key, idx, valid, (uint32_t)a.k, n_valid, keep, hist, bc);
+  keep_top_k<N, kCandThreads>(key, idx, valid, (uint32_t)a.k, n_valid, keep, hist, bc, red);
   if (tid == 0) cnt = 0;
   __syncthreads();
   uint32_t* ck = a.cand_key + (size_t)blockIdx.x * kMaxTopK;
@@ -245,10 +255,14 @@ __global__ void __launch_bounds__(kCandThreads) sample_candidates_kernel(const S
   if (tid == 0) a.cand_count[blockIdx.x] = cnt;
 }
 
+// N: candidate slots per thread; the slices' candidates are read compacted (slice s's kept items
+// at offsets off[s] .. off[s + 1] of one list), so N * kFinalThreads only has to cover their count.
+template <int N>
 __global__ void __launch_bounds__(kFinalThreads) sample_final_kernel(const SampleArgs a, int slices) {
-  constexpr int N = kMaxSlices * kMaxTopK / kFinalThreads;  // 32
   __shared__ uint32_t hist[256], bc[2], red[kFinalThreads / 32], cnt;
   __shared__ uint32_t sk[kMaxTopK], si[kMaxTopK], ok[kMaxTopK], oi[kMaxTopK];
+  __shared__ uint32_t off[kMaxSlices + 1];
+  __shared__ float ew[kMaxTopK];
   const int tid = threadIdx.x;
   const uint32_t fl = *a.flags;
   const uint32_t status = (fl & kFlagNonFinite) ? 1u : ((fl & kFlagFinite) ? 0u : 2u);
@@ -268,14 +282,51 @@ __global__ void __launch_bounds__(kFinalThreads) sample_final_kernel(const Sampl
       token = best_i == 0xFFFFFFFFu ? 0u : best_i;
     }
   } else {
+    // exclusive prefix of the slices' candidate counts (warp 0: 4 slices per lane)
+    static_assert(kMaxSlices == 32 * 4, "one warp scans the slice counts");
+    if (tid < 32) {
+      uint32_t c[4], sum = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int sl = tid * 4 + i;
+        c[i] = sl < slices ? a.cand_count[sl] : 0u;
+        sum += c[i];
+      }
+      uint32_t incl = sum;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (tid >= o) incl += v;
+      }
+      uint32_t run = incl - sum;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        off[tid * 4 + i] = run;
+        run += c[i];
+      }
+      if (tid == 31) off[kMaxSlices] = incl;
+    }
+    __syncthreads();
+    const uint32_t total = off[kMaxSlices];
     uint32_t key[N], idx[N];
     bool valid[N];
 #pragma unroll
     for (int j = 0; j < N; ++j) {
-      const int e = j * kFinalThreads + tid, s = e / kMaxTopK, p = e % kMaxTopK;
-      valid[j] = s < slices && (uint32_t)p < a.cand_count[s];
-      key[j] = valid[j] ? a.cand_key[e] : 0u;
-      idx[j] = valid[j] ? a.cand_idx[e] : 0u;
+      const uint32_t e = (uint32_t)(j * kFinalThreads + tid);
+      valid[j] = e < total;
+      key[j] = 0u;
+      idx[j] = 0u;
+      if (valid[j]) {
+        int lo = 0, hi = slices - 1;  // the slice holding candidate e: last s with off[s] <= e
+        while (lo < hi) {
+          const int mid = (lo + hi + 1) >> 1;
+          if (off[mid] <= e) lo = mid;
+          else hi = mid - 1;
+        }
+        const size_t q = (size_t)lo * kMaxTopK + (e - off[lo]);
+        key[j] = a.cand_key[q];
+        idx[j] = a.cand_idx[q];
+      }
     }
     uint32_t nv = 0;
 #pragma unroll
@@ -283,7 +334,7 @@ __global__ void __launch_bounds__(kFinalThreads) sample_final_kernel(const Sampl
     const uint32_t n_valid = block_count<kFinalThreads>(nv, red);
     const uint32_t k = min((uint32_t)a.k, n_valid);
     bool keep[N];
-    keep_top_k<N, kFinalThreads>(key, idx, valid, k, n_valid, keep, hist, bc);
+    keep_top_k<N, kFinalThreads>(key, idx, valid, k, n_valid, keep, hist, bc, red);
     if (tid == 0) cnt = 0;
     __syncthreads();
 #pragma unroll
@@ -303,22 +354,24 @@ __global__ void __launch_bounds__(kFinalThreads) sample_final_kernel(const Sampl
       oi[r] = si[tid];
     }
     __syncthreads();
+    // the weights exp((l - top) / T) in parallel (each value as the reference computes it)
+    if ((uint32_t)tid < n) ew[tid] = expf((key_f(ok[tid]) - key_f(ok[0])) / a.temperature);
+    __syncthreads();
     if (tid == 0 && n > 0 && status == 0) {
       // The reference's arithmetic, in its order (src/sampling.rs:105-133).
-      const float t = a.temperature, top = key_f(ok[0]);
-      float total = 0.f;
-      for (uint32_t j = 0; j < n; ++j) total += expf((key_f(ok[j]) - top) / t);
+      float wsum = 0.f;
+      for (uint32_t j = 0; j < n; ++j) wsum += ew[j];
       float kept = 0.f;
       uint32_t m = 0;
       for (uint32_t j = 0; j < n; ++j) {
-        kept += expf((key_f(ok[j]) - top) / t);
+        kept += ew[j];
         ++m;
-        if (kept >= a.top_p * total) break;
+        if (kept >= a.top_p * wsum) break;
       }
       float r = a.u * kept;
       token = oi[m - 1];
       for (uint32_t j = 0; j < m; ++j) {
-        r -= expf((key_f(ok[j]) - top) / t);
+        r -= ew[j];
         if (r <= 0.f) {
           token = oi[j];
           break;
@@ -404,7 +457,9 @@ struct Sampler {
     sample_candidates_kernel<<<slices, kCandThreads, 0, s>>>(a);
     cuda_check(cudaGetLastError(), "sampling launch");
     count_launch();
-    sample_final_kernel<<<1, kFinalThreads, 0, s>>>(a, slices);
+    // candidate slots: every slice keeps at most k; 4 per thread cover up to 4096 of them
+    if ((size_t)slices * (size_t)a.k <= 4u * kFinalThreads) sample_final_kernel<4><<<1, kFinalThreads, 0, s>>>(a, slices);
+    else sample_final_kernel<kMaxSlices * kMaxTopK / kFinalThreads><<<1, kFinalThreads, 0, s>>>(a, slices);
     cuda_check(cudaGetLastError(), "sampling launch");
     cuda_check(cudaMemcpyAsync(pinned, result, 8, cudaMemcpyDeviceToHost, s), "sampling result");
     m->sync(600000);
