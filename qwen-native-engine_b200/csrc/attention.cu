@@ -62,9 +62,11 @@ size_t attention_scratch_bytes(int batch) {
 }
 
 cudaError_t launch_attention(const AttnArgs& a, uint32_t pool_pages, int split_tokens,
-                             cudaStream_t stream, bool pdl) {
+                             cudaStream_t stream, bool pdl, int rows_per_item) {
   // A split is whole 64-token sub-blocks, and the scratch holds at most kMaxSplits of them.
   if (split_tokens < kSub || split_tokens % kSub) return cudaErrorInvalidValue;
+  if (rows_per_item != 1 && (rows_per_item != 2 || a.impl != 0 || !a.kv_appended || a.page_table_stride != 0))
+    return cudaErrorInvalidValue;
   KernelArgs ka;
   ka.a = a;
   ka.split = split_tokens;
@@ -72,12 +74,14 @@ cudaError_t launch_attention(const AttnArgs& a, uint32_t pool_pages, int split_t
   const int max_splits = (kMaxContext + split_tokens - 1) / split_tokens;
   ka.max_splits = max_splits;
   const bool tc = a.impl == 0;
-  auto kernel = tc ? attention_kernel<AttnTcItem, AttnTcShared> : attention_kernel<AttnItem, AttnShared>;
-  const size_t smem = tc ? sizeof(AttnTcShared) : sizeof(AttnShared);
+  auto kernel = rows_per_item == 2 ? attention_kernel<AttnTcItemT<2>, AttnTcSharedT<8>>
+                : tc               ? attention_kernel<AttnTcItem, AttnTcShared>
+                                   : attention_kernel<AttnItem, AttnShared>;
+  const size_t smem = rows_per_item == 2 ? sizeof(AttnTcSharedT<8>) : tc ? sizeof(AttnTcShared) : sizeof(AttnShared);
   const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(max_splits, kKvHeads, a.batch);
+  cfg.gridDim = dim3(max_splits, kKvHeads, (a.batch + rows_per_item - 1) / rows_per_item);
   cfg.blockDim = dim3(256);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;

@@ -125,9 +125,11 @@ __device__ __forceinline__ void merge_parts(const float* acc, const float* ml, i
 // o of head t / 64, dims 4 (t % 64) .. +3, and sh.run_m / run_l hold the running max and sum per
 // head -- then merges partials in two ticketed levels (groups of kGroup splits, then groups); the
 // CTA that completes the last merge applies the output gate and stores. Ends with __syncthreads.
+// col0: the first of the item's 4 columns (query heads) of sequence row b in sh.run_m / run_l
+// (items with two query rows hold them at columns 0-3 and 4-7).
 template <class SH>
 __device__ __forceinline__ void attn_merge_store(const AttnArgs& a, SH& sh, int b, int kvh, int split, int nsplit,
-                                               float4 o) {
+                                               float4 o, int col0 = 0) {
   const int t = threadIdx.x;
   const int hh = t >> 6, d0 = (t & 63) * 4;
   const float* pr = a.proj + (size_t)b * kAttnProj;
@@ -137,15 +139,15 @@ __device__ __forceinline__ void attn_merge_store(const AttnArgs& a, SH& sh, int 
   const int gsize = min(kGroup, nsplit - group * kGroup);
   float* gacc = S.gacc + (sk * kMaxGroups) * kPart;
   float* gml = S.gml + (sk * kMaxGroups) * kQPerKv * 2;
-  float L = sh.run_l[hh];
+  float L = sh.run_l[col0 + hh];
   bool done = nsplit == 1;  // a single split needs no merge
   if (!done) {
     float* pacc = S.acc + (sk * kMaxSplits + split) * kPart;
     float* pml = S.ml + (sk * kMaxSplits + split) * kQPerKv * 2;
     *reinterpret_cast<float4*>(pacc + hh * kHeadDim + d0) = o;
     if (t < kQPerKv) {
-      pml[t * 2 + 0] = sh.run_m[t];
-      pml[t * 2 + 1] = sh.run_l[t];
+      pml[t * 2 + 0] = sh.run_m[col0 + t];
+      pml[t * 2 + 1] = sh.run_l[col0 + t];
     }
     // Merge level 1: the last split of each group of 8 merges the group; level 2: the last
     // group to finish merges the groups. Each level is entered by one CTA only.
@@ -194,7 +196,7 @@ __device__ __forceinline__ void attn_merge_store(const AttnArgs& a, SH& sh, int 
 // sh.vc_s; running max / sum reset. Ends with __syncthreads.
 template <class SH>
 __device__ __forceinline__ void attn_prologue(const KernelArgs& ka, SH& sh, int b, int kvh, uint32_t pos, bool owner,
-                                              const uint32_t* pt) {
+                                              const uint32_t* pt, int col0 = 0) {
   const AttnArgs& a = ka.a;
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const float* pr = a.proj + (size_t)b * kAttnProj;
@@ -218,7 +220,7 @@ __device__ __forceinline__ void attn_prologue(const KernelArgs& ka, SH& sh, int 
       float sum = 0.f;
 #pragma unroll
       for (int w = 0; w < 8; ++w) sum += sh.red[w][hh];
-      sh.q_s[hh][t] = xq[hh] * rsqrtf(sum / (float)kHeadDim + 1e-6f) * a.norms[t];
+      sh.q_s[col0 + hh][t] = xq[hh] * rsqrtf(sum / (float)kHeadDim + 1e-6f) * a.norms[t];
     }
     if (owner) {
       float sum = 0.f;
@@ -232,21 +234,21 @@ __device__ __forceinline__ void attn_prologue(const KernelArgs& ka, SH& sh, int 
     float qr[kQPerKv];
     float kr = 0.f;
 #pragma unroll
-    for (int hh = 0; hh < kQPerKv; ++hh) qr[hh] = sh.q_s[hh][t];
+    for (int hh = 0; hh < kQPerKv; ++hh) qr[hh] = sh.q_s[col0 + hh][t];
     if (owner) kr = sh.kc_s[t];
     if (t < 2 * kRopeHalf) {
       const int i = t & (kRopeHalf - 1);
       const float c = rc[i], sn = rs[i];
 #pragma unroll
       for (int hh = 0; hh < kQPerKv; ++hh)
-        qr[hh] = (t < kRopeHalf) ? sh.q_s[hh][t] * c - sh.q_s[hh][t + kRopeHalf] * sn
-                                 : sh.q_s[hh][t] * c + sh.q_s[hh][t - kRopeHalf] * sn;
+        qr[hh] = (t < kRopeHalf) ? sh.q_s[col0 + hh][t] * c - sh.q_s[col0 + hh][t + kRopeHalf] * sn
+                                 : sh.q_s[col0 + hh][t] * c + sh.q_s[col0 + hh][t - kRopeHalf] * sn;
       if (owner)
         kr = (t < kRopeHalf) ? sh.kc_s[t] * c - sh.kc_s[t + kRopeHalf] * sn : sh.kc_s[t] * c + sh.kc_s[t - kRopeHalf] * sn;
     }
     __syncthreads();
 #pragma unroll
-    for (int hh = 0; hh < kQPerKv; ++hh) sh.q_s[hh][t] = qr[hh] * 0.0625f;  // 1/sqrt(256), exact
+    for (int hh = 0; hh < kQPerKv; ++hh) sh.q_s[col0 + hh][t] = qr[hh] * 0.0625f;  // 1/sqrt(256), exact
     if (owner) {
       // Append the current key and value, rounded to f16, and use the rounded values below.
       const uint32_t page = pt[pos / kPageTokens];
@@ -265,8 +267,8 @@ __device__ __forceinline__ void attn_prologue(const KernelArgs& ka, SH& sh, int 
       }
     }
     if (t < kQPerKv) {
-      sh.run_m[t] = -INFINITY;
-      sh.run_l[t] = 0.f;
+      sh.run_m[col0 + t] = -INFINITY;
+      sh.run_l[col0 + t] = 0.f;
     }
   }
   __syncthreads();

@@ -21,25 +21,30 @@
 namespace qne {
 namespace dev {
 
-struct AttnTcShared {
+// C = the MMA columns in use: the 4 query heads of the KV head for each of the item's query rows
+// (C = 4: one row; C = 8: two rows, the prompt path).
+template <int C>
+struct AttnTcSharedT {
   __align__(128) uint4 kst[kSub][kHeadDim / 8];  // 64 tokens x 32 chunks of 8 f16, permuted
   __align__(128) uint4 vst[kSub][kHeadDim / 8];
-  __align__(16) float q_s[kQPerKv][kHeadDim];
+  __align__(16) float q_s[C][kHeadDim];
   __align__(16) float kc_s[kHeadDim];  // the current token's key and value (f16-rounded)
   __align__(16) float vc_s[kHeadDim];
-  // Rows padded by 8 floats so the 4 heads' rows start in different banks (the PV fragment loads
-  // read the same token offset of all 4 heads at once).
-  float spart[2][kQPerKv][kSub + 8];  // scores of the two dim halves
-  float sc[kQPerKv][kSub + 8];        // probabilities of the sub-block
+  // Rows padded by 8 floats so the columns' rows start in different banks (the PV fragment loads
+  // read the same token offset of all columns at once).
+  float spart[2][C][kSub + 8];  // scores of the two dim halves
+  float sc[C][kSub + 8];        // probabilities of the sub-block
   float red[8][kQPerKv];
   float redk[8];
-  float blk_scale[kQPerKv];
-  float run_m[kQPerKv], run_l[kQPerKv];
+  float blk_scale[C];
+  float run_m[C], run_l[C];
   uint32_t flag;
-  // After the last sub-block: the output accumulator [4 heads][256 dims], in the K area.
+  // After the last sub-block: the output accumulator [C columns][256 dims], in the K area.
   __device__ __forceinline__ float* o_s() { return reinterpret_cast<float*>(&kst[0][0]); }
+  static_assert(sizeof(kst) >= C * kHeadDim * sizeof(float), "o_s aliases the K staging area");
+  static_assert(C == 4 || C == 8, "one or two query rows per item");
 };
-static_assert(sizeof(AttnTcShared::kst) >= kQPerKv * kHeadDim * sizeof(float), "o_s aliases the K staging area");
+using AttnTcShared = AttnTcSharedT<4>;
 
 __device__ __forceinline__ int swz(int row, int chunk) { return chunk ^ (row & 7); }
 
@@ -71,17 +76,24 @@ __device__ __forceinline__ void mma_attn(float* c, uint32_t a0, uint32_t a1, uin
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-struct AttnTcItem {
+// G = query rows per item (1: decode; 2: the prompt path, whose rows are consecutive positions
+// of one sequence reading one cache, kv_appended and page_table_stride 0).
+template <int G>
+struct AttnTcItemT {
+  static constexpr int kCols = 4 * G;
+  using Shared = AttnTcSharedT<kCols>;
   int split, kvh, b, len, nsplit, l0, l1;
   uint32_t pos;
   bool valid, owner;
   const uint32_t* pt;
+  uint32_t pos_r[G];   // position of each query row (pos = the largest)
+  bool rowok[G];       // row inside the batch
 
   // Stages K (kind 0) or V (kind 1) of the 64 tokens from sb and commits them as one cp.async
   // group (an empty group past the split's end). Thread t copies chunk t % 32 of rows t / 32 +
   // 8 i. Rows outside [l0, l1) and rows of an out-of-range page are zero-filled; the row of the
   // token this item appends is left to patch_current().
-  __device__ __forceinline__ void stage(const KernelArgs& ka, AttnTcShared& sh, int sb, int kind) const {
+  __device__ __forceinline__ void stage(const KernelArgs& ka, Shared& sh, int sb, int kind) const {
     const int t = threadIdx.x, c = t & 31;
     if (sb < l1) {
 #pragma unroll 1
@@ -98,7 +110,7 @@ struct AttnTcItem {
   }
 
   // Writes the appended token's f16 key and value rows into the staging area (sub-block sb).
-  __device__ __forceinline__ void patch_current(AttnTcShared& sh, int sb) const {
+  __device__ __forceinline__ void patch_current(Shared& sh, int sb) const {
     const int t = threadIdx.x;
     if (!owner || (int)pos < sb || (int)pos >= sb + kSub || t >= 64) return;
     const int r = (int)pos - sb, c = t & 31;
@@ -111,16 +123,23 @@ struct AttnTcItem {
     (t < 32 ? sh.kst : sh.vst)[r][swz(r, c)] = v;
   }
 
-  __device__ __forceinline__ void prefetch(const KernelArgs& ka, AttnTcShared& sh, int item) {
+  __device__ __forceinline__ void prefetch(const KernelArgs& ka, Shared& sh, int item) {
     const AttnArgs& a = ka.a;
     split = item % ka.max_splits;
     kvh = (item / ka.max_splits) % kKvHeads;
-    b = item / (ka.max_splits * kKvHeads);
-    pos = a.pos[(size_t)b * a.pos_stride];
-    if (pos >= (uint32_t)kMaxContext) {
-      if (a.flags && threadIdx.x == 0 && split == 0 && kvh == 0)
-        atomicOr(a.flags + (size_t)b * a.flags_stride, kFlagPosClamped);
-      pos = kMaxContext - 1;
+    b = (item / (ka.max_splits * kKvHeads)) * G;
+    pos = 0;
+#pragma unroll
+    for (int r = 0; r < G; ++r) {
+      rowok[r] = b + r < a.batch;
+      uint32_t p = rowok[r] ? a.pos[(size_t)(b + r) * a.pos_stride] : 0u;
+      if (p >= (uint32_t)kMaxContext) {
+        if (a.flags && threadIdx.x == 0 && split == 0 && kvh == 0)
+          atomicOr(a.flags + (size_t)(b + r) * a.flags_stride, kFlagPosClamped);
+        p = kMaxContext - 1;
+      }
+      pos_r[r] = p;
+      if (rowok[r] && p > pos) pos = p;
     }
     len = (int)pos + 1;
     nsplit = (len + ka.split - 1) / ka.split;
@@ -128,18 +147,31 @@ struct AttnTcItem {
     if (!valid) return;
     l0 = split * ka.split;
     l1 = min(l0 + ka.split, len);
-    owner = !a.kv_appended && (int)pos >= l0 && (int)pos < l1;
+    owner = G == 1 && !a.kv_appended && (int)pos >= l0 && (int)pos < l1;
     pt = a.page_table + (size_t)b * a.page_table_stride;
     stage(ka, sh, l0, 0);
     stage(ka, sh, l0, 1);
   }
 
-  __device__ __forceinline__ void run(const KernelArgs& ka, AttnTcShared& sh) {
+  __device__ __forceinline__ void run(const KernelArgs& ka, Shared& sh) {
     const AttnArgs& a = ka.a;
     if (!valid) return;
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const int g = lane >> 2, tq = lane & 3;
-    attn_prologue(ka, sh, b, kvh, pos, owner, pt);
+#pragma unroll 1
+    for (int r = 0; r < G; ++r) {
+      if (rowok[r]) {
+        attn_prologue(ka, sh, b + r, kvh, pos_r[r], owner && r == 0, pt, 4 * r);
+      } else {  // a row past the batch: zero query, an empty softmax, never stored
+#pragma unroll
+        for (int hh = 0; hh < kQPerKv; ++hh) sh.q_s[4 * r + hh][t] = 0.f;
+        if (t < kQPerKv) {
+          sh.run_m[4 * r + t] = -INFINITY;
+          sh.run_l[4 * r + t] = 0.f;
+        }
+        __syncthreads();
+      }
+    }
 
     // B fragments of q (head g, zero for g >= 4) for this warp's dim half: 8 k-steps, hi and lo.
     const int dh = warp >> 2, tt = warp & 3;
@@ -148,7 +180,7 @@ struct AttnTcItem {
     for (int kk = 0; kk < 8; ++kk) {
       const int d = dh * 128 + kk * 16 + 2 * tq;
       float q0 = 0.f, q1 = 0.f, q2 = 0.f, q3 = 0.f;
-      if (g < kQPerKv) {
+      if (g < kCols) {
         q0 = sh.q_s[g][d];
         q1 = sh.q_s[g][d + 1];
         q2 = sh.q_s[g][d + 8];
@@ -184,7 +216,7 @@ struct AttnTcItem {
           mma_attn(s, a0, a1, a2, a3, qh[kk][0], qh[kk][1]);
           mma_attn(s, a0, a1, a2, a3, ql[kk][0], ql[kk][1]);
         }
-        if (tq < 2) {
+        if (2 * tq < kCols) {
           sh.spart[dh][2 * tq][tt * 16 + g] = s[0];
           sh.spart[dh][2 * tq + 1][tt * 16 + g] = s[1];
           sh.spart[dh][2 * tq][tt * 16 + g + 8] = s[2];
@@ -194,31 +226,52 @@ struct AttnTcItem {
       __syncthreads();  // K(sb) is read, the score halves are visible
       stage(ka, sh, sb + kSub, 0);
       {
-        // Online softmax per head: thread (hh = t / 64, j = t % 64).
+        // Online softmax per column: thread (hh = t / 64, j = t % 64) takes token j of columns
+        // hh + 4 r (query head hh of each row r; a row's tokens end at its own position).
         const int hh = t >> 6, j = t & 63;
-        const float sval = (sb + j < l1) ? sh.spart[0][hh][j] + sh.spart[1][hh][j] : -INFINITY;
-        const float m = warp_max(sval);
-        if (lane == 0) sh.red[warp][0] = m;
-        __syncthreads();
-        if (j == 0) {
-          const float mb = fmaxf(sh.red[2 * hh][0], sh.red[2 * hh + 1][0]);
-          const float mnew = fmaxf(sh.run_m[hh], mb);
-          sh.blk_scale[hh] = (sh.run_m[hh] == -INFINITY) ? 0.f : expf(sh.run_m[hh] - mnew);
-          sh.run_m[hh] = mnew;
+        float sval[G];
+#pragma unroll
+        for (int r = 0; r < G; ++r) {
+          const int c = hh + 4 * r;
+          const int lim = G == 1 ? l1 : min(l1, (int)pos_r[r] + 1);
+          sval[r] = (rowok[r] && sb + j < lim) ? sh.spart[0][c][j] + sh.spart[1][c][j] : -INFINITY;
+          const float m = warp_max(sval[r]);
+          if (lane == 0) sh.red[warp][2 * r] = m;
         }
         __syncthreads();
-        const float p = (sval == -INFINITY) ? 0.f : expf(sval - sh.run_m[hh]);
-        sh.sc[hh][j] = p;
-        const float ps = warp_sum(p);
-        if (lane == 0) sh.red[warp][1] = ps;
+        if (j == 0) {
+#pragma unroll
+          for (int r = 0; r < G; ++r) {
+            const int c = hh + 4 * r;
+            const float mb = fmaxf(sh.red[2 * hh][2 * r], sh.red[2 * hh + 1][2 * r]);
+            const float mnew = fmaxf(sh.run_m[c], mb);
+            sh.blk_scale[c] = (sh.run_m[c] == -INFINITY) ? 0.f : expf(sh.run_m[c] - mnew);
+            sh.run_m[c] = mnew;
+          }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int r = 0; r < G; ++r) {
+          const int c = hh + 4 * r;
+          const float p = (sval[r] == -INFINITY) ? 0.f : expf(sval[r] - sh.run_m[c]);
+          sh.sc[c][j] = p;
+          const float ps = warp_sum(p);
+          if (lane == 0) sh.red[warp][2 * r + 1] = ps;
+        }
         asm volatile("cp.async.wait_group 1;" ::: "memory");  // V(sb)
         __syncthreads();
-        if (j == 0) sh.run_l[hh] = sh.run_l[hh] * sh.blk_scale[hh] + sh.red[2 * hh][1] + sh.red[2 * hh + 1][1];
+        if (j == 0) {
+#pragma unroll
+          for (int r = 0; r < G; ++r) {
+            const int c = hh + 4 * r;
+            sh.run_l[c] = sh.run_l[c] * sh.blk_scale[c] + sh.red[2 * hh][2 * r + 1] + sh.red[2 * hh + 1][2 * r + 1];
+          }
+        }
       }
       {
         // O[dim][head] (dims 32 warp .. +31) = blk_scale * O + V^T P.
         float f0 = 0.f, f1 = 0.f;
-        if (tq < 2) {
+        if (2 * tq < kCols) {
           f0 = sh.blk_scale[2 * tq];
           f1 = sh.blk_scale[2 * tq + 1];
         }
@@ -232,7 +285,7 @@ struct AttnTcItem {
 #pragma unroll
         for (int kt = 0; kt < kSub / 16; ++kt) {
           float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
-          if (g < kQPerKv) {
+          if (g < kCols) {
             p0 = sh.sc[g][kt * 16 + 2 * tq];
             p1 = sh.sc[g][kt * 16 + 2 * tq + 1];
             p2 = sh.sc[g][kt * 16 + 2 * tq + 8];
@@ -258,7 +311,7 @@ struct AttnTcItem {
     asm volatile("cp.async.wait_group 0;" ::: "memory");  // (only empty groups remain)
     __syncthreads();  // o_s reuses the K area
     float* os = sh.o_s();
-    if (tq < 2) {
+    if (2 * tq < kCols) {
 #pragma unroll
       for (int m = 0; m < 2; ++m) {
         const int d = warp * 32 + m * 16 + g;
@@ -269,10 +322,16 @@ struct AttnTcItem {
       }
     }
     __syncthreads();
-    const float4 o = *reinterpret_cast<const float4*>(os + (t >> 6) * kHeadDim + (t & 63) * 4);
-    attn_merge_store(a, sh, b, kvh, split, nsplit, o);
+#pragma unroll 1
+    for (int r = 0; r < G; ++r) {
+      const int nsplit_r = ((int)pos_r[r] + ka.split) / ka.split;  // splits of row r: ceil((pos + 1) / split)
+      if (!rowok[r] || split >= nsplit_r) continue;  // uniform across the CTA
+      const float4 o = *reinterpret_cast<const float4*>(os + (4 * r + (t >> 6)) * kHeadDim + (t & 63) * 4);
+      attn_merge_store(a, sh, b + r, kvh, split, nsplit_r, o, 4 * r);
+    }
   }
 };
+using AttnTcItem = AttnTcItemT<1>;
 
 }  // namespace dev
 }  // namespace qne

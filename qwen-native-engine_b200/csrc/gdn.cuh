@@ -41,8 +41,10 @@ struct AttnArgs {
 };
 size_t attention_scratch_bytes(int batch);
 // split_tokens: context tokens per CTA, a multiple of 64. pool_pages bounds the page ids.
+// rows_per_item 2 (prompt rows only: kv_appended, page_table_stride 0, tensor-core kernel): each CTA
+// serves two consecutive query rows, so the cached keys and values are read half as often.
 cudaError_t launch_attention(const AttnArgs& a, uint32_t pool_pages, int split_tokens,
-                             cudaStream_t stream, bool pdl);
+                             cudaStream_t stream, bool pdl, int rows_per_item = 1);
 cudaError_t launch_kv_gather(const uint16_t* kv, const uint32_t* page_table, uint32_t len,
                              uint16_t* out_k, uint16_t* out_v, cudaStream_t stream);
 // Host: fills rope[2][4096][32] with cos/sin(pos * theta^(-2i/64)) computed in double precision.

@@ -414,7 +414,8 @@ void PrefillRunner::record(int n, cudaStream_t s) {
       at.batch = n;
       at.scratch = attn_scratch;
       at.scratch_rows = kRows;  // one layout for every chunk size, so tickets stay where they were reset
-      cuda_check(launch_attention(at, r->st.pool_pages, n >= 8 ? 512 : 64, s, true), "prefill attention launch");
+      cuda_check(launch_attention(at, r->st.pool_pages, n >= 8 ? 512 : 64, s, true, n >= 2 ? 2 : 1),
+                 "prefill attention launch");
       ++cnt;
       q.mode = kPrepCopy;
     } else {
