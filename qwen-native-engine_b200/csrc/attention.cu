@@ -10,8 +10,12 @@
 // B200 design: the cache is paged (16-token f16 pages, per-sequence page tables); one CTA per
 // (context split, KV head, sequence) serves the 4 query heads of the KV head, stages its
 // split's K and V rows in shared memory with cp.async, keeps an online softmax per head, and
-// writes a partial (max, sum, 4 x 256 accumulator). The last CTA of each (sequence, KV head) to
-// finish merges the partials and applies the output gate. The default work item (attn_tc.cuh)
+// writes a partial (max, sum, 4 x 256 accumulator). The partials of each (sequence, KV head) are
+// merged in one of two ways: with one sequence whose grid is resident at once, the last 8 splits
+// each merge one 128-wide slice of the output over all splits once every split has arrived
+// (attn_spread_merge); otherwise by tickets, the last split of each group of 8 merging the group
+// and the last group merging the groups. The merger applies the output gate. The default work
+// item (attn_tc.cuh)
 // computes the scores and the PV product with mma.sync (q and the probabilities as hi + lo f16
 // halves); the CUDA-core item (attn_dev.cuh, also used by the fused layer kernels) reduces each
 // token's dot products across a warp.
@@ -39,8 +43,17 @@ __global__ void __launch_bounds__(256, 2) attention_kernel(const KernelArgs ka) 
   const int item = (blockIdx.z * kKvHeads + blockIdx.y) * ka.max_splits + blockIdx.x;
   Item it;
   pdl_launch();
-  pdl_wait();
-  it.prefetch(ka, sh, item);
+  if (!ka.a.kv_appended) {
+    // Decode: the positions, the page tables and every cached row a split stages were written
+    // before this launch's graph or stream work began (the positions advance in the step's last
+    // kernel, the page tables by host copies, and the current token's row is appended by this
+    // kernel), so the split is staged under the previous kernel's tail.
+    it.prefetch(ka, sh, item);
+    pdl_wait();
+  } else {
+    pdl_wait();  // prompt rows: the previous kernel appended the chunk's keys and values
+    it.prefetch(ka, sh, item);
+  }
   it.run(ka, sh);
 }
 
@@ -80,6 +93,16 @@ cudaError_t launch_attention(const AttnArgs& a, uint32_t pool_pages, int split_t
   const size_t smem = rows_per_item == 2 ? sizeof(AttnTcSharedT<8>) : tc ? sizeof(AttnTcShared) : sizeof(AttnShared);
   const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
+  // Spread merge for one sequence, when every CTA of the grid can be resident at once: its
+  // mergers wait for the other splits of their KV head.
+  if (a.batch == 1 && rows_per_item == 1) {
+    int dev = 0, sms = 0, occ = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess &&
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, 256, smem) == cudaSuccess)
+      ka.spread = (long)max_splits * kKvHeads <= (long)occ * sms ? 1 : 0;
+    cudaGetLastError();
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(max_splits, kKvHeads, (a.batch + rows_per_item - 1) / rows_per_item);
   cfg.blockDim = dim3(256);

@@ -65,6 +65,7 @@ struct KernelArgs {
   int split;        // tokens per item (multiple of kSub)
   int max_splits;   // items per (sequence, KV head) = ceil(4096 / split)
   uint32_t pool_pages;
+  int spread = 0;   // 1: spread merge (every CTA of the launch is resident at once; host-checked)
 };
 
 // Shared memory of one attention work item (about 71 KB, so it is dynamic shared memory).
@@ -121,18 +122,152 @@ __device__ __forceinline__ void merge_parts(const float* acc, const float* ml, i
   }
 }
 
+constexpr int kSpread = 8;                        // mergers of a spread merge
+constexpr uint64_t kMergeWaitNs = 1000000000ull;  // bound of a spread merger's wait (1 s)
+
+__device__ __forceinline__ uint64_t attn_global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ uint32_t attn_ld_acquire(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Spread merge of the partials of (sequence b, KV head kvh), entered by every split after its
+// partial is stored; used when all CTAs of the launch are resident at once (the host checks the
+// grid against the occupancy), since mergers wait for the other splits. Every split arrives on a
+// counter with a release reduction (no round trip); the last nm = min(nsplit, 8) splits are the
+// mergers: merger j waits (bounded by kMergeWaitNs; on timeout kFlagTimeout goes to the flags
+// word) until every split has arrived, then merges output slices j, j + nm, ... (slice s: head
+// s / 2, dims 128 (s % 2) .. +127) over all splits in split order -- thread (g, f) combines splits
+// g, g + 8, ... of float4 f, and the 8 groups are combined through shared memory (the V staging
+// area, free after the last sub-block) -- applies the output gate and stores. The last merger to
+// count itself out clears the counters for the next launch. Ends with __syncthreads.
+template <class SH>
+__device__ __forceinline__ void attn_spread_merge(const AttnArgs& a, SH& sh, int b, int kvh, int split, int nsplit,
+                                                  const Scratch& S, size_t sk) {
+  const int t = threadIdx.x;
+  uint32_t* arrive = S.ticket + sk;
+  uint32_t* leave = S.gticket + sk * kMaxGroups;  // group tickets are unused by this merge
+  const int nm = min(nsplit, kSpread);
+  const int j = split - (nsplit - nm);  // merger index; negative: not a merger
+  __syncthreads();  // the CTA's partial stores precede thread 0's release
+  if (t == 0) {
+    __threadfence();
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(arrive) : "memory");
+  }
+  if (j < 0) {
+    __syncthreads();  // shared memory is reused by the next item
+    return;
+  }
+  if (t == 0) {
+    const uint64_t t0 = attn_global_ns();
+    uint32_t rounds = 0;
+    while (attn_ld_acquire(arrive) < (uint32_t)nsplit) {
+      if ((++rounds & 63u) == 0u && attn_global_ns() - t0 > kMergeWaitNs) {
+        if (a.flags) atomicOr(a.flags + (size_t)b * a.flags_stride, kFlagTimeout);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  uint32_t left = 0;
+  if (t == 0) left = atomicAdd(leave, 1u);  // its value is needed only at the end
+  float* ws = reinterpret_cast<float*>(&sh.vst[0][0]);  // [8 groups][32] float4, then [8] max, [8] sum
+  float4* ws4 = reinterpret_cast<float4*>(ws);
+  const int f = t & 31, g = t >> 5;
+  const float* pr = a.proj + (size_t)b * kAttnProj;
+#pragma unroll 1
+  for (int sl = j; sl < kSpread; sl += nm) {
+    const int hs = sl >> 1, dd = (sl & 1) * 128 + 4 * f, h = kvh * kQPerKv + hs;
+    float4 gate = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (g == 0) gate = *reinterpret_cast<const float4*>(pr + 2048 + h * kHeadDim + dd);
+    float mv[8], lv[8];
+    float4 av[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int u = g + 8 * q;
+      mv[q] = -INFINITY;
+      lv[q] = 0.f;
+      av[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (u < nsplit) {
+        const float* ml = S.ml + ((sk * kMaxSplits + u) * kQPerKv + hs) * 2;
+        mv[q] = __ldcg(ml);
+        lv[q] = __ldcg(ml + 1);
+        av[q] = __ldcg(reinterpret_cast<const float4*>(S.acc + (sk * kMaxSplits + u) * kPart + hs * kHeadDim + dd));
+      }
+    }
+    float Mg = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) Mg = fmaxf(Mg, mv[q]);
+    float Lg = 0.f;
+    float4 og = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float w = (mv[q] == -INFINITY) ? 0.f : expf(mv[q] - Mg);
+      Lg = fmaf(w, lv[q], Lg);
+      og.x = fmaf(w, av[q].x, og.x);
+      og.y = fmaf(w, av[q].y, og.y);
+      og.z = fmaf(w, av[q].z, og.z);
+      og.w = fmaf(w, av[q].w, og.w);
+    }
+    ws4[g * 32 + f] = og;
+    if (f == 0) {
+      ws[1024 + g] = Mg;
+      ws[1032 + g] = Lg;
+    }
+    __syncthreads();
+    if (g == 0) {
+      float M = -INFINITY;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) M = fmaxf(M, ws[1024 + q]);
+      float L = 0.f;
+      float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float mq = ws[1024 + q];
+        const float w = (mq == -INFINITY) ? 0.f : expf(mq - M);
+        const float4 x = ws4[q * 32 + f];
+        L = fmaf(w, ws[1032 + q], L);
+        o.x = fmaf(w, x.x, o.x);
+        o.y = fmaf(w, x.y, o.y);
+        o.z = fmaf(w, x.z, o.z);
+        o.w = fmaf(w, x.w, o.w);
+      }
+      float4 r;
+      r.x = o.x / L / (1.0f + expf(-gate.x));
+      r.y = o.y / L / (1.0f + expf(-gate.y));
+      r.z = o.z / L / (1.0f + expf(-gate.z));
+      r.w = o.w / L / (1.0f + expf(-gate.w));
+      *reinterpret_cast<float4*>(a.out + (size_t)b * kMixerOut + h * kHeadDim + dd) = r;
+    }
+    __syncthreads();  // ws is rewritten by the next slice / the next item
+  }
+  if (t == 0 && left == (uint32_t)nm - 1) {  // every merger has passed its wait
+    *arrive = 0u;
+    *leave = 0u;
+  }
+}
+
 // Writes a split's partial for (sequence b, KV head kvh) -- thread t holds the unnormalized sums
 // o of head t / 64, dims 4 (t % 64) .. +3, and sh.run_m / run_l hold the running max and sum per
-// head -- then merges partials in two ticketed levels (groups of kGroup splits, then groups); the
-// CTA that completes the last merge applies the output gate and stores. Ends with __syncthreads.
+// head -- then merges partials: spread (attn_spread_merge) when the launch allows it, else in two
+// ticketed levels (groups of kGroup splits, then groups), where the CTA that completes the last
+// merge applies the output gate and stores. Ends with __syncthreads.
 // col0: the first of the item's 4 columns (query heads) of sequence row b in sh.run_m / run_l
 // (items with two query rows hold them at columns 0-3 and 4-7).
 template <class SH>
 __device__ __forceinline__ void attn_merge_store(const AttnArgs& a, SH& sh, int b, int kvh, int split, int nsplit,
-                                               float4 o, int col0 = 0) {
+                                               float4 o, int col0 = 0, bool spread = false) {
   const int t = threadIdx.x;
   const int hh = t >> 6, d0 = (t & 63) * 4;
   const float* pr = a.proj + (size_t)b * kAttnProj;
+  // The output gate, requested before the ticket round trips (only the last merger uses it).
+  const int h = kvh * kQPerKv + hh;
+  const float4 gate = *reinterpret_cast<const float4*>(pr + 2048 + h * kHeadDim + d0);
   Scratch S = carve(a.scratch, a.scratch_rows > 0 ? a.scratch_rows : a.batch);
   const size_t sk = (size_t)b * kKvHeads + kvh;  // (sequence, KV head)
   const int group = split / kGroup, ngroups = (nsplit + kGroup - 1) / kGroup;
@@ -148,6 +283,10 @@ __device__ __forceinline__ void attn_merge_store(const AttnArgs& a, SH& sh, int 
     if (t < kQPerKv) {
       pml[t * 2 + 0] = sh.run_m[col0 + t];
       pml[t * 2 + 1] = sh.run_l[col0 + t];
+    }
+    if (spread) {
+      attn_spread_merge(a, sh, b, kvh, split, nsplit, S, sk);
+      return;
     }
     // Merge level 1: the last split of each group of 8 merges the group; level 2: the last
     // group to finish merges the groups. Each level is entered by one CTA only.
@@ -179,8 +318,6 @@ __device__ __forceinline__ void attn_merge_store(const AttnArgs& a, SH& sh, int 
       }
     }
   }
-  const int h = kvh * kQPerKv + hh;
-  const float4 gate = *reinterpret_cast<const float4*>(pr + 2048 + h * kHeadDim + d0);
   float4 r;
   r.x = o.x / L / (1.0f + expf(-gate.x));
   r.y = o.y / L / (1.0f + expf(-gate.y));
@@ -190,19 +327,34 @@ __device__ __forceinline__ void attn_merge_store(const AttnArgs& a, SH& sh, int 
   __syncthreads();  // shared memory is reused by the next item
 }
 
+// The prologue's per-thread constants (thread t = dim t): q_norm[t], k_norm[t] and, for the
+// rotated dims (t < 64), the cosine and sine of the pair's angle at pos. Nothing a previous
+// kernel writes, so items load them with their staging, before the dependency wait.
+__device__ __forceinline__ float4 attn_consts(const AttnArgs& a, uint32_t pos) {
+  const int t = threadIdx.x;
+  float4 c;
+  c.x = a.norms[t];
+  c.y = a.norms[kHeadDim + t];
+  c.z = c.w = 0.f;
+  if (t < 2 * kRopeHalf) {
+    const int i = t & (kRopeHalf - 1);
+    c.z = a.rope[(size_t)pos * kRopeHalf + i];
+    c.w = a.rope[(size_t)kMaxContext * kRopeHalf + (size_t)pos * kRopeHalf + i];
+  }
+  return c;
+}
+
 // Prologue of a work item: q of the 4 heads of KV head kvh (RMSNorm with q_norm, RoPE at pos,
 // times 1/16) into sh.q_s; for the item that holds pos (owner), the current key (RMSNorm with
 // k_norm, RoPE) and value rounded to f16, appended to the cache page and kept in sh.kc_s /
-// sh.vc_s; running max / sum reset. Ends with __syncthreads.
+// sh.vc_s; running max / sum reset. cst = attn_consts(a, pos). Ends with __syncthreads.
 template <class SH>
 __device__ __forceinline__ void attn_prologue(const KernelArgs& ka, SH& sh, int b, int kvh, uint32_t pos, bool owner,
-                                              const uint32_t* pt, int col0 = 0) {
+                                              const uint32_t* pt, float4 cst, int col0 = 0) {
   const AttnArgs& a = ka.a;
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const float* pr = a.proj + (size_t)b * kAttnProj;
   // ---- q of the 4 heads (and the current k): RMSNorm, RoPE ----
-  const float* rc = a.rope + (size_t)pos * kRopeHalf;                                  // cos
-  const float* rs = a.rope + (size_t)kMaxContext * kRopeHalf + (size_t)pos * kRopeHalf;  // sin
   {
     float xq[kQPerKv];
 #pragma unroll
@@ -220,13 +372,13 @@ __device__ __forceinline__ void attn_prologue(const KernelArgs& ka, SH& sh, int 
       float sum = 0.f;
 #pragma unroll
       for (int w = 0; w < 8; ++w) sum += sh.red[w][hh];
-      sh.q_s[col0 + hh][t] = xq[hh] * rsqrtf(sum / (float)kHeadDim + 1e-6f) * a.norms[t];
+      sh.q_s[col0 + hh][t] = xq[hh] * rsqrtf(sum / (float)kHeadDim + 1e-6f) * cst.x;
     }
     if (owner) {
       float sum = 0.f;
 #pragma unroll
       for (int w = 0; w < 8; ++w) sum += sh.redk[w];
-      sh.kc_s[t] = xk * rsqrtf(sum / (float)kHeadDim + 1e-6f) * a.norms[kHeadDim + t];
+      sh.kc_s[t] = xk * rsqrtf(sum / (float)kHeadDim + 1e-6f) * cst.y;
     }
   }
   __syncthreads();
@@ -237,8 +389,7 @@ __device__ __forceinline__ void attn_prologue(const KernelArgs& ka, SH& sh, int 
     for (int hh = 0; hh < kQPerKv; ++hh) qr[hh] = sh.q_s[col0 + hh][t];
     if (owner) kr = sh.kc_s[t];
     if (t < 2 * kRopeHalf) {
-      const int i = t & (kRopeHalf - 1);
-      const float c = rc[i], sn = rs[i];
+      const float c = cst.z, sn = cst.w;
 #pragma unroll
       for (int hh = 0; hh < kQPerKv; ++hh)
         qr[hh] = (t < kRopeHalf) ? sh.q_s[col0 + hh][t] * c - sh.q_s[col0 + hh][t + kRopeHalf] * sn
@@ -285,20 +436,23 @@ struct AttnItem {
   uint32_t pos;
   bool valid, owner;
   const uint32_t* pt;
+  float4 cst;  // attn_consts at pos
 
   // Stages K (kind 0) or V (kind 1) of tokens sb + 8w .. sb + 8w + 7 (this warp's share of a
   // sub-block) and commits them as one cp.async group: one 16-byte cp.async per row and lane.
   // Tokens outside [l0, l1), the current token when this item appends it (taken from kc_s / vc_s
   // instead) and rows of an out-of-range page are zero-filled. A lane later reads only the
-  // chunks it staged itself, so a group needs no barrier beyond the lane's own wait.
+  // chunks it staged itself, so a group needs no barrier beyond the lane's own wait. The warp's
+  // 8 rows lie in one page, whose id is read once.
   __device__ __forceinline__ void stage(const KernelArgs& ka, AttnShared& sh, int sb, int kind) const {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     if (sb < l1) {
+      const uint32_t pg = pt[(sb + warp * 8) / kPageTokens];
 #pragma unroll 1
       for (int i = 0; i < 8; ++i) {
         const int t = warp * 8 + i, l = sb + t;
         uint4* d = reinterpret_cast<uint4*>(kind == 0 ? &sh.kst[t][lane * 8] : &sh.vst[t][lane * 8]);
-        const uint32_t page = (l < l1 && !(owner && l == (int)pos)) ? pt[l / kPageTokens] : 0xFFFFFFFFu;
+        const uint32_t page = (l < l1 && !(owner && l == (int)pos)) ? pg : 0xFFFFFFFFu;
         if (page < ka.pool_pages) cp_async16_attn(d, kv_row(ka.a.kv, page, kind, kvh, l % kPageTokens) + lane * 8);
         else *d = make_uint4(0u, 0u, 0u, 0u);
       }
@@ -327,6 +481,7 @@ struct AttnItem {
     l1 = min(l0 + ka.split, len);
     owner = !a.kv_appended && (int)pos >= l0 && (int)pos < l1;
     pt = a.page_table + (size_t)b * a.page_table_stride;
+    cst = attn_consts(a, pos);
     stage(ka, sh, l0, 0);
     stage(ka, sh, l0, 1);
   }
@@ -335,7 +490,7 @@ struct AttnItem {
     const AttnArgs& a = ka.a;
     if (!valid) return;
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-    attn_prologue(ka, sh, b, kvh, pos, owner, pt);
+    attn_prologue(ka, sh, b, kvh, pos, owner, pt, cst);
 
     // This lane's 8 dims of q for the 4 heads stay in registers for the whole split.
     float q[kQPerKv][8];
@@ -457,7 +612,7 @@ struct AttnItem {
       o.z += v.z;
       o.w += v.w;
     }
-    attn_merge_store(a, sh, b, kvh, split, nsplit, o);
+    attn_merge_store(a, sh, b, kvh, split, nsplit, o, 0, ka.spread != 0);
   }
 };
 

@@ -88,20 +88,34 @@ struct AttnTcItemT {
   const uint32_t* pt;
   uint32_t pos_r[G];   // position of each query row (pos = the largest)
   bool rowok[G];       // row inside the batch
+  float4 cst[G];       // attn_consts at each row's position
 
   // Stages K (kind 0) or V (kind 1) of the 64 tokens from sb and commits them as one cp.async
   // group (an empty group past the split's end). Thread t copies chunk t % 32 of rows t / 32 +
   // 8 i. Rows outside [l0, l1) and rows of an out-of-range page are zero-filled; the row of the
-  // token this item appends is left to patch_current().
+  // token this item appends is left to patch_current(). The sub-block's four page ids are read
+  // together (row t / 32 + 8 i lies in page i / 2; sb <= 4032, so the ids stay inside the
+  // 256-entry table), one round trip before the copies instead of one per row.
   __device__ __forceinline__ void stage(const KernelArgs& ka, Shared& sh, int sb, int kind) const {
+    uint32_t pg[4];
+    if (sb < l1) load_pages(sb, pg);
+    stage_pages(ka, sh, sb, kind, pg);
+  }
+  __device__ __forceinline__ void load_pages(int sb, uint32_t (&pg)[4]) const {
+    static_assert(kSub == 4 * kPageTokens, "a sub-block spans four pages");
+#pragma unroll
+    for (int p = 0; p < 4; ++p) pg[p] = pt[sb / kPageTokens + p];
+  }
+  __device__ __forceinline__ void stage_pages(const KernelArgs& ka, Shared& sh, int sb, int kind,
+                                              const uint32_t (&pg)[4]) const {
     const int t = threadIdx.x, c = t & 31;
     if (sb < l1) {
-#pragma unroll 1
+#pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int r = (t >> 5) + 8 * i, l = sb + r;
         if (owner && l == (int)pos) continue;
         uint4* d = kind == 0 ? &sh.kst[r][swz(r, c)] : &sh.vst[r][swz(r, c)];
-        const uint32_t page = l < l1 ? pt[l / kPageTokens] : 0xFFFFFFFFu;
+        const uint32_t page = l < l1 ? pg[i >> 1] : 0xFFFFFFFFu;
         if (page < ka.pool_pages) cp_async16_attn(d, kv_row(ka.a.kv, page, kind, kvh, l % kPageTokens) + c * 8);
         else *d = make_uint4(0u, 0u, 0u, 0u);
       }
@@ -128,6 +142,10 @@ struct AttnTcItemT {
     split = item % ka.max_splits;
     kvh = (item / ka.max_splits) % kKvHeads;
     b = (item / (ka.max_splits * kKvHeads)) * G;
+    // The first sub-block's page ids do not depend on the positions: requested with them.
+    pt = a.page_table + (size_t)b * a.page_table_stride;
+    uint32_t pg[4];
+    load_pages(split * ka.split, pg);
     pos = 0;
 #pragma unroll
     for (int r = 0; r < G; ++r) {
@@ -148,9 +166,10 @@ struct AttnTcItemT {
     l0 = split * ka.split;
     l1 = min(l0 + ka.split, len);
     owner = G == 1 && !a.kv_appended && (int)pos >= l0 && (int)pos < l1;
-    pt = a.page_table + (size_t)b * a.page_table_stride;
-    stage(ka, sh, l0, 0);
-    stage(ka, sh, l0, 1);
+#pragma unroll
+    for (int r = 0; r < G; ++r) cst[r] = attn_consts(a, pos_r[r]);
+    stage_pages(ka, sh, l0, 0, pg);
+    stage_pages(ka, sh, l0, 1, pg);
   }
 
   __device__ __forceinline__ void run(const KernelArgs& ka, Shared& sh) {
@@ -161,7 +180,7 @@ struct AttnTcItemT {
 #pragma unroll 1
     for (int r = 0; r < G; ++r) {
       if (rowok[r]) {
-        attn_prologue(ka, sh, b + r, kvh, pos_r[r], owner && r == 0, pt, 4 * r);
+        attn_prologue(ka, sh, b + r, kvh, pos_r[r], owner && r == 0, pt, cst[r], 4 * r);
       } else {  // a row past the batch: zero query, an empty softmax, never stored
 #pragma unroll
         for (int hh = 0; hh < kQPerKv; ++hh) sh.q_s[4 * r + hh][t] = 0.f;
@@ -327,7 +346,7 @@ struct AttnTcItemT {
       const int nsplit_r = ((int)pos_r[r] + ka.split) / ka.split;  // splits of row r: ceil((pos + 1) / split)
       if (!rowok[r] || split >= nsplit_r) continue;  // uniform across the CTA
       const float4 o = *reinterpret_cast<const float4*>(os + (4 * r + (t >> 6)) * kHeadDim + (t & 63) * 4);
-      attn_merge_store(a, sh, b + r, kvh, split, nsplit_r, o, 4 * r);
+      attn_merge_store(a, sh, b + r, kvh, split, nsplit_r, o, 4 * r, ka.spread != 0);
     }
   }
 };

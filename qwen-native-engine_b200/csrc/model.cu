@@ -874,6 +874,7 @@ size_t Model::read_phase_trace(uint64_t* out, size_t cap, size_t* ctas) {
 void Model::check_flags(uint32_t flags) {
   if (!(flags & kFlagTimeout)) return;
   cuda_check(cudaMemsetAsync(single_->barrier, 0, 64, stream()), "clear barrier");
+  cuda_check(cudaMemsetAsync(single_->attn_scratch, 0, attention_scratch_bytes(1), stream()), "clear attention tickets");
   cuda_check(cudaMemsetAsync(&single_->st.ctl->flags, 0, 4, stream()), "clear flags");
   cuda_check(cudaStreamSynchronize(stream()), "clear flags");
   throw QneError(kETimeout, "a device-side wait timed out; the token's results are invalid");
