@@ -27,19 +27,20 @@ namespace {
 
 using namespace dev;
 
-// kPre: the constant operands are loaded before the dependency wait (one sequence: 128 CTAs, one
-// wave, latency-bound); with many sequences the kernel keeps the smaller register footprint, so
-// more CTAs stay resident per SM.
+// kPre: the constant operands, the state slice and the conv window are loaded before the
+// dependency wait (one sequence: 128 CTAs, one wave, latency-bound); with many sequences the kernel
+// keeps the smaller register footprint, so more CTAs stay resident per SM.
 template <bool kPre>
 __global__ void __launch_bounds__(256, kPre ? 1 : 6) gdn_step_kernel(const GdnArgs a) {
   __shared__ GdnShared sh;
   const int item = (blockIdx.z * kGdnHeads + blockIdx.y) * kSlices + blockIdx.x;
   GdnItem it;
   pdl_launch();
-  // Programmatic launch only guarantees that the previous kernel has started: warm L2 with the
-  // state slice, read it after the wait.
-  it.warm_l2(a, item);
+  // One sequence: the constants, the state slice and the conv window go to registers before the
+  // wait (preload); with many sequences (register budget) the state slice is only warmed in L2
+  // and read after the wait.
   if (kPre) it.preload(a, item);
+  else it.warm_l2(a, item);
   pdl_wait();
   it.prefetch(a, item);
   it.run(a, sh);

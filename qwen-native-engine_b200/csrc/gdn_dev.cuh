@@ -49,6 +49,7 @@ struct GdnItem {
   bool pre = false;
   float4 cw, cvw;
   float pA, pDt;
+  float rv[4], vrv[4];  // the conv window slots of this thread's channels (preload only)
 
   // L2 warm-up of the item's state rows: a hint only, safe before any dependency wait.
   __device__ __forceinline__ void warm_l2(const GdnArgs& a, int item) const {
@@ -57,27 +58,42 @@ struct GdnItem {
     if (threadIdx.x < kGdnDim) asm volatile("prefetch.global.L2 [%0];" ::"l"(base + (size_t)threadIdx.x * kGdnDim));
   }
 
-  // Constant operands into registers and the item's conv window slots into L2 (a hint): safe
-  // before any dependency wait.
+  // Constant operands, the item's state slice and its conv window slots into registers. The
+  // state and the window were last written by this layer's step of an earlier token (an earlier
+  // graph or stream launch; the slot this step overwrites is read too and discarded), so this is
+  // safe before the dependency wait of a decode step. Not for prompt chunks.
   __device__ __forceinline__ void preload(const GdnArgs& a, int item) {
-    const int ss = item % kSlices, hh = (item / kSlices) % kGdnHeads, bb = item / kGdnItemsPerSeq;
+    geometry(a, item);
     const int tid = threadIdx.x;
-    const int ch = (tid < kGdnDim ? 0 : 2048) + hh * kGdnDim + (tid & (kGdnDim - 1));
-    const int cv = 4096 + hh * kGdnDim + ss * kSlice + (tid & (kSlice - 1));
+    const int ch = (tid < kGdnDim ? 0 : 2048) + h * kGdnDim + (tid & (kGdnDim - 1));
+    const int cv = 4096 + h * kGdnDim + s * kSlice + (tid & (kSlice - 1));
     cw = __ldg(reinterpret_cast<const float4*>(a.conv_w + (size_t)ch * 4));
     cvw = tid < kSlice ? __ldg(reinterpret_cast<const float4*>(a.conv_w + (size_t)cv * 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
-    pA = __ldg(a.params + 16 + hh);
-    pDt = __ldg(a.params + hh);
-    const float* ring = a.conv + (size_t)bb * kConvSlots * kConvChannels;
+    pA = __ldg(a.params + 16 + h);
+    pDt = __ldg(a.params + h);
+    const float* ring = a.conv + (size_t)b * kConvSlots * kConvChannels;
 #pragma unroll
     for (int r = 0; r < kConvSlots; ++r) {
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(ring + r * kConvChannels + ch));
-      if (tid < kSlice) asm volatile("prefetch.global.L2 [%0];" ::"l"(ring + r * kConvChannels + cv));
+      rv[r] = ring[r * kConvChannels + ch];
+      vrv[r] = tid < kSlice ? ring[r * kConvChannels + cv] : 0.f;
     }
+    load_state();
     pre = true;
   }
 
+  // Loads the item's state slice (after geometry) unless preload() did.
   __device__ __forceinline__ void prefetch(const GdnArgs& a, int item) {
+    if (pre) return;
+    geometry(a, item);
+    load_state();
+  }
+
+  __device__ __forceinline__ void load_state() {
+#pragma unroll
+    for (int jj = 0; jj < 8; ++jj) sv[jj] = S[(size_t)(jg * 8 + jj) * kGdnDim];
+  }
+
+  __device__ __forceinline__ void geometry(const GdnArgs& a, int item) {
     s = item % kSlices;
     h = (item / kSlices) % kGdnHeads;
     b = item / kGdnItemsPerSeq;
@@ -86,8 +102,6 @@ struct GdnItem {
     jg = tid >> 4;
     tl = tid & 15;  // state slice: column t0 + tl, rows jg*8 .. jg*8+7
     S = a.state + ((size_t)b * kGdnHeads + h) * kGdnDim * kGdnDim + t0 + tl;
-#pragma unroll
-    for (int jj = 0; jj < 8; ++jj) sv[jj] = S[(size_t)(jg * 8 + jj) * kGdnDim];
   }
 
   __device__ __forceinline__ void run(const GdnArgs& a, GdnShared& sh) { run_with(a, sh, BlockSync()); }
@@ -111,17 +125,24 @@ struct GdnItem {
     // the decay and write-strength inputs of the head, with the other step inputs (one round trip)
     const float ga = pr[8192 + h], gb = pr[8208 + h];
     const float4 w = pre ? cw : *reinterpret_cast<const float4*>(a.conv_w + (size_t)ch * 4);
-    float rv[4];
+    if (!pre) {
 #pragma unroll
-    for (int r = 0; r < 4; ++r) rv[r] = ring[r * kConvChannels + ch];
-    float vx = 0.f, vrv[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int r = 0; r < 4; ++r) rv[r] = ring[r * kConvChannels + ch];
+    }
+    float vx = 0.f;
     float4 vw = make_float4(0.f, 0.f, 0.f, 0.f);
     const int cv = 4096 + h * kGdnDim + t0 + (tid & (kSlice - 1));
+    if (!pre) {
+#pragma unroll
+      for (int r = 0; r < 4; ++r) vrv[r] = 0.f;
+    }
     if (tid < kSlice) {
       vx = pr[cv];
       vw = pre ? cvw : *reinterpret_cast<const float4*>(a.conv_w + (size_t)cv * 4);
+      if (!pre) {
 #pragma unroll
-      for (int r = 0; r < 4; ++r) vrv[r] = ring[r * kConvChannels + cv];
+        for (int r = 0; r < 4; ++r) vrv[r] = ring[r * kConvChannels + cv];
+      }
     }
     const int slot_new = (int)((cnt - 1u) & 3u);
     const int s2 = (int)((cnt - 2u) & 3u);  // previous input
