@@ -17,10 +17,14 @@
 //  * warp 1 lane 0 issues tcgen05.mma (M = 128, K = 16, f32 accumulators in tensor memory), one
 //    of width 2N per k-step over the hi and lo tiles together, and frees each stage with
 //    tcgen05.commit;
-//  * split-K runs across the CTAs of a thread-block cluster: every CTA moves its accumulator
-//    from tensor memory to shared memory, and after a cluster barrier each CTA reduces a slice of
-//    the rows over all ranks' shared memory in rank order (deterministic) and applies the
-//    epilogue (store, accumulate, or SwiGLU written as the next GEMM's hi/lo planes).
+//  * split-K runs across the CTAs of a thread-block cluster, each CTA owning a slice of the
+//    tile's output rows. Where a receive area fits beside the ring (N <= 32), every CTA stores
+//    each accumulator row from tensor memory straight into the receive area of the row's owner
+//    (st.shared::cluster, posted), and after one cluster barrier the owner sums its slice over
+//    the ranks in rank order from its own shared memory; otherwise (N = 64) every CTA moves its
+//    accumulator to its own shared memory and the owners read the other ranks' partials through
+//    the cluster window. Either way the sum is deterministic, and the owner applies the epilogue
+//    (store, accumulate, or SwiGLU written as the next GEMM's hi/lo planes).
 // No load uses cluster multicast: every CTA fetches its own tiles.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -159,6 +163,13 @@ __device__ __forceinline__ uint32_t cluster_addr(uint32_t local_addr, uint32_t r
   asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
   return remote;
 }
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, float a, float b, float c, float d) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
 // Volatile keeps the loads after the cluster barrier; callers issue the loads of all ranks
 // before the sums that consume them, so they are in flight together.
 __device__ __forceinline__ float4 ld_cluster_v4(uint32_t addr) {
@@ -202,6 +213,21 @@ __device__ __forceinline__ void split_hilo_tc(float x, __half& hi, __half& lo) {
   lo = __float2half_rn(x - __half2float(hi));
 }
 
+// Push mode (split-K partials sent to their owners' receive areas) when the receive area fits
+// beside the stage ring; the other instances read the partials through the cluster window.
+template <int N, int ST, int Q>
+__host__ __device__ constexpr int stage_bytes() {
+  return kTileA + 2 * N * kBK * 2 + (Q != kF16 ? 128 * kBK / 2 : 0);
+}
+template <int N>
+__host__ __device__ constexpr int recv_bytes() {
+  return 128 * (N + 4) * 4;
+}
+template <int N, int ST, int Q>
+__host__ __device__ constexpr bool push_mode() {
+  return ST == kTcStages && ST * stage_bytes<N, ST, Q>() + 1024 + recv_bytes<N>() + 4096 <= 232448;
+}
+
 template <int N, bool SW, int ST, int Q>
 __global__ void __launch_bounds__(Q != kF16 ? 2 * kTcThreads : kTcThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap txh,
@@ -215,8 +241,10 @@ __global__ void __launch_bounds__(Q != kF16 ? 2 * kTcThreads : kTcThreads, 1)
   constexpr int kLoadF16 = kTileA + 2 * kTileB;  // bytes of one stage's TMA loads (f16 weights)
   constexpr int kRaw = kQ ? 128 * kBK / 2 : 0;   // int4: the stage's packed nibbles (4 KB)
   constexpr int kStage = kTileA + 2 * kTileB + kRaw;
+  static_assert(kStage == stage_bytes<N, ST, Q>(), "stage layout");
   constexpr int kTmemCols = 2 * N < 32 ? 32 : 2 * N;  // accumulator columns: N of hi, then N of lo
   constexpr int kPitch = N + 4;  // partial rows in shared memory: 16-byte aligned, conflict-free v4 stores
+  constexpr bool kPush = push_mode<N, ST, Q>();  // split-K partials pushed to their owners
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(base);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -248,6 +276,9 @@ __global__ void __launch_bounds__(Q != kF16 ? 2 * kTcThreads : kTcThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
+  // Push mode: the first cluster barrier phase tells each rank that every rank has started, so
+  // its receive area may be written; arrive now, wait just before the pushes.
+  if (kPush) cluster_arrive_relaxed();
   pdl_launch();
 
   bool ok = true;
@@ -469,9 +500,17 @@ __global__ void __launch_bounds__(Q != kF16 ? 2 * kTcThreads : kTcThreads, 1)
     }
   }
 
-  // Accumulator -> shared memory (the stage ring is free once accb fired: every MMA completed,
-  // so every TMA load it consumed had landed). Thread t holds row t of the tile.
+  // Accumulator -> shared memory. Pull mode: each rank's own partial goes to its stage ring (free
+  // once accb fired: every MMA completed, so every TMA load it consumed had landed), and the
+  // owners read the other ranks' partials through the cluster window. Push mode: thread t sends
+  // row t of the tile to the receive area of the rank that owns that output row (a region of its
+  // own after the ring, so a rank still streaming is not disturbed), at [source rank][row of the
+  // owner's slice], and the owners sum in their own shared memory after one cluster barrier.
+  // Thread t holds row t of the tile.
   float* part = reinterpret_cast<float*>(base);
+  float* recv = reinterpret_cast<float*>(base + (size_t)ST * kStage);
+  const int rows_per_src = SW ? 2 * slice : slice;
+  if (kPush) cluster_wait();  // every rank has started (first barrier phase)
   if (warp < 4) {  // the tile's 128 accumulator lanes (the int4 converter warps hold none)
     float v[N];
     if (nkb > 0) {
@@ -487,11 +526,25 @@ __global__ void __launch_bounds__(Q != kF16 ? 2 * kTcThreads : kTcThreads, 1)
 #pragma unroll
       for (int c = 0; c < N; ++c) v[c] = 0.f;
     }
+    if (!ok) {
 #pragma unroll
-    for (int c = 0; c < N; c += 4)
-      *reinterpret_cast<float4*>(part + tid * kPitch + c) =
-          ok ? make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]) : make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int c = 0; c < N; ++c) v[c] = 0.f;
+    }
+    if (kPush) {
+      const int orow_t = SW ? (tid & 63) : tid;  // output row of the tile this accumulator row feeds
+      const int q = orow_t / slice;              // its owner rank
+      const int lr = (SW ? (tid >> 6) * slice : 0) + (orow_t - q * slice);
+      const uint32_t dst =
+          cluster_addr(smem_u32(recv) + (uint32_t)(((int)rank * rows_per_src + lr) * kPitch * 4), (uint32_t)q);
+#pragma unroll
+      for (int c = 0; c < N; c += 4) st_cluster_v4(dst + (uint32_t)(c * 4), v[c], v[c + 1], v[c + 2], v[c + 3]);
+    } else {
+#pragma unroll
+      for (int c = 0; c < N; c += 4)
+        *reinterpret_cast<float4*>(part + tid * kPitch + c) = make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]);
+    }
   }
+
   tc_fence_before();
   cluster_sync_all();  // every rank's partial is in its shared memory (and inv_s is visible)
 
@@ -510,11 +563,22 @@ __global__ void __launch_bounds__(Q != kF16 ? 2 * kTcThreads : kTcThreads, 1)
     }
     if (act) {
       float4 pv[kMaxCluster], pu[kMaxCluster];
+      if (kPush) {
+        const int lr = j - o0;
 #pragma unroll
-      for (int q = 0; q < kMaxCluster; ++q) {
-        if (q < nrank) {
-          pv[q] = ld_cluster_v4(cluster_addr(pbase + (uint32_t)((j * kPitch + b0) * 4), (uint32_t)q));
-          if (SW) pu[q] = ld_cluster_v4(cluster_addr(pbase + (uint32_t)(((64 + j) * kPitch + b0) * 4), (uint32_t)q));
+        for (int q = 0; q < kMaxCluster; ++q) {
+          if (q < nrank) {
+            pv[q] = *reinterpret_cast<const float4*>(recv + (size_t)((q * rows_per_src + lr) * kPitch + b0));
+            if (SW) pu[q] = *reinterpret_cast<const float4*>(recv + (size_t)((q * rows_per_src + slice + lr) * kPitch + b0));
+          }
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < kMaxCluster; ++q) {
+          if (q < nrank) {
+            pv[q] = ld_cluster_v4(cluster_addr(pbase + (uint32_t)((j * kPitch + b0) * 4), (uint32_t)q));
+            if (SW) pu[q] = ld_cluster_v4(cluster_addr(pbase + (uint32_t)(((64 + j) * kPitch + b0) * 4), (uint32_t)q));
+          }
         }
       }
 #pragma unroll
@@ -534,7 +598,7 @@ __global__ void __launch_bounds__(Q != kF16 ? 2 * kTcThreads : kTcThreads, 1)
       }
     }
   }
-  cluster_arrive();
+  if (!kPush) cluster_arrive();
 
 #pragma unroll
   for (int it = 0; it < kIt; ++it) {
@@ -589,7 +653,7 @@ __global__ void __launch_bounds__(Q != kF16 ? 2 * kTcThreads : kTcThreads, 1)
       }
     }
   }
-  cluster_wait();  // no CTA leaves while another still reads its shared memory
+  if (!kPush) cluster_wait();  // no CTA leaves while another still reads its shared memory
   if (warp == 0) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(kTmemCols) : "memory");
@@ -677,8 +741,8 @@ int max_clusters(K kernel, size_t smem, int ranks, int threads) {
 template <int N, bool SW, int ST, int Q>
 cudaError_t launch_tc(const GemmArgs& g, cudaStream_t stream, bool pdl) {
   auto kernel = gemm_tc_kernel<N, SW, ST, Q>;
-  constexpr int kStage = kTileA + 2 * N * kBK * 2 + (Q != kF16 ? 128 * kBK / 2 : 0);
-  const size_t smem = (size_t)ST * kStage + 1024;
+  constexpr int kStage = stage_bytes<N, ST, Q>();
+  const size_t smem = (size_t)ST * kStage + 1024 + (push_mode<N, ST, Q>() ? recv_bytes<N>() : 0);
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   TcArgs a;
