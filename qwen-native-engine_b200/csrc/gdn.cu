@@ -29,8 +29,8 @@ using namespace dev;
 
 // kPre: the constant operands, the state slice and the conv window are loaded before the
 // dependency wait (one sequence: 128 CTAs, one wave, latency-bound); with many sequences the kernel
-// keeps the smaller register footprint (36 registers: seven CTAs per SM), so more state slices
-// are in flight per SM.
+// keeps the smaller register footprint (32 registers, so at least seven CTAs fit per SM), so more
+// state slices are in flight per SM.
 template <bool kPre>
 __global__ void __launch_bounds__(256, kPre ? 1 : 7) gdn_step_kernel(const GdnArgs a) {
   __shared__ GdnShared sh;
