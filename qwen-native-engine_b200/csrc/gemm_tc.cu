@@ -459,15 +459,16 @@ __global__ void __launch_bounds__(Q != kF16 ? 2 * kTcThreads : kTcThreads, 1)
   // Residual values prefetched into registers during the MMAs (kIt of them per thread); at
   // N = 64 that would be 64 more registers, so there the epilogue reads them when it stores.
   constexpr int kYv = kIt <= 8 ? kIt : 1;
-  const int slice = kOutTile / nrank;
+  const int slice = kOutTile / nrank;  // a power of two (cluster sizes are)
+  const int slice_log2 = __ffs(slice) - 1;
   const int o0 = (int)rank * slice;
   const int B = a.batch;
   const int groups = (B + 3) / 4;
   const int total = slice * groups;
   auto item_of = [&](int it, int& b0, int& j) {
     const int e = it * kTcThreads + tid;
-    b0 = (e / slice) * 4;
-    j = o0 + e % slice;
+    b0 = (e >> slice_log2) * 4;
+    j = o0 + (e & (slice - 1));
     return tid < kTcThreads && e < total;  // the converter warps of the int4 instances hold no items
   };
 
@@ -532,7 +533,7 @@ __global__ void __launch_bounds__(Q != kF16 ? 2 * kTcThreads : kTcThreads, 1)
     }
     if (kPush) {
       const int orow_t = SW ? (tid & 63) : tid;  // output row of the tile this accumulator row feeds
-      const int q = orow_t / slice;              // its owner rank
+      const int q = orow_t >> slice_log2;        // its owner rank
       const int lr = (SW ? (tid >> 6) * slice : 0) + (orow_t - q * slice);
       const uint32_t dst =
           cluster_addr(smem_u32(recv) + (uint32_t)(((int)rank * rows_per_src + lr) * kPitch * 4), (uint32_t)q);
@@ -608,33 +609,40 @@ __global__ void __launch_bounds__(Q != kF16 ? 2 * kTcThreads : kTcThreads, 1)
     const int orow = tile * kOutTile + j;
     float sq[4] = {0.f, 0.f, 0.f, 0.f};
     if (act && orow < a.out_rows) {
+      // The four columns are independent: their arithmetic is unconditional, so it interleaves,
+      // and only the stores (and loads) of columns past the batch are predicated off.
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int b = b0 + i;
-        if (b >= B) break;
+        const bool in = b < B;
         float v = vv[it][i], u = SW ? uu[SW ? it : 0][i] : 0.f;
         if (a.sumsq_in) {
-          v *= inv_s[b];
-          u *= inv_s[b];
+          const float is = inv_s[b < kGemmMaxRows ? b : kGemmMaxRows - 1];
+          v *= is;
+          u *= is;
         }
         if (SW) {
           __half hi, lo;
           split_hilo_tc(silu(v) * u, hi, lo);
-          a.yh[(size_t)b * a.ldy + orow] = __half_as_ushort(hi);
-          a.yl[(size_t)b * a.ldy + orow] = __half_as_ushort(lo);
+          if (in) {
+            a.yh[(size_t)b * a.ldy + orow] = __half_as_ushort(hi);
+            a.yl[(size_t)b * a.ldy + orow] = __half_as_ushort(lo);
+          }
         } else if (a.epi == kAccumulate) {
-          const float prev = kYv == kIt ? yv[SW || kYv != kIt ? 0 : it][i] : a.y[(size_t)b * a.ldy + orow];
+          const float prev = kYv == kIt ? yv[SW || kYv != kIt ? 0 : it][i] : (in ? a.y[(size_t)b * a.ldy + orow] : 0.f);
           const float hn = prev + v;
-          a.y[(size_t)b * a.ldy + orow] = hn;
+          if (in) a.y[(size_t)b * a.ldy + orow] = hn;
           if (a.norm_w_out) {
             // producer of a folded RMSNorm: the next GEMM's planes of h * norm_w, and h^2
             __half hi, lo;
             split_hilo_tc(hn * a.norm_w_out[orow], hi, lo);
-            a.out_xh[(size_t)b * a.out_ldx + orow] = __half_as_ushort(hi);
-            a.out_xl[(size_t)b * a.out_ldx + orow] = __half_as_ushort(lo);
-            sq[i] = hn * hn;
+            if (in) {
+              a.out_xh[(size_t)b * a.out_ldx + orow] = __half_as_ushort(hi);
+              a.out_xl[(size_t)b * a.out_ldx + orow] = __half_as_ushort(lo);
+            }
+            sq[i] = in ? hn * hn : 0.f;
           }
-        } else {
+        } else if (in) {
           a.y[(size_t)b * a.ldy + orow] = v;
         }
       }
