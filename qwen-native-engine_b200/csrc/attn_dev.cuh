@@ -122,6 +122,24 @@ __device__ __forceinline__ void merge_parts(const float* acc, const float* ml, i
   }
 }
 
+// Writes the 4 merged outputs r at (row b, column col) also as f16 hi / lo planes when the
+// caller asked for them: the form the tensor-core GEMMs read their activations in, so the
+// out-projection needs no separate conversion launch.
+__device__ __forceinline__ void attn_store_planes(const AttnArgs& a, int b, int col, float4 r) {
+  if (!a.out_xh) return;
+  const float v[4] = {r.x, r.y, r.z, r.w};
+  uint16_t hi[4], lo[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const __half h = __float2half_rn(v[e]);
+    hi[e] = __half_as_ushort(h);
+    lo[e] = __half_as_ushort(__float2half_rn(v[e] - __half2float(h)));
+  }
+  const size_t o = (size_t)b * a.out_ldx + col;
+  *reinterpret_cast<uint2*>(a.out_xh + o) = make_uint2(hi[0] | ((uint32_t)hi[1] << 16), hi[2] | ((uint32_t)hi[3] << 16));
+  *reinterpret_cast<uint2*>(a.out_xl + o) = make_uint2(lo[0] | ((uint32_t)lo[1] << 16), lo[2] | ((uint32_t)lo[3] << 16));
+}
+
 constexpr int kSpread = 8;                        // mergers of a spread merge
 constexpr uint64_t kMergeWaitNs = 1000000000ull;  // bound of a spread merger's wait (1 s)
 
@@ -243,6 +261,7 @@ __device__ __forceinline__ void attn_spread_merge(const AttnArgs& a, SH& sh, int
       r.z = o.z / L / (1.0f + expf(-gate.z));
       r.w = o.w / L / (1.0f + expf(-gate.w));
       *reinterpret_cast<float4*>(a.out + (size_t)b * kMixerOut + h * kHeadDim + dd) = r;
+      attn_store_planes(a, b, h * kHeadDim + dd, r);
     }
     __syncthreads();  // ws is rewritten by the next slice / the next item
   }
@@ -324,6 +343,7 @@ __device__ __forceinline__ void attn_merge_store(const AttnArgs& a, SH& sh, int 
   r.z = o.z / L / (1.0f + expf(-gate.z));
   r.w = o.w / L / (1.0f + expf(-gate.w));
   *reinterpret_cast<float4*>(a.out + (size_t)b * kMixerOut + h * kHeadDim + d0) = r;
+  attn_store_planes(a, b, h * kHeadDim + d0, r);
   __syncthreads();  // shared memory is reused by the next item
 }
 

@@ -228,11 +228,13 @@ void BatchRunner::record(bool greedy, cudaStream_t s) {
       at.flags = &st.ctl->flags;
       at.flags_stride = 4;
       at.out = raw;
+      at.out_xh = x0h;  // the out-projection's activation planes, written by the merge itself
+      at.out_xl = x0l;
+      at.out_ldx = ldx0;
       at.batch = B;
       at.scratch = attn_scratch;
       cuda_check(launch_attention(at, pool_pages, B >= 8 ? 256 : 64, s, true), "attention launch");
       ++n;
-      q.mode = kPrepCopy;
     } else {
       cuda_check(launch_gdn_step(proj, st.conv[i], L.conv_w, st.rec[i], L.gdn_params, &st.ctl->count, 4, raw, B, s,
                                  true),
@@ -242,7 +244,7 @@ void BatchRunner::record(bool greedy, cudaStream_t s) {
       q.zgate = proj;
       q.norm_w = L.gdn_params + 32;
     }
-    prep(q);
+    if (!L.attention) prep(q);
     gemm(L.out, x0h, x0l, ldx0, kAccumulate, h, nullptr, nullptr, c.hidden, L.post_norm, false);
     gemm(L.gate_up, xnh, xnl, c.hidden, kSwiGlu, nullptr, x1h, x1l, c.inter, nullptr, true);
     const float* next_norm = i + 1 < c.layers ? M.layers[i + 1].input_norm : M.final_norm;

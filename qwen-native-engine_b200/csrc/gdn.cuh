@@ -32,6 +32,11 @@ struct AttnArgs {
   uint32_t* flags = nullptr;    // optional: kFlagPosClamped is or-ed in when pos >= 4096
   int flags_stride = 1;
   float* out = nullptr;         // [batch][2048]
+  // Optional: the merged output also as hi = f16(v), lo = f16(v - hi) planes [batch][out_ldx]
+  // (the next tensor-core GEMM's activations), so no separate conversion launch is needed.
+  uint16_t* out_xh = nullptr;
+  uint16_t* out_xl = nullptr;
+  int out_ldx = 0;
   int batch = 1;
   void* scratch = nullptr;
   int page_table_stride = kPagesPerSeq;  // 0: every row reads one sequence's page table (prefill)

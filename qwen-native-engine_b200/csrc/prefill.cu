@@ -411,13 +411,15 @@ void PrefillRunner::record(int n, cudaStream_t s) {
       at.flags = &r->st.ctl->flags;
       at.flags_stride = 0;
       at.out = raw;
+      at.out_xh = x0h;  // the out-projection's activation planes, written by the merge itself
+      at.out_xl = x0l;
+      at.out_ldx = ldx0;
       at.batch = n;
       at.scratch = attn_scratch;
       at.scratch_rows = kRows;  // one layout for every chunk size, so tickets stay where they were reset
       cuda_check(launch_attention(at, r->st.pool_pages, n >= 8 ? 512 : 64, s, true, n >= 2 ? 2 : 1),
                  "prefill attention launch");
       ++cnt;
-      q.mode = kPrepCopy;
     } else {
       const ScanArgs sa{proj, r->st.conv[i], L.conv_w, r->st.rec[i], L.gdn_params, r->st.ctl, n, raw, conv_tail};
       cudaLaunchConfig_t cfg = make_cfg(dim3(kSlices, kGdnHeads), dim3(kScanThreads), s, true, attr);
@@ -433,7 +435,7 @@ void PrefillRunner::record(int n, cudaStream_t s) {
       q.conv_ctl = r->st.ctl;
       q.conv_n = n;
     }
-    prep(q);
+    if (!L.attention) prep(q);
     gemm(L.out, x0h, x0l, ldx0, kAccumulate, h, nullptr, nullptr, c.hidden, L.post_norm, false);
     gemm(L.gate_up, xnh, xnl, c.hidden, kSwiGlu, nullptr, x1h, x1l, c.inter, nullptr, true);
     // the next layer's input norm (after the last layer the B = 1 LM head normalizes h itself)

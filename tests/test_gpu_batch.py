@@ -112,7 +112,8 @@ def test_int4_batched_decode_matches_oracle(cuda, kind):
     for t in range(L):
         launches0 = qne.kernel_launches()
         nxt, lg = bt.step(prompts[:, t], np.full(B, t), want_logits=True)
-        assert qne.kernel_launches() - launches0 == 6 * m.layers + 3  # no decode-to-f16 launches
+        # no decode-to-f16 launches; the attention layers' merge writes the out-projection's planes
+        assert qne.kernel_launches() - launches0 == 6 * m.layers + 3 - m.layers // 4
     ids = [nxt.copy()]
     cur = nxt.copy()
     for i in range(steps):
