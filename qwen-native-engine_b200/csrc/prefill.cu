@@ -14,8 +14,10 @@
 //
 // Numerics follow the per-token kernels: the GDN scan and the key normalization repeat the
 // decode kernels' arithmetic per token; the GEMMs accumulate in f32 from f16 weights and hi/lo
-// f16 activations (the batched decode GEMM). int4 decoder matrices are decoded to f16 (one
-// rounding of each dequantized weight) by one more launch before each GEMM.
+// f16 activations (the batched decode GEMM). int4 decoder matrices feed the int4 tcgen05 GEMM,
+// which widens the nibbles to f16 in shared memory (one rounding of each dequantized weight, the
+// value the per-token kernels use); shapes it does not take are decoded to f16 by one more launch
+// before the GEMM.
 #include <algorithm>
 #include <string>
 
